@@ -1,0 +1,403 @@
+#!/usr/bin/env python
+"""Benchmark of the K-quant x @ W^T hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the Q6_K vocab-head GEMV, M=1, K=2560,
+N=151936 -- 319 MB of quantized weights, larger than L2, so every timed step
+streams the weights from HBM.  A step is one pass of the hot path: Q8_K
+quantization of x then the GEMV.  At N>1 GPUs the rows are sharded N/P per
+rank and the fp32 logits are all-gathered over NVLink (NCCL); total work is
+fixed (strong scaling).  Time is measured on the device with CUDA events,
+max over ranks.
+
+`--impl reference` times the reference's CPU implementation of the same
+workload (the C restatement of its AVX2 kernels under oracle/, all host
+threads); under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qwen3.5sharp_b200"))
+
+METRIC = "K-quant GEMV HBM GB/s (frac of 8 TB/s); M=512 GEMM TFLOP/s; 1/2/4/8 GPU"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+CFG = dict(qtype=14, m=1, k=2560, n=151936, seed_w=1, seed_x=2)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.tmp.flush()
+        self.tmp.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.tmp.read())) if len(r) >= 9]
+        os.unlink(self.tmp.name)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def traffic_from_profile():
+    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "gemv_q6k_vocab_m1.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(w_blocks, x, budget_s: float = 10.0):
+    """The reference's CPU GEMV (C restatement of its AVX2 kernels, oracle/)
+    on the full workload, with the reference's default worker count
+    (CpuTopology.ChooseWorkerCount) and with all host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    from q35k import synth
+
+    oracle.build()
+    topo = oracle.host_topology()
+    W = oracle.Weight(CFG["qtype"], w_blocks, CFG["k"], w_blocks.shape[0])
+    nbytes = synth.algorithmic_bytes(CFG["qtype"], CFG["m"], CFG["k"], w_blocks.shape[0])
+    out = {}
+    for label, threads in (("reference_workers", topo["reference_workers"]), ("all_threads", topo["logical"])):
+        W.matmul(x, threads=threads)  # warm-up (page-in, pool start)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            W.matmul(x, threads=threads)
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s / 2 or n >= 200:
+                break
+        out[label] = dict(value=nbytes / (el / n) / 1e9, cores=threads, calls=n, seconds=el)
+    return out, topo
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    from q35k import synth
+
+    oracle.build()
+    topo = oracle.host_topology()
+    threads = topo["logical"]
+    w = synth.kquant_blocks(CFG["qtype"], CFG["n"], CFG["k"], seed=CFG["seed_w"])
+    x = synth.activations(CFG["m"], CFG["k"], seed=CFG["seed_x"])
+    W = oracle.Weight(CFG["qtype"], w, CFG["k"], CFG["n"])
+    nbytes = synth.algorithmic_bytes(CFG["qtype"], CFG["m"], CFG["k"], CFG["n"])
+    for _ in range(args.warmup):
+        W.matmul(x, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        W.matmul(x, threads=threads)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = nbytes / (ms / 1e3) / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": 1,
+                   "k": 2560, "n": 151936, "l2": "inputs > L2 (319 MB of weights)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "full cfg1 GEMV per step (Q8K.QuantizeRow + Q6K.GemvPrequant over all "
+                                   "151936 rows), C restatement of the reference's AVX2 kernels, "
+                                   f"static row partition over {threads} threads"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "host": topo,
+    }
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import q35k
+    from q35k import synth
+
+    rank, world, local = dist_env()
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    peaks, peak_kind = load_peaks()
+    qt, M, K, N = CFG["qtype"], CFG["m"], CFG["k"], CFG["n"]
+    assert N % world == 0
+    rows = N // world
+    r0 = rank * rows
+    w = synth.kquant_blocks(qt, rows, K, seed=CFG["seed_w"], row_start=r0)
+    x = synth.activations(M, K, seed=CFG["seed_x"])
+
+    ctx = q35k.Context(local)
+    W = ctx.upload(qt, w, K, rows)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    dx = torch.from_numpy(x).cuda()
+    dq8 = torch.empty(M * (K // 256) * 292, dtype=torch.uint8, device="cuda")
+    dy_full = torch.empty((world, M, rows), dtype=torch.float32, device="cuda")
+    dy = dy_full[rank] if world > 1 else dy_full[0]
+    dy_local = torch.empty((M, rows), dtype=torch.float32, device="cuda") if world > 1 else dy
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        ctx.quantize_q8k_dev(dx, dq8, K, M, sh)
+        if ev:
+            ev[1].record(stream)
+        ctx.matmul_q8k_dev(W, dq8, dy_local, M, sh)
+        if ev:
+            ev[2].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(dy_full, dy_local)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = start.elapsed_time(end)
+    gemv_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    quant_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    ms_step = total_ms / args.steps
+    if world > 1:
+        t = torch.tensor([ms_step], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+
+    nbytes_total = synth.algorithmic_bytes(qt, M, K, N)
+    nbytes_local = synth.algorithmic_bytes(qt, M, K, rows)
+    value = nbytes_total / (ms_step / 1e3) / 1e9
+
+    # End to end through the public host-pointer API (q35k_matmul): x from
+    # host memory, y back to host memory, every step.
+    e2e = None
+    if world == 1:
+        for _ in range(3):
+            ctx.matmul(W, x)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            y_host = ctx.matmul(W, x)
+        e2e_s = (time.perf_counter() - t0) / args.steps
+        e2e = {"value": nbytes_total / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
+               "d2h_bytes_per_step": int(y_host.nbytes), "ms_per_step": e2e_s * 1e3,
+               "api": "q35k_matmul (host pointers, synchronous)"}
+    else:
+        xh = torch.from_numpy(x).pin_memory()
+        yh = torch.empty((world, M, rows), dtype=torch.float32).pin_memory()
+        for _ in range(3):
+            dx.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(dy_full, non_blocking=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            dx.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(dy_full, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        e2e = {"value": nbytes_total / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
+               "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": e2e_ms,
+               "api": "pinned H2D of x + q35k_quantize_q8k_dev + q35k_matmul_q8k_dev + NCCL all-gather + D2H of y"}
+
+    gemv_avg = sum(gemv_ms) / len(gemv_ms)
+    achieved = nbytes_local / (gemv_avg / 1e3) / 1e9
+    traffic = traffic_from_profile() if world == 1 else None
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
+                "kernel": "gemv_kernel<Q6_K,1>", "kernel_ms": gemv_avg,
+                "algorithmic_bytes_per_launch": nbytes_local}
+
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra = secondary_configs(ctx, torch, np, synth, peaks)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        w_full = w  # world == 1: the full matrix
+        res, topo = cpu_baseline(w_full, x)
+        ref = res["reference_workers"]
+        cpu = {"value": ref["value"], "unit": "GB/s", "cores": ref["cores"], "kind": "port",
+               "sample": f"{ref['calls']} full cfg1 GEMV calls ({ref['seconds']:.1f} s), C restatement of the "
+                         f"reference's AVX2 Q6K.Gemv, reference worker count {ref['cores']}",
+               "all_threads": res["all_threads"], "host": topo}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": M,
+                       "k": K, "n": N, "rows_per_gpu": rows, "l2": "inputs > L2 (319 MB of weights)",
+                       "parallelism": f"row-sharded N/{world} + NCCL all-gather" if world > 1 else "single GPU"},
+            "frac_of_nominal_8tbs": value / NOMINAL_HBM_GBS,
+            "quantize_ms": sum(quant_ms) / len(quant_ms), "gemv_ms": gemv_avg,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": 2 * args.steps, "also": extra,
+        }
+        print(json.dumps(line))
+    W.free()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def secondary_configs(ctx, torch, np, synth, peaks):
+    """Kernel-only numbers for the other configs (parity-tested shapes), with
+    an L2 flush between timed launches since they fit in L2."""
+    out = {}
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    cases = [("cfg0_q4k_m1", 12, 1, 2560, 9728, 1.0), ("cfg2_q5k_m8", 13, 8, 9728, 2560, 0.5),
+             ("cfg4_q4k_m1_p1", 12, 1, 5120, 27648, 1.0), ("cfg4_q4k_m8_p1", 12, 8, 5120, 27648, 1.0)]
+    for name, qt, m, k, n, scale in cases:
+        w = synth.kquant_blocks(qt, n, k, seed=1)
+        x = synth.activations(m, k, seed=2, scale=scale)
+        W = ctx.upload(qt, w, k, n)
+        dx = torch.from_numpy(x).cuda()
+        dq8 = torch.empty(m * (k // 256) * 292, dtype=torch.uint8, device="cuda")
+        dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        ctx.quantize_q8k_dev(dx, dq8, k, m, sh)
+        times = []
+        for i in range(23):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ctx.matmul_q8k_dev(W, dq8, dy, m, sh)
+            b.record(stream)
+            if i >= 3:
+                times.append((a, b))
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in times)
+        nbytes = synth.algorithmic_bytes(qt, m, k, n)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"gemv_ms": ms, "GB/s": gbs, "frac_measured_hbm": gbs / peaks["hbm_gbs"],
+                     "frac_nominal_8tbs": gbs / NOMINAL_HBM_GBS, "l2": "flushed before each launch"}
+        W.free()
+    del flush
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the secondary configs")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+/*
+ * q35k.h -- C ABI of libq35k, the B200 (sm_100a) implementation of the
+ * Qwen35Sharp quantized y = x @ W^T path for GGUF Q4_K, Q5_K and Q6_K weights.
+ *
+ * Each entry point replaces one reference kernel entry point the model
+ * forward pass calls (reference paths are relative to the DracoUnion/
+ * Qwen3.5Sharp tree; "Kernels/" = src/Qwen35Sharp.Kernels/, "Model/" =
+ * src/Qwen35Sharp.Model/).  The C# binding a maintainer adds is in
+ * INTEGRATION.md.
+ *
+ * Conventions (mirroring the reference's, Model/Qwen35Model.Decode.cs:13-112):
+ *   - Matrices are row-major: x is [tokens][n_in] fp32, y is [tokens][n_out]
+ *     fp32; weights are GGUF rows of n_in/256 super-blocks (dim0 innermost).
+ *   - n_in must be a multiple of 256 (Model/Qwen35Model.cs:480-481).
+ *   - Host-pointer calls are synchronous: y is complete on return.  The
+ *     `_dev` variants take device pointers and a cudaStream_t (as void*) and
+ *     are asynchronous on that stream.
+ *   - One context per caller thread.  Calls on one context must not overlap
+ *     on the GPU (the context's split-K scratch is shared), exactly as the
+ *     reference's CpuThreadPool/ScratchArena pair is not re-entrant.
+ *   - Every call returns a status; q35k_last_error() describes the last
+ *     failure.  The C# shim maps statuses to the exception types the
+ *     reference throws.
+ *   - There is no CPU fallback: a context cannot be created without an
+ *     sm_100 device.
+ */
+#ifndef Q35K_H
+#define Q35K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define Q35K_OK 0
+#define Q35K_EINVAL 1   /* bad argument           -> ArgumentException */
+#define Q35K_ENOTSUP 2  /* unsupported type/shape -> NotSupportedException */
+#define Q35K_ENOMEM 3   /* device/host allocation -> InsufficientMemoryException */
+#define Q35K_ECUDA 4    /* CUDA runtime error     -> InvalidOperationException */
+#define Q35K_ETIMEOUT 5 /* a bounded device wait expired -> TimeoutException */
+#define Q35K_ENCCL 6    /* NCCL error             -> InvalidOperationException */
+
+/* GGML tensor type codes (src/Qwen35Sharp.Gguf/GgmlTensorType.cs). */
+#define Q35K_TYPE_Q4_K 12
+#define Q35K_TYPE_Q5_K 13
+#define Q35K_TYPE_Q6_K 14
+
+/* Wire sizes (Kernels/BlockLayout.cs:8-29). */
+#define Q35K_QK 256
+#define Q35K_Q4K_BYTES 144
+#define Q35K_Q5K_BYTES 176
+#define Q35K_Q6K_BYTES 210
+#define Q35K_Q8K_BYTES 292
+
+typedef struct q35k_ctx q35k_ctx;
+typedef struct q35k_weight q35k_weight;
+
+/* ---- Context ----------------------------------------------------------- */
+
+/* Create a context on CUDA device `device` (must be sm_100).  Replaces the
+ * reference's per-model CpuThreadPool + ScratchArena pair
+ * (Kernels/CpuThreadPool.cs:25-44, Kernels/ScratchArena.cs:7-47). */
+int q35k_create(int device, q35k_ctx** out);
+int q35k_destroy(q35k_ctx* ctx);
+/* Message of the last failure on this context (never NULL). */
+const char* q35k_last_error(const q35k_ctx* ctx);
+/* Library version string. */
+const char* q35k_version(void);
+/* Wait for the context's stream and report any device-side error word
+ * (a bounded wait that expired inside a kernel). */
+int q35k_sync(q35k_ctx* ctx);
+
+/* ---- Weights (Model/Qwen35Model.cs:463-565, LoadWeights) --------------- */
+
+/* Upload n_out rows of GGUF blocks of type ggml_type from host memory, once
+ * per tensor; the handle owns the device copy (re-laid out for the kernels;
+ * the block bytes are unchanged).  Replaces the load-time copy + repack
+ * (Model/Qwen35Model.cs:498-524, Kernels/RepackQ4K.cs:71-130). */
+int q35k_weight_upload(q35k_ctx* ctx, int ggml_type, const void* blocks, int n_in, int n_out,
+                       q35k_weight** out);
+int q35k_weight_free(q35k_ctx* ctx, q35k_weight* w);
+int q35k_weight_info(const q35k_weight* w, int* ggml_type, int* n_in, int* n_out, size_t* device_bytes);
+
+/* ---- Matmul ------------------------------------------------------------ */
+
+/* y[tokens][n_out] = x[tokens][n_in] @ W^T with the reference's arithmetic:
+ * x rows are quantized to Q8_K, per-super-block integer dots are scaled by the
+ * fp16 block scales.  Host pointers, synchronous.  Replaces
+ *   Linear       (Model/Qwen35Model.Decode.cs:22-52)  -> MulMatQ4K.Gemm
+ *                (Kernels/MulMatQ4K.cs:45-127), Q5K.Gemm (Kernels/Q5K.cs:114-118),
+ *                Q6K.Gemm (Kernels/Q6K.cs:317-353);
+ *   DecodeLinear (Model/Qwen35Model.Decode.cs:59-87)  -> MulMatQ4K.Gemv
+ *                (Kernels/MulMatQ4K.cs:12-26), Q5K.Gemv (Kernels/Q5K.cs:89-95),
+ *                Q6K.Gemv (Kernels/Q6K.cs:301-315). */
+int q35k_matmul(q35k_ctx* ctx, const q35k_weight* w, const float* x, float* y, int tokens);
+
+/* Same with `tokens` caller-quantized Q8_K rows (BlockQ8K, 292 bytes per 256
+ * values, Kernels/BlockLayout.cs:41-46).  Replaces GemvPrequant
+ * (Model/Qwen35Model.Decode.cs:89-112) -> MulMatQ4K.GemvPrequant
+ * (Kernels/MulMatQ4K.cs:28-43), Q5K.GemvPrequant (Kernels/Q5K.cs:97-112),
+ * Q6K.GemvPrequant (Kernels/Q6K.cs:415-430). */
+int q35k_matmul_q8k(q35k_ctx* ctx, const q35k_weight* w, const void* q8k, float* y, int tokens);
+
+/* Device-pointer variants of the two calls above, asynchronous on `stream`
+ * (a cudaStream_t; NULL = the context's own stream). */
+int q35k_matmul_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_x, float* d_y, int tokens,
+                    void* stream);
+int q35k_matmul_q8k_dev(q35k_ctx* ctx, const q35k_weight* w, const void* d_q8k, float* d_y, int tokens,
+                        void* stream);
+
+/* ---- Utilities ---------------------------------------------------------- */
+
+/* Q8K.QuantizeRow (Kernels/Q8K.cs:12-77) on `rows` rows of k floats:
+ * bit-exact BlockQ8K bytes (rows * k/256 * 292). */
+int q35k_quantize_q8k(q35k_ctx* ctx, const float* x, void* q8k, int k, int rows);
+int q35k_quantize_q8k_dev(q35k_ctx* ctx, const float* d_x, void* d_q8k, int k, int rows, void* stream);
+
+/* Q4K/Q5K/Q6K.DequantizeRow (Kernels/Q4K.cs:35-60, Kernels/Q5K.cs:5-35,
+ * Kernels/Q6K.cs:9-39) on `rows` rows of k values: bit-exact fp32. */
+int q35k_dequantize(q35k_ctx* ctx, int ggml_type, const void* blocks, float* y, int k, int rows);
+int q35k_dequantize_dev(q35k_ctx* ctx, int ggml_type, const void* d_blocks, float* d_y, int k, int rows,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,417 @@
+// api.cu -- the C ABI of libq35k (include/q35k.h): contexts, weight upload,
+// matmul dispatch, utilities.  All compute runs in the CUDA kernels of this
+// library; there is no CPU fallback.
+#include "../../include/q35k.h"
+#include "device_common.cuh"
+#include "kernels.h"
+#include "api_internal.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+using namespace q35k;
+
+namespace q35k {
+void configure_gemv_kernels();
+}
+
+int q35k_ctx::fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    err = buf;
+    return code;
+}
+
+int q35k_ctx::cuda_fail(cudaError_t e, const char* what) {
+    return fail(Q35K_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int q35k_ctx::ensure_dev(void** p, size_t* cap, size_t bytes, bool zero) {
+    if (bytes <= *cap) return Q35K_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    size_t want = std::max(bytes, (size_t)256);
+    cudaError_t e = cudaMalloc(p, want);
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        cudaGetLastError();
+        return fail(Q35K_ENOMEM, "cudaMalloc(%zu) failed: %s", want, cudaGetErrorString(e));
+    }
+    if (zero) {
+        e = cudaMemset(*p, 0, want);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset");
+    }
+    *cap = want;
+    return Q35K_OK;
+}
+
+int q35k_ctx::ensure_host(void** p, size_t* cap, size_t bytes) {
+    if (bytes <= *cap) return Q35K_OK;
+    if (*p) cudaFreeHost(*p);
+    *p = nullptr;
+    *cap = 0;
+    size_t want = std::max(bytes, (size_t)4096);
+    cudaError_t e = cudaMallocHost(p, want);
+    if (e != cudaSuccess) {
+        *p = nullptr;
+        cudaGetLastError();
+        return fail(Q35K_ENOMEM, "cudaMallocHost(%zu) failed: %s", want, cudaGetErrorString(e));
+    }
+    *cap = want;
+    return Q35K_OK;
+}
+
+int q35k_ctx::check_device_error() {
+    unsigned word = 0;
+    cudaError_t e = cudaMemcpy(&word, d_err, sizeof word, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+    if (word) return on_device_error(word);
+    return Q35K_OK;
+}
+
+int q35k_ctx::on_device_error(unsigned word) {
+    // Reset the error word and the split-K arrival counters (a CTA that gave
+    // up may have left a counter non-zero).
+    cudaMemset(d_err, 0, sizeof(unsigned));
+    if (d_counters) cudaMemset(d_counters, 0, counters_cap);
+    cudaDeviceSynchronize();
+    return fail(Q35K_ETIMEOUT, "a bounded device wait expired inside a kernel (error word 0x%x)", word);
+}
+
+static bool valid_type(int t) { return t == Q35K_TYPE_Q4_K || t == Q35K_TYPE_Q5_K || t == Q35K_TYPE_Q6_K; }
+
+static thread_local std::string g_create_error;
+
+extern "C" {
+
+const char* q35k_version(void) { return "q35k 0.1 (sm_100a)"; }
+
+int q35k_create(int device, q35k_ctx** out) {
+    if (!out) return Q35K_EINVAL;
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        g_create_error = "no CUDA device is visible (libq35k has no CPU fallback)";
+        cudaGetLastError();
+        return Q35K_ECUDA;
+    }
+    if (device < 0 || device >= count) {
+        g_create_error = "device index out of range";
+        return Q35K_EINVAL;
+    }
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) {
+        g_create_error = cudaGetErrorString(e);
+        return Q35K_ECUDA;
+    }
+    if (prop.major != 10) {
+        g_create_error = "libq35k is built for sm_100a (B200); device is sm_" + std::to_string(prop.major) +
+                         std::to_string(prop.minor);
+        return Q35K_ENOTSUP;
+    }
+    if ((e = cudaSetDevice(device)) != cudaSuccess) {
+        g_create_error = cudaGetErrorString(e);
+        return Q35K_ECUDA;
+    }
+    q35k_ctx* c = new (std::nothrow) q35k_ctx();
+    if (!c) return Q35K_ENOMEM;
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaMalloc(&c->d_err, sizeof(unsigned))) != cudaSuccess ||
+        (e = cudaMemset(c->d_err, 0, sizeof(unsigned))) != cudaSuccess) {
+        g_create_error = cudaGetErrorString(e);
+        delete c;
+        return Q35K_ECUDA;
+    }
+    configure_gemv_kernels();
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+        g_create_error = std::string("kernel configuration: ") + cudaGetErrorString(e);
+        delete c;
+        return Q35K_ECUDA;
+    }
+    *out = c;
+    return Q35K_OK;
+}
+
+int q35k_destroy(q35k_ctx* c) {
+    if (!c) return Q35K_OK;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    delete c;
+    return Q35K_OK;
+}
+
+const char* q35k_last_error(const q35k_ctx* c) {
+    if (!c) return g_create_error.c_str();
+    return c->err.c_str();
+}
+
+int q35k_sync(q35k_ctx* c) {
+    if (!c) return Q35K_EINVAL;
+    cudaSetDevice(c->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return c->cuda_fail(e, "cudaDeviceSynchronize");
+    return c->check_device_error();
+}
+
+int q35k_weight_upload(q35k_ctx* c, int type, const void* blocks, int n_in, int n_out, q35k_weight** out) {
+    if (!c || !out) return Q35K_EINVAL;
+    *out = nullptr;
+    if (!valid_type(type)) return c->fail(Q35K_ENOTSUP, "ggml type %d is not a K-quant weight (12, 13, 14)", type);
+    if (!blocks) return c->fail(Q35K_EINVAL, "blocks is NULL");
+    if (n_in <= 0 || n_in % QK != 0) return c->fail(Q35K_ENOTSUP, "nIn=%d is not a multiple of 256", n_in);
+    if (n_out <= 0) return c->fail(Q35K_EINVAL, "nOut must be positive");
+    cudaSetDevice(c->device);
+    const int nb = n_in / QK, bb = block_bytes(type);
+    const int n_pad = (n_out + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
+    const size_t raw_bytes = (size_t)n_out * nb * bb;
+    const size_t tile_bytes = (size_t)n_pad * nb * bb;
+    q35k_weight* w = new (std::nothrow) q35k_weight();
+    if (!w) return Q35K_ENOMEM;
+    w->type = type;
+    w->n_in = n_in;
+    w->n_out = n_out;
+    w->nb = nb;
+    w->n_pad = n_pad;
+    w->device = c->device;
+    w->bytes = tile_bytes;
+    uint8_t* raw = nullptr;
+    cudaError_t e = cudaMalloc(&w->tiles, tile_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&raw, raw_bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (w->tiles) cudaFree(w->tiles);
+        delete w;
+        return c->fail(Q35K_ENOMEM, "weight upload: cudaMalloc(%zu) failed", tile_bytes + raw_bytes);
+    }
+    e = cudaMemcpyAsync(raw, blocks, raw_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_repack_tiles(type, raw, w->tiles, nb, n_out, n_pad, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(raw);
+    if (e != cudaSuccess) {
+        cudaFree(w->tiles);
+        delete w;
+        return c->cuda_fail(e, "weight upload");
+    }
+    *out = w;
+    return Q35K_OK;
+}
+
+int q35k_weight_free(q35k_ctx* c, q35k_weight* w) {
+    if (!w) return Q35K_OK;
+    if (c) cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    cudaFree(w->tiles);
+    delete w;
+    return Q35K_OK;
+}
+
+int q35k_weight_info(const q35k_weight* w, int* type, int* n_in, int* n_out, size_t* device_bytes) {
+    if (!w) return Q35K_EINVAL;
+    if (type) *type = w->type;
+    if (n_in) *n_in = w->n_in;
+    if (n_out) *n_out = w->n_out;
+    if (device_bytes) *device_bytes = w->bytes;
+    return Q35K_OK;
+}
+
+}  // extern "C"
+
+// Launch the GEMV for `tokens` Q8_K rows already on the device.
+int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s) {
+    const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, GEMV_CHUNK, num_sms);
+    int rc;
+    if ((rc = ensure_dev((void**)&d_partial, &partial_cap, p.partial_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = ensure_dev((void**)&d_counters, &counters_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
+    for (int t0 = 0; t0 < tokens; t0 += GEMV_CHUNK) {
+        GemvArgs a{};
+        a.tiles = w->tiles;
+        a.q8 = d_q8 + (size_t)t0 * w->nb * Q8K_BYTES;
+        a.y = d_y + (size_t)t0 * w->n_out;
+        a.ldy = w->n_out;
+        a.n_out = w->n_out;
+        a.nb = w->nb;
+        a.tokens = std::min(GEMV_CHUNK, tokens - t0);
+        a.partial = d_partial;
+        a.counters = d_counters;
+        a.err = d_err;
+        a.num_sms = num_sms;
+        cudaError_t e = launch_gemv(w->type, a, s);
+        if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+    }
+    return Q35K_OK;
+}
+
+static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, const void* y, int tokens) {
+    if (!c) return Q35K_EINVAL;
+    if (!w) return c->fail(Q35K_EINVAL, "weight handle is NULL");
+    if (!x || !y) return c->fail(Q35K_EINVAL, "input/output pointer is NULL");
+    if (tokens <= 0) return c->fail(Q35K_EINVAL, "tokens must be positive");
+    if (w->device != c->device) return c->fail(Q35K_EINVAL, "weight lives on device %d, context on %d", w->device, c->device);
+    return Q35K_OK;
+}
+
+static cudaStream_t pick(q35k_ctx* c, void* stream) { return stream ? (cudaStream_t)stream : c->stream; }
+
+// Device buffers handed in by the caller: the quantizer reads x as float4,
+// the GEMV reads Q8_K blocks and writes y as 32-bit words.
+static int check_alignment(q35k_ctx* c, const void* x, size_t x_align, const void* y, size_t y_align) {
+    if ((uintptr_t)x % x_align) return c->fail(Q35K_EINVAL, "input pointer must be %zu-byte aligned", x_align);
+    if ((uintptr_t)y % y_align) return c->fail(Q35K_EINVAL, "output pointer must be %zu-byte aligned", y_align);
+    return Q35K_OK;
+}
+
+extern "C" {
+
+int q35k_matmul_q8k_dev(q35k_ctx* c, const q35k_weight* w, const void* d_q8k, float* d_y, int tokens, void* stream) {
+    int rc = check_matmul_args(c, w, d_q8k, d_y, tokens);
+    if (rc) return rc;
+    if ((rc = check_alignment(c, d_q8k, 4, d_y, 4)) != Q35K_OK) return rc;
+    cudaSetDevice(c->device);
+    return c->gemv(w, (const uint8_t*)d_q8k, d_y, tokens, pick(c, stream));
+}
+
+int q35k_matmul_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* d_y, int tokens, void* stream) {
+    int rc = check_matmul_args(c, w, d_x, d_y, tokens);
+    if (rc) return rc;
+    if ((rc = check_alignment(c, d_x, 16, d_y, 4)) != Q35K_OK) return rc;
+    cudaSetDevice(c->device);
+    cudaStream_t s = pick(c, stream);
+    const size_t q8_bytes = (size_t)tokens * w->nb * Q8K_BYTES;
+    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_bytes, false)) != Q35K_OK) return rc;
+    cudaError_t e = launch_quantize_q8k(d_x, c->d_q8, w->n_in, tokens, s);
+    if (e != cudaSuccess) return c->cuda_fail(e, "Q8_K quantize launch");
+    return c->gemv(w, c->d_q8, d_y, tokens, s);
+}
+
+int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int tokens) {
+    int rc = check_matmul_args(c, w, x, y, tokens);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)tokens * w->n_in * sizeof(float);
+    const size_t out_bytes = (size_t)tokens * w->n_out * sizeof(float);
+    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
+    std::memcpy(c->h_in, x, in_bytes);
+    cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of x");
+    if ((rc = q35k_matmul_dev(c, w, c->d_x, c->d_y, tokens, c->stream)) != Q35K_OK) return rc;
+    unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
+    e = cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "matmul");
+    if (*h_err) return c->on_device_error(*h_err);
+    std::memcpy(y, c->h_out, out_bytes);
+    return Q35K_OK;
+}
+
+int q35k_matmul_q8k(q35k_ctx* c, const q35k_weight* w, const void* q8k, float* y, int tokens) {
+    int rc = check_matmul_args(c, w, q8k, y, tokens);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)tokens * w->nb * Q8K_BYTES;
+    const size_t out_bytes = (size_t)tokens * w->n_out * sizeof(float);
+    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
+    std::memcpy(c->h_in, q8k, in_bytes);
+    cudaError_t e = cudaMemcpyAsync(c->d_q8, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of q8k");
+    if ((rc = c->gemv(w, c->d_q8, c->d_y, tokens, c->stream)) != Q35K_OK) return rc;
+    unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
+    e = cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "matmul_q8k");
+    if (*h_err) return c->on_device_error(*h_err);
+    std::memcpy(y, c->h_out, out_bytes);
+    return Q35K_OK;
+}
+
+int q35k_quantize_q8k_dev(q35k_ctx* c, const float* d_x, void* d_q8k, int k, int rows, void* stream) {
+    if (!c) return Q35K_EINVAL;
+    if (!d_x || !d_q8k) return c->fail(Q35K_EINVAL, "NULL pointer");
+    if (k <= 0 || k % QK) return c->fail(Q35K_EINVAL, "k=%d is not a multiple of 256", k);
+    if (rows <= 0) return c->fail(Q35K_EINVAL, "rows must be positive");
+    int rc = check_alignment(c, d_x, 16, d_q8k, 4);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    cudaError_t e = launch_quantize_q8k(d_x, (uint8_t*)d_q8k, k, rows, pick(c, stream));
+    return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "Q8_K quantize launch");
+}
+
+int q35k_quantize_q8k(q35k_ctx* c, const float* x, void* q8k, int k, int rows) {
+    if (!c) return Q35K_EINVAL;
+    if (!x || !q8k) return c->fail(Q35K_EINVAL, "NULL pointer");
+    if (k <= 0 || k % QK) return c->fail(Q35K_EINVAL, "k=%d is not a multiple of 256", k);
+    if (rows <= 0) return c->fail(Q35K_EINVAL, "rows must be positive");
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)rows * k * sizeof(float);
+    const size_t out_bytes = (size_t)rows * (k / QK) * Q8K_BYTES;
+    int rc;
+    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, out_bytes, false)) != Q35K_OK) return rc;
+    cudaError_t e = cudaMemcpyAsync(c->d_x, x, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_quantize_q8k(c->d_x, c->d_q8, k, rows, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(q8k, c->d_q8, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "quantize_q8k");
+}
+
+int q35k_dequantize_dev(q35k_ctx* c, int type, const void* d_blocks, float* d_y, int k, int rows, void* stream) {
+    if (!c) return Q35K_EINVAL;
+    if (!valid_type(type)) return c->fail(Q35K_ENOTSUP, "ggml type %d is not a K-quant type", type);
+    if (!d_blocks || !d_y) return c->fail(Q35K_EINVAL, "NULL pointer");
+    if (k <= 0 || k % QK) return c->fail(Q35K_EINVAL, "k=%d is not a multiple of 256", k);
+    if (rows <= 0) return c->fail(Q35K_EINVAL, "rows must be positive");
+    int rc = check_alignment(c, d_blocks, 1, d_y, 4);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    cudaError_t e = launch_dequantize(type, (const uint8_t*)d_blocks, d_y, k, rows, pick(c, stream));
+    return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "dequantize launch");
+}
+
+int q35k_dequantize(q35k_ctx* c, int type, const void* blocks, float* y, int k, int rows) {
+    if (!c) return Q35K_EINVAL;
+    if (!valid_type(type)) return c->fail(Q35K_ENOTSUP, "ggml type %d is not a K-quant type", type);
+    if (!blocks || !y) return c->fail(Q35K_EINVAL, "NULL pointer");
+    if (k <= 0 || k % QK) return c->fail(Q35K_EINVAL, "k=%d is not a multiple of 256", k);
+    if (rows <= 0) return c->fail(Q35K_EINVAL, "rows must be positive");
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)rows * (k / QK) * block_bytes(type);
+    const size_t out_bytes = (size_t)rows * k * sizeof(float);
+    void* d_in = nullptr;
+    float* d_out = nullptr;
+    cudaError_t e = cudaMalloc(&d_in, in_bytes);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&d_out, out_bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(d_in);
+        return c->fail(Q35K_ENOMEM, "dequantize: cudaMalloc failed");
+    }
+    e = cudaMemcpyAsync(d_in, blocks, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_dequantize(type, (const uint8_t*)d_in, d_out, k, rows, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(y, d_out, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(d_in);
+    cudaFree(d_out);
+    return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "dequantize");
+}
+
+}  // extern "C"

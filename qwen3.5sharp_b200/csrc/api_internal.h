@@ -1,0 +1,65 @@
+// api_internal.h -- context and weight objects behind the opaque handles of
+// include/q35k.h (internal to libq35k).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace q35k {
+constexpr int GEMV_CHUNK = 8;  // tokens per GEMV launch
+}
+
+struct q35k_weight {
+    int type = 0, n_in = 0, n_out = 0, nb = 0, n_pad = 0, device = 0;
+    uint8_t* tiles = nullptr;  // 32-row chunk-major tiles (device_common.cuh)
+    size_t bytes = 0;
+};
+
+struct q35k_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+
+    // Device scratch, grown on demand and reused across calls.
+    float* d_x = nullptr;
+    size_t x_cap = 0;
+    uint8_t* d_q8 = nullptr;
+    size_t q8_cap = 0;
+    float* d_y = nullptr;
+    size_t y_cap = 0;
+    float* d_partial = nullptr;
+    size_t partial_cap = 0;
+    int* d_counters = nullptr;  // split-K arrival counters; zero between calls
+    size_t counters_cap = 0;
+    unsigned* d_err = nullptr;  // device error word (bounded waits that expired)
+
+    // Pinned host staging for the synchronous host-pointer calls.
+    void* h_in = nullptr;
+    size_t h_in_cap = 0;
+    void* h_out = nullptr;
+    size_t h_out_cap = 0;
+
+    ~q35k_ctx() {
+        if (d_x) cudaFree(d_x);
+        if (d_q8) cudaFree(d_q8);
+        if (d_y) cudaFree(d_y);
+        if (d_partial) cudaFree(d_partial);
+        if (d_counters) cudaFree(d_counters);
+        if (d_err) cudaFree(d_err);
+        if (h_in) cudaFreeHost(h_in);
+        if (h_out) cudaFreeHost(h_out);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    int fail(int code, const char* fmt, ...);
+    int cuda_fail(cudaError_t e, const char* what);
+    int ensure_dev(void** p, size_t* cap, size_t bytes, bool zero);
+    int ensure_host(void** p, size_t* cap, size_t bytes);
+    int check_device_error();
+    int on_device_error(unsigned word);
+    int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s);
+};

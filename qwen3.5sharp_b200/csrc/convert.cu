@@ -1,0 +1,211 @@
+// convert.cu -- Q8_K activation quantization, bit-exact dequantization and the
+// upload-time tile repack.
+//
+// Bit-exactness: every fp32 operation below is an explicitly rounded
+// intrinsic (__fdiv_rn, __fmul_rn, __fsub_rn, __float2int_rn), so nvcc cannot
+// contract or reassociate it; each mirrors one separately rounded C#
+// operation of the reference (RyuJIT emits no FMA on these paths).
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace q35k {
+
+// ---------------------------------------------------------------------------
+// Q8_K quantization: one warp per 256-value super-block.
+// Follows Q8K.QuantizeRow + Q8K.ScaleBlock (Kernels/Q8K.cs:12-146):
+//   amax = max |x|; max = the first element (lowest index) with |x| == amax,
+//   sign kept; iscale = -127/max; d = 1/iscale (a true reciprocal);
+//   q = clamp(round_half_even(x * iscale), -127, 127); bsums = sums of 16.
+//   amax == 0 -> an all-zero block (d = 0).
+// Lane l owns values 4l..4l+3 and 128+4l..128+4l+3 (two coalesced float4s).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, uint8_t* __restrict__ q8,
+                                                           int nb, int total_blocks) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= total_blocks) return;
+    const int row = warp / nb, b = warp % nb;
+    const float* src = x + (size_t)row * nb * QK + (size_t)b * QK;
+    float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
+    float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
+    float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+
+    uint32_t* out = reinterpret_cast<uint32_t*>(q8 + (size_t)warp * Q8K_BYTES);
+    if (amax == 0.f) {
+        // 73 words: d, 64 words of qs, 8 words of bsums.
+        for (int w = lane; w < Q8K_BYTES / 4; w += 32) out[w] = 0u;
+        return;
+    }
+    // First index whose |x| equals amax, and its signed value.
+    int idx = 1 << 30;
+    float val = 0.f;
+#pragma unroll
+    for (int i = 7; i >= 0; i--) {
+        int pos = (i < 4) ? (4 * lane + i) : (128 + 4 * lane + (i - 4));
+        if (fabsf(v[i]) == amax) {
+            idx = pos;
+            val = v[i];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        float ov = __shfl_xor_sync(0xffffffffu, val, o);
+        if (oi < idx) {
+            idx = oi;
+            val = ov;
+        }
+    }
+    const float iscale = __fdiv_rn(-127.f, val);
+    const float d = __fdiv_rn(1.f, iscale);
+
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int t = __float2int_rn(__fmul_rn(v[i], iscale));
+        q[i] = min(127, max(-127, t));
+    }
+    uint32_t w0 = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    uint32_t w1 = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    if (lane == 0) out[0] = __float_as_uint(d);
+    out[1 + lane] = w0;
+    out[1 + 32 + lane] = w1;
+
+    int s0 = q[0] + q[1] + q[2] + q[3];
+    int s1 = q[4] + q[5] + q[6] + q[7];
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    if ((lane & 3) == 0) {
+        int16_t* bs = reinterpret_cast<int16_t*>(q8 + (size_t)warp * Q8K_BYTES + 260);
+        bs[lane >> 2] = static_cast<int16_t>(s0);
+        bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
+    }
+}
+
+cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, cudaStream_t s) {
+    const int nb = k / QK;
+    const int total = nb * rows;
+    if (total == 0) return cudaSuccess;
+    const int warps_per_cta = 8;
+    const int grid = (total + warps_per_cta - 1) / warps_per_cta;
+    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, q8, nb, total);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Dequantization: one CTA of 256 threads per super-block, thread l -> value l.
+// Q4K.DequantizeRow (Kernels/Q4K.cs:35-60), Q5K.DequantizeRow
+// (Kernels/Q5K.cs:5-35), Q6K.DequantizeRow (Kernels/Q6K.cs:9-39).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* s, int& sc, int& m) {
+    // Q4K.GetScaleMin (Kernels/Q4K.cs:7-18).
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+__global__ void __launch_bounds__(256) dequant_kernel(int type, const uint8_t* __restrict__ blocks,
+                                                      float* __restrict__ y) {
+    const int blk = blockIdx.x;
+    const int l = threadIdx.x;
+    const int bb = block_bytes(type);
+    const uint8_t* b = blocks + (size_t)blk * bb;
+    float out;
+    if (type == TYPE_Q6_K) {
+        // value l: half h = l/128, within-half position p, quarter qq = p/32, l32 = p%32
+        const int h = l >> 7, p = l & 127, qq = p >> 5, l32 = p & 31;
+        const uint8_t* ql = b + 64 * h;
+        const uint8_t* qh = b + 128 + 32 * h;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192) + 8 * h;
+        const float d = fp16_bits_to_float(b[208] | (b[209] << 8));
+        const int lo_src = (qq & 1) ? ql[l32 + 32] : ql[l32];
+        const int nib = (qq < 2) ? (lo_src & 0xF) : (lo_src >> 4);
+        const int hb = (qh[l32] >> (2 * qq)) & 3;
+        const int q = nib | (hb << 4);
+        const int is = l32 / 16 + 2 * qq;
+        out = __fmul_rn(__fmul_rn(d, (float)sc[is]), (float)(q - 32));
+    } else {
+        const float d = fp16_bits_to_float(b[0] | (b[1] << 8));
+        const float dmin = fp16_bits_to_float(b[2] | (b[3] << 8));
+        const int c = l >> 6, hi = (l >> 5) & 1, l32 = l & 31;
+        int sc, m;
+        scale_min_k4(2 * c + hi, b + 4, sc, m);
+        int q;
+        if (type == TYPE_Q4_K) {
+            const uint8_t byte = b[16 + 32 * c + l32];
+            q = hi ? (byte >> 4) : (byte & 0xF);
+        } else {
+            const uint8_t byte = b[48 + 32 * c + l32];
+            const uint8_t h = b[16 + l32];
+            q = (hi ? (byte >> 4) : (byte & 0xF)) + (((h >> (2 * c + hi)) & 1) ? 16 : 0);
+        }
+        const float d1 = __fmul_rn(d, (float)sc);
+        const float m1 = __fmul_rn(dmin, (float)m);
+        out = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    y[(size_t)blk * QK + l] = out;
+}
+
+cudaError_t launch_dequantize(int type, const uint8_t* blocks, float* y, int k, int rows, cudaStream_t s) {
+    const long total = (long)(k / QK) * rows;
+    if (total == 0) return cudaSuccess;
+    dequant_kernel<<<(unsigned)total, 256, 0, s>>>(type, blocks, y);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Upload-time repack: GGUF rows -> 32-row chunk-major tiles.  One thread per
+// (row, block, 16-byte chunk); rows >= n_out become zero blocks (d = 0, so
+// they contribute nothing and their outputs are never stored).
+// ---------------------------------------------------------------------------
+__global__ void repack_tiles_kernel(int type, const uint8_t* __restrict__ src, uint8_t* __restrict__ tiles, int nb,
+                                    int n_out, int n_pad) {
+    const int bb = block_bytes(type);
+    const int chunks = (bb + 15) / 16;  // 9, 11, 14 (Q6_K: 13 full + tail)
+    const long tid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long total = (long)n_pad * nb * chunks;
+    if (tid >= total) return;
+    const int c = (int)(tid % chunks);
+    const long rb = tid / chunks;
+    const int b = (int)(rb % nb);
+    const int row = (int)(rb / nb);
+    const int g = row / TILE_ROWS, r = row % TILE_ROWS;
+    uint8_t* tile = tiles + ((size_t)g * nb + b) * (size_t)(TILE_ROWS * bb);
+    const uint8_t* blk = src + ((size_t)row * nb + b) * bb;
+    const bool live = row < n_out;
+    if (type == TYPE_Q6_K && c == 13) {
+        uint8_t* dst = tile + 13 * 512 + r * 2;
+        dst[0] = live ? blk[208] : 0;
+        dst[1] = live ? blk[209] : 0;
+        return;
+    }
+    uint8_t* dst = tile + c * 512 + r * 16;
+#pragma unroll
+    for (int i = 0; i < 16; i++) dst[i] = live ? blk[c * 16 + i] : 0;
+}
+
+cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tiles, int nb, int n_out, int n_pad,
+                                cudaStream_t s) {
+    const int bb = block_bytes(type);
+    const int chunks = (bb + 15) / 16;
+    const long total = (long)n_pad * nb * chunks;
+    if (total == 0) return cudaSuccess;
+    const int threads = 256;
+    repack_tiles_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, s>>>(type, rows_src, tiles, nb,
+                                                                                        n_out, n_pad);
+    return cudaGetLastError();
+}
+
+}  // namespace q35k

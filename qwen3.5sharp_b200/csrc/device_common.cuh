@@ -1,0 +1,123 @@
+// device_common.cuh -- constants, tile layout and sm_100a PTX helpers shared
+// by the libq35k kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q35k {
+
+constexpr int QK = 256;
+constexpr int Q8K_BYTES = 292;  // f32 d | s8 qs[256] | s16 bsums[16]
+constexpr int TYPE_Q4_K = 12, TYPE_Q5_K = 13, TYPE_Q6_K = 14;
+
+// Device error word bits (read back by the host after a call).
+constexpr unsigned DEV_ERR_TIMEOUT = 1u;
+
+// Rows per tile: one warp lane per weight row.
+constexpr int TILE_ROWS = 32;
+
+// ---------------------------------------------------------------------------
+// HBM tile layout of an uploaded weight.
+//
+// Rows are grouped 32 at a time (padded with zero blocks to a multiple of 32).
+// Tile (g, b) holds super-block b of rows 32g..32g+31 and sits at byte offset
+// (g * nb + b) * TILE_BYTES, so the tiles of one row group are contiguous in
+// K.  Inside a tile the block bytes are stored chunk-major: 16-byte chunk c of
+// row r is at c * 512 + r * 16.  A warp whose lane r decodes row r therefore
+// reads each chunk as one contiguous, bank-conflict-free 512-byte line.
+// Q6_K blocks (210 B = 13 chunks + 2 bytes) keep their trailing fp16 d in a
+// 64-byte row-indexed tail at 13 * 512.  The block bytes are unchanged; only
+// their placement differs from the GGUF rows, so a tile is exactly
+// 32 * block_bytes bytes.
+// ---------------------------------------------------------------------------
+template <int TYPE> struct Fmt;
+template <> struct Fmt<TYPE_Q4_K> {
+    static constexpr int BLOCK = 144, CHUNKS = 9, TILE = 32 * 144;
+};
+template <> struct Fmt<TYPE_Q5_K> {
+    static constexpr int BLOCK = 176, CHUNKS = 11, TILE = 32 * 176;
+};
+template <> struct Fmt<TYPE_Q6_K> {
+    static constexpr int BLOCK = 210, CHUNKS = 13, TILE = 32 * 210;
+    static constexpr int D_OFFSET = 13 * 512;
+};
+
+__host__ __device__ inline int block_bytes(int type) {
+    return type == TYPE_Q4_K ? 144 : type == TYPE_Q5_K ? 176 : type == TYPE_Q6_K ? 210 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// PTX helpers (mbarrier + bulk async copy, sm_90+ / sm_100a).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+// dst/src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on an mbarrier phase.  Gives up after `limit_ns` of wall time,
+// records DEV_ERR_TIMEOUT in *err and returns false: no device wait here can
+// spin forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err,
+                                                  uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t start = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && globaltimer_ns() - start > limit_ns) {
+            atomicOr(err, DEV_ERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+__device__ __forceinline__ float fp16_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
+}
+
+}  // namespace q35k

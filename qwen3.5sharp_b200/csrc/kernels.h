@@ -1,0 +1,43 @@
+// kernels.h -- host-side launchers of the libq35k kernels (internal to the
+// library; the public surface is include/q35k.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace q35k {
+
+// Q8_K quantization of rows x [rows][k] -> BlockQ8K bytes.
+cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, cudaStream_t s);
+
+// Bit-exact dequantization of `rows` GGUF rows of k values.
+cudaError_t launch_dequantize(int type, const uint8_t* blocks, float* y, int k, int rows, cudaStream_t s);
+
+// GGUF rows -> 32-row chunk-major tiles (layout in device_common.cuh).
+cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tiles, int nb, int n_out,
+                                int n_pad, cudaStream_t s);
+
+struct GemvArgs {
+    const uint8_t* tiles;  // uploaded weight tiles
+    const uint8_t* q8;     // tokens x nb BlockQ8K
+    float* y;              // [tokens][ldy]
+    int ldy;
+    int n_out, nb, tokens;
+    float* partial;     // split-K partial sums [splits][tokens][n_pad]
+    int* counters;      // one arrival counter per row group, zero between calls
+    unsigned* err;      // device error word
+    int num_sms;
+};
+
+// Scratch the GEMV needs for a given shape (bytes of `partial`, number of
+// counters).  The plan is deterministic in (type, nb, n_out, tokens, sms).
+struct GemvPlan {
+    int splits, bps, groups, n_pad;
+    size_t partial_bytes, counters;
+    size_t smem_bytes;
+};
+GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms);
+cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s);
+
+}  // namespace q35k

@@ -1,0 +1,347 @@
+"""q35k -- Python host mirror of the Qwen35Sharp K-quant kernel entry points,
+running on the B200 kernels of libq35k.so (C ABI: include/q35k.h).
+
+The static classes below keep the reference's names, argument meaning and
+error behaviour (src/Qwen35Sharp.Kernels/*.cs), so code and tests written
+against the reference read the same here:
+
+    MulMatQ4K.Gemv / GemvPrequant / Gemm     (Kernels/MulMatQ4K.cs:12-127)
+    Q5K.Gemv / GemvPrequant / Gemm / DequantizeRow   (Kernels/Q5K.cs)
+    Q6K.Gemv / GemvPrequant / Gemm / DequantizeRow   (Kernels/Q6K.cs)
+    Q4K.DequantizeRow                         (Kernels/Q4K.cs:35-60)
+    Q8K.QuantizeRow                           (Kernels/Q8K.cs:12-77)
+
+Where the reference takes a host pointer to GGUF blocks, these take either a
+device-resident `Weight` (uploaded once, as LoadWeights does in
+Model/Qwen35Model.cs:463-565) or a uint8 numpy array of the raw blocks
+(uploaded for the call).  Outputs are written into the given float32 array,
+as the reference writes through `float* output`.
+
+Exceptions mirror the reference's: ArgumentException (ValueError),
+NotSupportedException (NotImplementedError), InsufficientMemoryException
+(MemoryError), InvalidOperationException (RuntimeError) and
+TimeoutException (TimeoutError).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import numpy as np
+
+from . import _lib
+from .synth import BLOCK_BYTES, Q4_K, Q5_K, Q6_K, Q8K_BYTES, QK
+
+__all__ = [
+    "Context", "Weight", "MulMatQ4K", "Q4K", "Q5K", "Q6K", "Q8K", "default_context",
+    "ArgumentException", "NotSupportedException", "InsufficientMemoryException",
+    "InvalidOperationException", "TimeoutException", "Q4_K", "Q5_K", "Q6_K", "QK",
+]
+
+
+class Q35KError(Exception):
+    code = -1
+
+
+class ArgumentException(Q35KError, ValueError):
+    code = _lib.EINVAL
+
+
+class NotSupportedException(Q35KError, NotImplementedError):
+    code = _lib.ENOTSUP
+
+
+class InsufficientMemoryException(Q35KError, MemoryError):
+    code = _lib.ENOMEM
+
+
+class InvalidOperationException(Q35KError, RuntimeError):
+    code = _lib.ECUDA
+
+
+class TimeoutException(Q35KError, TimeoutError):
+    code = _lib.ETIMEOUT
+
+
+_EXC = {
+    _lib.EINVAL: ArgumentException,
+    _lib.ENOTSUP: NotSupportedException,
+    _lib.ENOMEM: InsufficientMemoryException,
+    _lib.ECUDA: InvalidOperationException,
+    _lib.ETIMEOUT: TimeoutException,
+    _lib.ENCCL: InvalidOperationException,
+}
+
+
+def _raise(rc: int, msg: str):
+    raise _EXC.get(rc, Q35KError)(msg)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u8(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+def _dev_ptr(t) -> int:
+    """Device address of a torch tensor / CuPy array / int."""
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return int(t.data_ptr())
+    raise TypeError("expected a device tensor (with .data_ptr()) or an int address")
+
+
+class Context:
+    """One libq35k context on one CUDA device (q35k_create)."""
+
+    def __init__(self, device: int = 0):
+        self.L = _lib.load()
+        h = ctypes.c_void_p()
+        rc = self.L.q35k_create(device, ctypes.byref(h))
+        if rc != _lib.OK:
+            _raise(rc, self.L.q35k_last_error(None).decode())
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.q35k_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int):
+        if rc != _lib.OK:
+            _raise(rc, self.L.q35k_last_error(self.h).decode())
+
+    def sync(self):
+        self._check(self.L.q35k_sync(self.h))
+
+    def upload(self, qtype: int, blocks: np.ndarray, n_in: int, n_out: int) -> "Weight":
+        blocks = _u8(blocks)
+        nb = n_in // QK if n_in > 0 else 0
+        if qtype in BLOCK_BYTES and blocks.size < n_out * nb * BLOCK_BYTES[qtype]:
+            raise ArgumentException("blocks buffer is smaller than nOut * nIn/256 blocks")
+        h = ctypes.c_void_p()
+        self._check(self.L.q35k_weight_upload(self.h, qtype, blocks.ctypes.data, n_in, n_out, ctypes.byref(h)))
+        return Weight(self, h, qtype, n_in, n_out)
+
+    # -- host-pointer calls (synchronous) --
+    def matmul(self, w: "Weight", x: np.ndarray, tokens: int | None = None) -> np.ndarray:
+        x = _f32(x)
+        tokens = x.size // w.n_in if tokens is None else tokens
+        if x.size < tokens * w.n_in:
+            raise ArgumentException("input is smaller than tokens * nIn")
+        y = np.empty((tokens, w.n_out), dtype=np.float32)
+        self._check(self.L.q35k_matmul(self.h, w.h, x.ctypes.data, y.ctypes.data, tokens))
+        return y
+
+    def matmul_q8k(self, w: "Weight", q8: np.ndarray, tokens: int) -> np.ndarray:
+        q8 = _u8(q8)
+        if q8.size < tokens * (w.n_in // QK) * Q8K_BYTES:
+            raise ArgumentException("q8k buffer is smaller than tokens * nIn/256 blocks")
+        y = np.empty((tokens, w.n_out), dtype=np.float32)
+        self._check(self.L.q35k_matmul_q8k(self.h, w.h, q8.ctypes.data, y.ctypes.data, tokens))
+        return y
+
+    def quantize_q8k(self, x: np.ndarray, k: int | None = None) -> np.ndarray:
+        x = _f32(x)
+        k = x.shape[-1] if k is None else k
+        rows = x.size // k
+        out = np.empty((rows, (k // QK) * Q8K_BYTES), dtype=np.uint8)
+        self._check(self.L.q35k_quantize_q8k(self.h, x.ctypes.data, out.ctypes.data, k, rows))
+        return out
+
+    def dequantize(self, qtype: int, blocks: np.ndarray, k: int, rows: int | None = None) -> np.ndarray:
+        blocks = _u8(blocks)
+        bb = BLOCK_BYTES.get(qtype, 1)
+        rows = blocks.size // max(1, (k // QK) * bb) if rows is None else rows
+        y = np.empty((rows, k), dtype=np.float32)
+        self._check(self.L.q35k_dequantize(self.h, qtype, blocks.ctypes.data, y.ctypes.data, k, rows))
+        return y
+
+    # -- device-pointer calls (asynchronous on `stream`, a cudaStream_t int) --
+    def matmul_dev(self, w: "Weight", d_x, d_y, tokens: int, stream: int = 0):
+        self._check(self.L.q35k_matmul_dev(self.h, w.h, _dev_ptr(d_x), _dev_ptr(d_y), tokens, stream or None))
+
+    def matmul_q8k_dev(self, w: "Weight", d_q8, d_y, tokens: int, stream: int = 0):
+        self._check(self.L.q35k_matmul_q8k_dev(self.h, w.h, _dev_ptr(d_q8), _dev_ptr(d_y), tokens, stream or None))
+
+    def quantize_q8k_dev(self, d_x, d_q8, k: int, rows: int, stream: int = 0):
+        self._check(self.L.q35k_quantize_q8k_dev(self.h, _dev_ptr(d_x), _dev_ptr(d_q8), k, rows, stream or None))
+
+    def dequantize_dev(self, qtype: int, d_blocks, d_y, k: int, rows: int, stream: int = 0):
+        self._check(self.L.q35k_dequantize_dev(self.h, qtype, _dev_ptr(d_blocks), _dev_ptr(d_y), k, rows,
+                                               stream or None))
+
+
+class Weight:
+    """A device-resident K-quant weight (q35k_weight_upload)."""
+
+    def __init__(self, ctx: Context, h, qtype: int, n_in: int, n_out: int):
+        self.ctx, self.h, self.qtype, self.n_in, self.n_out = ctx, h, qtype, n_in, n_out
+        self.nb = n_in // QK
+
+    def free(self):
+        if getattr(self, "h", None) and self.ctx.h:
+            self.ctx.L.q35k_weight_free(self.ctx.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    @property
+    def device_bytes(self) -> int:
+        sz = ctypes.c_size_t()
+        self.ctx.L.q35k_weight_info(self.h, None, None, None, ctypes.byref(sz))
+        return sz.value
+
+
+_tls = threading.local()
+
+
+def default_context(device: int = 0) -> Context:
+    """The calling thread's context on `device` (one per thread, as the
+    reference keeps one pool + scratch arena per model)."""
+    cache = getattr(_tls, "ctx", None)
+    if cache is None:
+        cache = _tls.ctx = {}
+    if device not in cache:
+        cache[device] = Context(device)
+    return cache[device]
+
+
+# ---------------------------------------------------------------------------
+# Reference-named entry points.
+# ---------------------------------------------------------------------------
+
+def _weight(qtype: int, weights, n_in: int, n_out: int) -> Weight:
+    if isinstance(weights, Weight):
+        if weights.qtype != qtype:
+            raise ArgumentException(f"weight type {weights.qtype} does not match {qtype}")
+        if weights.n_in != n_in or weights.n_out != n_out:
+            raise ArgumentException("nIn/nOut do not match the uploaded weight")
+        return weights
+    return default_context().upload(qtype, weights, n_in, n_out)
+
+
+def _store(output, y: np.ndarray):
+    if output is None:
+        return y
+    out = np.asarray(output)
+    if out.dtype != np.float32 or not out.flags.c_contiguous:
+        raise ArgumentException("output must be a contiguous float32 array")
+    out.reshape(-1)[: y.size] = y.reshape(-1)
+    return out
+
+
+def _check_nin(n_in: int):
+    if n_in <= 0 or n_in % QK:
+        raise NotSupportedException(f"nIn={n_in} is not a multiple of 256")
+
+
+class _KQuantKernels:
+    qtype = 0
+
+    @classmethod
+    def Gemv(cls, weights, input, output, nIn: int, nOut: int, pool=None, scratch=None):
+        """Q8K.QuantizeRow(input) then one dot per output row (1 token)."""
+        _check_nin(nIn)
+        w = _weight(cls.qtype, weights, nIn, nOut)
+        return _store(output, w.ctx.matmul(w, _f32(input).reshape(-1)[:nIn], 1).reshape(-1))
+
+    @classmethod
+    def GemvPrequant(cls, weights, y, output, nIn: int, nOut: int, pool=None):
+        """One dot per output row against a caller-quantized Q8_K row."""
+        _check_nin(nIn)
+        w = _weight(cls.qtype, weights, nIn, nOut)
+        return _store(output, w.ctx.matmul_q8k(w, y, 1).reshape(-1))
+
+    @classmethod
+    def _gemm(cls, weights, input, output, nIn: int, nOut: int, tokens: int):
+        _check_nin(nIn)
+        if tokens <= 0:
+            raise ArgumentException("tokens must be positive")
+        w = _weight(cls.qtype, weights, nIn, nOut)
+        return _store(output, w.ctx.matmul(w, input, tokens))
+
+
+class MulMatQ4K(_KQuantKernels):
+    """Q4_K x F32 matmul (Kernels/MulMatQ4K.cs)."""
+
+    qtype = Q4_K
+
+    @classmethod
+    def Gemm(cls, packed, rows, input, output, nIn: int, nOut: int, tokens: int, pool=None, scratch=None,
+             meta=None):
+        """Prefill/decode for any token count (MulMatQ4K.cs:45-127).  `packed`
+        and `meta` (the CPU panel formats) are not needed: `rows` is the
+        weight (a Weight or raw blocks)."""
+        return cls._gemm(rows if rows is not None else packed, input, output, nIn, nOut, tokens)
+
+
+class Q5K(_KQuantKernels):
+    """Q5_K kernels (Kernels/Q5K.cs)."""
+
+    qtype = Q5_K
+
+    @classmethod
+    def Gemm(cls, weights, input, output, nIn: int, nOut: int, tokens: int, pool=None):
+        return cls._gemm(weights, input, output, nIn, nOut, tokens)
+
+    @staticmethod
+    def DequantizeRow(x, y, k: int):
+        return _store(y, default_context().dequantize(Q5_K, x, k).reshape(-1))
+
+
+class Q6K(_KQuantKernels):
+    """Q6_K kernels (Kernels/Q6K.cs)."""
+
+    qtype = Q6_K
+
+    @classmethod
+    def Gemm(cls, weights, input, output, nIn: int, nOut: int, tokens: int, pool=None, scratch=None):
+        return cls._gemm(weights, input, output, nIn, nOut, tokens)
+
+    @staticmethod
+    def DequantizeRow(x, y, k: int):
+        return _store(y, default_context().dequantize(Q6_K, x, k).reshape(-1))
+
+
+class Q4K:
+    """Q4_K block helpers (Kernels/Q4K.cs)."""
+
+    @staticmethod
+    def DequantizeRow(x, y, k: int):
+        return _store(y, default_context().dequantize(Q4_K, x, k).reshape(-1))
+
+
+class Q8K:
+    """Q8_K activation quantizer (Kernels/Q8K.cs)."""
+
+    @staticmethod
+    def QuantizeRow(x, y, k: int):
+        """Bit-exact BlockQ8K bytes of k values; written into y (uint8) if given."""
+        if k <= 0 or k % QK:
+            raise ArgumentException(f"k={k} is not a multiple of 256")
+        q = default_context().quantize_q8k(_f32(x).reshape(-1)[:k], k).reshape(-1)
+        if y is None:
+            return q
+        out = np.asarray(y)
+        out.reshape(-1).view(np.uint8)[: q.size] = q
+        return out
+
+    @staticmethod
+    def RowBytes(k: int) -> int:
+        return (k // QK) * Q8K_BYTES

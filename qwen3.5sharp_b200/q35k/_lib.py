@@ -1,0 +1,68 @@
+"""ctypes binding of libq35k.so (the C ABI declared in include/q35k.h).
+
+There is deliberately no fallback: if the shared library is missing or no
+sm_100 GPU is present, every compute call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libq35k.so")
+
+OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL = 0, 1, 2, 3, 4, 5, 6
+
+# Symbols declared in include/q35k.h, with their ctypes signatures.
+_vp, _i32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+_pp = ctypes.POINTER(ctypes.c_void_p)
+SIGNATURES = {
+    "q35k_version": ([], ctypes.c_char_p),
+    "q35k_create": ([_i32, _pp], _i32),
+    "q35k_destroy": ([_vp], _i32),
+    "q35k_last_error": ([_vp], ctypes.c_char_p),
+    "q35k_sync": ([_vp], _i32),
+    "q35k_weight_upload": ([_vp, _i32, _vp, _i32, _i32, _pp], _i32),
+    "q35k_weight_free": ([_vp, _vp], _i32),
+    "q35k_weight_info": ([_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                          ctypes.POINTER(_sz)], _i32),
+    "q35k_matmul": ([_vp, _vp, _vp, _vp, _i32], _i32),
+    "q35k_matmul_q8k": ([_vp, _vp, _vp, _vp, _i32], _i32),
+    "q35k_matmul_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
+    "q35k_matmul_q8k_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
+    "q35k_quantize_q8k": ([_vp, _vp, _vp, _i32, _i32], _i32),
+    "q35k_quantize_q8k_dev": ([_vp, _vp, _vp, _i32, _i32, _vp], _i32),
+    "q35k_dequantize": ([_vp, _i32, _vp, _vp, _i32, _i32], _i32),
+    "q35k_dequantize_dev": ([_vp, _i32, _vp, _vp, _i32, _i32, _vp], _i32),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class LibraryNotBuilt(ImportError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load libq35k.so and declare every exported entry point."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise LibraryNotBuilt(
+                f"{LIB_PATH} is not built; run `python qwen3.5sharp_b200/build.py` (there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+        return L
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
