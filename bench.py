@@ -210,7 +210,9 @@ def run_ours(args):
 
     ctx = q35k.Context(local)
     W = ctx.upload(qt, w, K, rows)
-    stream = torch.cuda.current_stream()
+    # One explicit stream for our kernels, the CUDA events and NCCL.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
     dx = torch.from_numpy(x).cuda()
     dq8 = torch.empty(M * (K // 256) * 292, dtype=torch.uint8, device="cuda")

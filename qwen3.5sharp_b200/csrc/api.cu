@@ -230,12 +230,14 @@ int q35k_weight_info(const q35k_weight* w, int* type, int* n_in, int* n_out, siz
 }  // extern "C"
 
 // Launch the GEMV for `tokens` Q8_K rows already on the device.
-int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s) {
-    const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, GEMV_CHUNK, num_sms);
+int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl) {
+    const int chunk = gemv_max_tokens(w->nb);
+    if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
+    const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, chunk, num_sms);
     int rc;
     if ((rc = ensure_dev((void**)&d_partial, &partial_cap, p.partial_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_counters, &counters_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
-    for (int t0 = 0; t0 < tokens; t0 += GEMV_CHUNK) {
+    for (int t0 = 0; t0 < tokens; t0 += chunk) {
         GemvArgs a{};
         a.tiles = w->tiles;
         a.q8 = d_q8 + (size_t)t0 * w->nb * Q8K_BYTES;
@@ -243,12 +245,12 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
         a.ldy = w->n_out;
         a.n_out = w->n_out;
         a.nb = w->nb;
-        a.tokens = std::min(GEMV_CHUNK, tokens - t0);
+        a.tokens = std::min(chunk, tokens - t0);
         a.partial = d_partial;
         a.counters = d_counters;
         a.err = d_err;
         a.num_sms = num_sms;
-        cudaError_t e = launch_gemv(w->type, a, s);
+        cudaError_t e = launch_gemv(w->type, a, s, pdl && t0 == 0);
         if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     }
     return Q35K_OK;

@@ -8,10 +8,6 @@
 
 #include <string>
 
-namespace q35k {
-constexpr int GEMV_CHUNK = 8;  // tokens per GEMV launch
-}
-
 struct q35k_weight {
     int type = 0, n_in = 0, n_out = 0, nb = 0, n_pad = 0, device = 0;
     uint8_t* tiles = nullptr;  // 32-row chunk-major tiles (device_common.cuh)
@@ -61,5 +57,7 @@ struct q35k_ctx {
     int ensure_host(void** p, size_t* cap, size_t bytes);
     int check_device_error();
     int on_device_error(unsigned word);
-    int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s);
+    // `pdl`: launch with programmatic stream serialization (the GEMV streams
+    // weights before the preceding kernel finishes; its Q8_K reads wait).
+    int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true);
 };

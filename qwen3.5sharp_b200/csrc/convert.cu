@@ -21,6 +21,10 @@ namespace q35k {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, uint8_t* __restrict__ q8,
                                                            int nb, int total_blocks) {
+    // A GEMV launched after this kernel with programmatic stream
+    // serialization may start now: it streams weights first and waits on the
+    // grid dependency (full completion of this grid) before reading q8.
+    asm volatile("griddepcontrol.launch_dependents;");
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= total_blocks) return;

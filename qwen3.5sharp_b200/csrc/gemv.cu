@@ -1,22 +1,30 @@
 // gemv.cu -- decode GEMV (1..8 tokens) for Q4_K / Q5_K / Q6_K weights.
 //
-// Memory-bound design (no tensor cores):
-//   * a CTA owns one 32-row group and a contiguous range of super-blocks
-//     (split-K when the matrix is too small to fill the GPU);
-//   * one thread issues every weight tile of the CTA as a 1-D bulk async copy
-//     (cp.async.bulk, no multicast) into shared memory at once, one mbarrier
-//     per tile, so the whole unit is in flight while compute starts on the
-//     first tile;
-//   * lane r of each warp decodes row r of a tile: the chunk-major tile layout
-//     makes every 16-byte load a contiguous 512-byte line per warp, and all
-//     lanes read the same Q8_K activation words (shared-memory broadcast);
+// HBM-streaming design (no tensor cores; the kernel is bound by the weight
+// stream):
+//   * persistent: one CTA per SM; the weight matrix is a flat sequence of
+//     tiles (32 rows x 1 super-block, see device_common.cuh) in row-group
+//     order and every CTA owns one contiguous, equal share of it (stream-K),
+//     so the load is balanced to one tile whatever the shape;
+//   * one producer lane streams the CTA's tiles through a deep shared-memory
+//     ring with 1-D bulk async copies (cp.async.bulk, no multicast), one
+//     full/empty mbarrier pair per stage, keeping ~100+ KB per SM in flight;
+//   * eight consumer warps take the tiles of each row group round-robin;
+//     lane r decodes row r (chunk-major tiles: every 16-byte load is one
+//     contiguous 512-byte line per warp), all lanes read the same Q8_K words
+//     (shared-memory broadcast);
 //   * integer dots with dp4a into exact int32 per super-block, scaled in fp32
 //     once per block: acc += (d_w*d_x)*S - (dmin_w*d_x)*Mn
 //     (VecDotQ4K.DotScalar, Kernels/VecDotQ4K.cs:42-61; Q5K.Dot,
-//     Kernels/Q5K.cs:62-83; Q6K.DotAvx2's bias form, Kernels/Q6K.cs:105-108,159);
-//   * warps split the tiles, reduce through shared memory; split-K partials
-//     are combined by the last-arriving CTA of a row group in fixed order
-//     (deterministic), which also resets the group's counter.
+//     Kernels/Q5K.cs:62-83; the Q6_K bias form of Q6K.DotAvx2,
+//     Kernels/Q6K.cs:105-108,159);
+//   * per row group the warps reduce through shared memory in fixed order; a
+//     row group cut by a CTA boundary is finished by whichever CTA arrives
+//     last, summing the pieces in CTA order (deterministic) and resetting the
+//     group's arrival counter for the next call;
+//   * the activation quantizer runs as the preceding kernel; with
+//     programmatic dependent launch the weight stream starts before it ends
+//     and only the consumers wait for its Q8_K output.
 #include "device_common.cuh"
 #include "kernels.h"
 
@@ -24,37 +32,48 @@
 
 namespace q35k {
 
-constexpr int GEMV_WARPS = 4;
+constexpr int GEMV_CONSUMERS = 8;                 // consumer warps
+constexpr int GEMV_THREADS = (GEMV_CONSUMERS + 1) * 32;
 constexpr int GEMV_MAX_TOKENS = 8;
-constexpr int GEMV_TARGET_UNIT_BYTES = 72 * 1024;
+constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
+constexpr int GEMV_RING_TARGET = 160 * 1024;     // bytes of weight ring per SM
+constexpr int GEMV_Q8_LIMIT = 96 * 1024;          // staged Q8_K activations per CTA
 
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct SmemLayout {
-    int bars, flags, tiles, q8s, q8d, q8b, red, total;
+    int full, empty, ring, q8s, q8d, q8b, red, total;
 };
 
-// Dynamic shared memory of one GEMV CTA (all offsets 16-byte aligned):
-// mbarriers | 2 int flags | weight tiles | Q8_K qs | Q8_K d | Q8_K bsums |
-// cross-warp reduction buffer.
-__host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int bps, int m) {
+// Dynamic shared memory of one GEMV CTA (16-byte aligned regions):
+// full mbarriers | empty mbarriers | weight ring | Q8_K qs | Q8_K d |
+// Q8_K bsums | double-buffered cross-warp reduction.
+__host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int stages, int m, int nb) {
     SmemLayout L;
-    L.bars = 0;
-    L.flags = 8 * bps;
-    L.tiles = align_up(L.flags + 8, 128);
-    L.q8s = L.tiles + bps * tile_bytes;
-    L.q8d = L.q8s + m * bps * QK;
-    L.q8b = L.q8d + align_up(m * bps * 4, 16);
-    L.red = L.q8b + align_up(m * bps * 32, 16);
-    L.total = L.red + GEMV_WARPS * m * 32 * 4;
+    L.full = 0;
+    L.empty = 8 * stages;
+    L.ring = align_up(16 * stages, 128);
+    L.q8s = L.ring + stages * tile_bytes;
+    L.q8d = L.q8s + m * nb * QK;
+    L.q8b = L.q8d + align_up(m * nb * 4, 16);
+    L.red = L.q8b + align_up(m * nb * 32, 16);
+    L.total = L.red + 2 * GEMV_CONSUMERS * m * 32 * 4;
     return L;
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void consumer_bar() {
+    asm volatile("bar.sync 1, %0;" ::"n"(GEMV_CONSUMERS * 32) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ int byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xff; }
 __device__ __forceinline__ int sbyte_of(uint32_t w, int k) { return (int)(int8_t)((w >> (8 * k)) & 0xff); }
 
-// Q4_K / Q5_K header: fp16 d, fp16 dmin, 12 bytes of 6-bit scales/mins.
-// Unpacked as Q4K.UnpackScales (Kernels/Q4K.cs:20-33).
+// Q4_K / Q5_K header: fp16 d, fp16 dmin, 12 bytes of 6-bit scales/mins,
+// unpacked as Q4K.UnpackScales (Kernels/Q4K.cs:20-33).
 struct KHeader {
     float d, dmin;
     uint32_t sc_lo, sc_hi, mn_lo, mn_hi;
@@ -70,12 +89,10 @@ __device__ __forceinline__ KHeader unpack_header(uint4 h) {
     k.mn_hi = ((u2 >> 4) & 0x0f0f0f0fu) | (((u1 >> 6) & 0x03030303u) << 4);
     return k;
 }
-__device__ __forceinline__ int k_scale(const KHeader& k, int j) {
-    return byte_of(j < 4 ? k.sc_lo : k.sc_hi, j & 3);
-}
+__device__ __forceinline__ int k_scale(const KHeader& k, int j) { return byte_of(j < 4 ? k.sc_lo : k.sc_hi, j & 3); }
 __device__ __forceinline__ int k_min(const KHeader& k, int j) { return byte_of(j < 4 ? k.mn_lo : k.mn_hi, j & 3); }
 
-// Sum_j mins_j * (bsums[2j] + bsums[2j+1]) from the 16 int16 bsums.
+// Sum_j mins_j * (bsums[2j] + bsums[2j+1]) from the 16 int16 block sums.
 __device__ __forceinline__ int mins_dot(const KHeader& k, const int16_t* bs) {
     const int4 b0 = *reinterpret_cast<const int4*>(bs);
     const int4 b1 = *reinterpret_cast<const int4*>(bs + 8);
@@ -90,9 +107,20 @@ __device__ __forceinline__ int mins_dot(const KHeader& k, const int16_t* bs) {
     return mn;
 }
 
+// Staged Q8_K activations: qs[m][nb][256], d[m][nb], bsums[m][nb][16].
+struct Q8Smem {
+    const int8_t* qs;
+    const float* d;
+    const int16_t* bs;
+    int nb;
+    __device__ __forceinline__ const int8_t* q(int m, int b) const { return qs + (m * nb + b) * QK; }
+    __device__ __forceinline__ float dx(int m, int b) const { return d[m * nb + b]; }
+    __device__ __forceinline__ const int16_t* bsums(int m, int b) const { return bs + (m * nb + b) * 16; }
+};
+
 template <int TYPE, int M>
-__device__ __forceinline__ void block_dot_k45(const uint8_t* __restrict__ tile, int r, const int8_t* q8s,
-                                              const float* q8d, const int16_t* q8b, int t, int bps, float* acc) {
+__device__ __forceinline__ void block_dot_k45(const uint8_t* __restrict__ tile, int r, const Q8Smem& q8, int b,
+                                              float* acc) {
     const KHeader hd = unpack_header(*reinterpret_cast<const uint4*>(tile + r * 16));
     uint32_t qh[8];
     if (TYPE == TYPE_Q5_K) {
@@ -125,31 +153,31 @@ __device__ __forceinline__ void block_dot_k45(const uint8_t* __restrict__ tile, 
         const int scl = k_scale(hd, 2 * gg), sch = k_scale(hd, 2 * gg + 1);
 #pragma unroll
         for (int m = 0; m < M; m++) {
-            const int4* qv = reinterpret_cast<const int4*>(q8s + (m * bps + t) * QK + 64 * gg);
+            const int4* qv = reinterpret_cast<const int4*>(q8.q(m, b) + 64 * gg);
             const int4 a0 = qv[0], a1 = qv[1], a2 = qv[2], a3 = qv[3];
-            int sl = dp4a(lo[0], a0.x, 0);
-            sl = dp4a(lo[1], a0.y, sl); sl = dp4a(lo[2], a0.z, sl); sl = dp4a(lo[3], a0.w, sl);
-            sl = dp4a(lo[4], a1.x, sl); sl = dp4a(lo[5], a1.y, sl); sl = dp4a(lo[6], a1.z, sl);
-            sl = dp4a(lo[7], a1.w, sl);
-            int sh = dp4a(hi[0], a2.x, 0);
-            sh = dp4a(hi[1], a2.y, sh); sh = dp4a(hi[2], a2.z, sh); sh = dp4a(hi[3], a2.w, sh);
-            sh = dp4a(hi[4], a3.x, sh); sh = dp4a(hi[5], a3.y, sh); sh = dp4a(hi[6], a3.z, sh);
-            sh = dp4a(hi[7], a3.w, sh);
-            S[m] += scl * sl + sch * sh;
+            int sl0 = dp4a(lo[0], a0.x, 0), sl1 = dp4a(lo[1], a0.y, 0);
+            sl0 = dp4a(lo[2], a0.z, sl0); sl1 = dp4a(lo[3], a0.w, sl1);
+            sl0 = dp4a(lo[4], a1.x, sl0); sl1 = dp4a(lo[5], a1.y, sl1);
+            sl0 = dp4a(lo[6], a1.z, sl0); sl1 = dp4a(lo[7], a1.w, sl1);
+            int sh0 = dp4a(hi[0], a2.x, 0), sh1 = dp4a(hi[1], a2.y, 0);
+            sh0 = dp4a(hi[2], a2.z, sh0); sh1 = dp4a(hi[3], a2.w, sh1);
+            sh0 = dp4a(hi[4], a3.x, sh0); sh1 = dp4a(hi[5], a3.y, sh1);
+            sh0 = dp4a(hi[6], a3.z, sh0); sh1 = dp4a(hi[7], a3.w, sh1);
+            S[m] += scl * (sl0 + sl1) + sch * (sh0 + sh1);
         }
     }
 #pragma unroll
     for (int m = 0; m < M; m++) {
-        const int Mn = mins_dot(hd, q8b + (m * bps + t) * 16);
-        const float dx = q8d[m * bps + t];
+        const int Mn = mins_dot(hd, q8.bsums(m, b));
+        const float dx = q8.dx(m, b);
         acc[m] = fmaf(hd.d * dx, (float)S[m], acc[m]);
         acc[m] = fmaf(-(hd.dmin * dx), (float)Mn, acc[m]);
     }
 }
 
 template <int M>
-__device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, int r, const int8_t* q8s,
-                                              const float* q8d, const int16_t* q8b, int t, int bps, float* acc) {
+__device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, int r, const Q8Smem& q8, int b,
+                                              float* acc) {
     const float d = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(tile + Fmt<TYPE_Q6_K>::D_OFFSET + r * 2));
     const uint4 scv = *reinterpret_cast<const uint4*>(tile + 12 * 512 + r * 16);
     int sc[16];
@@ -169,20 +197,20 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
             const uint4 B = *reinterpret_cast<const uint4*>(tile + (4 * h + 2 + lg) * 512 + r * 16);
             const uint4 H = *reinterpret_cast<const uint4*>(tile + (8 + 2 * h + lg) * 512 + r * 16);
             const uint32_t a[4] = {A.x, A.y, A.z, A.w};
-            const uint32_t b[4] = {B.x, B.y, B.z, B.w};
+            const uint32_t bq[4] = {B.x, B.y, B.z, B.w};
             const uint32_t hh[4] = {H.x, H.y, H.z, H.w};
             int q1[4], q2[4], q3[4], q4[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 q1[i] = (int)((a[i] & 0x0f0f0f0fu) | ((hh[i] << 4) & 0x30303030u));
-                q2[i] = (int)((b[i] & 0x0f0f0f0fu) | ((hh[i] << 2) & 0x30303030u));
+                q2[i] = (int)((bq[i] & 0x0f0f0f0fu) | ((hh[i] << 2) & 0x30303030u));
                 q3[i] = (int)(((a[i] >> 4) & 0x0f0f0f0fu) | (hh[i] & 0x30303030u));
-                q4[i] = (int)(((b[i] >> 4) & 0x0f0f0f0fu) | ((hh[i] >> 2) & 0x30303030u));
+                q4[i] = (int)(((bq[i] >> 4) & 0x0f0f0f0fu) | ((hh[i] >> 2) & 0x30303030u));
             }
             const int s1 = sc[8 * h + lg], s2 = sc[8 * h + 2 + lg], s3 = sc[8 * h + 4 + lg], s4 = sc[8 * h + 6 + lg];
 #pragma unroll
             for (int m = 0; m < M; m++) {
-                const int8_t* base = q8s + (m * bps + t) * QK + 128 * h + 16 * lg;
+                const int8_t* base = q8.q(m, b) + 128 * h + 16 * lg;
                 const int4 x1 = *reinterpret_cast<const int4*>(base);
                 const int4 x2 = *reinterpret_cast<const int4*>(base + 32);
                 const int4 x3 = *reinterpret_cast<const int4*>(base + 64);
@@ -198,145 +226,188 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
 #pragma unroll
     for (int m = 0; m < M; m++) {
         // -32 bias folded through the Q8_K block sums (Kernels/Q6K.cs:105-108).
-        const int4 b0 = *reinterpret_cast<const int4*>(q8b + (m * bps + t) * 16);
-        const int4 b1 = *reinterpret_cast<const int4*>(q8b + (m * bps + t) * 16 + 8);
+        const int16_t* bsp = q8.bsums(m, b);
+        const int4 b0 = *reinterpret_cast<const int4*>(bsp);
+        const int4 b1 = *reinterpret_cast<const int4*>(bsp + 8);
         const uint32_t w[8] = {(uint32_t)b0.x, (uint32_t)b0.y, (uint32_t)b0.z, (uint32_t)b0.w,
                                (uint32_t)b1.x, (uint32_t)b1.y, (uint32_t)b1.z, (uint32_t)b1.w};
         int bias = 0;
 #pragma unroll
         for (int j = 0; j < 8; j++)
             bias += sc[2 * j] * (int)(int16_t)(w[j] & 0xffffu) + sc[2 * j + 1] * (int)(int16_t)(w[j] >> 16);
-        const float dx = q8d[m * bps + t];
-        acc[m] = fmaf(d * dx, (float)(S[m] - 32 * bias), acc[m]);
+        acc[m] = fmaf(d * q8.dx(m, b), (float)(S[m] - 32 * bias), acc[m]);
     }
 }
 
+// Which CTA owns tile T when `tiles` tiles are split evenly over `grid` CTAs
+// (CTA i owns [tiles*i/grid, tiles*(i+1)/grid)).
+__device__ __forceinline__ int tile_owner(long T, long tiles, int grid) {
+    return (int)(((T + 1) * (long)grid - 1) / tiles);
+}
+
 template <int TYPE, int M>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_kernel(GemvArgs a, int splits, int bps, int n_pad) {
+__global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(GemvArgs a, GemvPlan p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
-    const SmemLayout L = gemv_smem_layout(TILE, bps, M);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-    uint8_t* wt = smem + L.tiles;
-    int8_t* q8s = reinterpret_cast<int8_t*>(smem + L.q8s);
-    float* q8d = reinterpret_cast<float*>(smem + L.q8d);
-    int16_t* q8b = reinterpret_cast<int16_t*>(smem + L.q8b);
-    float* red = reinterpret_cast<float*>(smem + L.red);
-    int& s_last = reinterpret_cast<int*>(smem + L.flags)[0];
-    int& s_timeout = reinterpret_cast<int*>(smem + L.flags)[1];
+    const SmemLayout L = gemv_smem_layout(TILE, p.stages, M, a.nb);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    uint8_t* ring = smem + L.ring;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.x / splits, s = blockIdx.x % splits;
-    const int b0 = s * bps;
-    const int kr = min(bps, a.nb - b0);
+    const int nb = a.nb;
+    const long tiles = (long)p.groups * nb;
+    const long T0 = tiles * blockIdx.x / gridDim.x;
+    const long T1 = tiles * (blockIdx.x + 1) / gridDim.x;
+    const int S = p.stages;
 
     if (tid == 0) {
-        s_timeout = 0;
-        for (int t = 0; t < kr; t++) mbar_init(&bars[t], 1);
+        for (int i = 0; i < S; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        const uint8_t* src = a.tiles + ((size_t)g * a.nb + b0) * TILE;
-        for (int t = 0; t < kr; t++) {
-            mbar_arrive_expect_tx(&bars[t], TILE);
-            bulk_g2s(wt + t * TILE, src + (size_t)t * TILE, TILE, &bars[t]);
-        }
-    }
-    // Stage the K-range of the Q8_K activations: 73 words per block
-    // (word 0 = d, 1..64 = qs, 65..72 = bsums).
-    for (int idx = tid; idx < M * kr * 73; idx += blockDim.x) {
-        const int m = idx / (kr * 73), rem = idx % (kr * 73), t = rem / 73, w = rem % 73;
-        const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(a.q8 + ((size_t)m * a.nb + b0 + t) * Q8K_BYTES) + w);
-        if (w == 0)
-            q8d[m * bps + t] = __uint_as_float(v);
-        else if (w <= 64)
-            reinterpret_cast<uint32_t*>(q8s + (m * bps + t) * QK)[w - 1] = v;
-        else
-            reinterpret_cast<uint32_t*>(q8b + (m * bps + t) * 16)[w - 65] = v;
-    }
-    __syncthreads();
 
-    float acc[M];
-#pragma unroll
-    for (int m = 0; m < M; m++) acc[m] = 0.f;
-    for (int t = warp; t < kr; t += GEMV_WARPS) {
-        if (!mbar_wait_bounded(&bars[t], 0, a.err)) {
-            s_timeout = 1;
-            break;
-        }
-        if (TYPE == TYPE_Q6_K)
-            block_dot_q6k<M>(wt + t * TILE, lane, q8s, q8d, q8b, t, bps, acc);
-        else
-            block_dot_k45<TYPE, M>(wt + t * TILE, lane, q8s, q8d, q8b, t, bps, acc);
-    }
-#pragma unroll
-    for (int m = 0; m < M; m++) red[(warp * M + m) * 32 + lane] = acc[m];
-    __syncthreads();
-
-    const int row = g * TILE_ROWS + lane;
-    if (warp == 0) {
-#pragma unroll
-        for (int m = 0; m < M; m++) {
-            float v = red[m * 32 + lane];
-#pragma unroll
-            for (int w = 1; w < GEMV_WARPS; w++) v += red[(w * M + m) * 32 + lane];
-            if (splits == 1) {
-                if (row < a.n_out) a.y[(size_t)m * a.ldy + row] = v;
-            } else {
-                a.partial[((size_t)s * M + m) * n_pad + row] = v;
+    if (warp == GEMV_CONSUMERS) {
+        // ---------------- producer: stream this CTA's tiles ----------------
+        if (lane == 0) {
+            for (long T = T0; T < T1; T++) {
+                const long c = T - T0;
+                const int st = (int)(c % S);
+                if (c >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((c / S) - 1) & 1), a.err)) break;
+                mbar_arrive_expect_tx(&full[st], TILE);
+                bulk_g2s(ring + (size_t)st * TILE, a.tiles + (size_t)T * TILE, TILE, &full[st]);
             }
         }
+        return;
     }
-    if (splits > 1) {
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) s_last = (atomicAdd(&a.counters[g], 1) == splits - 1);
-        __syncthreads();
-        if (s_last && warp == 0) {
-            __threadfence();
+
+    // ---------------- consumers ----------------
+    griddep_wait();  // the Q8_K activations come from the preceding kernel
+    int8_t* q8s = reinterpret_cast<int8_t*>(smem + L.q8s);
+    float* q8d = reinterpret_cast<float*>(smem + L.q8d);
+    int16_t* q8b = reinterpret_cast<int16_t*>(smem + L.q8b);
+    // 73 words per BlockQ8K: word 0 = d, 1..64 = qs, 65..72 = bsums.
+    for (int idx = tid; idx < M * nb * 73; idx += GEMV_CONSUMERS * 32) {
+        const int mb = idx / 73, w = idx % 73;
+        const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(a.q8 + (size_t)mb * Q8K_BYTES) + w);
+        if (w == 0)
+            q8d[mb] = __uint_as_float(v);
+        else if (w <= 64)
+            reinterpret_cast<uint32_t*>(q8s + mb * QK)[w - 1] = v;
+        else
+            reinterpret_cast<uint32_t*>(q8b + mb * 16)[w - 65] = v;
+    }
+    consumer_bar();
+    const Q8Smem q8{q8s, q8d, q8b, nb};
+    float* red = reinterpret_cast<float*>(smem + L.red);
+
+    int par = 0;
+    bool timed_out = false;
+    const long g_first = T0 / nb, g_last = (T1 - 1) / nb;
+    for (long g = g_first; T1 > T0 && g <= g_last; g++) {
+        const long tb0 = max(T0, g * nb), tb1 = min(T1, (g + 1) * nb);
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[m] = 0.f;
+        for (long T = tb0 + warp; T < tb1; T += GEMV_CONSUMERS) {
+            const long c = T - T0;
+            const int st = (int)(c % S);
+            if (!timed_out && !mbar_wait_bounded(&full[st], (uint32_t)((c / S) & 1), a.err)) timed_out = true;
+            if (!timed_out) {
+                const uint8_t* tile = ring + (size_t)st * TILE;
+                const int b = (int)(T - g * nb);
+                if (TYPE == TYPE_Q6_K)
+                    block_dot_q6k<M>(tile, lane, q8, b, acc);
+                else
+                    block_dot_k45<TYPE, M>(tile, lane, q8, b, acc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        float* rbuf = red + par * GEMV_CONSUMERS * M * 32;
+#pragma unroll
+        for (int m = 0; m < M; m++) rbuf[(warp * M + m) * 32 + lane] = acc[m];
+        consumer_bar();
+        if (warp == 0) {
+            const int row = (int)g * TILE_ROWS + lane;
+            const bool whole = (tb0 == g * nb) && (tb1 == (g + 1) * nb);
+            float v[M];
 #pragma unroll
             for (int m = 0; m < M; m++) {
-                float v = 0.f;
-                for (int k = 0; k < splits; k++) v += __ldcg(&a.partial[((size_t)k * M + m) * n_pad + row]);
-                if (row < a.n_out) a.y[(size_t)m * a.ldy + row] = v;
+                v[m] = rbuf[m * 32 + lane];
+#pragma unroll
+                for (int w = 1; w < GEMV_CONSUMERS; w++) v[m] += rbuf[(w * M + m) * 32 + lane];
             }
-            if (lane == 0) a.counters[g] = 0;
+            if (whole) {
+                if (row < a.n_out)
+#pragma unroll
+                    for (int m = 0; m < M; m++) a.y[(size_t)m * a.ldy + row] = v[m];
+            } else {
+                // Row group cut by a CTA boundary: publish this piece, and
+                // the last piece to arrive sums all of them in CTA order.
+                const int first = tile_owner(g * nb, tiles, gridDim.x);
+                const int pieces = tile_owner((g + 1) * nb - 1, tiles, gridDim.x) - first + 1;
+                const int piece = (int)blockIdx.x - first;
+                float* part = a.partial + ((size_t)g * p.max_pieces) * M * 32;
+#pragma unroll
+                for (int m = 0; m < M; m++) part[((size_t)piece * M + m) * 32 + lane] = v[m];
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) last = atomicAdd(&a.counters[g], 1) == pieces - 1;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        float s = 0.f;
+                        for (int k = 0; k < pieces; k++) s += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
+                        if (row < a.n_out) a.y[(size_t)m * a.ldy + row] = s;
+                    }
+                    if (lane == 0) a.counters[g] = 0;
+                }
+            }
         }
-    }
-    if (s_timeout) {
-        // Give the copies still in flight a bounded chance to land before the
-        // CTA's shared memory is released.
-        __syncthreads();
-        if (tid == 0)
-            for (int t = 0; t < kr; t++) mbar_wait_bounded(&bars[t], 0, a.err, 100000000ull);
+        par ^= 1;
     }
 }
 
 GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     GemvPlan p{};
     const int tile = TILE_ROWS * block_bytes(type);
+    const int m = std::min(std::max(tokens, 1), GEMV_MAX_TOKENS);
     p.groups = (n_out + TILE_ROWS - 1) / TILE_ROWS;
     p.n_pad = p.groups * TILE_ROWS;
-    const int bps_max = std::max(1, std::min(nb, GEMV_TARGET_UNIT_BYTES / tile));
-    int splits = (nb + bps_max - 1) / bps_max;
-    while ((long)p.groups * splits < 2L * num_sms && splits < nb) splits++;
-    p.bps = (nb + splits - 1) / splits;
-    p.splits = (nb + p.bps - 1) / p.bps;
-    const int m = std::min(std::max(tokens, 1), GEMV_MAX_TOKENS);
-    p.smem_bytes = (size_t)gemv_smem_layout(tile, p.bps, m).total;
-    p.partial_bytes = p.splits > 1 ? (size_t)p.splits * GEMV_MAX_TOKENS * p.n_pad * sizeof(float) : 0;
+    const long tiles = (long)p.groups * nb;
+    p.grid = (int)std::min<long>(tiles, num_sms);
+    // Stages: fill the ring target within the shared-memory limit.
+    const SmemLayout base = gemv_smem_layout(tile, 0, m, nb);
+    const int room = GEMV_SMEM_LIMIT - base.total - 256;
+    p.stages = std::max(2, std::min(GEMV_RING_TARGET, room) / (tile + 16));
+    p.smem_bytes = (size_t)gemv_smem_layout(tile, p.stages, m, nb).total;
+    // A row group spans at most this many CTAs.
+    const long per_cta = std::max<long>(1, tiles / p.grid);
+    p.max_pieces = (int)std::min<long>(p.grid, (nb + per_cta - 1) / per_cta + 1);
+    p.partial_bytes = (size_t)p.groups * p.max_pieces * GEMV_MAX_TOKENS * 32 * sizeof(float);
     p.counters = (size_t)p.groups;
+    p.fits = (long)m * nb * Q8K_BYTES <= GEMV_Q8_LIMIT && p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;
     return p;
+}
+
+int gemv_max_tokens(int nb) {
+    // Tokens per launch so that the staged Q8_K activations fit.
+    const int m = GEMV_Q8_LIMIT / (nb * Q8K_BYTES);
+    return std::max(0, std::min(GEMV_MAX_TOKENS, m));
 }
 
 // Opt-in shared memory for every instantiation on the current device
 // (called once per context).
-constexpr int GEMV_MAX_SMEM = 227 * 1024;
-
 template <int TYPE, int M>
 static void configure_typed() {
-    cudaFuncSetAttribute(gemv_kernel<TYPE, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_MAX_SMEM);
+    cudaFuncSetAttribute(gemv_kernel<TYPE, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
 }
 
 template <int TYPE>
@@ -358,34 +429,42 @@ void configure_gemv_kernels() {
 }
 
 template <int TYPE, int M>
-static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream_t s) {
-    if (p.smem_bytes > (size_t)GEMV_MAX_SMEM) return cudaErrorInvalidConfiguration;
-    const unsigned grid = (unsigned)p.groups * (unsigned)p.splits;
-    gemv_kernel<TYPE, M><<<grid, GEMV_WARPS * 32, p.smem_bytes, s>>>(a, p.splits, p.bps, p.n_pad);
-    return cudaGetLastError();
+static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
+    if (!p.fits) return cudaErrorInvalidConfiguration;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)p.grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, M>, a, p);
 }
 
 template <int TYPE>
-static cudaError_t launch_m(const GemvArgs& a, const GemvPlan& p, cudaStream_t s) {
+static cudaError_t launch_m(const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
     switch (a.tokens) {
-    case 1: return launch_typed<TYPE, 1>(a, p, s);
-    case 2: return launch_typed<TYPE, 2>(a, p, s);
-    case 3: return launch_typed<TYPE, 3>(a, p, s);
-    case 4: return launch_typed<TYPE, 4>(a, p, s);
-    case 5: return launch_typed<TYPE, 5>(a, p, s);
-    case 6: return launch_typed<TYPE, 6>(a, p, s);
-    case 7: return launch_typed<TYPE, 7>(a, p, s);
-    case 8: return launch_typed<TYPE, 8>(a, p, s);
+    case 1: return launch_typed<TYPE, 1>(a, p, s, pdl);
+    case 2: return launch_typed<TYPE, 2>(a, p, s, pdl);
+    case 3: return launch_typed<TYPE, 3>(a, p, s, pdl);
+    case 4: return launch_typed<TYPE, 4>(a, p, s, pdl);
+    case 5: return launch_typed<TYPE, 5>(a, p, s, pdl);
+    case 6: return launch_typed<TYPE, 6>(a, p, s, pdl);
+    case 7: return launch_typed<TYPE, 7>(a, p, s, pdl);
+    case 8: return launch_typed<TYPE, 8>(a, p, s, pdl);
     default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s) {
+cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl) {
     const GemvPlan p = plan_gemv(type, a.nb, a.n_out, a.tokens, a.num_sms);
     switch (type) {
-    case TYPE_Q4_K: return launch_m<TYPE_Q4_K>(a, p, s);
-    case TYPE_Q5_K: return launch_m<TYPE_Q5_K>(a, p, s);
-    case TYPE_Q6_K: return launch_m<TYPE_Q6_K>(a, p, s);
+    case TYPE_Q4_K: return launch_m<TYPE_Q4_K>(a, p, s, pdl);
+    case TYPE_Q5_K: return launch_m<TYPE_Q5_K>(a, p, s, pdl);
+    case TYPE_Q6_K: return launch_m<TYPE_Q6_K>(a, p, s, pdl);
     default: return cudaErrorInvalidValue;
     }
 }

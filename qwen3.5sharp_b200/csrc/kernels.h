@@ -8,7 +8,9 @@
 
 namespace q35k {
 
-// Q8_K quantization of rows x [rows][k] -> BlockQ8K bytes.
+// Q8_K quantization of rows x [rows][k] -> BlockQ8K bytes.  The kernel lets a
+// dependent kernel launched with programmatic stream serialization start
+// early (that kernel must wait on the grid dependency before reading q8).
 cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, cudaStream_t s);
 
 // Bit-exact dequantization of `rows` GGUF rows of k values.
@@ -24,20 +26,23 @@ struct GemvArgs {
     float* y;              // [tokens][ldy]
     int ldy;
     int n_out, nb, tokens;
-    float* partial;     // split-K partial sums [splits][tokens][n_pad]
+    float* partial;     // pieces of row groups cut by a CTA boundary
     int* counters;      // one arrival counter per row group, zero between calls
     unsigned* err;      // device error word
     int num_sms;
 };
 
-// Scratch the GEMV needs for a given shape (bytes of `partial`, number of
-// counters).  The plan is deterministic in (type, nb, n_out, tokens, sms).
+// Launch plan of the persistent GEMV; deterministic in (type, nb, n_out,
+// tokens, sms).  `partial_bytes` / `counters` size the scratch it needs.
 struct GemvPlan {
-    int splits, bps, groups, n_pad;
-    size_t partial_bytes, counters;
-    size_t smem_bytes;
+    int groups, n_pad, grid, stages, max_pieces;
+    size_t smem_bytes, partial_bytes, counters;
+    bool fits;
 };
 GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms);
-cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s);
+// Largest token count per GEMV launch for nb super-blocks per row (0: the
+// row is too long to stage one token's activations).
+int gemv_max_tokens(int nb);
+cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl);
 
 }  // namespace q35k

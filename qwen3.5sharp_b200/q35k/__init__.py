@@ -86,6 +86,19 @@ def _u8(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.uint8)
 
 
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
+
+
+def _stream(stream):
+    """Map a caller stream to the C ABI: None -> the context's own stream;
+    0 (torch's default stream handle) -> cudaStreamLegacy; else the handle."""
+    if stream is None:
+        return None
+    if hasattr(stream, "cuda_stream"):
+        stream = stream.cuda_stream
+    return stream if stream != 0 else _CUDA_STREAM_LEGACY
+
+
 def _dev_ptr(t) -> int:
     """Device address of a torch tensor / CuPy array / int."""
     if isinstance(t, int):
@@ -168,19 +181,20 @@ class Context:
         self._check(self.L.q35k_dequantize(self.h, qtype, blocks.ctypes.data, y.ctypes.data, k, rows))
         return y
 
-    # -- device-pointer calls (asynchronous on `stream`, a cudaStream_t int) --
-    def matmul_dev(self, w: "Weight", d_x, d_y, tokens: int, stream: int = 0):
-        self._check(self.L.q35k_matmul_dev(self.h, w.h, _dev_ptr(d_x), _dev_ptr(d_y), tokens, stream or None))
+    # -- device-pointer calls (asynchronous on `stream`: a torch.cuda.Stream,
+    #    a cudaStream_t int, or None for the context's own stream) --
+    def matmul_dev(self, w: "Weight", d_x, d_y, tokens: int, stream=None):
+        self._check(self.L.q35k_matmul_dev(self.h, w.h, _dev_ptr(d_x), _dev_ptr(d_y), tokens, _stream(stream)))
 
-    def matmul_q8k_dev(self, w: "Weight", d_q8, d_y, tokens: int, stream: int = 0):
-        self._check(self.L.q35k_matmul_q8k_dev(self.h, w.h, _dev_ptr(d_q8), _dev_ptr(d_y), tokens, stream or None))
+    def matmul_q8k_dev(self, w: "Weight", d_q8, d_y, tokens: int, stream=None):
+        self._check(self.L.q35k_matmul_q8k_dev(self.h, w.h, _dev_ptr(d_q8), _dev_ptr(d_y), tokens, _stream(stream)))
 
-    def quantize_q8k_dev(self, d_x, d_q8, k: int, rows: int, stream: int = 0):
-        self._check(self.L.q35k_quantize_q8k_dev(self.h, _dev_ptr(d_x), _dev_ptr(d_q8), k, rows, stream or None))
+    def quantize_q8k_dev(self, d_x, d_q8, k: int, rows: int, stream=None):
+        self._check(self.L.q35k_quantize_q8k_dev(self.h, _dev_ptr(d_x), _dev_ptr(d_q8), k, rows, _stream(stream)))
 
-    def dequantize_dev(self, qtype: int, d_blocks, d_y, k: int, rows: int, stream: int = 0):
+    def dequantize_dev(self, qtype: int, d_blocks, d_y, k: int, rows: int, stream=None):
         self._check(self.L.q35k_dequantize_dev(self.h, qtype, _dev_ptr(d_blocks), _dev_ptr(d_y), k, rows,
-                                               stream or None))
+                                               _stream(stream)))
 
 
 class Weight:
