@@ -6,20 +6,22 @@
 //     tiles (32 rows x 1 super-block, see device_common.cuh) in row-group
 //     order and every CTA owns one contiguous, equal share of it (stream-K),
 //     so the load is balanced to one tile whatever the shape;
-//   * one producer lane streams the CTA's tiles through a deep shared-memory
-//     ring with 1-D bulk async copies (cp.async.bulk, no multicast), one
-//     full/empty mbarrier pair per stage, keeping ~100+ KB per SM in flight;
-//   * eight consumer warps take the tiles of each row group round-robin;
-//     lane r decodes row r (chunk-major tiles: every 16-byte load is one
-//     contiguous 512-byte line per warp), all lanes read the same Q8_K words
+//   * one producer lane streams the CTA's tiles through a power-of-two ring
+//     of shared-memory stages with 1-D bulk async copies (cp.async.bulk, no
+//     multicast), one full/empty mbarrier pair per stage;
+//   * each consumer warp owns whole row groups (lane r = row r), so no
+//     cross-warp reduction or barrier sits in the main loop: the producer
+//     interleaves the tiles of the row groups the warps are working on
+//     ("rounds" of up to NW row groups, tile t of every row group in turn);
+//   * the chunk-major tile layout makes every 16-byte load a contiguous
+//     512-byte line per warp; all lanes read the same Q8_K words
 //     (shared-memory broadcast);
-//   * integer dots with dp4a into exact int32 per super-block, scaled in fp32
-//     once per block: acc += (d_w*d_x)*S - (dmin_w*d_x)*Mn
+//   * integer dots (dp4a, dp2a) into exact int32 per super-block, scaled in
+//     fp32 once per block: acc += (d_w*d_x)*S - (dmin_w*d_x)*Mn
 //     (VecDotQ4K.DotScalar, Kernels/VecDotQ4K.cs:42-61; Q5K.Dot,
 //     Kernels/Q5K.cs:62-83; the Q6_K bias form of Q6K.DotAvx2,
 //     Kernels/Q6K.cs:105-108,159);
-//   * per row group the warps reduce through shared memory in fixed order; a
-//     row group cut by a CTA boundary is finished by whichever CTA arrives
+//   * a row group cut by a CTA boundary is finished by whichever CTA arrives
 //     last, summing the pieces in CTA order (deterministic) and resetting the
 //     group's arrival counter for the next call;
 //   * the activation quantizer runs as the preceding kernel; with
@@ -32,45 +34,54 @@
 
 namespace q35k {
 
-constexpr int GEMV_CONSUMERS = 8;                 // consumer warps
-constexpr int GEMV_THREADS = (GEMV_CONSUMERS + 1) * 32;
 constexpr int GEMV_MAX_TOKENS = 8;
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
-constexpr int GEMV_RING_TARGET = 160 * 1024;     // bytes of weight ring per SM
-constexpr int GEMV_Q8_LIMIT = 96 * 1024;          // staged Q8_K activations per CTA
+constexpr int GEMV_MAX_STAGES = 32;
+constexpr int GEMV_Q8_LIMIT = 96 * 1024;  // staged Q8_K activations per CTA
+
+// Consumer warps: more for few tokens (fewer registers per thread).
+__host__ __device__ constexpr int gemv_consumers(int m) { return m <= 2 ? 12 : 8; }
 
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct SmemLayout {
-    int full, empty, ring, q8s, q8d, q8b, red, total;
+    int full, empty, ring, q8s, q8d, q8b, total;
 };
 
 // Dynamic shared memory of one GEMV CTA (16-byte aligned regions):
-// full mbarriers | empty mbarriers | weight ring | Q8_K qs | Q8_K d |
-// Q8_K bsums | double-buffered cross-warp reduction.
+// full mbarriers | empty mbarriers | weight ring | Q8_K qs | Q8_K d | Q8_K bsums.
 __host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int stages, int m, int nb) {
     SmemLayout L;
     L.full = 0;
-    L.empty = 8 * stages;
-    L.ring = align_up(16 * stages, 128);
+    L.empty = 8 * GEMV_MAX_STAGES;
+    L.ring = 16 * GEMV_MAX_STAGES;
     L.q8s = L.ring + stages * tile_bytes;
     L.q8d = L.q8s + m * nb * QK;
     L.q8b = L.q8d + align_up(m * nb * 4, 16);
-    L.red = L.q8b + align_up(m * nb * 32, 16);
-    L.total = L.red + 2 * GEMV_CONSUMERS * m * 32 * 4;
+    L.total = L.q8b + align_up(m * nb * 32, 16);
     return L;
 }
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+template <int NTHREADS>
 __device__ __forceinline__ void consumer_bar() {
-    asm volatile("bar.sync 1, %0;" ::"n"(GEMV_CONSUMERS * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(NTHREADS) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-
+// dp4a with unsigned a bytes (0..255) and signed b bytes.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// Sign-extend byte k of w (PRMT with sign replication).
+__device__ __forceinline__ int sext_byte(uint32_t w, int k) {
+    const int sel = k | ((k | 8) << 4) | ((k | 8) << 8) | ((k | 8) << 12);
+    return (int)__byte_perm(w, 0u, (unsigned)sel);
+}
 __device__ __forceinline__ int byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xff; }
-__device__ __forceinline__ int sbyte_of(uint32_t w, int k) { return (int)(int8_t)((w >> (8 * k)) & 0xff); }
 
 // Q4_K / Q5_K header: fp16 d, fp16 dmin, 12 bytes of 6-bit scales/mins,
 // unpacked as Q4K.UnpackScales (Kernels/Q4K.cs:20-33).
@@ -90,22 +101,6 @@ __device__ __forceinline__ KHeader unpack_header(uint4 h) {
     return k;
 }
 __device__ __forceinline__ int k_scale(const KHeader& k, int j) { return byte_of(j < 4 ? k.sc_lo : k.sc_hi, j & 3); }
-__device__ __forceinline__ int k_min(const KHeader& k, int j) { return byte_of(j < 4 ? k.mn_lo : k.mn_hi, j & 3); }
-
-// Sum_j mins_j * (bsums[2j] + bsums[2j+1]) from the 16 int16 block sums.
-__device__ __forceinline__ int mins_dot(const KHeader& k, const int16_t* bs) {
-    const int4 b0 = *reinterpret_cast<const int4*>(bs);
-    const int4 b1 = *reinterpret_cast<const int4*>(bs + 8);
-    const uint32_t w[8] = {(uint32_t)b0.x, (uint32_t)b0.y, (uint32_t)b0.z, (uint32_t)b0.w,
-                           (uint32_t)b1.x, (uint32_t)b1.y, (uint32_t)b1.z, (uint32_t)b1.w};
-    int mn = 0;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int pair = (int)(int16_t)(w[j] & 0xffffu) + (int)(int16_t)(w[j] >> 16);
-        mn += k_min(k, j) * pair;
-    }
-    return mn;
-}
 
 // Staged Q8_K activations: qs[m][nb][256], d[m][nb], bsums[m][nb][16].
 struct Q8Smem {
@@ -138,40 +133,54 @@ __device__ __forceinline__ void block_dot_k45(const uint8_t* __restrict__ tile, 
         const uint4 c0 = *reinterpret_cast<const uint4*>(tile + (QS_CHUNK + 2 * gg) * 512 + r * 16);
         const uint4 c1 = *reinterpret_cast<const uint4*>(tile + (QS_CHUNK + 1 + 2 * gg) * 512 + r * 16);
         const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        int lo[8], hi[8];
+        // lo: low nibbles; hi16: high nibbles left in place (16 x value), so
+        // no shift is needed; the 16 is divided out exactly after the dots.
+        uint32_t lo[8], hi16[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            uint32_t l = w[i] & 0x0f0f0f0fu;
-            uint32_t h = (w[i] >> 4) & 0x0f0f0f0fu;
+            lo[i] = w[i] & 0x0f0f0f0fu;
+            hi16[i] = w[i] & 0xf0f0f0f0u;
             if (TYPE == TYPE_Q5_K) {
-                l |= ((qh[i] >> (2 * gg)) & 0x01010101u) << 4;
-                h |= ((qh[i] >> (2 * gg + 1)) & 0x01010101u) << 4;
+                lo[i] |= ((qh[i] >> (2 * gg)) & 0x01010101u) << 4;
+                hi16[i] = (hi16[i] >> 4) | (((qh[i] >> (2 * gg + 1)) & 0x01010101u) << 4);
             }
-            lo[i] = (int)l;
-            hi[i] = (int)h;
         }
         const int scl = k_scale(hd, 2 * gg), sch = k_scale(hd, 2 * gg + 1);
 #pragma unroll
         for (int m = 0; m < M; m++) {
             const int4* qv = reinterpret_cast<const int4*>(q8.q(m, b) + 64 * gg);
             const int4 a0 = qv[0], a1 = qv[1], a2 = qv[2], a3 = qv[3];
-            int sl0 = dp4a(lo[0], a0.x, 0), sl1 = dp4a(lo[1], a0.y, 0);
-            sl0 = dp4a(lo[2], a0.z, sl0); sl1 = dp4a(lo[3], a0.w, sl1);
-            sl0 = dp4a(lo[4], a1.x, sl0); sl1 = dp4a(lo[5], a1.y, sl1);
-            sl0 = dp4a(lo[6], a1.z, sl0); sl1 = dp4a(lo[7], a1.w, sl1);
-            int sh0 = dp4a(hi[0], a2.x, 0), sh1 = dp4a(hi[1], a2.y, 0);
-            sh0 = dp4a(hi[2], a2.z, sh0); sh1 = dp4a(hi[3], a2.w, sh1);
-            sh0 = dp4a(hi[4], a3.x, sh0); sh1 = dp4a(hi[5], a3.y, sh1);
-            sh0 = dp4a(hi[6], a3.z, sh0); sh1 = dp4a(hi[7], a3.w, sh1);
-            S[m] += scl * (sl0 + sl1) + sch * (sh0 + sh1);
+            int sl0 = dp4a_us(lo[0], a0.x, 0), sl1 = dp4a_us(lo[1], a0.y, 0);
+            sl0 = dp4a_us(lo[2], a0.z, sl0); sl1 = dp4a_us(lo[3], a0.w, sl1);
+            sl0 = dp4a_us(lo[4], a1.x, sl0); sl1 = dp4a_us(lo[5], a1.y, sl1);
+            sl0 = dp4a_us(lo[6], a1.z, sl0); sl1 = dp4a_us(lo[7], a1.w, sl1);
+            int sh0 = dp4a_us(hi16[0], a2.x, 0), sh1 = dp4a_us(hi16[1], a2.y, 0);
+            sh0 = dp4a_us(hi16[2], a2.z, sh0); sh1 = dp4a_us(hi16[3], a2.w, sh1);
+            sh0 = dp4a_us(hi16[4], a3.x, sh0); sh1 = dp4a_us(hi16[5], a3.y, sh1);
+            sh0 = dp4a_us(hi16[6], a3.z, sh0); sh1 = dp4a_us(hi16[7], a3.w, sh1);
+            const int sh = (TYPE == TYPE_Q5_K) ? (sh0 + sh1) : ((sh0 + sh1) >> 4);
+            S[m] += scl * (sl0 + sl1) + sch * sh;
         }
     }
+    // Mins: sum_j m_j * (bsums[2j] + bsums[2j+1]) with dp2a against [m_j, m_j]
+    // byte pairs (6-bit mins are non-negative bytes).
+    const uint32_t mp0 = __byte_perm(hd.mn_lo, 0u, 0x1100u), mp1 = __byte_perm(hd.mn_lo, 0u, 0x3322u);
+    const uint32_t mp2 = __byte_perm(hd.mn_hi, 0u, 0x1100u), mp3 = __byte_perm(hd.mn_hi, 0u, 0x3322u);
 #pragma unroll
     for (int m = 0; m < M; m++) {
-        const int Mn = mins_dot(hd, q8.bsums(m, b));
+        const int4 b0 = *reinterpret_cast<const int4*>(q8.bsums(m, b));
+        const int4 b1 = *reinterpret_cast<const int4*>(q8.bsums(m, b) + 8);
+        int mn = __dp2a_lo(b0.x, (int)mp0, 0);
+        mn = __dp2a_hi(b0.y, (int)mp0, mn);
+        mn = __dp2a_lo(b0.z, (int)mp1, mn);
+        mn = __dp2a_hi(b0.w, (int)mp1, mn);
+        mn = __dp2a_lo(b1.x, (int)mp2, mn);
+        mn = __dp2a_hi(b1.y, (int)mp2, mn);
+        mn = __dp2a_lo(b1.z, (int)mp3, mn);
+        mn = __dp2a_hi(b1.w, (int)mp3, mn);
         const float dx = q8.dx(m, b);
         acc[m] = fmaf(hd.d * dx, (float)S[m], acc[m]);
-        acc[m] = fmaf(-(hd.dmin * dx), (float)Mn, acc[m]);
+        acc[m] = fmaf(-(hd.dmin * dx), (float)mn, acc[m]);
     }
 }
 
@@ -180,12 +189,7 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
                                               float* acc) {
     const float d = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(tile + Fmt<TYPE_Q6_K>::D_OFFSET + r * 2));
     const uint4 scv = *reinterpret_cast<const uint4*>(tile + 12 * 512 + r * 16);
-    int sc[16];
-    {
-        const uint32_t s4[4] = {scv.x, scv.y, scv.z, scv.w};
-#pragma unroll
-        for (int j = 0; j < 16; j++) sc[j] = sbyte_of(s4[j >> 2], j & 3);
-    }
+    const uint32_t s4[4] = {scv.x, scv.y, scv.z, scv.w};
     int S[M];
 #pragma unroll
     for (int m = 0; m < M; m++) S[m] = 0;
@@ -207,7 +211,9 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
                 q3[i] = (int)(((a[i] >> 4) & 0x0f0f0f0fu) | (hh[i] & 0x30303030u));
                 q4[i] = (int)(((bq[i] >> 4) & 0x0f0f0f0fu) | ((hh[i] >> 2) & 0x30303030u));
             }
-            const int s1 = sc[8 * h + lg], s2 = sc[8 * h + 2 + lg], s3 = sc[8 * h + 4 + lg], s4 = sc[8 * h + 6 + lg];
+            // 16-value sub-block scales 8h+lg, +2, +4, +6 (signed bytes).
+            const int s1 = sext_byte(s4[2 * h], lg), s2 = sext_byte(s4[2 * h], 2 + lg);
+            const int s3 = sext_byte(s4[2 * h + 1], lg), s4v = sext_byte(s4[2 * h + 1], 2 + lg);
 #pragma unroll
             for (int m = 0; m < M; m++) {
                 const int8_t* base = q8.q(m, b) + 128 * h + 16 * lg;
@@ -219,22 +225,24 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
                 int d2 = dp4a(q2[0], x2.x, 0); d2 = dp4a(q2[1], x2.y, d2); d2 = dp4a(q2[2], x2.z, d2); d2 = dp4a(q2[3], x2.w, d2);
                 int d3 = dp4a(q3[0], x3.x, 0); d3 = dp4a(q3[1], x3.y, d3); d3 = dp4a(q3[2], x3.z, d3); d3 = dp4a(q3[3], x3.w, d3);
                 int d4 = dp4a(q4[0], x4.x, 0); d4 = dp4a(q4[1], x4.y, d4); d4 = dp4a(q4[2], x4.z, d4); d4 = dp4a(q4[3], x4.w, d4);
-                S[m] += s1 * d1 + s2 * d2 + s3 * d3 + s4 * d4;
+                S[m] += s1 * d1 + s2 * d2 + s3 * d3 + s4v * d4;
             }
         }
     }
 #pragma unroll
     for (int m = 0; m < M; m++) {
-        // -32 bias folded through the Q8_K block sums (Kernels/Q6K.cs:105-108).
-        const int16_t* bsp = q8.bsums(m, b);
-        const int4 b0 = *reinterpret_cast<const int4*>(bsp);
-        const int4 b1 = *reinterpret_cast<const int4*>(bsp + 8);
-        const uint32_t w[8] = {(uint32_t)b0.x, (uint32_t)b0.y, (uint32_t)b0.z, (uint32_t)b0.w,
-                               (uint32_t)b1.x, (uint32_t)b1.y, (uint32_t)b1.z, (uint32_t)b1.w};
-        int bias = 0;
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-            bias += sc[2 * j] * (int)(int16_t)(w[j] & 0xffffu) + sc[2 * j + 1] * (int)(int16_t)(w[j] >> 16);
+        // -32 bias folded through the Q8_K block sums (Kernels/Q6K.cs:105-108):
+        // sum_j sc_j * bsums_j with dp2a (int16 bsums x signed-byte scales).
+        const int4 b0 = *reinterpret_cast<const int4*>(q8.bsums(m, b));
+        const int4 b1 = *reinterpret_cast<const int4*>(q8.bsums(m, b) + 8);
+        int bias = __dp2a_lo(b0.x, (int)s4[0], 0);
+        bias = __dp2a_hi(b0.y, (int)s4[0], bias);
+        bias = __dp2a_lo(b0.z, (int)s4[1], bias);
+        bias = __dp2a_hi(b0.w, (int)s4[1], bias);
+        bias = __dp2a_lo(b1.x, (int)s4[2], bias);
+        bias = __dp2a_hi(b1.y, (int)s4[2], bias);
+        bias = __dp2a_lo(b1.z, (int)s4[3], bias);
+        bias = __dp2a_hi(b1.w, (int)s4[3], bias);
         acc[m] = fmaf(d * q8.dx(m, b), (float)(S[m] - 32 * bias), acc[m]);
     }
 }
@@ -245,8 +253,67 @@ __device__ __forceinline__ int tile_owner(long T, long tiles, int grid) {
     return (int)(((T + 1) * (long)grid - 1) / tiles);
 }
 
+// The CTA's share [T0, T1) of the tile sequence as work items, in issue order:
+//   head  : a partial first row group (tiles tb..te-1), warp 0;
+//   rounds: full row groups, NW at a time; in round r the j-th row group goes
+//           to warp (j + hoff) % NW and tile t of it sits at ring position
+//           base_r + t * nj + j;
+//   tail  : a partial last row group, the next warp in rotation.
+struct Share {
+    long g_head;
+    int head_tb, head_te;  // head piece (head_te > head_tb if present)
+    long g_full0;          // first full row group
+    int nfull;             // number of full row groups
+    long g_tail;
+    int tail_te;           // tail piece tiles 0..tail_te-1 (tail_te > 0 if present)
+    int hoff;              // 1 if a head piece exists
+};
+
+__device__ __forceinline__ Share make_share(long T0, long T1, int nb) {
+    Share s{};
+    const long gA = T0 / nb, gZ = (T1 - 1) / nb;
+    const int ta = (int)(T0 - gA * nb);       // first tile inside gA
+    const int tz = (int)(T1 - gZ * nb);       // tiles of gZ inside the share
+    if (gA == gZ) {
+        if (ta == 0 && tz == nb) {
+            s.g_full0 = gA;
+            s.nfull = 1;
+        } else {
+            s.g_head = gA;
+            s.head_tb = ta;
+            s.head_te = tz;
+        }
+    } else {
+        long f0 = gA, f1 = gZ + 1;  // full row groups [f0, f1)
+        if (ta != 0) {
+            s.g_head = gA;
+            s.head_tb = ta;
+            s.head_te = nb;
+            f0 = gA + 1;
+        }
+        if (tz != nb) {
+            s.g_tail = gZ;
+            s.tail_te = tz;
+            f1 = gZ;
+        }
+        s.g_full0 = f0;
+        s.nfull = (int)(f1 - f0);
+    }
+    s.hoff = s.head_te > s.head_tb ? 1 : 0;
+    return s;
+}
+
 template <int TYPE, int M>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(GemvArgs a, GemvPlan p) {
+__device__ __forceinline__ void tile_dot(const uint8_t* tile, int lane, const Q8Smem& q8, int b, float* acc) {
+    if (TYPE == TYPE_Q6_K)
+        block_dot_q6k<M>(tile, lane, q8, b, acc);
+    else
+        block_dot_k45<TYPE, M>(tile, lane, q8, b, acc);
+}
+
+template <int TYPE, int M>
+__global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(GemvArgs a, GemvPlan p) {
+    constexpr int NW = gemv_consumers(M);
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
     const SmemLayout L = gemv_smem_layout(TILE, p.stages, M, a.nb);
@@ -259,10 +326,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(GemvArgs a, GemvP
     const long tiles = (long)p.groups * nb;
     const long T0 = tiles * blockIdx.x / gridDim.x;
     const long T1 = tiles * (blockIdx.x + 1) / gridDim.x;
-    const int S = p.stages;
+    const int smask = p.stages - 1, slog = p.stage_log2;
+    const Share sh = make_share(T0, T1, nb);
+    const int head_len = sh.head_te - sh.head_tb;
 
     if (tid == 0) {
-        for (int i = 0; i < S; i++) {
+        for (int i = 0; i < p.stages; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
@@ -270,17 +339,27 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(GemvArgs a, GemvP
     }
     __syncthreads();
 
-    if (warp == GEMV_CONSUMERS) {
-        // ---------------- producer: stream this CTA's tiles ----------------
-        if (lane == 0) {
-            for (long T = T0; T < T1; T++) {
-                const long c = T - T0;
-                const int st = (int)(c % S);
-                if (c >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((c / S) - 1) & 1), a.err)) break;
+    if (warp == NW) {
+        // ---------------- producer: issue tiles in ring-position order ----------------
+        if (lane != 0) return;
+        int c = 0;
+        bool ok = true;
+        auto issue = [&](long T) {
+            const int st = c & smask;
+            if (c > smask) ok = ok && mbar_wait_bounded(&empty[st], (uint32_t)(((c >> slog) - 1) & 1), a.err);
+            if (ok) {
                 mbar_arrive_expect_tx(&full[st], TILE);
                 bulk_g2s(ring + (size_t)st * TILE, a.tiles + (size_t)T * TILE, TILE, &full[st]);
             }
+            c++;
+        };
+        for (int t = sh.head_tb; t < sh.head_te && ok; t++) issue(sh.g_head * nb + t);
+        for (int r0 = 0; r0 < sh.nfull && ok; r0 += NW) {
+            const int nj = min(NW, sh.nfull - r0);
+            for (int t = 0; t < nb && ok; t++)
+                for (int j = 0; j < nj; j++) issue((sh.g_full0 + r0 + j) * nb + t);
         }
+        for (int t = 0; t < sh.tail_te && ok; t++) issue(sh.g_tail * nb + t);
         return;
     }
 
@@ -290,7 +369,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(GemvArgs a, GemvP
     float* q8d = reinterpret_cast<float*>(smem + L.q8d);
     int16_t* q8b = reinterpret_cast<int16_t*>(smem + L.q8b);
     // 73 words per BlockQ8K: word 0 = d, 1..64 = qs, 65..72 = bsums.
-    for (int idx = tid; idx < M * nb * 73; idx += GEMV_CONSUMERS * 32) {
+    for (int idx = tid; idx < M * nb * 73; idx += NW * 32) {
         const int mb = idx / 73, w = idx % 73;
         const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(a.q8 + (size_t)mb * Q8K_BYTES) + w);
         if (w == 0)
@@ -300,78 +379,77 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(GemvArgs a, GemvP
         else
             reinterpret_cast<uint32_t*>(q8b + mb * 16)[w - 65] = v;
     }
-    consumer_bar();
+    consumer_bar<NW * 32>();
     const Q8Smem q8{q8s, q8d, q8b, nb};
-    float* red = reinterpret_cast<float*>(smem + L.red);
 
-    int par = 0;
-    bool timed_out = false;
-    const long g_first = T0 / nb, g_last = (T1 - 1) / nb;
-    for (long g = g_first; T1 > T0 && g <= g_last; g++) {
-        const long tb0 = max(T0, g * nb), tb1 = min(T1, (g + 1) * nb);
+    bool ok = true;
+    // Process ring position c (tile b of the warp's current row group).
+    auto consume = [&](int c, int b, float* acc) {
+        const int st = c & smask;
+        if (ok && !mbar_wait_bounded(&full[st], (uint32_t)((c >> slog) & 1), a.err)) ok = false;
+        if (ok) tile_dot<TYPE, M>(ring + (size_t)st * TILE, lane, q8, b, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    };
+    auto store_whole = [&](long g, const float* acc) {
+        const int row = (int)g * TILE_ROWS + lane;
+        if (row < a.n_out)
+#pragma unroll
+            for (int m = 0; m < M; m++) a.y[(size_t)m * a.ldy + row] = acc[m];
+    };
+    // A row group cut by a CTA boundary: publish this CTA's piece; the last
+    // piece to arrive sums all pieces in CTA order and stores y.
+    auto store_piece = [&](long g, const float* acc) {
+        const int row = (int)g * TILE_ROWS + lane;
+        const int first = tile_owner(g * nb, tiles, gridDim.x);
+        const int pieces = tile_owner((g + 1) * nb - 1, tiles, gridDim.x) - first + 1;
+        const int piece = (int)blockIdx.x - first;
+        float* part = a.partial + (size_t)g * p.max_pieces * M * 32;
+#pragma unroll
+        for (int m = 0; m < M; m++) part[((size_t)piece * M + m) * 32 + lane] = acc[m];
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&a.counters[g], 1) == pieces - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence();
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                float s = 0.f;
+                for (int k = 0; k < pieces; k++) s += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
+                if (row < a.n_out) a.y[(size_t)m * a.ldy + row] = s;
+            }
+            if (lane == 0) a.counters[g] = 0;
+        }
+    };
+
+    if (head_len > 0 && warp == 0) {
         float acc[M];
 #pragma unroll
         for (int m = 0; m < M; m++) acc[m] = 0.f;
-        for (long T = tb0 + warp; T < tb1; T += GEMV_CONSUMERS) {
-            const long c = T - T0;
-            const int st = (int)(c % S);
-            if (!timed_out && !mbar_wait_bounded(&full[st], (uint32_t)((c / S) & 1), a.err)) timed_out = true;
-            if (!timed_out) {
-                const uint8_t* tile = ring + (size_t)st * TILE;
-                const int b = (int)(T - g * nb);
-                if (TYPE == TYPE_Q6_K)
-                    block_dot_q6k<M>(tile, lane, q8, b, acc);
-                else
-                    block_dot_k45<TYPE, M>(tile, lane, q8, b, acc);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+        for (int t = sh.head_tb; t < sh.head_te; t++) consume(t - sh.head_tb, t, acc);
+        store_piece(sh.g_head, acc);
+    }
+    int base = head_len;
+    for (int r0 = 0; r0 < sh.nfull; r0 += NW) {
+        const int nj = min(NW, sh.nfull - r0);
+        const int j = (warp - sh.hoff + NW) % NW;
+        if (j < nj) {
+            float acc[M];
+#pragma unroll
+            for (int m = 0; m < M; m++) acc[m] = 0.f;
+            for (int t = 0; t < nb; t++) consume(base + t * nj + j, t, acc);
+            store_whole(sh.g_full0 + r0 + j, acc);
         }
-        float* rbuf = red + par * GEMV_CONSUMERS * M * 32;
+        base += nb * nj;
+    }
+    if (sh.tail_te > 0 && warp == (sh.hoff + sh.nfull) % NW) {
+        float acc[M];
 #pragma unroll
-        for (int m = 0; m < M; m++) rbuf[(warp * M + m) * 32 + lane] = acc[m];
-        consumer_bar();
-        if (warp == 0) {
-            const int row = (int)g * TILE_ROWS + lane;
-            const bool whole = (tb0 == g * nb) && (tb1 == (g + 1) * nb);
-            float v[M];
-#pragma unroll
-            for (int m = 0; m < M; m++) {
-                v[m] = rbuf[m * 32 + lane];
-#pragma unroll
-                for (int w = 1; w < GEMV_CONSUMERS; w++) v[m] += rbuf[(w * M + m) * 32 + lane];
-            }
-            if (whole) {
-                if (row < a.n_out)
-#pragma unroll
-                    for (int m = 0; m < M; m++) a.y[(size_t)m * a.ldy + row] = v[m];
-            } else {
-                // Row group cut by a CTA boundary: publish this piece, and
-                // the last piece to arrive sums all of them in CTA order.
-                const int first = tile_owner(g * nb, tiles, gridDim.x);
-                const int pieces = tile_owner((g + 1) * nb - 1, tiles, gridDim.x) - first + 1;
-                const int piece = (int)blockIdx.x - first;
-                float* part = a.partial + ((size_t)g * p.max_pieces) * M * 32;
-#pragma unroll
-                for (int m = 0; m < M; m++) part[((size_t)piece * M + m) * 32 + lane] = v[m];
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) last = atomicAdd(&a.counters[g], 1) == pieces - 1;
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-#pragma unroll
-                    for (int m = 0; m < M; m++) {
-                        float s = 0.f;
-                        for (int k = 0; k < pieces; k++) s += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
-                        if (row < a.n_out) a.y[(size_t)m * a.ldy + row] = s;
-                    }
-                    if (lane == 0) a.counters[g] = 0;
-                }
-            }
-        }
-        par ^= 1;
+        for (int m = 0; m < M; m++) acc[m] = 0.f;
+        for (int t = 0; t < sh.tail_te; t++) consume(base + t, t, acc);
+        store_piece(sh.g_tail, acc);
     }
 }
 
@@ -383,10 +461,12 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.n_pad = p.groups * TILE_ROWS;
     const long tiles = (long)p.groups * nb;
     p.grid = (int)std::min<long>(tiles, num_sms);
-    // Stages: fill the ring target within the shared-memory limit.
-    const SmemLayout base = gemv_smem_layout(tile, 0, m, nb);
-    const int room = GEMV_SMEM_LIMIT - base.total - 256;
-    p.stages = std::max(2, std::min(GEMV_RING_TARGET, room) / (tile + 16));
+    // Stages: the largest power of two (<= 32) that fits next to the staged
+    // activations.
+    const int room = GEMV_SMEM_LIMIT - gemv_smem_layout(tile, 0, m, nb).total;
+    p.stage_log2 = 1;
+    while (p.stage_log2 < 5 && (2 << p.stage_log2) * tile <= room) p.stage_log2++;
+    p.stages = 1 << p.stage_log2;
     p.smem_bytes = (size_t)gemv_smem_layout(tile, p.stages, m, nb).total;
     // A row group spans at most this many CTAs.
     const long per_cta = std::max<long>(1, tiles / p.grid);
@@ -394,6 +474,7 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.partial_bytes = (size_t)p.groups * p.max_pieces * GEMV_MAX_TOKENS * 32 * sizeof(float);
     p.counters = (size_t)p.groups;
     p.fits = (long)m * nb * Q8K_BYTES <= GEMV_Q8_LIMIT && p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;
+    p.threads = (gemv_consumers(m) + 1) * 32;
     return p;
 }
 
@@ -433,7 +514,7 @@ static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream
     if (!p.fits) return cudaErrorInvalidConfiguration;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)p.grid);
-    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.blockDim = dim3((unsigned)p.threads);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
