@@ -76,11 +76,8 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
-// Sign-extend byte k of w (PRMT with sign replication).
-__device__ __forceinline__ int sext_byte(uint32_t w, int k) {
-    const int sel = k | ((k | 8) << 4) | ((k | 8) << 8) | ((k | 8) << 12);
-    return (int)__byte_perm(w, 0u, (unsigned)sel);
-}
+// Sign-extend byte k of w.
+__device__ __forceinline__ int sext_byte(uint32_t w, int k) { return (int)(int8_t)(uint8_t)(w >> (8 * k)); }
 __device__ __forceinline__ int byte_of(uint32_t w, int k) { return (w >> (8 * k)) & 0xff; }
 
 // Q4_K / Q5_K header: fp16 d, fp16 dmin, 12 bytes of 6-bit scales/mins,
