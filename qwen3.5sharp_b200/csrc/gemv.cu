@@ -36,7 +36,8 @@ namespace q35k {
 
 constexpr int GEMV_MAX_TOKENS = 8;
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
-constexpr int GEMV_MAX_STAGES = 32;
+constexpr int GEMV_MAX_STAGES = 48;                // consumer warps x stages per warp
+constexpr int GEMV_RING_BUDGET = 180 * 1024;       // weight bytes in flight per SM (upper bound)
 constexpr int GEMV_Q8_LIMIT = 96 * 1024;  // staged Q8_K activations per CTA
 
 // Consumer warps: more for few tokens (fewer registers per thread).
@@ -323,12 +324,15 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     const long tiles = (long)p.groups * nb;
     const long T0 = tiles * blockIdx.x / gridDim.x;
     const long T1 = tiles * (blockIdx.x + 1) / gridDim.x;
-    const int smask = p.stages - 1, slog = p.stage_log2;
+    // Each consumer warp owns a private run of 2^wlog stages and consumes it
+    // in order (the single-consumer pipeline that mbarrier phase parity
+    // needs); its i-th tile lands in stage warp*2^wlog + i % 2^wlog.
+    const int wlog = p.warp_stage_log2, wmask = (1 << wlog) - 1;
     const Share sh = make_share(T0, T1, nb);
     const int head_len = sh.head_te - sh.head_tb;
 
     if (tid == 0) {
-        for (int i = 0; i < p.stages; i++) {
+        for (int i = 0; i < NW << wlog; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
@@ -337,26 +341,34 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     __syncthreads();
 
     if (warp == NW) {
-        // ---------------- producer: issue tiles in ring-position order ----------------
+        // ---------------- producer: issue tiles round by round ----------------
+        // Tile t of the j-th row group of round R goes to warp w = (j + hoff)
+        // % NW as that warp's tile number i = (head tiles of w) + R*nb + t.
         if (lane != 0) return;
-        int c = 0;
         bool ok = true;
-        auto issue = [&](long T) {
-            const int st = c & smask;
-            if (c > smask) ok = ok && mbar_wait_bounded(&empty[st], (uint32_t)(((c >> slog) - 1) & 1), a.err);
+        auto issue = [&](long T, int w, int i) {
+            const int st = (w << wlog) + (i & wmask);
+            if (i > wmask) ok = ok && mbar_wait_bounded(&empty[st], (uint32_t)(((i >> wlog) - 1) & 1), a.err);
             if (ok) {
                 mbar_arrive_expect_tx(&full[st], TILE);
                 bulk_g2s(ring + (size_t)st * TILE, a.tiles + (size_t)T * TILE, TILE, &full[st]);
             }
-            c++;
         };
-        for (int t = sh.head_tb; t < sh.head_te && ok; t++) issue(sh.g_head * nb + t);
-        for (int r0 = 0; r0 < sh.nfull && ok; r0 += NW) {
+        for (int t = sh.head_tb; t < sh.head_te && ok; t++) issue(sh.g_head * nb + t, 0, t - sh.head_tb);
+        int R = 0;
+        for (int r0 = 0; r0 < sh.nfull && ok; r0 += NW, R++) {
             const int nj = min(NW, sh.nfull - r0);
             for (int t = 0; t < nb && ok; t++)
-                for (int j = 0; j < nj; j++) issue((sh.g_full0 + r0 + j) * nb + t);
+                for (int j = 0; j < nj; j++) {
+                    const int w = (j + sh.hoff) % NW;
+                    issue((sh.g_full0 + r0 + j) * nb + t, w, (w == 0 ? head_len : 0) + R * nb + t);
+                }
         }
-        for (int t = 0; t < sh.tail_te && ok; t++) issue(sh.g_tail * nb + t);
+        if (sh.tail_te > 0) {
+            const int w = (sh.hoff + sh.nfull) % NW;
+            const int i0 = (w == 0 ? head_len : 0) + (sh.nfull / NW) * nb;
+            for (int t = 0; t < sh.tail_te && ok; t++) issue(sh.g_tail * nb + t, w, i0 + t);
+        }
         return;
     }
 
@@ -380,13 +392,15 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     const Q8Smem q8{q8s, q8d, q8b, nb};
 
     bool ok = true;
-    // Process ring position c (tile b of the warp's current row group).
-    auto consume = [&](int c, int b, float* acc) {
-        const int st = c & smask;
-        if (ok && !mbar_wait_bounded(&full[st], (uint32_t)((c >> slog) & 1), a.err)) ok = false;
+    int i_tile = 0;  // this warp's tile counter (its private stages, in order)
+    // Process the warp's next tile: super-block b of its current row group.
+    auto consume = [&](int b, float* acc) {
+        const int st = (warp << wlog) + (i_tile & wmask);
+        if (ok && !mbar_wait_bounded(&full[st], (uint32_t)((i_tile >> wlog) & 1), a.err)) ok = false;
         if (ok) tile_dot<TYPE, M>(ring + (size_t)st * TILE, lane, q8, b, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
+        i_tile++;
     };
     auto store_whole = [&](long g, const float* acc) {
         const int row = (int)g * TILE_ROWS + lane;
@@ -425,10 +439,9 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
         float acc[M];
 #pragma unroll
         for (int m = 0; m < M; m++) acc[m] = 0.f;
-        for (int t = sh.head_tb; t < sh.head_te; t++) consume(t - sh.head_tb, t, acc);
+        for (int t = sh.head_tb; t < sh.head_te; t++) consume(t, acc);
         store_piece(sh.g_head, acc);
     }
-    int base = head_len;
     for (int r0 = 0; r0 < sh.nfull; r0 += NW) {
         const int nj = min(NW, sh.nfull - r0);
         const int j = (warp - sh.hoff + NW) % NW;
@@ -436,16 +449,15 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
             float acc[M];
 #pragma unroll
             for (int m = 0; m < M; m++) acc[m] = 0.f;
-            for (int t = 0; t < nb; t++) consume(base + t * nj + j, t, acc);
+            for (int t = 0; t < nb; t++) consume(t, acc);
             store_whole(sh.g_full0 + r0 + j, acc);
         }
-        base += nb * nj;
     }
     if (sh.tail_te > 0 && warp == (sh.hoff + sh.nfull) % NW) {
         float acc[M];
 #pragma unroll
         for (int m = 0; m < M; m++) acc[m] = 0.f;
-        for (int t = 0; t < sh.tail_te; t++) consume(base + t, t, acc);
+        for (int t = 0; t < sh.tail_te; t++) consume(t, acc);
         store_piece(sh.g_tail, acc);
     }
 }
@@ -458,12 +470,13 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.n_pad = p.groups * TILE_ROWS;
     const long tiles = (long)p.groups * nb;
     p.grid = (int)std::min<long>(tiles, num_sms);
-    // Stages: the largest power of two (<= 32) that fits next to the staged
-    // activations.
-    const int room = GEMV_SMEM_LIMIT - gemv_smem_layout(tile, 0, m, nb).total;
-    p.stage_log2 = 1;
-    while (p.stage_log2 < 5 && (2 << p.stage_log2) * tile <= room) p.stage_log2++;
-    p.stages = 1 << p.stage_log2;
+    // Stages per consumer warp: the largest power of two (<= 4) whose ring
+    // fits next to the staged activations and within the in-flight budget.
+    const int nw = gemv_consumers(m);
+    const int room = std::min(GEMV_SMEM_LIMIT - gemv_smem_layout(tile, 0, m, nb).total, GEMV_RING_BUDGET);
+    p.warp_stage_log2 = 0;
+    while (p.warp_stage_log2 < 2 && nw * (2 << p.warp_stage_log2) * tile <= room) p.warp_stage_log2++;
+    p.stages = nw << p.warp_stage_log2;
     p.smem_bytes = (size_t)gemv_smem_layout(tile, p.stages, m, nb).total;
     // A row group spans at most this many CTAs.
     const long per_cta = std::max<long>(1, tiles / p.grid);

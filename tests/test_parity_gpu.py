@@ -55,6 +55,24 @@ def test_small_shapes(ctx, oracle_mod, qt, k, n, m):
     assert rel_err(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("qt,k,n,m", [
+    (Q6_K, 256, 200_000, 1),    # nb=1: ~42 row groups per CTA, every stage reused many times
+    (Q4_K, 768, 50_001, 2),     # ragged N, 3 blocks per row, two tokens
+    (Q5_K, 1280, 40_000, 3),    # 8 consumer warps, more stages per warp
+    (Q4_K, 5120, 27_648, 7),
+    (Q6_K, 2560, 60_000, 8),
+])
+def test_ring_reuse_shapes(ctx, oracle_mod, qt, k, n, m):
+    """Shapes whose per-SM share is many times the stage ring, so every stage
+    and mbarrier phase is reused (the pipeline's steady state)."""
+    w = synth.kquant_blocks(qt, n, k, seed=n + m)
+    x = synth.activations(m, k, seed=m)
+    W = ctx.upload(qt, w, k, n)
+    y = ctx.matmul(W, x)
+    ref = oracle_mod.Weight(qt, w, k, n).matmul(x, threads=os.cpu_count() or 1)
+    assert rel_err(y, ref) <= TOL
+
+
 @pytest.mark.parametrize("qt", TYPES)
 def test_dequant_bit_exact_random(ctx, oracle_mod, qt):
     w = synth.kquant_blocks(qt, 64, 2048, seed=qt)
