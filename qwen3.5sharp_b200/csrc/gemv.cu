@@ -6,13 +6,17 @@
 //     tiles (32 rows x 1 super-block, see device_common.cuh) in row-group
 //     order and every CTA owns one contiguous, equal share of it (stream-K),
 //     so the load is balanced to one tile whatever the shape;
-//   * one producer lane streams the CTA's tiles through a power-of-two ring
-//     of shared-memory stages with 1-D bulk async copies (cp.async.bulk, no
-//     multicast), one full/empty mbarrier pair per stage;
-//   * each consumer warp owns whole row groups (lane r = row r), so no
-//     cross-warp reduction or barrier sits in the main loop: the producer
-//     interleaves the tiles of the row groups the warps are working on
-//     ("rounds" of up to NW row groups, tile t of every row group in turn);
+//   * one producer lane streams the CTA's tiles, in order, through a ring of
+//     S = NW * k shared-memory stages with 1-D bulk async copies
+//     (cp.async.bulk, no multicast), one full/empty mbarrier pair per stage;
+//   * tile c of the share goes to consumer warp c % NW and stage c % S, so
+//     every stage has exactly one consumer warp that takes its tiles in
+//     order (the single-consumer discipline mbarrier phase parity needs),
+//     and all NW warps stay busy whatever the shape;
+//   * lane r of a warp decodes row r of its tile; a row group's partial sums
+//     meet in a small ring of shared-memory slots, where the last warp to
+//     arrive adds them in tile order (deterministic) -- no barrier in the
+//     main loop;
 //   * the chunk-major tile layout makes every 16-byte load a contiguous
 //     512-byte line per warp; all lanes read the same Q8_K words
 //     (shared-memory broadcast);
@@ -46,20 +50,30 @@ __host__ __device__ constexpr int gemv_consumers(int m) { return m <= 2 ? 12 : 8
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct SmemLayout {
-    int full, empty, ring, q8s, q8d, q8b, total;
+    int full, empty, slot_cnt, ring, q8s, q8d, q8b, slots, total;
 };
 
+// Slots for row-group partial sums: a row group can be open in at most
+// ceil(S/nb)+1 slots at once (all tiles before the oldest unreleased one are
+// done), plus one of margin; each slot holds min(nb, NW) warp partials.
+__host__ __device__ constexpr int gemv_nslot(int stages, int nb) { return (stages + nb - 1) / nb + 2; }
+constexpr int GEMV_MAX_SLOTS = GEMV_MAX_STAGES + 2;
+
 // Dynamic shared memory of one GEMV CTA (16-byte aligned regions):
-// full mbarriers | empty mbarriers | weight ring | Q8_K qs | Q8_K d | Q8_K bsums.
-__host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int stages, int m, int nb) {
+// full mbarriers | empty mbarriers | slot counters | weight ring | Q8_K qs |
+// Q8_K d | Q8_K bsums | row-group partial slots.
+__host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int stages, int m, int nb, int nw) {
     SmemLayout L;
     L.full = 0;
     L.empty = 8 * GEMV_MAX_STAGES;
-    L.ring = 16 * GEMV_MAX_STAGES;
+    L.slot_cnt = 16 * GEMV_MAX_STAGES;
+    L.ring = align_up(L.slot_cnt + 4 * GEMV_MAX_SLOTS, 128);
     L.q8s = L.ring + stages * tile_bytes;
     L.q8d = L.q8s + m * nb * QK;
     L.q8b = L.q8d + align_up(m * nb * 4, 16);
-    L.total = L.q8b + align_up(m * nb * 32, 16);
+    L.slots = L.q8b + align_up(m * nb * 32, 16);
+    const int e = nb < nw ? nb : nw;
+    L.total = L.slots + (stages ? gemv_nslot(stages, nb) : 0) * e * m * 32 * 4;
     return L;
 }
 
@@ -251,55 +265,6 @@ __device__ __forceinline__ int tile_owner(long T, long tiles, int grid) {
     return (int)(((T + 1) * (long)grid - 1) / tiles);
 }
 
-// The CTA's share [T0, T1) of the tile sequence as work items, in issue order:
-//   head  : a partial first row group (tiles tb..te-1), warp 0;
-//   rounds: full row groups, NW at a time; in round r the j-th row group goes
-//           to warp (j + hoff) % NW and tile t of it sits at ring position
-//           base_r + t * nj + j;
-//   tail  : a partial last row group, the next warp in rotation.
-struct Share {
-    long g_head;
-    int head_tb, head_te;  // head piece (head_te > head_tb if present)
-    long g_full0;          // first full row group
-    int nfull;             // number of full row groups
-    long g_tail;
-    int tail_te;           // tail piece tiles 0..tail_te-1 (tail_te > 0 if present)
-    int hoff;              // 1 if a head piece exists
-};
-
-__device__ __forceinline__ Share make_share(long T0, long T1, int nb) {
-    Share s{};
-    const long gA = T0 / nb, gZ = (T1 - 1) / nb;
-    const int ta = (int)(T0 - gA * nb);       // first tile inside gA
-    const int tz = (int)(T1 - gZ * nb);       // tiles of gZ inside the share
-    if (gA == gZ) {
-        if (ta == 0 && tz == nb) {
-            s.g_full0 = gA;
-            s.nfull = 1;
-        } else {
-            s.g_head = gA;
-            s.head_tb = ta;
-            s.head_te = tz;
-        }
-    } else {
-        long f0 = gA, f1 = gZ + 1;  // full row groups [f0, f1)
-        if (ta != 0) {
-            s.g_head = gA;
-            s.head_tb = ta;
-            s.head_te = nb;
-            f0 = gA + 1;
-        }
-        if (tz != nb) {
-            s.g_tail = gZ;
-            s.tail_te = tz;
-            f1 = gZ;
-        }
-        s.g_full0 = f0;
-        s.nfull = (int)(f1 - f0);
-    }
-    s.hoff = s.head_te > s.head_tb ? 1 : 0;
-    return s;
-}
 
 template <int TYPE, int M>
 __device__ __forceinline__ void tile_dot(const uint8_t* tile, int lane, const Q8Smem& q8, int b, float* acc) {
@@ -314,25 +279,22 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     constexpr int NW = gemv_consumers(M);
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
-    const SmemLayout L = gemv_smem_layout(TILE, p.stages, M, a.nb);
+    const SmemLayout L = gemv_smem_layout(TILE, p.stages, M, a.nb, NW);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    int* slot_cnt = reinterpret_cast<int*>(smem + L.slot_cnt);
     uint8_t* ring = smem + L.ring;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nb = a.nb;
+    const int S = p.stages;  // a multiple of NW
     const long tiles = (long)p.groups * nb;
     const long T0 = tiles * blockIdx.x / gridDim.x;
     const long T1 = tiles * (blockIdx.x + 1) / gridDim.x;
-    // Each consumer warp owns a private run of 2^wlog stages and consumes it
-    // in order (the single-consumer pipeline that mbarrier phase parity
-    // needs); its i-th tile lands in stage warp*2^wlog + i % 2^wlog.
-    const int wlog = p.warp_stage_log2, wmask = (1 << wlog) - 1;
-    const Share sh = make_share(T0, T1, nb);
-    const int head_len = sh.head_te - sh.head_tb;
+    const int n_tiles = (int)(T1 - T0);
 
     if (tid == 0) {
-        for (int i = 0; i < NW << wlog; i++) {
+        for (int i = 0; i < S; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
@@ -341,33 +303,18 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     __syncthreads();
 
     if (warp == NW) {
-        // ---------------- producer: issue tiles round by round ----------------
-        // Tile t of the j-th row group of round R goes to warp w = (j + hoff)
-        // % NW as that warp's tile number i = (head tiles of w) + R*nb + t.
+        // ---------------- producer: this CTA's tiles in order ----------------
         if (lane != 0) return;
-        bool ok = true;
-        auto issue = [&](long T, int w, int i) {
-            const int st = (w << wlog) + (i & wmask);
-            if (i > wmask) ok = ok && mbar_wait_bounded(&empty[st], (uint32_t)(((i >> wlog) - 1) & 1), a.err);
-            if (ok) {
-                mbar_arrive_expect_tx(&full[st], TILE);
-                bulk_g2s(ring + (size_t)st * TILE, a.tiles + (size_t)T * TILE, TILE, &full[st]);
+        int st = 0;
+        uint32_t ph = 0;  // phase of the stage's current use
+        for (int c = 0; c < n_tiles; c++) {
+            if (c >= S && !mbar_wait_bounded(&empty[st], ph ^ 1u, a.err)) break;
+            mbar_arrive_expect_tx(&full[st], TILE);
+            bulk_g2s(ring + (size_t)st * TILE, a.tiles + (size_t)(T0 + c) * TILE, TILE, &full[st]);
+            if (++st == S) {
+                st = 0;
+                ph ^= 1u;
             }
-        };
-        for (int t = sh.head_tb; t < sh.head_te && ok; t++) issue(sh.g_head * nb + t, 0, t - sh.head_tb);
-        int R = 0;
-        for (int r0 = 0; r0 < sh.nfull && ok; r0 += NW, R++) {
-            const int nj = min(NW, sh.nfull - r0);
-            for (int t = 0; t < nb && ok; t++)
-                for (int j = 0; j < nj; j++) {
-                    const int w = (j + sh.hoff) % NW;
-                    issue((sh.g_full0 + r0 + j) * nb + t, w, (w == 0 ? head_len : 0) + R * nb + t);
-                }
-        }
-        if (sh.tail_te > 0) {
-            const int w = (sh.hoff + sh.nfull) % NW;
-            const int i0 = (w == 0 ? head_len : 0) + (sh.nfull / NW) * nb;
-            for (int t = 0; t < sh.tail_te && ok; t++) issue(sh.g_tail * nb + t, w, i0 + t);
         }
         return;
     }
@@ -388,36 +335,31 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
         else
             reinterpret_cast<uint32_t*>(q8b + mb * 16)[w - 65] = v;
     }
+    const int nslot = gemv_nslot(S, nb);
+    for (int i = tid; i < nslot; i += NW * 32) slot_cnt[i] = 0;
     consumer_bar<NW * 32>();
     const Q8Smem q8{q8s, q8d, q8b, nb};
+    const int E = min(nb, NW);
+    float* slots = reinterpret_cast<float*>(smem + L.slots);
 
-    bool ok = true;
-    int i_tile = 0;  // this warp's tile counter (its private stages, in order)
-    // Process the warp's next tile: super-block b of its current row group.
-    auto consume = [&](int b, float* acc) {
-        const int st = (warp << wlog) + (i_tile & wmask);
-        if (ok && !mbar_wait_bounded(&full[st], (uint32_t)((i_tile >> wlog) & 1), a.err)) ok = false;
-        if (ok) tile_dot<TYPE, M>(ring + (size_t)st * TILE, lane, q8, b, acc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        i_tile++;
-    };
-    auto store_whole = [&](long g, const float* acc) {
+    // Final value of row group g's rows: whole groups store y; a group cut by
+    // a CTA boundary publishes this CTA's piece and the last piece to arrive
+    // sums all pieces in CTA order.
+    auto finish = [&](long g, const float* v) {
         const int row = (int)g * TILE_ROWS + lane;
-        if (row < a.n_out)
+        const bool whole = g * nb >= T0 && (g + 1) * nb <= T1;
+        if (whole) {
+            if (row < a.n_out)
 #pragma unroll
-            for (int m = 0; m < M; m++) a.y[(size_t)m * a.ldy + row] = acc[m];
-    };
-    // A row group cut by a CTA boundary: publish this CTA's piece; the last
-    // piece to arrive sums all pieces in CTA order and stores y.
-    auto store_piece = [&](long g, const float* acc) {
-        const int row = (int)g * TILE_ROWS + lane;
+                for (int m = 0; m < M; m++) a.y[(size_t)m * a.ldy + row] = v[m];
+            return;
+        }
         const int first = tile_owner(g * nb, tiles, gridDim.x);
         const int pieces = tile_owner((g + 1) * nb - 1, tiles, gridDim.x) - first + 1;
         const int piece = (int)blockIdx.x - first;
         float* part = a.partial + (size_t)g * p.max_pieces * M * 32;
 #pragma unroll
-        for (int m = 0; m < M; m++) part[((size_t)piece * M + m) * 32 + lane] = acc[m];
+        for (int m = 0; m < M; m++) part[((size_t)piece * M + m) * 32 + lane] = v[m];
         __threadfence();
         __syncwarp();
         int last = 0;
@@ -434,31 +376,76 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
             if (lane == 0) a.counters[g] = 0;
         }
     };
-
-    if (head_len > 0 && warp == 0) {
-        float acc[M];
+    // This warp has done its last tile of row group g: add its partial to the
+    // group's slot; the last warp of the group sums the slot in tile order.
+    auto flush = [&](long g, const float* acc) {
+        const int a0 = (int)(max(T0, g * nb) - T0);
+        const int touched = min(NW, (int)(min(T1, (g + 1) * nb) - T0) - a0);
+        if (touched == 1) {
+            finish(g, acc);
+            return;
+        }
+        const int slot = (int)(g % nslot);
+        const int e = (warp - a0 % NW + NW) % NW;
+        float* sl = slots + (size_t)slot * E * M * 32;
 #pragma unroll
-        for (int m = 0; m < M; m++) acc[m] = 0.f;
-        for (int t = sh.head_tb; t < sh.head_te; t++) consume(t, acc);
-        store_piece(sh.g_head, acc);
-    }
-    for (int r0 = 0; r0 < sh.nfull; r0 += NW) {
-        const int nj = min(NW, sh.nfull - r0);
-        const int j = (warp - sh.hoff + NW) % NW;
-        if (j < nj) {
-            float acc[M];
+        for (int m = 0; m < M; m++) sl[(e * M + m) * 32 + lane] = acc[m];
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&slot_cnt[slot], 1) == touched - 1;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            float v[M];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                v[m] = 0.f;
+                for (int k = 0; k < touched; k++) v[m] += sl[(k * M + m) * 32 + lane];
+            }
+            __syncwarp();
+            if (lane == 0) slot_cnt[slot] = 0;
+            finish(g, v);
+        }
+    };
+
+    int c = warp;
+    long g = (T0 + c) / nb;
+    int b = (int)(T0 + c - g * nb);
+    int st = c;          // stage c % S (S is a multiple of NW, so it stays this warp's)
+    uint32_t ph = 0;
+    bool ok = true;
+    float acc[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) acc[m] = 0.f;
+    while (c < n_tiles) {
+        if (ok && !mbar_wait_bounded(&full[st], ph, a.err)) ok = false;
+        if (ok) tile_dot<TYPE, M>(ring + (size_t)st * TILE, lane, q8, b, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        // advance by NW tiles
+        const int cn = c + NW;
+        int bn = b + NW;
+        long gn = g;
+        while (bn >= nb) {
+            bn -= nb;
+            gn++;
+        }
+        if (cn >= n_tiles || gn != g) {
+            flush(g, acc);
 #pragma unroll
             for (int m = 0; m < M; m++) acc[m] = 0.f;
-            for (int t = 0; t < nb; t++) consume(t, acc);
-            store_whole(sh.g_full0 + r0 + j, acc);
         }
-    }
-    if (sh.tail_te > 0 && warp == (sh.hoff + sh.nfull) % NW) {
-        float acc[M];
-#pragma unroll
-        for (int m = 0; m < M; m++) acc[m] = 0.f;
-        for (int t = 0; t < sh.tail_te; t++) consume(t, acc);
-        store_piece(sh.g_tail, acc);
+        c = cn;
+        b = bn;
+        g = gn;
+        st += NW;
+        if (st >= S) {
+            st -= S;
+            ph ^= 1u;
+        }
     }
 }
 
@@ -470,14 +457,18 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.n_pad = p.groups * TILE_ROWS;
     const long tiles = (long)p.groups * nb;
     p.grid = (int)std::min<long>(tiles, num_sms);
-    // Stages per consumer warp: the largest power of two (<= 4) whose ring
-    // fits next to the staged activations and within the in-flight budget.
+    // Stages: NW x k (k = 4, 2 or 1) -- the largest ring that fits next to
+    // the staged activations and the partial slots, within the in-flight budget.
     const int nw = gemv_consumers(m);
-    const int room = std::min(GEMV_SMEM_LIMIT - gemv_smem_layout(tile, 0, m, nb).total, GEMV_RING_BUDGET);
-    p.warp_stage_log2 = 0;
-    while (p.warp_stage_log2 < 2 && nw * (2 << p.warp_stage_log2) * tile <= room) p.warp_stage_log2++;
-    p.stages = nw << p.warp_stage_log2;
-    p.smem_bytes = (size_t)gemv_smem_layout(tile, p.stages, m, nb).total;
+    p.stages = nw;
+    for (int k = 4; k >= 1; k /= 2) {
+        const int s = nw * k;
+        if (s * tile <= GEMV_RING_BUDGET && gemv_smem_layout(tile, s, m, nb, nw).total <= GEMV_SMEM_LIMIT) {
+            p.stages = s;
+            break;
+        }
+    }
+    p.smem_bytes = (size_t)gemv_smem_layout(tile, p.stages, m, nb, nw).total;
     // A row group spans at most this many CTAs.
     const long per_cta = std::max<long>(1, tiles / p.grid);
     p.max_pieces = (int)std::min<long>(p.grid, (nb + per_cta - 1) / per_cta + 1);

@@ -35,7 +35,7 @@ struct GemvArgs {
 // Launch plan of the persistent GEMV; deterministic in (type, nb, n_out,
 // tokens, sms).  `partial_bytes` / `counters` size the scratch it needs.
 struct GemvPlan {
-    int groups, n_pad, grid, stages, warp_stage_log2, max_pieces, threads;
+    int groups, n_pad, grid, stages, max_pieces, threads;
     size_t smem_bytes, partial_bytes, counters;
     bool fits;
 };
