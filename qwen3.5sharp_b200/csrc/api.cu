@@ -229,18 +229,23 @@ int q35k_weight_info(const q35k_weight* w, int* type, int* n_in, int* n_out, siz
 
 }  // extern "C"
 
-// Launch the GEMV for `tokens` Q8_K rows already on the device.
+// Tokens per GEMV launch for this weight (0: rows too long for the GEMV).
+static int gemv_chunk(const q35k_weight* w) { return gemv_max_tokens(w->nb); }
+
+// Launch the GEMV for `tokens` rows of planar Q8_K (in chunks of
+// gemv_chunk(w) rows) already on the device.
 int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl) {
-    const int chunk = gemv_max_tokens(w->nb);
+    const int chunk = gemv_chunk(w);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, chunk, num_sms);
     int rc;
     if ((rc = ensure_dev((void**)&d_partial, &partial_cap, p.partial_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_counters, &counters_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
+    const size_t chunk_stride = q8_planar(chunk, w->nb).bytes;
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         GemvArgs a{};
         a.tiles = w->tiles;
-        a.q8 = d_q8 + (size_t)t0 * w->nb * Q8K_BYTES;
+        a.q8 = d_q8 + (size_t)(t0 / chunk) * chunk_stride;
         a.y = d_y + (size_t)t0 * w->n_out;
         a.ldy = w->n_out;
         a.n_out = w->n_out;
@@ -282,7 +287,15 @@ int q35k_matmul_q8k_dev(q35k_ctx* c, const q35k_weight* w, const void* d_q8k, fl
     if (rc) return rc;
     if ((rc = check_alignment(c, d_q8k, 4, d_y, 4)) != Q35K_OK) return rc;
     cudaSetDevice(c->device);
-    return c->gemv(w, (const uint8_t*)d_q8k, d_y, tokens, pick(c, stream));
+    cudaStream_t s = pick(c, stream);
+    const int chunk = gemv_chunk(w);
+    if (chunk <= 0) return c->fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
+    // The caller's BlockQ8K rows -> the GEMV's planar layout.
+    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK)
+        return rc;
+    cudaError_t e = launch_q8k_to_planar((const uint8_t*)d_q8k, c->d_q8, w->n_in, tokens, chunk, s);
+    if (e != cudaSuccess) return c->cuda_fail(e, "Q8_K repack launch");
+    return c->gemv(w, c->d_q8, d_y, tokens, s);
 }
 
 int q35k_matmul_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* d_y, int tokens, void* stream) {
@@ -291,9 +304,11 @@ int q35k_matmul_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* 
     if ((rc = check_alignment(c, d_x, 16, d_y, 4)) != Q35K_OK) return rc;
     cudaSetDevice(c->device);
     cudaStream_t s = pick(c, stream);
-    const size_t q8_bytes = (size_t)tokens * w->nb * Q8K_BYTES;
-    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_bytes, false)) != Q35K_OK) return rc;
-    cudaError_t e = launch_quantize_q8k(d_x, c->d_q8, w->n_in, tokens, s);
+    const int chunk = gemv_chunk(w);
+    if (chunk <= 0) return c->fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
+    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK)
+        return rc;
+    cudaError_t e = launch_quantize_q8k(d_x, c->d_q8, w->n_in, tokens, chunk, s);
     if (e != cudaSuccess) return c->cuda_fail(e, "Q8_K quantize launch");
     return c->gemv(w, c->d_q8, d_y, tokens, s);
 }
@@ -328,14 +343,14 @@ int q35k_matmul_q8k(q35k_ctx* c, const q35k_weight* w, const void* q8k, float* y
     cudaSetDevice(c->device);
     const size_t in_bytes = (size_t)tokens * w->nb * Q8K_BYTES;
     const size_t out_bytes = (size_t)tokens * w->n_out * sizeof(float);
-    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_q8raw, &c->q8raw_cap, in_bytes, false)) != Q35K_OK) return rc;
     if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
     if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
     if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
     std::memcpy(c->h_in, q8k, in_bytes);
-    cudaError_t e = cudaMemcpyAsync(c->d_q8, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    cudaError_t e = cudaMemcpyAsync(c->d_q8raw, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of q8k");
-    if ((rc = c->gemv(w, c->d_q8, c->d_y, tokens, c->stream)) != Q35K_OK) return rc;
+    if ((rc = q35k_matmul_q8k_dev(c, w, c->d_q8raw, c->d_y, tokens, c->stream)) != Q35K_OK) return rc;
     unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
     e = cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
@@ -354,7 +369,7 @@ int q35k_quantize_q8k_dev(q35k_ctx* c, const float* d_x, void* d_q8k, int k, int
     int rc = check_alignment(c, d_x, 16, d_q8k, 4);
     if (rc) return rc;
     cudaSetDevice(c->device);
-    cudaError_t e = launch_quantize_q8k(d_x, (uint8_t*)d_q8k, k, rows, pick(c, stream));
+    cudaError_t e = launch_quantize_q8k(d_x, (uint8_t*)d_q8k, k, rows, 0, pick(c, stream));
     return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "Q8_K quantize launch");
 }
 
@@ -368,10 +383,10 @@ int q35k_quantize_q8k(q35k_ctx* c, const float* x, void* q8k, int k, int rows) {
     const size_t out_bytes = (size_t)rows * (k / QK) * Q8K_BYTES;
     int rc;
     if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
-    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_q8raw, &c->q8raw_cap, out_bytes, false)) != Q35K_OK) return rc;
     cudaError_t e = cudaMemcpyAsync(c->d_x, x, in_bytes, cudaMemcpyHostToDevice, c->stream);
-    if (e == cudaSuccess) e = launch_quantize_q8k(c->d_x, c->d_q8, k, rows, c->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(q8k, c->d_q8, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = launch_quantize_q8k(c->d_x, c->d_q8raw, k, rows, 0, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(q8k, c->d_q8raw, out_bytes, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "quantize_q8k");
 }

@@ -23,8 +23,10 @@ struct q35k_ctx {
     // Device scratch, grown on demand and reused across calls.
     float* d_x = nullptr;
     size_t x_cap = 0;
-    uint8_t* d_q8 = nullptr;
+    uint8_t* d_q8 = nullptr;  // planar Q8_K (the GEMV's input)
     size_t q8_cap = 0;
+    uint8_t* d_q8raw = nullptr;  // BlockQ8K bytes (caller format)
+    size_t q8raw_cap = 0;
     float* d_y = nullptr;
     size_t y_cap = 0;
     float* d_partial = nullptr;
@@ -42,6 +44,7 @@ struct q35k_ctx {
     ~q35k_ctx() {
         if (d_x) cudaFree(d_x);
         if (d_q8) cudaFree(d_q8);
+        if (d_q8raw) cudaFree(d_q8raw);
         if (d_y) cudaFree(d_y);
         if (d_partial) cudaFree(d_partial);
         if (d_counters) cudaFree(d_counters);

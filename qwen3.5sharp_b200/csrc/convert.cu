@@ -19,8 +19,35 @@ namespace q35k {
 //   amax == 0 -> an all-zero block (d = 0).
 // Lane l owns values 4l..4l+3 and 128+4l..128+4l+3 (two coalesced float4s).
 // ---------------------------------------------------------------------------
+// Output goes either to BlockQ8K blocks (chunk == 0) or to the planar layout
+// (device_common.cuh) in chunks of `chunk` rows.
+struct Q8Out {
+    uint32_t* d;   // the block's d word
+    uint32_t* qs;  // 64 words of qs
+    int16_t* bs;   // 16 bsums
+};
+__device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int rows, int chunk) {
+    Q8Out o;
+    if (chunk == 0) {
+        uint8_t* blk = q8 + ((size_t)row * nb + b) * Q8K_BYTES;
+        o.d = reinterpret_cast<uint32_t*>(blk);
+        o.qs = reinterpret_cast<uint32_t*>(blk + 4);
+        o.bs = reinterpret_cast<int16_t*>(blk + 260);
+    } else {
+        const int j = row / chunk, rr = row % chunk;
+        const int mj = min(chunk, rows - j * chunk);
+        uint8_t* base = q8 + (size_t)j * q8_planar(chunk, nb).bytes;
+        const Q8Planar pl = q8_planar(mj, nb);
+        const size_t blk = (size_t)rr * nb + b;
+        o.d = reinterpret_cast<uint32_t*>(base + pl.d) + blk;
+        o.qs = reinterpret_cast<uint32_t*>(base + pl.qs + blk * QK);
+        o.bs = reinterpret_cast<int16_t*>(base + pl.bs + blk * 32);
+    }
+    return o;
+}
+
 __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, uint8_t* __restrict__ q8,
-                                                           int nb, int total_blocks) {
+                                                           int nb, int total_blocks, int rows, int chunk) {
     // A GEMV launched after this kernel with programmatic stream
     // serialization may start now: it streams weights first and waits on the
     // grid dependency (full completion of this grid) before reading q8.
@@ -40,10 +67,13 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
 
-    uint32_t* out = reinterpret_cast<uint32_t*>(q8 + (size_t)warp * Q8K_BYTES);
+    const Q8Out out = q8_out(q8, row, b, nb, rows, chunk);
     if (amax == 0.f) {
-        // 73 words: d, 64 words of qs, 8 words of bsums.
-        for (int w = lane; w < Q8K_BYTES / 4; w += 32) out[w] = 0u;
+        // An all-zero block: d = 0, qs = 0, bsums = 0.
+        if (lane == 0) *out.d = 0u;
+        out.qs[lane] = 0u;
+        out.qs[32 + lane] = 0u;
+        if (lane < 16) out.bs[lane] = 0;
         return;
     }
     // First index whose |x| equals amax, and its signed value.
@@ -77,9 +107,9 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     }
     uint32_t w0 = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
     uint32_t w1 = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-    if (lane == 0) out[0] = __float_as_uint(d);
-    out[1 + lane] = w0;
-    out[1 + 32 + lane] = w1;
+    if (lane == 0) *out.d = __float_as_uint(d);
+    out.qs[lane] = w0;
+    out.qs[32 + lane] = w1;
 
     int s0 = q[0] + q[1] + q[2] + q[3];
     int s1 = q[4] + q[5] + q[6] + q[7];
@@ -88,19 +118,44 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
     s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
     if ((lane & 3) == 0) {
-        int16_t* bs = reinterpret_cast<int16_t*>(q8 + (size_t)warp * Q8K_BYTES + 260);
-        bs[lane >> 2] = static_cast<int16_t>(s0);
-        bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
+        out.bs[lane >> 2] = static_cast<int16_t>(s0);
+        out.bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
     }
 }
 
-cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, cudaStream_t s) {
+cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s) {
     const int nb = k / QK;
     const int total = nb * rows;
     if (total == 0) return cudaSuccess;
     const int warps_per_cta = 8;
     const int grid = (total + warps_per_cta - 1) / warps_per_cta;
-    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, q8, nb, total);
+    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, q8, nb, total, rows, planar_chunk);
+    return cudaGetLastError();
+}
+
+// BlockQ8K rows (a caller's pre-quantized activations) -> the planar layout,
+// one warp per block: word 0 = d, 1..64 = qs, 65..72 = bsums.
+__global__ void __launch_bounds__(256) q8k_to_planar_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                            int nb, int total_blocks, int rows, int chunk) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= total_blocks) return;
+    const uint32_t* in = reinterpret_cast<const uint32_t*>(src + (size_t)warp * Q8K_BYTES);
+    const Q8Out out = q8_out(dst, warp / nb, warp % nb, nb, rows, chunk);
+    if (lane == 0) *out.d = __ldg(in);
+    out.qs[lane] = __ldg(in + 1 + lane);
+    out.qs[32 + lane] = __ldg(in + 33 + lane);
+    if (lane < 8) reinterpret_cast<uint32_t*>(out.bs)[lane] = __ldg(in + 65 + lane);
+}
+
+cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s) {
+    const int nb = k / QK;
+    const int total = nb * rows;
+    if (total == 0) return cudaSuccess;
+    const int warps_per_cta = 8;
+    q8k_to_planar_kernel<<<(total + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, 0, s>>>(src, dst, nb,
+                                                                                                      total, rows, chunk);
     return cudaGetLastError();
 }
 

@@ -49,6 +49,33 @@ __host__ __device__ inline int block_bytes(int type) {
 }
 
 // ---------------------------------------------------------------------------
+// Planar Q8_K activations, the GEMV's input layout: the same values as
+// BlockQ8K (Kernels/BlockLayout.cs:41-46) split into three 16-byte aligned
+// planes so a CTA can stage them with three bulk copies:
+//   qs [rows][nb][256] int8 | d [rows][nb] f32 (padded to 16 B) |
+//   bsums [rows][nb][16] int16.
+// Tokens are grouped in chunks of `chunk` rows (one GEMV launch each); chunk
+// j starts at j * q8_planar(chunk, nb).bytes and its planes are sized by its
+// own row count.
+// ---------------------------------------------------------------------------
+struct Q8Planar {
+    size_t qs, d, bs, bytes;
+};
+__host__ __device__ inline Q8Planar q8_planar(int rows, int nb) {
+    Q8Planar p;
+    p.qs = 0;
+    p.d = (size_t)rows * nb * QK;
+    p.bs = p.d + (((size_t)rows * nb * 4 + 15) / 16) * 16;
+    p.bytes = p.bs + (size_t)rows * nb * 32;
+    return p;
+}
+// Total bytes of `rows` tokens stored in chunks of `chunk`.
+__host__ __device__ inline size_t q8_planar_total(int rows, int nb, int chunk) {
+    const int full = rows / chunk, rem = rows % chunk;
+    return (size_t)full * q8_planar(chunk, nb).bytes + (rem ? q8_planar(rem, nb).bytes : 0);
+}
+
+// ---------------------------------------------------------------------------
 // PTX helpers (mbarrier + bulk async copy, sm_90+ / sm_100a).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -6,31 +6,29 @@
 //     tiles (32 rows x 1 super-block, see device_common.cuh) in row-group
 //     order and every CTA owns one contiguous, equal share of it (stream-K),
 //     so the load is balanced to one tile whatever the shape;
-//   * one producer lane streams the CTA's tiles, in order, through a ring of
-//     S = NW * k shared-memory stages with 1-D bulk async copies
-//     (cp.async.bulk, no multicast), one full/empty mbarrier pair per stage;
-//   * tile c of the share goes to consumer warp c % NW and stage c % S, so
-//     every stage has exactly one consumer warp that takes its tiles in
-//     order (the single-consumer discipline mbarrier phase parity needs),
-//     and all NW warps stay busy whatever the shape;
-//   * lane r of a warp decodes row r of its tile; a row group's partial sums
-//     meet in a small ring of shared-memory slots, where the last warp to
-//     arrive adds them in tile order (deterministic) -- no barrier in the
-//     main loop;
-//   * the chunk-major tile layout makes every 16-byte load a contiguous
-//     512-byte line per warp; all lanes read the same Q8_K words
-//     (shared-memory broadcast);
+//   * tile c of the share belongs to warp c % NW; every warp prefetches its
+//     own tiles into its own K shared-memory stages with 1-D bulk async copies
+//     (cp.async.bulk, no multicast) and refills a stage the moment it has
+//     consumed it, so NW*K tiles stay in flight per SM with no producer warp,
+//     no empty barriers and no cross-warp waits (one full mbarrier per stage,
+//     one consumer, phases in order);
+//   * lane r of a warp decodes row r of its tile; the chunk-major tile layout
+//     makes every 16-byte load a contiguous 512-byte line per warp, and all
+//     lanes read the same Q8_K words (shared-memory broadcast);
 //   * integer dots (dp4a, dp2a) into exact int32 per super-block, scaled in
 //     fp32 once per block: acc += (d_w*d_x)*S - (dmin_w*d_x)*Mn
 //     (VecDotQ4K.DotScalar, Kernels/VecDotQ4K.cs:42-61; Q5K.Dot,
 //     Kernels/Q5K.cs:62-83; the Q6_K bias form of Q6K.DotAvx2,
 //     Kernels/Q6K.cs:105-108,159);
-//   * a row group cut by a CTA boundary is finished by whichever CTA arrives
-//     last, summing the pieces in CTA order (deterministic) and resetting the
-//     group's arrival counter for the next call;
-//   * the activation quantizer runs as the preceding kernel; with
-//     programmatic dependent launch the weight stream starts before it ends
-//     and only the consumers wait for its Q8_K output.
+//   * a row group's warp partials meet in a small ring of shared-memory
+//     slots, where the last warp to arrive adds them in tile order; a row
+//     group cut by a CTA boundary is finished by whichever CTA arrives last,
+//     summing the pieces in CTA order and resetting the group's arrival
+//     counter.  Every sum has a fixed order, so results are deterministic;
+//   * the Q8_K activations arrive in a planar layout (qs | d | bsums) that the
+//     CTA stages with three bulk copies; with programmatic dependent launch
+//     the weight prefetch starts before the producing kernel ends and only
+//     the activation copy waits for it.
 #include "device_common.cuh"
 #include "kernels.h"
 
@@ -40,9 +38,9 @@ namespace q35k {
 
 constexpr int GEMV_MAX_TOKENS = 8;
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
-constexpr int GEMV_MAX_STAGES = 48;                // consumer warps x stages per warp
-constexpr int GEMV_RING_BUDGET = 180 * 1024;       // weight bytes in flight per SM (upper bound)
-constexpr int GEMV_Q8_LIMIT = 96 * 1024;  // staged Q8_K activations per CTA
+constexpr int GEMV_MAX_STAGES = 48;           // consumer warps x stages per warp
+constexpr int GEMV_RING_BUDGET = 180 * 1024;  // weight bytes in flight per SM (upper bound)
+constexpr int GEMV_Q8_LIMIT = 96 * 1024;      // staged Q8_K activations per CTA
 
 // Consumer warps: more for few tokens (fewer registers per thread).
 __host__ __device__ constexpr int gemv_consumers(int m) { return m <= 2 ? 12 : 8; }
@@ -50,28 +48,28 @@ __host__ __device__ constexpr int gemv_consumers(int m) { return m <= 2 ? 12 : 8
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct SmemLayout {
-    int full, empty, slot_cnt, ring, q8s, q8d, q8b, slots, total;
+    int full, q8bar, slot_cnt, slot_owner, ring, q8, slots, total;
 };
 
-// Slots for row-group partial sums: a row group can be open in at most
-// ceil(S/nb)+1 slots at once (all tiles before the oldest unreleased one are
-// done), plus one of margin; each slot holds min(nb, NW) warp partials.
+// Slots for row-group partial sums (row group g uses slot g % nslot); each
+// holds min(nb, NW) warp partials.  Slot ownership passes from row group g to
+// g + nslot once g has been summed, so a warp running ahead waits rather than
+// overwrite; ceil(S/nb)+2 slots keep such waits rare.
 __host__ __device__ constexpr int gemv_nslot(int stages, int nb) { return (stages + nb - 1) / nb + 2; }
 constexpr int GEMV_MAX_SLOTS = GEMV_MAX_STAGES + 2;
 
 // Dynamic shared memory of one GEMV CTA (16-byte aligned regions):
-// full mbarriers | empty mbarriers | slot counters | weight ring | Q8_K qs |
-// Q8_K d | Q8_K bsums | row-group partial slots.
+// full mbarriers | activation mbarrier | slot counters | slot owners |
+// weight stages | planar Q8_K (qs | d | bsums) | row-group partial slots.
 __host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int stages, int m, int nb, int nw) {
     SmemLayout L;
     L.full = 0;
-    L.empty = 8 * GEMV_MAX_STAGES;
-    L.slot_cnt = 16 * GEMV_MAX_STAGES;
-    L.ring = align_up(L.slot_cnt + 4 * GEMV_MAX_SLOTS, 128);
-    L.q8s = L.ring + stages * tile_bytes;
-    L.q8d = L.q8s + m * nb * QK;
-    L.q8b = L.q8d + align_up(m * nb * 4, 16);
-    L.slots = L.q8b + align_up(m * nb * 32, 16);
+    L.q8bar = 8 * GEMV_MAX_STAGES;
+    L.slot_cnt = L.q8bar + 16;
+    L.slot_owner = L.slot_cnt + 4 * GEMV_MAX_SLOTS;
+    L.ring = align_up(L.slot_owner + 4 * GEMV_MAX_SLOTS, 128);
+    L.q8 = L.ring + stages * tile_bytes;
+    L.slots = L.q8 + align_up((int)q8_planar(m, nb).bytes, 16);
     const int e = nb < nw ? nb : nw;
     L.total = L.slots + (stages ? gemv_nslot(stages, nb) : 0) * e * m * 32 * 4;
     return L;
@@ -81,9 +79,6 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 template <int NTHREADS>
 __device__ __forceinline__ void consumer_bar() {
     asm volatile("bar.sync 1, %0;" ::"n"(NTHREADS) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // dp4a with unsigned a bytes (0..255) and signed b bytes.
 __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
@@ -114,7 +109,7 @@ __device__ __forceinline__ KHeader unpack_header(uint4 h) {
 }
 __device__ __forceinline__ int k_scale(const KHeader& k, int j) { return byte_of(j < 4 ? k.sc_lo : k.sc_hi, j & 3); }
 
-// Staged Q8_K activations: qs[m][nb][256], d[m][nb], bsums[m][nb][16].
+// Staged planar Q8_K activations: qs[m][nb][256], d[m][nb], bsums[m][nb][16].
 struct Q8Smem {
     const int8_t* qs;
     const float* d;
@@ -259,13 +254,6 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
     }
 }
 
-// Which CTA owns tile T when `tiles` tiles are split evenly over `grid` CTAs
-// (CTA i owns [tiles*i/grid, tiles*(i+1)/grid)).
-__device__ __forceinline__ int tile_owner(long T, long tiles, int grid) {
-    return (int)(((T + 1) * (long)grid - 1) / tiles);
-}
-
-
 template <int TYPE, int M>
 __device__ __forceinline__ void tile_dot(const uint8_t* tile, int lane, const Q8Smem& q8, int b, float* acc) {
     if (TYPE == TYPE_Q6_K)
@@ -274,71 +262,77 @@ __device__ __forceinline__ void tile_dot(const uint8_t* tile, int lane, const Q8
         block_dot_k45<TYPE, M>(tile, lane, q8, b, acc);
 }
 
+// Which CTA owns tile T when `tiles` tiles are split evenly over `grid` CTAs
+// (CTA i owns [tiles*i/grid, tiles*(i+1)/grid)).
+__device__ __forceinline__ int tile_owner(long T, long tiles, int grid) {
+    return (int)(((T + 1) * (long)grid - 1) / tiles);
+}
+
 template <int TYPE, int M>
-__global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(GemvArgs a, GemvPlan p) {
+__global__ void __launch_bounds__(gemv_consumers(M) * 32, 1) gemv_kernel(GemvArgs a, GemvPlan p) {
     constexpr int NW = gemv_consumers(M);
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
+    const int K = p.stages / NW;  // stages per warp
     const SmemLayout L = gemv_smem_layout(TILE, p.stages, M, a.nb, NW);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
-    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+    uint64_t* q8bar = reinterpret_cast<uint64_t*>(smem + L.q8bar);
     int* slot_cnt = reinterpret_cast<int*>(smem + L.slot_cnt);
+    volatile int* slot_owner = reinterpret_cast<volatile int*>(smem + L.slot_owner);
     uint8_t* ring = smem + L.ring;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nb = a.nb;
-    const int S = p.stages;  // a multiple of NW
     const long tiles = (long)p.groups * nb;
     const long T0 = tiles * blockIdx.x / gridDim.x;
     const long T1 = tiles * (blockIdx.x + 1) / gridDim.x;
     const int n_tiles = (int)(T1 - T0);
+    const int nslot = gemv_nslot(p.stages, nb);
+    const long g_first = T0 / nb;
 
     if (tid == 0) {
-        for (int i = 0; i < S; i++) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-        }
+        for (int i = 0; i < p.stages; i++) mbar_init(&full[i], 1);
+        mbar_init(q8bar, 1);
         fence_mbar_init();
+    }
+    for (int i = tid; i < nslot; i += NW * 32) {
+        slot_cnt[i] = 0;
+        // the first row group of this CTA that maps to slot i
+        slot_owner[i] = (int)(g_first + ((i - (int)(g_first % nslot)) + nslot) % nslot);
     }
     __syncthreads();
 
-    if (warp == NW) {
-        // ---------------- producer: this CTA's tiles in order ----------------
-        if (lane != 0) return;
-        int st = 0;
-        uint32_t ph = 0;  // phase of the stage's current use
-        for (int c = 0; c < n_tiles; c++) {
-            if (c >= S && !mbar_wait_bounded(&empty[st], ph ^ 1u, a.err)) break;
-            mbar_arrive_expect_tx(&full[st], TILE);
-            bulk_g2s(ring + (size_t)st * TILE, a.tiles + (size_t)(T0 + c) * TILE, TILE, &full[st]);
-            if (++st == S) {
-                st = 0;
-                ph ^= 1u;
-            }
+    // This warp's tiles are c = warp + NW*i; tile i lives in stage warp*K + i%K.
+    uint8_t* my_ring = ring + (size_t)warp * K * TILE;
+    uint64_t* my_full = full + warp * K;
+    auto prefetch = [&](int i) {
+        const int c = warp + NW * i;
+        if (c < n_tiles) {
+            const int k = i % K;
+            mbar_arrive_expect_tx(&my_full[k], TILE);
+            bulk_g2s(my_ring + (size_t)k * TILE, a.tiles + (size_t)(T0 + c) * TILE, TILE, &my_full[k]);
         }
-        return;
-    }
+    };
+    // Weights first: they do not depend on the preceding kernel.
+    if (lane == 0)
+        for (int i = 0; i < K; i++) prefetch(i);
 
-    // ---------------- consumers ----------------
-    griddep_wait();  // the Q8_K activations come from the preceding kernel
-    int8_t* q8s = reinterpret_cast<int8_t*>(smem + L.q8s);
-    float* q8d = reinterpret_cast<float*>(smem + L.q8d);
-    int16_t* q8b = reinterpret_cast<int16_t*>(smem + L.q8b);
-    // 73 words per BlockQ8K: word 0 = d, 1..64 = qs, 65..72 = bsums.
-    for (int idx = tid; idx < M * nb * 73; idx += NW * 32) {
-        const int mb = idx / 73, w = idx % 73;
-        const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(a.q8 + (size_t)mb * Q8K_BYTES) + w);
-        if (w == 0)
-            q8d[mb] = __uint_as_float(v);
-        else if (w <= 64)
-            reinterpret_cast<uint32_t*>(q8s + mb * QK)[w - 1] = v;
-        else
-            reinterpret_cast<uint32_t*>(q8b + mb * 16)[w - 65] = v;
+    // Then the activations, once the producing kernel has completed.
+    const Q8Planar pl = q8_planar(M, nb);
+    uint8_t* q8smem = smem + L.q8;
+    if (tid == 0) {
+        griddep_wait();
+        const uint32_t qs_bytes = (uint32_t)(pl.d - pl.qs);
+        const uint32_t d_bytes = (uint32_t)(pl.bs - pl.d);
+        const uint32_t bs_bytes = (uint32_t)(pl.bytes - pl.bs);
+        mbar_arrive_expect_tx(q8bar, qs_bytes + d_bytes + bs_bytes);
+        bulk_g2s(q8smem + pl.qs, a.q8 + pl.qs, qs_bytes, q8bar);
+        bulk_g2s(q8smem + pl.d, a.q8 + pl.d, d_bytes, q8bar);
+        bulk_g2s(q8smem + pl.bs, a.q8 + pl.bs, bs_bytes, q8bar);
     }
-    const int nslot = gemv_nslot(S, nb);
-    for (int i = tid; i < nslot; i += NW * 32) slot_cnt[i] = 0;
-    consumer_bar<NW * 32>();
-    const Q8Smem q8{q8s, q8d, q8b, nb};
+    bool ok = mbar_wait_bounded(q8bar, 0, a.err);
+    const Q8Smem q8{reinterpret_cast<const int8_t*>(q8smem + pl.qs), reinterpret_cast<const float*>(q8smem + pl.d),
+                    reinterpret_cast<const int16_t*>(q8smem + pl.bs), nb};
     const int E = min(nb, NW);
     float* slots = reinterpret_cast<float*>(smem + L.slots);
 
@@ -381,11 +375,26 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     auto flush = [&](long g, const float* acc) {
         const int a0 = (int)(max(T0, g * nb) - T0);
         const int touched = min(NW, (int)(min(T1, (g + 1) * nb) - T0) - a0);
+        const int slot = (int)(g % nslot);
         if (touched == 1) {
+            // One warp holds the whole (piece of the) row group: no slot.  The
+            // first row group still hands its slot on to g + nslot.
+            if (g == g_first && lane == 0) slot_owner[slot] = (int)(g + nslot);
             finish(g, acc);
             return;
         }
-        const int slot = (int)(g % nslot);
+        if (lane == 0) {
+            // Wait (bounded) until row group g owns the slot.
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t it = 0; slot_owner[slot] != (int)g; it++) {
+                if ((it & 1023u) == 1023u && globaltimer_ns() - t0 > 2000000000ull) {
+                    atomicOr(a.err, DEV_ERR_TIMEOUT);
+                    break;
+                }
+            }
+            __threadfence_block();
+        }
+        __syncwarp();
         const int e = (warp - a0 % NW + NW) % NW;
         float* sl = slots + (size_t)slot * E * M * 32;
 #pragma unroll
@@ -406,7 +415,11 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
                 for (int k = 0; k < touched; k++) v[m] += sl[(k * M + m) * 32 + lane];
             }
             __syncwarp();
-            if (lane == 0) slot_cnt[slot] = 0;
+            if (lane == 0) {
+                slot_cnt[slot] = 0;
+                __threadfence_block();
+                slot_owner[slot] = (int)(g + nslot);  // hand the slot on
+            }
             finish(g, v);
         }
     };
@@ -414,18 +427,18 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
     int c = warp;
     long g = (T0 + c) / nb;
     int b = (int)(T0 + c - g * nb);
-    int st = c;          // stage c % S (S is a multiple of NW, so it stays this warp's)
-    uint32_t ph = 0;
-    bool ok = true;
+    int k = 0;        // stage of tile i (i % K)
+    uint32_t ph = 0;  // its phase ((i / K) & 1)
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; m++) acc[m] = 0.f;
-    while (c < n_tiles) {
-        if (ok && !mbar_wait_bounded(&full[st], ph, a.err)) ok = false;
-        if (ok) tile_dot<TYPE, M>(ring + (size_t)st * TILE, lane, q8, b, acc);
+    for (int i = 0; c < n_tiles; i++) {
+        if (ok && !mbar_wait_bounded(&my_full[k], ph, a.err)) ok = false;
+        if (ok) tile_dot<TYPE, M>(my_ring + (size_t)k * TILE, lane, q8, b, acc);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        // advance by NW tiles
+        // The stage is consumed: refill it with this warp's tile i + K.
+        if (lane == 0 && ok) prefetch(i + K);
+        // Advance by NW tiles.
         const int cn = c + NW;
         int bn = b + NW;
         long gn = g;
@@ -441,11 +454,17 @@ __global__ void __launch_bounds__((gemv_consumers(M) + 1) * 32, 1) gemv_kernel(G
         c = cn;
         b = bn;
         g = gn;
-        st += NW;
-        if (st >= S) {
-            st -= S;
+        if (++k == K) {
+            k = 0;
             ph ^= 1u;
         }
+    }
+    if (!ok) {
+        // A wait gave up: give this warp's copies in flight a bounded chance
+        // to land before the CTA's shared memory is released.
+        __syncwarp();
+        if (lane == 0)
+            for (int s = 0; s < K; s++) mbar_wait_bounded(&my_full[s], ph ^ (s < k ? 1u : 0u), a.err, 100000000ull);
     }
 }
 
@@ -457,11 +476,11 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.n_pad = p.groups * TILE_ROWS;
     const long tiles = (long)p.groups * nb;
     p.grid = (int)std::min<long>(tiles, num_sms);
-    // Stages: NW x k (k = 4, 2 or 1) -- the largest ring that fits next to
-    // the staged activations and the partial slots, within the in-flight budget.
+    // Stages: NW x K (K = 4, 3, 2 or 1 per warp) -- the largest ring that fits
+    // next to the activations and the partial slots, within the in-flight budget.
     const int nw = gemv_consumers(m);
     p.stages = nw;
-    for (int k = 4; k >= 1; k /= 2) {
+    for (int k = 4; k >= 1; k--) {
         const int s = nw * k;
         if (s * tile <= GEMV_RING_BUDGET && gemv_smem_layout(tile, s, m, nb, nw).total <= GEMV_SMEM_LIMIT) {
             p.stages = s;
@@ -474,15 +493,16 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.max_pieces = (int)std::min<long>(p.grid, (nb + per_cta - 1) / per_cta + 1);
     p.partial_bytes = (size_t)p.groups * p.max_pieces * GEMV_MAX_TOKENS * 32 * sizeof(float);
     p.counters = (size_t)p.groups;
-    p.fits = (long)m * nb * Q8K_BYTES <= GEMV_Q8_LIMIT && p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;
-    p.threads = (gemv_consumers(m) + 1) * 32;
+    p.fits = (long)q8_planar(m, nb).bytes <= GEMV_Q8_LIMIT && p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;
+    p.threads = nw * 32;
     return p;
 }
 
 int gemv_max_tokens(int nb) {
     // Tokens per launch so that the staged Q8_K activations fit.
-    const int m = GEMV_Q8_LIMIT / (nb * Q8K_BYTES);
-    return std::max(0, std::min(GEMV_MAX_TOKENS, m));
+    int m = GEMV_MAX_TOKENS;
+    while (m > 0 && q8_planar(m, nb).bytes > (size_t)GEMV_Q8_LIMIT) m--;
+    return m;
 }
 
 // Opt-in shared memory for every instantiation on the current device

@@ -8,10 +8,14 @@
 
 namespace q35k {
 
-// Q8_K quantization of rows x [rows][k] -> BlockQ8K bytes.  The kernel lets a
+// Q8_K quantization of rows x [rows][k]: BlockQ8K bytes (planar_chunk == 0)
+// or the planar layout in chunks of planar_chunk rows.  The kernel lets a
 // dependent kernel launched with programmatic stream serialization start
 // early (that kernel must wait on the grid dependency before reading q8).
-cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, cudaStream_t s);
+cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s);
+
+// BlockQ8K rows -> planar layout in chunks of `chunk` rows.
+cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s);
 
 // Bit-exact dequantization of `rows` GGUF rows of k values.
 cudaError_t launch_dequantize(int type, const uint8_t* blocks, float* y, int k, int rows, cudaStream_t s);
@@ -22,7 +26,7 @@ cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tile
 
 struct GemvArgs {
     const uint8_t* tiles;  // uploaded weight tiles
-    const uint8_t* q8;     // tokens x nb BlockQ8K
+    const uint8_t* q8;     // planar Q8_K of `tokens` rows (16-byte aligned)
     float* y;              // [tokens][ldy]
     int ldy;
     int n_out, nb, tokens;
