@@ -38,8 +38,8 @@ __device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int
         const int mj = min(chunk, rows - j * chunk);
         uint8_t* base = q8 + (size_t)j * q8_planar(chunk, nb).bytes;
         const Q8Planar pl = q8_planar(mj, nb);
-        const size_t blk = (size_t)rr * nb + b;
-        o.d = reinterpret_cast<uint32_t*>(base + pl.d) + blk;
+        const size_t blk = (size_t)b * mj + rr;  // block-major
+        o.d = reinterpret_cast<uint32_t*>(base + pl.d) + (size_t)b * pl.rows4 + rr;
         o.qs = reinterpret_cast<uint32_t*>(base + pl.qs + blk * QK);
         o.bs = reinterpret_cast<int16_t*>(base + pl.bs + blk * 32);
     }

@@ -50,23 +50,27 @@ __host__ __device__ inline int block_bytes(int type) {
 
 // ---------------------------------------------------------------------------
 // Planar Q8_K activations, the GEMV's input layout: the same values as
-// BlockQ8K (Kernels/BlockLayout.cs:41-46) split into three 16-byte aligned
-// planes so a CTA can stage them with three bulk copies:
-//   qs [rows][nb][256] int8 | d [rows][nb] f32 (padded to 16 B) |
-//   bsums [rows][nb][16] int16.
+// BlockQ8K (Kernels/BlockLayout.cs:41-46) split into three planes, block-major
+// so that the super-blocks [b0, b0+n) of all rows are one contiguous,
+// 16-byte aligned range per plane (three bulk copies stage a K-range):
+//   qs [nb][rows][256] int8 | d [nb][rows4] f32 (rows4 = rows rounded up
+//   to 4) | bsums [nb][rows][16] int16.
 // Tokens are grouped in chunks of `chunk` rows (one GEMV launch each); chunk
 // j starts at j * q8_planar(chunk, nb).bytes and its planes are sized by its
 // own row count.
 // ---------------------------------------------------------------------------
 struct Q8Planar {
     size_t qs, d, bs, bytes;
+    int rows, rows4;
 };
 __host__ __device__ inline Q8Planar q8_planar(int rows, int nb) {
     Q8Planar p;
+    p.rows = rows;
+    p.rows4 = (rows + 3) / 4 * 4;
     p.qs = 0;
-    p.d = (size_t)rows * nb * QK;
-    p.bs = p.d + (((size_t)rows * nb * 4 + 15) / 16) * 16;
-    p.bytes = p.bs + (size_t)rows * nb * 32;
+    p.d = (size_t)nb * rows * QK;
+    p.bs = p.d + (size_t)nb * p.rows4 * 4;
+    p.bytes = p.bs + (size_t)nb * rows * 32;
     return p;
 }
 // Total bytes of `rows` tokens stored in chunks of `chunk`.

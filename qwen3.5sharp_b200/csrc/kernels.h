@@ -36,10 +36,11 @@ struct GemvArgs {
     int num_sms;
 };
 
-// Launch plan of the persistent GEMV; deterministic in (type, nb, n_out,
-// tokens, sms).  `partial_bytes` / `counters` size the scratch it needs.
+// Launch plan of the GEMV: one CTA per (row group, run of unit_blocks
+// super-blocks); deterministic in (type, nb, n_out, tokens, sms).
+// `partial_bytes` / `counters` size the split-K scratch it needs.
 struct GemvPlan {
-    int groups, n_pad, grid, stages, max_pieces, threads;
+    int groups, n_pad, grid, splits, unit_blocks, warps, threads;
     size_t smem_bytes, partial_bytes, counters;
     bool fits;
 };
