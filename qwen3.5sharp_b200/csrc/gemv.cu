@@ -27,8 +27,8 @@
 namespace q35k {
 
 constexpr int GEMV_MAX_TOKENS = 8;
-constexpr int GEMV_MAX_WARPS = 8;
-constexpr int GEMV_UNIT_BYTES = 36 * 1024;  // weight bytes per work unit (target)
+constexpr int GEMV_MAX_WARPS = 10;
+constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per work unit (target)
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
 
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -157,8 +157,9 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     const int m = std::min(std::max(tokens, 1), GEMV_MAX_TOKENS);
     p.groups = (n_out + TILE_ROWS - 1) / TILE_ROWS;
     p.n_pad = p.groups * TILE_ROWS;
-    // Units of ~GEMV_UNIT_BYTES; split K further while the grid is small
-    // (fewer than ~8 units per SM) so that enough CTAs stream at once.
+    // Units of up to ~GEMV_UNIT_BYTES (a whole row group when it fits: no
+    // split-K fix-up at all); split K further while the grid is small (fewer
+    // than ~8 units per SM) so that enough CTAs stream at once.
     int u = std::max(1, std::min(nb, GEMV_UNIT_BYTES / tile));
     int splits = (nb + u - 1) / u;
     while (splits < nb && (long)p.groups * splits < 8L * num_sms) splits++;
