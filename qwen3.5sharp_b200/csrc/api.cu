@@ -234,7 +234,8 @@ static int gemv_chunk(const q35k_weight* w) { return gemv_max_tokens(w->nb); }
 
 // Launch the GEMV for `tokens` rows of planar Q8_K (in chunks of
 // gemv_chunk(w) rows) already on the device.
-int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl) {
+int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl,
+                   const float* d_x) {
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, chunk, num_sms);
@@ -245,7 +246,12 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
     for (int t0 = 0; t0 < tokens; t0 += chunk) {
         GemvArgs a{};
         a.tiles = w->tiles;
-        a.q8 = d_q8 + (size_t)(t0 / chunk) * chunk_stride;
+        if (d_x) {
+            a.x = d_x + (size_t)t0 * w->n_in;
+            a.ldx = w->n_in;
+        } else {
+            a.q8 = d_q8 + (size_t)(t0 / chunk) * chunk_stride;
+        }
         a.y = d_y + (size_t)t0 * w->n_out;
         a.ldy = w->n_out;
         a.n_out = w->n_out;
@@ -306,6 +312,9 @@ int q35k_matmul_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* 
     cudaStream_t s = pick(c, stream);
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return c->fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
+    // Decode: the GEMV quantizes its own slices of x (one kernel per call).
+    if (tokens <= chunk && gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, c->num_sms))
+        return c->gemv(w, nullptr, d_y, tokens, s, true, d_x);
     if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK)
         return rc;
     cudaError_t e = launch_quantize_q8k(d_x, c->d_q8, w->n_in, tokens, chunk, s);

@@ -62,5 +62,6 @@ struct q35k_ctx {
     int on_device_error(unsigned word);
     // `pdl`: launch with programmatic stream serialization (the GEMV streams
     // weights before the preceding kernel finishes; its Q8_K reads wait).
-    int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true);
+    int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true,
+             const float* d_x = nullptr);
 };

@@ -7,25 +7,15 @@
 // operation of the reference (RyuJIT emits no FMA on these paths).
 #include "device_common.cuh"
 #include "kernels.h"
+#include "q8k_quant.cuh"
 
 namespace q35k {
 
 // ---------------------------------------------------------------------------
-// Q8_K quantization: one warp per 256-value super-block.
-// Follows Q8K.QuantizeRow + Q8K.ScaleBlock (Kernels/Q8K.cs:12-146):
-//   amax = max |x|; max = the first element (lowest index) with |x| == amax,
-//   sign kept; iscale = -127/max; d = 1/iscale (a true reciprocal);
-//   q = clamp(round_half_even(x * iscale), -127, 127); bsums = sums of 16.
-//   amax == 0 -> an all-zero block (d = 0).
-// Lane l owns values 4l..4l+3 and 128+4l..128+4l+3 (two coalesced float4s).
-// ---------------------------------------------------------------------------
+// Q8_K quantization: one warp per 256-value super-block (q8k_quant.cuh).
 // Output goes either to BlockQ8K blocks (chunk == 0) or to the planar layout
 // (device_common.cuh) in chunks of `chunk` rows.
-struct Q8Out {
-    uint32_t* d;   // the block's d word
-    uint32_t* qs;  // 64 words of qs
-    int16_t* bs;   // 16 bsums
-};
+// ---------------------------------------------------------------------------
 __device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int rows, int chunk) {
     Q8Out o;
     if (chunk == 0) {
@@ -56,71 +46,7 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     const int lane = threadIdx.x & 31;
     if (warp >= total_blocks) return;
     const int row = warp / nb, b = warp % nb;
-    const float* src = x + (size_t)row * nb * QK + (size_t)b * QK;
-    float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
-    float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
-    float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-
-    const Q8Out out = q8_out(q8, row, b, nb, rows, chunk);
-    if (amax == 0.f) {
-        // An all-zero block: d = 0, qs = 0, bsums = 0.
-        if (lane == 0) *out.d = 0u;
-        out.qs[lane] = 0u;
-        out.qs[32 + lane] = 0u;
-        if (lane < 16) out.bs[lane] = 0;
-        return;
-    }
-    // First index whose |x| equals amax, and its signed value.
-    int idx = 1 << 30;
-    float val = 0.f;
-#pragma unroll
-    for (int i = 7; i >= 0; i--) {
-        int pos = (i < 4) ? (4 * lane + i) : (128 + 4 * lane + (i - 4));
-        if (fabsf(v[i]) == amax) {
-            idx = pos;
-            val = v[i];
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        float ov = __shfl_xor_sync(0xffffffffu, val, o);
-        if (oi < idx) {
-            idx = oi;
-            val = ov;
-        }
-    }
-    const float iscale = __fdiv_rn(-127.f, val);
-    const float d = __fdiv_rn(1.f, iscale);
-
-    int q[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        int t = __float2int_rn(__fmul_rn(v[i], iscale));
-        q[i] = min(127, max(-127, t));
-    }
-    uint32_t w0 = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
-    uint32_t w1 = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-    if (lane == 0) *out.d = __float_as_uint(d);
-    out.qs[lane] = w0;
-    out.qs[32 + lane] = w1;
-
-    int s0 = q[0] + q[1] + q[2] + q[3];
-    int s1 = q[4] + q[5] + q[6] + q[7];
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-    if ((lane & 3) == 0) {
-        out.bs[lane >> 2] = static_cast<int16_t>(s0);
-        out.bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
-    }
+    warp_quantize_q8k_block(x + (size_t)row * nb * QK + (size_t)b * QK, q8_out(q8, row, b, nb, rows, chunk), lane);
 }
 
 cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s) {

@@ -21,6 +21,7 @@
 #include "device_common.cuh"
 #include "gemv_dot.cuh"
 #include "kernels.h"
+#include "q8k_quant.cuh"
 
 #include <algorithm>
 
@@ -28,6 +29,7 @@ namespace q35k {
 
 constexpr int GEMV_MAX_TOKENS = 8;
 constexpr int GEMV_MAX_WARPS = 10;
+constexpr int GEMV_FUSED_MAX_TOKENS = 2;  // token counts with a fused-quantize variant
 constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per work unit (target)
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
 
@@ -54,7 +56,11 @@ __host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int units
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-template <int TYPE, int M>
+// FUSED: quantize this CTA's K-range of the fp32 activations (a.x) to Q8_K in
+// shared memory (q8k_quant.cuh, the same bytes as the standalone quantizer)
+// while the weight tiles are in flight, instead of staging planar Q8_K from
+// a.q8 -- one kernel per call, used when that slice is small (decode).
+template <int TYPE, int M, bool FUSED>
 __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, GemvPlan p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
@@ -83,20 +89,36 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             mbar_arrive_expect_tx(&bars[t], TILE);
             bulk_g2s(tiles + (size_t)t * TILE, src + (size_t)t * TILE, TILE, &bars[t]);
         }
-        // Then the activations, once the producing kernel has completed.
-        griddep_wait();
-        mbar_arrive_expect_tx(&bars[kr], qs_bytes + d_bytes + bs_bytes);
-        bulk_g2s(q8s, a.q8 + pl.qs + (size_t)b0 * M * QK, qs_bytes, &bars[kr]);
-        bulk_g2s(q8s + qs_bytes, a.q8 + pl.d + (size_t)b0 * pl.rows4 * 4, d_bytes, &bars[kr]);
-        bulk_g2s(q8s + qs_bytes + d_bytes, a.q8 + pl.bs + (size_t)b0 * M * 32, bs_bytes, &bars[kr]);
+        if (!FUSED) {
+            // Then the activations, once the producing kernel has completed.
+            griddep_wait();
+            mbar_arrive_expect_tx(&bars[kr], qs_bytes + d_bytes + bs_bytes);
+            bulk_g2s(q8s, a.q8 + pl.qs + (size_t)b0 * M * QK, qs_bytes, &bars[kr]);
+            bulk_g2s(q8s + qs_bytes, a.q8 + pl.d + (size_t)b0 * pl.rows4 * 4, d_bytes, &bars[kr]);
+            bulk_g2s(q8s + qs_bytes + d_bytes, a.q8 + pl.bs + (size_t)b0 * M * 32, bs_bytes, &bars[kr]);
+        }
     }
     const Q8Smem q8{reinterpret_cast<const int8_t*>(q8s), reinterpret_cast<const float*>(q8s + qs_bytes),
                     reinterpret_cast<const int16_t*>(q8s + qs_bytes + d_bytes), M, pl.rows4};
+    bool ok = true;
+    if (FUSED) {
+        griddep_wait();  // x comes from the preceding kernel
+        for (int job = warp; job < M * kr; job += W) {
+            const int m = job / kr, t = job % kr;
+            Q8Out out;
+            out.d = reinterpret_cast<uint32_t*>(q8s + qs_bytes) + t * pl.rows4 + m;
+            out.qs = reinterpret_cast<uint32_t*>(q8s + (size_t)(t * M + m) * QK);
+            out.bs = reinterpret_cast<int16_t*>(q8s + qs_bytes + d_bytes) + (t * M + m) * 16;
+            warp_quantize_q8k_block(a.x + (size_t)m * a.ldx + (size_t)(b0 + t) * QK, out, lane);
+        }
+        __syncthreads();
+    } else {
+        ok = mbar_wait_bounded(&bars[kr], 0, a.err);
+    }
 
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; m++) acc[m] = 0.f;
-    bool ok = mbar_wait_bounded(&bars[kr], 0, a.err);
     for (int t = warp; ok && t < kr; t += W) {
         if (!mbar_wait_bounded(&bars[t], 0, a.err)) {
             ok = false;
@@ -147,7 +169,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     if (!ok && tid == 0) {
         // A wait gave up: give the copies in flight a bounded chance to land
         // before the CTA's shared memory is released.
-        for (int t = 0; t <= kr; t++) mbar_wait_bounded(&bars[t], 0, a.err, 100000000ull);
+        for (int t = 0; t < kr + (FUSED ? 0 : 1); t++) mbar_wait_bounded(&bars[t], 0, a.err, 100000000ull);
     }
 }
 
@@ -189,7 +211,10 @@ int gemv_max_tokens(int nb) {
 // (called once per context).
 template <int TYPE, int M>
 static void configure_typed() {
-    cudaFuncSetAttribute(gemv_kernel<TYPE, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+    cudaFuncSetAttribute(gemv_kernel<TYPE, M, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+    if (M <= GEMV_FUSED_MAX_TOKENS)
+        cudaFuncSetAttribute(gemv_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
 }
 
 template <int TYPE>
@@ -223,7 +248,11 @@ static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, M>, a, p);
+    // The fused variant exists for small token counts only.
+    if (a.x != nullptr && M <= GEMV_FUSED_MAX_TOKENS)
+        return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>, a, p);
+    if (a.x != nullptr) return cudaErrorInvalidValue;
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, M, false>, a, p);
 }
 
 template <int TYPE>
@@ -239,6 +268,13 @@ static cudaError_t launch_m(const GemvArgs& a, const GemvPlan& p, cudaStream_t s
     case 8: return launch_typed<TYPE, 8>(a, p, s, pdl);
     default: return cudaErrorInvalidValue;
     }
+}
+
+bool gemv_fuses_quantize(int type, int nb, int n_out, int tokens, int num_sms) {
+    if (tokens > GEMV_FUSED_MAX_TOKENS) return false;
+    const GemvPlan p = plan_gemv(type, nb, n_out, tokens, num_sms);
+    // Each warp quantizes at most two super-blocks of the unit's K-range.
+    return tokens * p.unit_blocks <= 2 * p.warps;
 }
 
 cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl) {

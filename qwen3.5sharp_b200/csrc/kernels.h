@@ -26,7 +26,9 @@ cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tile
 
 struct GemvArgs {
     const uint8_t* tiles;  // uploaded weight tiles
-    const uint8_t* q8;     // planar Q8_K of `tokens` rows (16-byte aligned)
+    const uint8_t* q8;     // planar Q8_K of `tokens` rows (16-byte aligned), or
+    const float* x;        // fp32 activations [tokens][ldx] to quantize in the
+    int ldx;               //   GEMV itself (x != nullptr; see gemv_fuses_quantize)
     float* y;              // [tokens][ldy]
     int ldy;
     int n_out, nb, tokens;
@@ -49,5 +51,8 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms);
 // row is too long to stage one token's activations).
 int gemv_max_tokens(int nb);
 cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl);
+// Whether the GEMV for this shape quantizes its own activations (small
+// slices per CTA: decode) instead of reading planar Q8_K.
+bool gemv_fuses_quantize(int type, int nb, int n_out, int tokens, int num_sms);
 
 }  // namespace q35k

@@ -1,0 +1,95 @@
+// q8k_quant.cuh -- bit-exact Q8_K quantization of one 256-value super-block
+// by one warp, shared by the standalone quantizer and the GEMV's fused
+// prologue (both must produce the same bytes).
+//
+// Follows Q8K.QuantizeRow + Q8K.ScaleBlock (Kernels/Q8K.cs:12-146):
+//   amax = max |x|; max = the first element (lowest index) with |x| == amax,
+//   sign kept; iscale = -127/max; d = 1/iscale (a true reciprocal);
+//   q = clamp(round_half_even(x * iscale), -127, 127); bsums = sums of 16.
+//   amax == 0 -> an all-zero block (d = 0).
+// Every fp32 operation is an explicitly rounded intrinsic (__fdiv_rn,
+// __fmul_rn, __float2int_rn), so nvcc cannot contract or reassociate it; each
+// mirrors one separately rounded C# operation of the reference.
+// Lane l owns values 4l..4l+3 and 128+4l..128+4l+3 (two coalesced float4s).
+#pragma once
+
+#include "device_common.cuh"
+
+namespace q35k {
+
+struct Q8Out {
+    uint32_t* d;   // the block's d word
+    uint32_t* qs;  // 64 words of qs
+    int16_t* bs;   // 16 bsums
+};
+
+// src: 256 floats, 16-byte aligned.  Writes d, qs, bsums through `out`.
+__device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict__ src, const Q8Out& out, int lane) {
+    const float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
+    const float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+
+    if (amax == 0.f) {
+        // An all-zero block: d = 0, qs = 0, bsums = 0.
+        if (lane == 0) *out.d = 0u;
+        out.qs[lane] = 0u;
+        out.qs[32 + lane] = 0u;
+        if (lane < 16) out.bs[lane] = 0;
+        return;
+    }
+    // First index whose |x| equals amax, and its signed value.
+    int idx = 1 << 30;
+    float val = 0.f;
+#pragma unroll
+    for (int i = 7; i >= 0; i--) {
+        const int pos = (i < 4) ? (4 * lane + i) : (128 + 4 * lane + (i - 4));
+        if (fabsf(v[i]) == amax) {
+            idx = pos;
+            val = v[i];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, val, o);
+        if (oi < idx) {
+            idx = oi;
+            val = ov;
+        }
+    }
+    const float iscale = __fdiv_rn(-127.f, val);
+    const float d = __fdiv_rn(1.f, iscale);
+
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int t = __float2int_rn(__fmul_rn(v[i], iscale));
+        q[i] = min(127, max(-127, t));
+    }
+    const uint32_t w0 =
+        (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    const uint32_t w1 =
+        (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    if (lane == 0) *out.d = __float_as_uint(d);
+    out.qs[lane] = w0;
+    out.qs[32 + lane] = w1;
+
+    int s0 = q[0] + q[1] + q[2] + q[3];
+    int s1 = q[4] + q[5] + q[6] + q[7];
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+    if ((lane & 3) == 0) {
+        out.bs[lane >> 2] = static_cast<int16_t>(s0);
+        out.bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
+    }
+}
+
+}  // namespace q35k
