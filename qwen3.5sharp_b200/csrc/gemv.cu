@@ -180,11 +180,11 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.groups = (n_out + TILE_ROWS - 1) / TILE_ROWS;
     p.n_pad = p.groups * TILE_ROWS;
     // Units of up to ~GEMV_UNIT_BYTES (a whole row group when it fits: no
-    // split-K fix-up at all); split K further while the grid is small (fewer
-    // than ~8 units per SM) so that enough CTAs stream at once.
+    // split-K fix-up at all, and a unit's tiles are decoded in parallel by
+    // its warps); split K further only while there are fewer units than SMs.
     int u = std::max(1, std::min(nb, GEMV_UNIT_BYTES / tile));
     int splits = (nb + u - 1) / u;
-    while (splits < nb && (long)p.groups * splits < 8L * num_sms) splits++;
+    while (splits < nb && (long)p.groups * splits < num_sms) splits++;
     u = (nb + splits - 1) / splits;
     // The activations of one unit must fit next to its tiles.
     while (u > 1 && gemv_smem_layout(tile, u, m, std::min(u, GEMV_MAX_WARPS)).total > GEMV_SMEM_LIMIT) u--;
