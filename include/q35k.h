@@ -124,6 +124,35 @@ int q35k_dequantize(q35k_ctx* ctx, int ggml_type, const void* blocks, float* y, 
 int q35k_dequantize_dev(q35k_ctx* ctx, int ggml_type, const void* d_blocks, float* d_y, int k, int rows,
                         void* stream);
 
+/* ---- Allocation-free decode matmul --------------------------------------
+ *
+ * No counterpart in the reference.  For callers that must not have a library
+ * allocate device memory during a call: a host whose device memory is all
+ * handed out by its own arena, or a latency-critical decode loop in which a
+ * cudaMalloc/cudaFree (which synchronize the device) would stall the
+ * pipeline.  q35k_matmul_dev grows its context's scratch with cudaMalloc on
+ * demand; this entry point instead keeps all of its scratch in one fixed
+ * array of Q35K_STATIC_SCRATCH_BYTES that every GPU loading libq35k holds
+ * until the process exits, and allocates nothing.
+ *
+ * Same result as q35k_matmul_dev for tokens <= Q35K_STATIC_MAX_TOKENS:
+ * d_y[tokens][n_out] = d_x[tokens][n_in] @ W^T, asynchronous on `stream` (a
+ * cudaStream_t; NULL = the legacy default stream).  The weight's device must
+ * be the current device.  Shapes whose scratch would not fit the array, or
+ * more tokens, return Q35K_EINVAL; q35k_last_error(NULL) says why.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - All calls share the array and it keeps the previous call's contents:
+ *     each call clears the counters it relies on before its kernels run, and
+ *     calls that overlap on the GPU (other streams, other host threads) race
+ *     on the array -- do not issue them.
+ *   - A bounded device wait that expires inside this call's kernels is not
+ *     reported (use q35k_matmul_dev + q35k_sync to observe those). */
+#define Q35K_STATIC_MAX_TOKENS 8
+#define Q35K_STATIC_SCRATCH_BYTES (8u << 20)
+int q35k_matmul_static_dev(const q35k_weight* w, const float* d_x, float* d_y, int tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,11 @@ static bool valid_type(int t) { return t == Q35K_TYPE_Q4_K || t == Q35K_TYPE_Q5_
 
 static thread_local std::string g_create_error;
 
+namespace q35k {
+// Errors of calls that have no context: reported by q35k_last_error(NULL).
+void set_thread_error(const std::string& msg) { g_create_error = msg; }
+}  // namespace q35k
+
 extern "C" {
 
 const char* q35k_version(void) { return "q35k 0.1 (sm_100a)"; }

@@ -36,6 +36,7 @@ SIGNATURES = {
     "q35k_quantize_q8k_dev": ([_vp, _vp, _vp, _i32, _i32, _vp], _i32),
     "q35k_dequantize": ([_vp, _i32, _vp, _vp, _i32, _i32], _i32),
     "q35k_dequantize_dev": ([_vp, _i32, _vp, _vp, _i32, _i32, _vp], _i32),
+    "q35k_matmul_static_dev": ([_vp, _vp, _vp, _i32, _vp], _i32),
 }
 
 _lib = None
