@@ -3,6 +3,7 @@
 // library; there is no CPU fallback.
 #include "../../include/q35k.h"
 #include "device_common.cuh"
+#include "gemm_tc.h"
 #include "kernels.h"
 #include "api_internal.h"
 
@@ -11,6 +12,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -84,6 +86,7 @@ int q35k_ctx::on_device_error(unsigned word) {
     // up may have left a counter non-zero).
     cudaMemset(d_err, 0, sizeof(unsigned));
     if (d_counters) cudaMemset(d_counters, 0, counters_cap);
+    if (d_gcnt) cudaMemset(d_gcnt, 0, gcnt_cap);
     cudaDeviceSynchronize();
     return fail(Q35K_ETIMEOUT, "a bounded device wait expired inside a kernel (error word 0x%x)", word);
 }
@@ -141,6 +144,12 @@ int q35k_create(int device, q35k_ctx** out) {
         return Q35K_ECUDA;
     }
     configure_gemv_kernels();
+    if ((e = configure_tc_gemm()) != cudaSuccess) {
+        g_create_error = std::string("GEMM configuration: ") + cudaGetErrorString(e);
+        delete c;
+        return Q35K_ECUDA;
+    }
+    if (const char* v = getenv("Q35K_GEMM_MIN_TOKENS")) c->gemm_min_tokens = std::max(1, atoi(v));
     if ((e = cudaGetLastError()) != cudaSuccess) {
         g_create_error = std::string("kernel configuration: ") + cudaGetErrorString(e);
         delete c;
@@ -272,6 +281,36 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
     return Q35K_OK;
 }
 
+int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s) {
+    const TcGemmPlan p = plan_tc_gemm(w->nb, w->n_pad, tokens, num_sms);
+    int rc;
+    if ((rc = ensure_dev(&d_xq, &xq_cap, p.xq_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = ensure_dev(&d_xe, &xe_cap, p.xe_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = ensure_dev((void**)&d_xd, &xd_cap, p.xd_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = ensure_dev((void**)&d_gws, &gws_cap, p.ws_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = ensure_dev((void**)&d_gcnt, &gcnt_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
+    cudaError_t e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, s);
+    if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
+    TcGemmArgs a{};
+    a.tiles = w->tiles;
+    a.xd = d_xd;
+    a.y = d_y;
+    a.ws = d_gws;
+    a.counters = d_gcnt;
+    a.err = d_err;
+    a.n_out = w->n_out;
+    a.n_pad = w->n_pad;
+    a.tokens = tokens;
+    a.m_pad = p.m_pad;
+    a.nb = w->nb;
+    a.tiles_t = p.tiles_t;
+    a.grid = p.grid;
+    a.units = p.units;
+    e = launch_tc_gemm(a, d_xq, d_xe, w->n_in, s, true);
+    if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+    return Q35K_OK;
+}
+
 static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, const void* y, int tokens) {
     if (!c) return Q35K_EINVAL;
     if (!w) return c->fail(Q35K_EINVAL, "weight handle is NULL");
@@ -315,6 +354,8 @@ int q35k_matmul_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* 
     if ((rc = check_alignment(c, d_x, 16, d_y, 4)) != Q35K_OK) return rc;
     cudaSetDevice(c->device);
     cudaStream_t s = pick(c, stream);
+    // Prefill: the tensor-core GEMM.
+    if (w->type == Q35K_TYPE_Q4_K && tokens >= c->gemm_min_tokens) return c->gemm(w, d_x, d_y, tokens, s);
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return c->fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     // Decode: the GEMV quantizes its own slices of x (one kernel per call).

@@ -35,6 +35,22 @@ struct q35k_ctx {
     size_t counters_cap = 0;
     unsigned* d_err = nullptr;  // device error word (bounded waits that expired)
 
+    // Prefill GEMM scratch (gemm_tc.h): fp16 Q8_K operands, partial tiles and
+    // arrival counters (zero between calls).
+    void* d_xq = nullptr;
+    size_t xq_cap = 0;
+    void* d_xe = nullptr;
+    size_t xe_cap = 0;
+    float* d_xd = nullptr;
+    size_t xd_cap = 0;
+    float* d_gws = nullptr;
+    size_t gws_cap = 0;
+    int* d_gcnt = nullptr;
+    size_t gcnt_cap = 0;
+    // Q4_K calls with at least this many tokens run on the tensor cores
+    // (environment variable Q35K_GEMM_MIN_TOKENS overrides it at creation).
+    int gemm_min_tokens = 16;
+
     // Pinned host staging for the synchronous host-pointer calls.
     void* h_in = nullptr;
     size_t h_in_cap = 0;
@@ -49,6 +65,11 @@ struct q35k_ctx {
         if (d_partial) cudaFree(d_partial);
         if (d_counters) cudaFree(d_counters);
         if (d_err) cudaFree(d_err);
+        if (d_xq) cudaFree(d_xq);
+        if (d_xe) cudaFree(d_xe);
+        if (d_xd) cudaFree(d_xd);
+        if (d_gws) cudaFree(d_gws);
+        if (d_gcnt) cudaFree(d_gcnt);
         if (h_in) cudaFreeHost(h_in);
         if (h_out) cudaFreeHost(h_out);
         if (stream) cudaStreamDestroy(stream);
@@ -64,4 +85,6 @@ struct q35k_ctx {
     // weights before the preceding kernel finishes; its Q8_K reads wait).
     int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true,
              const float* d_x = nullptr);
+    // Tensor-core prefill GEMM (Q4_K): quantize x, then the GEMM.
+    int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s);
 };

@@ -1,0 +1,36 @@
+// gemm_tc.h -- host interface of the tensor-core prefill GEMM (gemm_tc.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace q35k {
+
+struct TcGemmArgs {
+    const uint8_t* tiles;  // uploaded Q4_K weight tiles (32-row chunk-major layout)
+    const float* xd;       // Q8_K block scales [nb][m_pad]
+    float* y;              // [tokens][n_out]
+    float* ws;             // partial tiles: [grid][2][128 tokens][128 rows]
+    int* counters;         // [tiles][8] arrival counters, zero between launches
+    unsigned* err;         // device error word
+    int n_out, n_pad, tokens, m_pad, nb, tiles_t, grid;
+    long long units;       // tiles * nb
+};
+
+struct TcGemmPlan {
+    int m_pad, tiles_w, tiles_t, tiles, grid;
+    long long units;
+    size_t xq_bytes, xe_bytes, xd_bytes, ws_bytes, counters, smem_bytes;
+};
+
+TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms);
+cudaError_t configure_tc_gemm();
+// Q8_K quantization of x [tokens][k] into the GEMM's operands: Xq [tokens][k]
+// fp16 q values, Xe [tokens][k/256*16] fp16 block sums, Xd [k/256][m_pad] d.
+cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd,
+                             cudaStream_t s);
+// The GEMM; `pdl` lets it start while the preparation kernel finishes.
+cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* xe, int k, cudaStream_t s, bool pdl);
+
+}  // namespace q35k

@@ -23,8 +23,10 @@ struct Q8Out {
     int16_t* bs;   // 16 bsums
 };
 
-// src: 256 floats, 16-byte aligned.  Writes d, qs, bsums through `out`.
-__device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict__ src, const Q8Out& out, int lane) {
+// The quantization itself: returns d (the same value on every lane) and this
+// lane's eight q values (q[0..3] = values 4l..4l+3, q[4..7] = 128+4l..+3).
+// An all-zero block gives d = 0 and q = 0.  src: 256 floats, 16-byte aligned.
+__device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, int lane, int (&q)[8]) {
     const float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
     const float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -36,12 +38,9 @@ __device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict_
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
 
     if (amax == 0.f) {
-        // An all-zero block: d = 0, qs = 0, bsums = 0.
-        if (lane == 0) *out.d = 0u;
-        out.qs[lane] = 0u;
-        out.qs[32 + lane] = 0u;
-        if (lane < 16) out.bs[lane] = 0;
-        return;
+#pragma unroll
+        for (int i = 0; i < 8; i++) q[i] = 0;
+        return 0.f;
     }
     // First index whose |x| equals amax, and its signed value.
     int idx = 1 << 30;
@@ -64,28 +63,38 @@ __device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict_
         }
     }
     const float iscale = __fdiv_rn(-127.f, val);
-    const float d = __fdiv_rn(1.f, iscale);
-
-    int q[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int t = __float2int_rn(__fmul_rn(v[i], iscale));
         q[i] = min(127, max(-127, t));
     }
-    const uint32_t w0 =
-        (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
-    const uint32_t w1 =
-        (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-    if (lane == 0) *out.d = __float_as_uint(d);
-    out.qs[lane] = w0;
-    out.qs[32 + lane] = w1;
+    return __fdiv_rn(1.f, iscale);
+}
 
-    int s0 = q[0] + q[1] + q[2] + q[3];
-    int s1 = q[4] + q[5] + q[6] + q[7];
+// Sums of 16 of the values returned by warp_q8k_values: s0 = bsums[lane/4]
+// and s1 = bsums[8 + lane/4], valid on lanes with lane % 4 == 0.
+__device__ __forceinline__ void warp_q8k_bsums(const int (&q)[8], int& s0, int& s1) {
+    s0 = q[0] + q[1] + q[2] + q[3];
+    s1 = q[4] + q[5] + q[6] + q[7];
     s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
     s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
     s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
     s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+}
+
+// src: 256 floats, 16-byte aligned.  Writes d, qs, bsums through `out`.
+__device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict__ src, const Q8Out& out, int lane) {
+    int q[8];
+    const float d = warp_q8k_values(src, lane, q);
+    if (lane == 0) *out.d = __float_as_uint(d);
+    const uint32_t w0 =
+        (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    const uint32_t w1 =
+        (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    out.qs[lane] = w0;
+    out.qs[32 + lane] = w1;
+    int s0, s1;
+    warp_q8k_bsums(q, s0, s1);
     if ((lane & 3) == 0) {
         out.bs[lane >> 2] = static_cast<int16_t>(s0);
         out.bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
