@@ -210,12 +210,27 @@ int q35k_weight_upload(q35k_ctx* c, int type, const void* blocks, int n_in, int 
         delete w;
         return c->fail(Q35K_ENOMEM, "weight upload: cudaMalloc(%zu) failed", tile_bytes + raw_bytes);
     }
+    if (type == Q35K_TYPE_Q4_K) {
+        // The prefill GEMM's per-block metadata, computed once here.
+        const size_t mb = q4k_meta_bytes(nb, n_pad), sb = q4k_scale_bytes(nb, n_pad);
+        if ((e = cudaMalloc(&w->meta, mb + sb)) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(w->tiles);
+            cudaFree(raw);
+            delete w;
+            return c->fail(Q35K_ENOMEM, "weight upload: cudaMalloc(%zu) failed", mb + sb);
+        }
+        w->scale = reinterpret_cast<float*>(w->meta + mb);
+        w->bytes += mb + sb;
+    }
     e = cudaMemcpyAsync(raw, blocks, raw_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) e = launch_repack_tiles(type, raw, w->tiles, nb, n_out, n_pad, c->stream);
+    if (e == cudaSuccess && w->meta) e = launch_q4k_meta(w->tiles, w->meta, w->scale, nb, n_pad, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     cudaFree(raw);
     if (e != cudaSuccess) {
         cudaFree(w->tiles);
+        if (w->meta) cudaFree(w->meta);
         delete w;
         return c->cuda_fail(e, "weight upload");
     }
@@ -228,6 +243,7 @@ int q35k_weight_free(q35k_ctx* c, q35k_weight* w) {
     if (c) cudaSetDevice(c->device);
     cudaDeviceSynchronize();
     cudaFree(w->tiles);
+    if (w->meta) cudaFree(w->meta);
     delete w;
     return Q35K_OK;
 }
@@ -293,6 +309,8 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
     TcGemmArgs a{};
     a.tiles = w->tiles;
+    a.meta = w->meta;
+    a.scale = w->scale;
     a.xd = d_xd;
     a.y = d_y;
     a.ws = d_gws;

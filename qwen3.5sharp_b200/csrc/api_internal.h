@@ -11,6 +11,8 @@
 struct q35k_weight {
     int type = 0, n_in = 0, n_out = 0, nb = 0, n_pad = 0, device = 0;
     uint8_t* tiles = nullptr;  // 32-row chunk-major tiles (device_common.cuh)
+    uint8_t* meta = nullptr;   // Q4_K: per-block GEMM metadata (gemm_tc.h)
+    float* scale = nullptr;    // Q4_K: per-block drain scales of the GEMM
     size_t bytes = 0;
 };
 

@@ -60,25 +60,46 @@ namespace q35k {
 namespace tcg {
 
 constexpr int TM = 128;  // weight rows per tile
+constexpr int Q4K_META_TILE = 3 * 512;  // GEMM metadata of one 32-row tile
 constexpr int TN = 128;  // tokens per tile
 // Five warpgroups of four warps; each warpgroup re-sizes its registers with
 // setmaxnreg.  Registers are split between an SM's four sub-partitions, one
 // warp of every warpgroup in each: 5 x 32 x 96 = 15360 <= 16384 at launch,
-// and afterwards 128 x (40 + 80 + 80 + 136 + 136) = 60416 <= 640 x 96.
+// and afterwards 128 x (32 + 72 + 72 + 152 + 152) = 61440 <= 640 x 96.
 constexpr int THREADS = 640;
 constexpr int LAUNCH_REGS = 96;
-constexpr int REGS_CTRL = 40, REGS_PROD = 80, REGS_DRAIN = 136;
-constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_PROD0 = 4, WARP_DRAIN0 = 12, NUM_DRAIN = 8;
-constexpr int STAGES = 3;
-constexpr int MAIN_BOX_BYTES = 64 * 2 * TN;                      // 64 fp16 K x 128 tokens
-constexpr int EXT_BOX_BYTES = 16 * 2 * TN;                       // 16 fp16 K x 128 tokens
-constexpr int STAGE_BYTES = 4 * MAIN_BOX_BYTES + EXT_BOX_BYTES;  // one super-block
-// A buffers: 64 value columns at 256 + 64 i, 8 min columns at 448 + 8 i.
-constexpr int A_BUFS = 3, A_COL0 = 256, E_COL0 = 448;
+constexpr int REGS_CTRL = 32, REGS_PROD = 72, REGS_DRAIN = 152;
+constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_WTMA = 2, WARP_PROD0 = 4, WARP_DRAIN0 = 12, NUM_DRAIN = 8;
+// Activation ring: half super-blocks (128 K x 128 tokens fp16 = two
+// 128-byte-swizzled boxes of 64 K), released by the MMA.
+constexpr int X_STAGES = 3;
+constexpr int X_BOX_BYTES = 64 * 2 * TN;           // 16 KB
+constexpr int X_STAGE_BYTES = 2 * X_BOX_BYTES;     // 32 KB
+// Weight ring, one stage per unit: the unit's block-sum operand Xe (16 x 128
+// fp16, 32-byte swizzle), the four 32-row weight tiles (4 x 4608 B), their
+// GEMM metadata (4 x 1536 B), the drain scales s (4 x 128 B) and the 128
+// token scales d8.  Released by the producers and the drains.
+constexpr int W_STAGES = 4;
+constexpr int Q4K_TILE = 32 * 144;                 // one 32-row tile of the uploaded layout
+constexpr int EXT_BOX_BYTES = 16 * 2 * TN;         // 4096
+constexpr int W_EXT_OFF = 0;                       // 1024-aligned (swizzled TMA destination)
+constexpr int W_TILE_OFF = EXT_BOX_BYTES;
+constexpr int W_META_OFF = W_TILE_OFF + 4 * Q4K_TILE;
+constexpr int W_S_OFF = W_META_OFF + 4 * Q4K_META_TILE;
+constexpr int W_DR_OFF = W_S_OFF + 4 * 32 * 4;
+constexpr int W_STAGE_BYTES = W_DR_OFF + TN * 4;   // 29696 (29 KB)
+static_assert(W_STAGE_BYTES % 1024 == 0, "weight stage alignment");
+constexpr int X_RING_BYTES = X_STAGES * X_STAGE_BYTES;
+constexpr int W_RING_BYTES = W_STAGES * W_STAGE_BYTES;
+constexpr int A_BUFS = 3;
+// TMEM: accumulators at columns 0 and 128; A buffers of 64 value columns at
+// 256 + 64 i; their 8 min columns at 448 + 8 i.
+constexpr int A_COL0 = 256, E_COL0 = 448;
 constexpr int TMEM_COLS = 512;
-constexpr int Q4K_TILE = 32 * 144;  // one 32-row tile of the uploaded layout
-constexpr int DR_BYTES = NUM_DRAIN * 64 * 4;  // per drain warp: the d8 of its 64 tokens
-constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + DR_BYTES;
+constexpr int NUM_BARS = 2 * X_STAGES + 3 * W_STAGES + 2 * A_BUFS + 4 + 1;
+constexpr size_t SMEM_BYTES = 1024 + (size_t)X_RING_BYTES + W_RING_BYTES + 256;
+static_assert(NUM_BARS * 8 + 8 <= 256, "barrier area");
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 }  // namespace tcg
@@ -86,7 +107,8 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 // ---------------------------------------------------------------------------
 // Activation preparation: Q8_K quantization (bit-exact) -> fp16 Xq, Xe and the
 // block scales d8 in Xd[b][m_pad] (zero for padded tokens).  One warp per
-// (token, super-block).
+// (token, super-block).  Xq holds each aligned group of four K values in the
+// order 0, 2, 1, 3; the MMA's K order only has to agree between its operands.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, int k, int tokens, int m_pad,
                                                        __half* __restrict__ xq, __half* __restrict__ xe,
@@ -104,10 +126,12 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     int q[8];
     const float d = warp_q8k_values(x + (size_t)r * k + (size_t)b * QK, lane, q);
     __half* row = xq + (size_t)r * k + (size_t)b * QK;
-    const __half2 p0 = __halves2half2(__int2half_rn(q[0]), __int2half_rn(q[1]));
-    const __half2 p1 = __halves2half2(__int2half_rn(q[2]), __int2half_rn(q[3]));
-    const __half2 p2 = __halves2half2(__int2half_rn(q[4]), __int2half_rn(q[5]));
-    const __half2 p3 = __halves2half2(__int2half_rn(q[6]), __int2half_rn(q[7]));
+    // K order within each group of four values: 0, 2, 1, 3 (the order in
+    // which the weight producers pair nibbles; see the decode in the GEMM).
+    const __half2 p0 = __halves2half2(__int2half_rn(q[0]), __int2half_rn(q[2]));
+    const __half2 p1 = __halves2half2(__int2half_rn(q[1]), __int2half_rn(q[3]));
+    const __half2 p2 = __halves2half2(__int2half_rn(q[4]), __int2half_rn(q[6]));
+    const __half2 p3 = __halves2half2(__int2half_rn(q[5]), __int2half_rn(q[7]));
     uint2 v0, v1;
     v0.x = *reinterpret_cast<const uint32_t*>(&p0);
     v0.y = *reinterpret_cast<const uint32_t*>(&p1);
@@ -190,13 +214,12 @@ __device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t 
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
-__device__ __forceinline__ uint32_t half2_bits(float v) {
-    const __half h = __float2half_rn(v);
-    const uint32_t u = __half_as_ushort(h);
-    return u | (u << 16);
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
-__device__ __forceinline__ uint4 ldg16(const uint8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 // Bounded wait; gives up when the CTA aborted or the time limit passed (the
 // latter records DEV_ERR_TIMEOUT and raises the CTA's abort flag).
@@ -204,8 +227,8 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, unsigne
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63u) == 0) {
+        if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
+        if ((it & 7u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer_ns() - start > tcg::WAIT_LIMIT_NS) {
                 atomicOr(err, DEV_ERR_TIMEOUT);
@@ -234,6 +257,29 @@ __device__ __forceinline__ bool warp_wait_bar(uint64_t* bar, uint32_t parity, un
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// (tile, super-block) of consecutive units without a division per step: the
+// integer divisions a role would otherwise do per unit run on the XU pipe,
+// which the whole CTA shares.
+struct UnitPos {
+    int t, b, tt, tw;  // tile, super-block, token tile, weight tile
+    __device__ __forceinline__ void init(int u, int nb, int tiles_t) {
+        t = u / nb;
+        b = u - t * nb;
+        tw = t / tiles_t;
+        tt = t - tw * tiles_t;
+    }
+    __device__ __forceinline__ void next(int nb, int tiles_t) {
+        if (++b == nb) {
+            b = 0;
+            ++t;
+            if (++tt == tiles_t) {
+                tt = 0;
+                ++tw;
+            }
+        }
+    }
+};
+
 // CTA whose unit range [c*U/G, (c+1)*U/G) contains unit u.
 __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
     return (int)(((u + 1) * G + U - 1) / U) - 1;
@@ -241,24 +287,72 @@ __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Per-block GEMM metadata, computed once when a Q4_K weight is uploaded (the
+// counterpart of the reference's load-time BlockQ4Kx8Meta,
+// Kernels/RepackQ4K.cs:91-130).  For tile (g, b), chunk-major like the
+// weight tile (16-byte chunk c of row r at c * 512 + r * 16):
+//   chunk 0: fp16 alpha * sc_j, j = 0..7        (the A operand's sub-block scales)
+//   chunk 1: fp16 high part of -beta * m_j, j = 0..7
+//   chunk 2: fp16 low part of -beta * m_j
+// and the drain's fp32 s of each row in s[(g nb + b) 32 + r] (q4k_block_scale).
+// One thread per (row, super-block).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ meta,
+                                                      float* __restrict__ s_out, int n_pad, int nb) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)n_pad * nb) return;
+    const int row = (int)(idx / nb), b = (int)(idx % nb);
+    const int g = row >> 5, r = row & 31;
+    const size_t tile = (size_t)g * nb + b;
+    const uint4 hdr = *reinterpret_cast<const uint4*>(tiles + tile * tcg::Q4K_TILE + r * 16);
+    const BlockScale bs = q4k_block_scale(hdr.x);
+    uint32_t sa[4], hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        uint16_t a2[2], h2[2], l2[2];
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+            int sc, m;
+            q4k_scale_min(j + t, hdr.y, hdr.z, hdr.w, sc, m);
+            a2[t] = __half_as_ushort(__float2half_rn((float)sc * bs.alpha));
+            const float v = -bs.beta * (float)m;
+            const __half h = __float2half_rn(v);
+            h2[t] = __half_as_ushort(h);
+            l2[t] = __half_as_ushort(__float2half_rn(v - __half2float(h)));
+        }
+        sa[j / 2] = a2[0] | ((uint32_t)a2[1] << 16);
+        hi[j / 2] = h2[0] | ((uint32_t)h2[1] << 16);
+        lo[j / 2] = l2[0] | ((uint32_t)l2[1] << 16);
+    }
+    uint8_t* mt = meta + tile * tcg::Q4K_META_TILE + r * 16;
+    *reinterpret_cast<uint4*>(mt) = make_uint4(sa[0], sa[1], sa[2], sa[3]);
+    *reinterpret_cast<uint4*>(mt + 512) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(mt + 1024) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    s_out[tile * 32 + r] = bs.s;
+}
+
 __global__ void __launch_bounds__(tcg::THREADS, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_e,
                        const TcGemmArgs a) {
     using namespace tcg;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* stages = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-    uint64_t* b_full = bars;          // [STAGES]
-    uint64_t* b_empty = bars + 3;     // [STAGES]
-    uint64_t* a_full = bars + 6;      // [A_BUFS]
-    uint64_t* a_empty = bars + 9;     // [A_BUFS]
-    uint64_t* acc_full = bars + 12;   // [2]
-    uint64_t* acc_empty = bars + 14;  // [2]
-    uint64_t* mma_done = bars + 16;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+    uint8_t* xring = smem;
+    uint8_t* wring = smem + X_RING_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + X_RING_BYTES + W_RING_BYTES);
+    uint64_t* x_full = bars;                      // [X_STAGES] activation half stage landed
+    uint64_t* x_empty = x_full + X_STAGES;        // [X_STAGES] its MMAs completed
+    uint64_t* w_full = x_empty + X_STAGES;        // [W_STAGES] weight tiles landed
+    uint64_t* e_full = w_full + W_STAGES;         // [W_STAGES] Xe + d8 landed
+    uint64_t* w_empty = e_full + W_STAGES;        // [W_STAGES] producers and drains done with it
+    uint64_t* a_full = w_empty + W_STAGES;        // [A_BUFS] TMEM A operand written
+    uint64_t* a_empty = a_full + A_BUFS;          // [A_BUFS] its MMAs completed
+    uint64_t* acc_full = a_empty + A_BUFS;        // [2]
+    uint64_t* acc_empty = acc_full + 2;           // [2]
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    float* dr_smem = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x;
@@ -267,11 +361,17 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     const int u1 = (int)((long long)(blockIdx.x + 1) * U / G);
     const int n_units = u1 - u0;
     const int nb = a.nb;
+    const int n_groups = a.n_pad / 32;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < STAGES; i++) {
-            mbar_init(b_full + i, 1);
-            mbar_init(b_empty + i, 1);
+        for (int i = 0; i < X_STAGES; i++) {
+            mbar_init(x_full + i, 1);
+            mbar_init(x_empty + i, 1);
+        }
+        for (int i = 0; i < W_STAGES; i++) {
+            mbar_init(w_full + i, 1);
+            mbar_init(e_full + i, 1);
+            mbar_init(w_empty + i, 16);  // 8 producer warps + 8 drain warps
         }
         for (int i = 0; i < A_BUFS; i++) {
             mbar_init(a_full + i, 8);
@@ -296,163 +396,206 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 
     const int wg = warp >> 2;
     if (wg == 0) {
-      setmaxnreg_dec<REGS_CTRL>();
-      if (warp == WARP_TMA) {
-        // ---------------- activation loads ----------------
-        if (lane == 0) {
-            griddep_wait();  // Xq / Xe come from the preparation kernel
+        setmaxnreg_dec<REGS_CTRL>();
+        if (warp == WARP_TMA && lane == 0) {
+            // ---------------- activation halves ----------------
+            griddep_wait();  // Xq comes from the preparation kernel
+            const int n = 2 * n_units;
             int issued = 0;
-            for (int i = 0; i < n_units; i++) {
-                const int u = u0 + i, t = u / nb, b = u % nb, tt = t % a.tiles_t;
-                const int st = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-                if (!wait_bar(b_empty + st, ph ^ 1u, a.err, abort_flag)) break;
-                mbar_arrive_expect_tx(b_full + st, STAGE_BYTES);
-                uint8_t* dst = stages + st * STAGE_BYTES;
-#pragma unroll
-                for (int j = 0; j < 4; j++) tma_load_2d(dst + j * MAIN_BOX_BYTES, &tm_q, b * QK + 64 * j, tt * TN, b_full + st);
-                tma_load_2d(dst + 4 * MAIN_BOX_BYTES, &tm_e, b * 16, tt * TN, b_full + st);
+            UnitPos p;
+            p.init(u0, nb, a.tiles_t);
+            for (int f = 0; f < n; f++) {
+                if (f > 0 && (f & 1) == 0) p.next(nb, a.tiles_t);
+                const int b = p.b, tt = p.tt;
+                const int xs = f % X_STAGES;
+                if (!wait_bar(x_empty + xs, ((uint32_t)(f / X_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
+                mbar_arrive_expect_tx(x_full + xs, X_STAGE_BYTES);
+                uint8_t* dst = xring + xs * X_STAGE_BYTES;
+                const int k0 = b * QK + 128 * (f & 1);
+                tma_load_2d(dst, &tm_q, k0, tt * TN, x_full + xs);
+                tma_load_2d(dst + X_BOX_BYTES, &tm_q, k0 + 64, tt * TN, x_full + xs);
+                issued = f + 1;
+            }
+            for (int f = (issued > X_STAGES ? issued - X_STAGES : 0); f < issued; f++)
+                wait_inflight(x_full + (f % X_STAGES), (uint32_t)(f / X_STAGES) & 1u, a.err);
+        } else if (warp == WARP_WTMA && lane == 0) {
+            // ---------------- weight tiles, Xe and d8 ----------------
+            bool dep_done = false;
+            int issued = 0;
+            UnitPos p;
+            p.init(u0, nb, a.tiles_t);
+            for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
+                const int b = p.b, tw = p.tw, tt = p.tt;
+                const int ws = i % W_STAGES;
+                if (!wait_bar(w_empty + ws, ((uint32_t)(i / W_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
+                uint8_t* dst = wring + ws * W_STAGE_BYTES;
+                int valid = 0;
+                for (int q = 0; q < 4; q++) valid += (tw * 4 + q < n_groups) ? 1 : 0;
+                mbar_arrive_expect_tx(w_full + ws, (uint32_t)(valid * (Q4K_TILE + Q4K_META_TILE + 128)));
+                for (int q = 0; q < 4; q++) {
+                    const int g = tw * 4 + q;
+                    if (g >= n_groups) continue;
+                    const size_t tile = (size_t)g * nb + b;
+                    bulk_g2s(dst + W_TILE_OFF + q * Q4K_TILE, a.tiles + tile * Q4K_TILE, Q4K_TILE, w_full + ws);
+                    bulk_g2s(dst + W_META_OFF + q * Q4K_META_TILE, a.meta + tile * Q4K_META_TILE, Q4K_META_TILE,
+                             w_full + ws);
+                    bulk_g2s(dst + W_S_OFF + q * 128, a.scale + tile * 32, 128, w_full + ws);
+                }
+                if (!dep_done) {
+                    griddep_wait();  // Xe and d8 come from the preparation kernel
+                    dep_done = true;
+                }
+                mbar_arrive_expect_tx(e_full + ws, EXT_BOX_BYTES + TN * 4);
+                tma_load_2d(dst + W_EXT_OFF, &tm_e, b * 16, tt * TN, e_full + ws);
+                bulk_g2s(dst + W_DR_OFF, a.xd + (size_t)b * a.m_pad + tt * TN, TN * 4, e_full + ws);
                 issued = i + 1;
             }
-            // Copies still in flight land before the CTA may exit.
-            for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
-                wait_inflight(b_full + (i % STAGES), (uint32_t)(i / STAGES) & 1u, a.err);
-        }
-      } else if (warp == WARP_MMA) {
-        // ---------------- MMA issue ----------------
-        if (lane == 0) {
+            for (int i = (issued > W_STAGES ? issued - W_STAGES : 0); i < issued; i++) {
+                wait_inflight(w_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
+                wait_inflight(e_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
+            }
+        } else if (warp == WARP_MMA && lane == 0) {
+            // ---------------- MMA issue ----------------
             const uint32_t idesc = tc_idesc_f16_f32(TM, TN);
             for (int i = 0; i < n_units; i++) {
-                const int st = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
                 const int accb = i & 1;
-                const uint32_t acc_ph = (uint32_t)(i >> 1) & 1u;
-                if (!wait_bar(acc_empty + accb, acc_ph ^ 1u, a.err, abort_flag)) break;
-                if (!wait_bar(b_full + st, ph, a.err, abort_flag)) break;
-                tc_fence_after();
-                const uint32_t b_base = smem_u32(stages + st * STAGE_BYTES);
+                const int ws = i % W_STAGES;
+                if (!wait_bar(acc_empty + accb, ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err, abort_flag)) break;
+                if (!wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
                 const uint32_t d_tmem = tmem + (uint32_t)(accb * TN);
+                const uint32_t ext_addr = smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF);
                 bool ok = true;
                 for (int h = 0; h < 2; h++) {
-                    const int hs = 2 * i + h;
-                    const int ab = hs % A_BUFS;
-                    const uint32_t aph = (uint32_t)(hs / A_BUFS) & 1u;
-                    if (!wait_bar(a_full + ab, aph, a.err, abort_flag)) {
+                    const int f = 2 * i + h;
+                    const int xs = f % X_STAGES, ab = f % A_BUFS;
+                    if (!wait_bar(x_full + xs, (uint32_t)(f / X_STAGES) & 1u, a.err, abort_flag) ||
+                        !wait_bar(a_full + ab, (uint32_t)(f / A_BUFS) & 1u, a.err, abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
+                    const uint32_t x_addr = smem_u32(xring + xs * X_STAGE_BYTES);
                     const uint32_t a_tmem = tmem + (uint32_t)(A_COL0 + 64 * ab);
 #pragma unroll
-                    for (int t = 0; t < 8; t++) {
-                        const int kk = 8 * h + t;  // 16-value K step within the super-block
-                        const uint64_t desc =
-                            tc_smem_desc(b_base + (kk >> 2) * MAIN_BOX_BYTES + (kk & 3) * 32, 1024, 2);
+                    for (int t = 0; t < 8; t++) {  // 16-value K steps of the half
+                        const uint64_t desc = tc_smem_desc(x_addr + (t >> 2) * X_BOX_BYTES + (t & 3) * 32, 1024, 2);
                         tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, desc, idesc, (h | t) != 0 ? 1u : 0u);
                     }
-                    tc_mma_f16_ts(d_tmem, tmem + (uint32_t)(E_COL0 + 8 * ab),
-                                  tc_smem_desc(b_base + 4 * MAIN_BOX_BYTES, 256, 6), idesc, 1u);
+                    tc_mma_f16_ts(d_tmem, tmem + (uint32_t)(E_COL0 + 8 * ab), tc_smem_desc(ext_addr, 256, 6), idesc,
+                                  1u);
                     tc_commit(a_empty + ab);
+                    tc_commit(x_empty + xs);
                 }
                 if (!ok) break;
-                tc_commit(b_empty + st);
                 tc_commit(acc_full + accb);
             }
             // Every MMA issued by this thread completes before TMEM is freed.
             tc_commit(mma_done);
             wait_inflight(mma_done, 0, a.err);
         }
-      }  // warps 2, 3: no role
     } else if (warp < WARP_DRAIN0) {
         setmaxnreg_dec<REGS_PROD>();
         // ---------------- weight producers ----------------
         // Every A buffer fill (one half super-block, in order) is built by all
         // eight producer warps: warp (q, part) writes the 32 value columns of
         // 64-value chunk 2h + part for lanes 32q..32q+31, and 4 of the 8 min
-        // columns.  Each warp waits on every buffer phase in turn.
+        // columns.  Each warp waits on every barrier phase in turn.  The
+        // stores of fill f complete while fill f + 1 is being decoded; fill f
+        // is published (a_full) once they have.
         const int q = warp & 3;                     // TMEM lane quadrant = 32-row group within the tile
-        const int part = (warp - WARP_PROD0) >> 2;  // which 64-value chunk of the half
+        const int part = (warp - WARP_PROD0) >> 2;  // which 64-value chunk of each half
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        const int n_groups = a.n_pad / 32;
+        // Per unit: this lane's fp16 sub-block scales alpha * sc_j (8 halves).
+        uint32_t sa[4];
+        int pending = -1;  // fill whose TMEM stores are in flight
         const int n_fills = 2 * n_units;
-        // Weight bytes of fill f: header chunk and the two 16-byte chunks of
-        // qs holding 64-value chunk c = 2h + part (chunks 1 + 2c, 2 + 2c).
-        auto load_fill = [&](int f, uint4& hdr, uint4& wa, uint4& wb) {
-            const int u = u0 + (f >> 1), t = u / nb, b = u % nb, tw = t / a.tiles_t;
-            const int g = tw * 4 + q;
-            const int c = 2 * (f & 1) + part;
-            if (g < n_groups) {
-                const uint8_t* tile = a.tiles + ((size_t)g * nb + b) * Q4K_TILE + lane * 16;
-                hdr = ldg16(tile);
-                wa = ldg16(tile + (1 + 2 * c) * 512);
-                wb = ldg16(tile + (2 + 2 * c) * 512);
-            } else {
-                hdr = wa = wb = make_uint4(0, 0, 0, 0);
-            }
-        };
-        uint4 hdr, wa, wb;
-        if (n_fills > 0) load_fill(0, hdr, wa, wb);
+        UnitPos p;
+        p.init(u0, nb, a.tiles_t);
         for (int f = 0; f < n_fills; f++) {
-            const int h = f & 1;
-            const int ab = f % A_BUFS;
-            const uint32_t aph = (uint32_t)(f / A_BUFS) & 1u;
-            uint4 nhdr, nwa, nwb;
-            if (f + 1 < n_fills) load_fill(f + 1, nhdr, nwa, nwb);
-            if (!warp_wait_bar(a_empty + ab, aph ^ 1u, a.err, abort_flag, lane)) break;
+            const int i = f >> 1, h = f & 1;
+            if (f > 0 && h == 0) p.next(nb, a.tiles_t);
+            const int tw = p.tw;
+            const bool valid = tw * 4 + q < n_groups;
+            const int ws = i % W_STAGES, ab = f % A_BUFS;
+            const uint8_t* stage = wring + ws * W_STAGE_BYTES;
+            const uint8_t* tile = stage + W_TILE_OFF + q * Q4K_TILE + lane * 16;
+            const uint8_t* mt = stage + W_META_OFF + q * Q4K_META_TILE + lane * 16;
+            if (h == 0) {
+                if (!warp_wait_bar(w_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag, lane)) break;
+                const uint4 v = valid ? *reinterpret_cast<const uint4*>(mt) : make_uint4(0, 0, 0, 0);
+                sa[0] = v.x;
+                sa[1] = v.y;
+                sa[2] = v.z;
+                sa[3] = v.w;
+            }
+            if (!warp_wait_bar(a_empty + ab, ((uint32_t)(f / A_BUFS) & 1u) ^ 1u, a.err, abort_flag, lane)) break;
             tc_fence_after();
-            const BlockScale bs = q4k_block_scale(hdr.x);
-            const uint32_t a_col = tmem + lane_base + (uint32_t)(A_COL0 + 64 * ab);
-            const uint32_t e_col = tmem + lane_base + (uint32_t)(E_COL0 + 8 * ab);
-            {
-                const int c = 2 * h + part;  // 64-value chunk of the super-block
-                int sc_lo, m_lo, sc_hi, m_hi;
-                q4k_scale_min(2 * c, hdr.y, hdr.z, hdr.w, sc_lo, m_lo);
-                q4k_scale_min(2 * c + 1, hdr.y, hdr.z, hdr.w, sc_hi, m_hi);
-                const uint32_t s_lo = half2_bits((float)sc_lo * bs.alpha);
-                const uint32_t n_lo = half2_bits(-1024.f * ((float)sc_lo * bs.alpha));
-                const uint32_t s_hi = half2_bits((float)sc_hi * bs.alpha);
-                const uint32_t n_hi = half2_bits(-1024.f * ((float)sc_hi * bs.alpha));
-                const uint32_t W[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-                uint32_t v[32];
-#pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    // bytes l = 4w..4w+3; low nibbles are values 64c+l, high nibbles 64c+32+l
-                    const uint32_t t0 = __byte_perm(W[w], 0u, 0x4140);  // b0, b1 -> 16-bit lanes
-                    const uint32_t t1 = __byte_perm(W[w], 0u, 0x4342);  // b2, b3
-                    const uint32_t l0 = (t0 & 0x000F000Fu) | 0x64006400u;  // fp16 1024 + q
-                    const uint32_t l1 = (t1 & 0x000F000Fu) | 0x64006400u;
-                    const uint32_t h0 = ((t0 >> 4) & 0x000F000Fu) | 0x64006400u;
-                    const uint32_t h1 = ((t1 >> 4) & 0x000F000Fu) | 0x64006400u;
-                    // (1024 + q) * s - 1024 * s = q * s, exact in fp16
-                    v[2 * w] = hfma2_bits(l0, s_lo, n_lo);
-                    v[2 * w + 1] = hfma2_bits(l1, s_lo, n_lo);
-                    v[16 + 2 * w] = hfma2_bits(h0, s_hi, n_hi);
-                    v[16 + 2 * w + 1] = hfma2_bits(h1, s_hi, n_hi);
-                }
-                tmem_st32(a_col + 32 * part, v);
+            // This lane's row: the two 16-byte chunks of qs holding 64-value
+            // chunk c = 2h + part (tile chunks 1 + 2c, 2 + 2c), and the min
+            // column parts of sub-blocks 4 part .. 4 part + 3 (high half for
+            // h = 0, low half for h = 1).
+            const int c = 2 * h + part;
+            uint4 wa = make_uint4(0, 0, 0, 0), wb = wa, em = wa;
+            if (valid) {
+                wa = *reinterpret_cast<const uint4*>(tile + (1 + 2 * c) * 512);
+                wb = *reinterpret_cast<const uint4*>(tile + (2 + 2 * c) * 512);
+                em = *reinterpret_cast<const uint4*>(mt + (1 + h) * 512);
             }
-            {
-                // Min column j: -beta * m_j for the block sums 2j, 2j+1;
-                // the fp16 high part in the first half of the super-block,
-                // the low part in the second.  This warp writes j = 4 part..+3.
-                uint32_t e[4];
-#pragma unroll
-                for (int jj = 0; jj < 4; jj++) {
-                    int sc, m;
-                    q4k_scale_min(4 * part + jj, hdr.y, hdr.z, hdr.w, sc, m);
-                    const float v = -bs.beta * (float)m;
-                    const float hi = __half2float(__float2half_rn(v));
-                    e[jj] = half2_bits(h == 0 ? hi : v - hi);
-                }
-                tmem_st4(e_col + 4 * part, e);
+            if (h == 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(w_empty + ws);  // this warp is done with the unit's tiles
             }
+            // fp16 scales of sub-blocks 2c (low nibbles) and 2c + 1 (high
+            // nibbles): word c of sa holds both.
+            const uint32_t sw = c == 0 ? sa[0] : c == 1 ? sa[1] : c == 2 ? sa[2] : sa[3];
+            const uint32_t s_lo = __byte_perm(sw, 0u, 0x1010), s_hi = __byte_perm(sw, 0u, 0x3232);
+            // Low nibbles become fp16 1024 + q; high nibbles, masked in place,
+            // fp16 1024 + 16 q.  (1024 + q) s - 1024 s and (1024 + 16 q) s/16
+            // - 64 s are q s exactly.
+            const uint32_t n_lo = hmul2_bits(s_lo, 0xE400E400u);   // -1024 s
+            const uint32_t s_h16 = hmul2_bits(s_hi, 0x2C002C00u);  // s / 16
+            const uint32_t n_hi = hmul2_bits(s_hi, 0xD400D400u);   // -64 s
+            const uint32_t W[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            uint32_t v[32];
+#pragma unroll
+            for (int w = 0; w < 8; w++) {
+                // bytes l = 4w..4w+3: low nibbles are values 64c+l, high nibbles
+                // 64c+32+l.  One fp16 pair takes the nibbles of bytes 0 and 2,
+                // the other those of bytes 1 and 3: K order 0, 2, 1, 3, as in Xq.
+                const uint32_t w8 = W[w] >> 8;
+                const uint32_t l02 = (W[w] & 0x000F000Fu) | 0x64006400u;
+                const uint32_t l13 = (w8 & 0x000F000Fu) | 0x64006400u;
+                const uint32_t h02 = (W[w] & 0x00F000F0u) | 0x64006400u;
+                const uint32_t h13 = (w8 & 0x00F000F0u) | 0x64006400u;
+                v[2 * w] = hfma2_bits(l02, s_lo, n_lo);
+                v[2 * w + 1] = hfma2_bits(l13, s_lo, n_lo);
+                v[16 + 2 * w] = hfma2_bits(h02, s_h16, n_hi);
+                v[16 + 2 * w + 1] = hfma2_bits(h13, s_h16, n_hi);
+            }
+            // min columns 4 part + k: both fp16 halves of the column hold the
+            // value of sub-block 4 part + k (block sums 2j and 2j + 1)
+            const uint32_t ew0 = part ? em.z : em.x, ew1 = part ? em.w : em.y;
+            uint32_t e[4];
+            e[0] = __byte_perm(ew0, 0u, 0x1010);
+            e[1] = __byte_perm(ew0, 0u, 0x3232);
+            e[2] = __byte_perm(ew1, 0u, 0x1010);
+            e[3] = __byte_perm(ew1, 0u, 0x3232);
+
+            if (pending >= 0) {
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full + pending % A_BUFS);
+            }
+            tmem_st32(tmem + lane_base + (uint32_t)(A_COL0 + 64 * ab + 32 * part), v);
+            tmem_st4(tmem + lane_base + (uint32_t)(E_COL0 + 8 * ab + 4 * part), e);
+            pending = f;
+        }
+        if (pending >= 0) {
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(a_full + ab);
-            hdr = nhdr;
-            wa = nwa;
-            wb = nwb;
+            if (lane == 0) mbar_arrive(a_full + pending % A_BUFS);
         }
     } else {
         setmaxnreg_inc<REGS_DRAIN>();
@@ -461,14 +604,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         const int q = warp & 3;    // lane quadrant = 32 weight rows of the tile
         const int th = dw >> 2;    // 64-token half of the tile
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        const int n_groups = a.n_pad / 32;
-        griddep_wait();  // Xd comes from the preparation kernel
         float out[64];
 #pragma unroll
         for (int j = 0; j < 64; j++) out[j] = 0.f;
         int seg_b0 = 0;
-        for (int i = 0; i < n_units; i++) {
-            const int u = u0 + i, t = u / nb, b = u % nb, tw = t / a.tiles_t, tt = t % a.tiles_t;
+        UnitPos p;
+        p.init(u0, nb, a.tiles_t);
+        for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
+            const int t = p.t, b = p.b, tw = p.tw, tt = p.tt;
             if (i == 0 || b == 0) {
 #pragma unroll
                 for (int j = 0; j < 64; j++) out[j] = 0.f;
@@ -476,50 +619,45 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             const int g = tw * 4 + q;
             const int row = g * 32 + lane;
-            float s = 0.f;
-            if (g < n_groups) {
-                const uint32_t hw =
-                    __ldg(reinterpret_cast<const uint32_t*>(a.tiles + ((size_t)g * nb + b) * Q4K_TILE + lane * 16));
-                s = q4k_block_scale(hw).s;
-            }
-            // This warp's 64 token scales, staged in shared memory (read back
-            // as broadcasts) to keep registers for the accumulators.
-            float* dr = dr_smem + dw * 64;
-            {
-                const float2 v = __ldg(reinterpret_cast<const float2*>(a.xd + (size_t)b * a.m_pad + tt * TN + th * 64) + lane);
-                __syncwarp();
-                reinterpret_cast<float2*>(dr)[lane] = v;
-                __syncwarp();
-            }
+            const int ws = i % W_STAGES;
+            const uint32_t wph = (uint32_t)(i / W_STAGES) & 1u;
             const int accb = i & 1;
-            const uint32_t acc_ph = (uint32_t)(i >> 1) & 1u;
-            if (!warp_wait_bar(acc_full + accb, acc_ph, a.err, abort_flag, lane)) break;
+            if (!warp_wait_bar(acc_full + accb, (uint32_t)(i >> 1) & 1u, a.err, abort_flag, lane) ||
+                !warp_wait_bar(w_full + ws, wph, a.err, abort_flag, lane) ||
+                !warp_wait_bar(e_full + ws, wph, a.err, abort_flag, lane))
+                break;
             tc_fence_after();
-#pragma unroll
-            for (int hh = 0; hh < 4; hh++) {
-                uint32_t r[16];
-                tmem_ld16(tmem + lane_base + (uint32_t)(accb * TN + th * 64 + hh * 16), r);
-                tmem_ld_wait(r);
-#pragma unroll
-                for (int j = 0; j < 16; j += 4) {
-                    const float4 d4 = *reinterpret_cast<const float4*>(dr + hh * 16 + j);
-                    // out += (d8 * s) * T, two tokens per packed instruction
-                    const float2 ss = make_float2(s, s);
-                    const float2 c0 = fmul2(make_float2(d4.x, d4.y), ss);
-                    const float2 c1 = fmul2(make_float2(d4.z, d4.w), ss);
-                    const float2 o0 = ffma2(c0, make_float2(__uint_as_float(r[j + 0]), __uint_as_float(r[j + 1])),
-                                            make_float2(out[hh * 16 + j + 0], out[hh * 16 + j + 1]));
-                    const float2 o1 = ffma2(c1, make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])),
-                                            make_float2(out[hh * 16 + j + 2], out[hh * 16 + j + 3]));
-                    out[hh * 16 + j + 0] = o0.x;
-                    out[hh * 16 + j + 1] = o0.y;
-                    out[hh * 16 + j + 2] = o1.x;
-                    out[hh * 16 + j + 3] = o1.y;
-                }
-            }
+            // Weight scale of this lane's row and the 64 token scales of this
+            // warp's half, from the unit's stage (then released).
+            const uint8_t* st = wring + ws * W_STAGE_BYTES;
+            const float s = (g < n_groups) ? reinterpret_cast<const float*>(st + W_S_OFF)[q * 32 + lane] : 0.f;
+            const float* dr = reinterpret_cast<const float*>(st + W_DR_OFF) + th * 64;
+            const float2 ss = make_float2(s, s);
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64), r0);
+            tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64 + 32), r1);
+            tmem_ld_wait2(r0, r1);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty + accb);
+            if (lane == 0) mbar_arrive(acc_empty + accb);  // the accumulator may be overwritten
+#pragma unroll
+            for (int j = 0; j < 64; j += 4) {
+                // out += (d8 * s) * T, two tokens per packed instruction
+                const float4 d4 = *reinterpret_cast<const float4*>(dr + j);
+                const uint32_t* r = j < 32 ? r0 + j : r1 + (j - 32);
+                const float2 c0 = __fmul2_rn(make_float2(d4.x, d4.y), ss);
+                const float2 c1 = __fmul2_rn(make_float2(d4.z, d4.w), ss);
+                const float2 o0 = __ffma2_rn(c0, make_float2(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                                             make_float2(out[j], out[j + 1]));
+                const float2 o1 = __ffma2_rn(c1, make_float2(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                                             make_float2(out[j + 2], out[j + 3]));
+                out[j] = o0.x;
+                out[j + 1] = o0.y;
+                out[j + 2] = o1.x;
+                out[j + 3] = o1.y;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(w_empty + ws);  // done with the unit's scales
 
             if (b != nb - 1 && i != n_units - 1) continue;  // the tile's segment goes on
             const int tok0 = tt * TN + th * 64;
@@ -538,11 +676,12 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             const int first = cta_of_unit(tu0, U, G), last = cta_of_unit(tu0 + nb - 1, U, G);
             const int me = blockIdx.x;
             const int local = (th * 64) * TM + q * 32 + lane;  // token-major piece of this warp
-            auto slot_of = [&](int c) -> int {
-                const long long cu0 = (long long)c * U / G;
-                return (cu0 / nb == t) ? 0 : 1;
+            // Slot 0 holds a CTA's first tile, slot 1 its last one.
+            auto piece = [&](int cta) -> float* {
+                const long long cu0 = (long long)cta * U / G;
+                return a.ws + ((size_t)cta * 2 + ((cu0 / nb == t) ? 0 : 1)) * (TM * TN) + local;
             };
-            float* mine = a.ws + ((size_t)me * 2 + slot_of(me)) * (TM * TN) + local;
+            float* mine = piece(me);
 #pragma unroll
             for (int j = 0; j < 64; j++) __stcg(mine + j * TM, out[j]);
             __threadfence();
@@ -557,15 +696,18 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             is_last = __shfl_sync(0xffffffffu, is_last, 0);
             if (!is_last) continue;
             __threadfence();
+            for (int cta = first; cta <= last; cta++) {
+                const float* p = piece(cta);
 #pragma unroll
-            for (int j = 0; j < 64; j++) {
-                float v = 0.f;
-                for (int c = first; c <= last; c++) {
-                    const float x = (c == me) ? out[j]
-                                              : __ldcg(a.ws + ((size_t)c * 2 + slot_of(c)) * (TM * TN) + local + j * TM);
-                    v = (c == first) ? x : v + x;
+                for (int j = 0; j < 64; j++) {
+                    const float v = __ldcg(p + j * TM);
+                    out[j] = (cta == first) ? v : out[j] + v;
                 }
-                if (row < a.n_out && tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.n_out + row] = v;
+            }
+            if (row < a.n_out) {
+#pragma unroll
+                for (int j = 0; j < 64; j++)
+                    if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.n_out + row] = out[j];
             }
         }
     }
@@ -581,6 +723,16 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
+size_t q4k_meta_bytes(int nb, int n_pad) { return (size_t)(n_pad / 32) * nb * tcg::Q4K_META_TILE; }
+size_t q4k_scale_bytes(int nb, int n_pad) { return (size_t)n_pad * nb * sizeof(float); }
+
+cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad, cudaStream_t s) {
+    const long long n = (long long)n_pad * nb;
+    if (n == 0) return cudaSuccess;
+    q4k_meta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(tiles, meta, scale, n_pad, nb);
+    return cudaGetLastError();
+}
+
 TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms) {
     TcGemmPlan p{};
     p.m_pad = (tokens + tcg::TN - 1) / tcg::TN * tcg::TN;

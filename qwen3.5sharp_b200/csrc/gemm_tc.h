@@ -9,6 +9,8 @@ namespace q35k {
 
 struct TcGemmArgs {
     const uint8_t* tiles;  // uploaded Q4_K weight tiles (32-row chunk-major layout)
+    const uint8_t* meta;   // their GEMM metadata (q4k_meta_kernel)
+    const float* scale;    // the drain scale s of every (row, super-block)
     const float* xd;       // Q8_K block scales [nb][m_pad]
     float* y;              // [tokens][n_out]
     float* ws;             // partial tiles: [grid][2][128 tokens][128 rows]
@@ -25,6 +27,10 @@ struct TcGemmPlan {
 };
 
 TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms);
+// GEMM metadata of an uploaded Q4_K weight: sizes and the kernel that fills it.
+size_t q4k_meta_bytes(int nb, int n_pad);
+size_t q4k_scale_bytes(int nb, int n_pad);
+cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad, cudaStream_t s);
 cudaError_t configure_tc_gemm();
 // Q8_K quantization of x [tokens][k] into the GEMM's operands: Xq [tokens][k]
 // fp16 q values, Xe [tokens][k/256*16] fp16 block sums, Xd [k/256][m_pad] d.
