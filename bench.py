@@ -412,6 +412,52 @@ def secondary_configs(ctx, torch, np, synth, peaks):
         del graph
         for W in Ws:
             W.free()
+    out.update(gemm_configs(ctx, torch, synth, peaks))
+    return out
+
+
+def gemm_configs(ctx, torch, synth, peaks):
+    """Tensor-core prefill GEMM (Q4_K, M = 512): BASELINE config 3 and config
+    4 at M = 512 on one GPU.  Device time per q35k_matmul_dev call (Q8_K
+    preparation kernel + GEMM kernel), CUDA-graph replay; the weights (14 and
+    80 MB) sit in L2 after the first call, as in any compute-bound GEMM.
+    TFLOP/s = 2 M N K / time against the measured dense bf16 peak."""
+    out = {}
+    stream = torch.cuda.current_stream()
+    bf16_peak = peaks.get("bf16_tflops")
+    for name, m, k, n in (("cfg3_q4k_gemm_m512", 512, 2560, 9728), ("cfg4_q4k_gemm_m512_p1", 512, 5120, 27648)):
+        w = synth.kquant_blocks(synth.Q4_K, n, k, seed=1)
+        x = synth.activations(m, k, seed=2)
+        W = ctx.upload(synth.Q4_K, w, k, n)
+        dx = torch.from_numpy(x).cuda()
+        dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            ctx.matmul_dev(W, dx, dy, m, stream)
+        torch.cuda.synchronize()
+        calls = 10
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cs = torch.cuda.current_stream()
+            for _ in range(calls):
+                ctx.matmul_dev(W, dx, dy, m, cs)
+        graph.replay()
+        torch.cuda.synchronize()
+        reps = 10
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / (reps * calls)
+        tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
+        out[name] = {"call_ms": ms, "TFLOP/s": tflops,
+                     "frac_measured_bf16": (tflops / bf16_peak) if bf16_peak else None,
+                     "peak_kind": "measured dense bf16 (MEASURED_PEAKS.json bf16_tflops)",
+                     "kernels": "gemm_prep_kernel + gemm_q4k_tc_kernel (tcgen05, TMEM, TMA)",
+                     "timing": f"CUDA-graph replay of {calls} calls x {reps}"}
+        del graph
+        W.free()
     return out
 
 

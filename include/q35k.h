@@ -124,6 +124,44 @@ int q35k_dequantize(q35k_ctx* ctx, int ggml_type, const void* blocks, float* y, 
 int q35k_dequantize_dev(q35k_ctx* ctx, int ggml_type, const void* d_blocks, float* d_y, int k, int rows,
                         void* stream);
 
+/* ---- Row-sharded matmul over the GPUs of one node ------------------------
+ *
+ * The reference splits output rows between the workers of its CpuThreadPool
+ * (Kernels/MulMatQ4K.cs:31-36, Kernels/CpuThreadPool.cs:46-92); here a group
+ * of GPUs ("ranks") each holds rows [r * n_shard, (r + 1) * n_shard) of a
+ * weight (n_shard = ceil(n_out / ranks) rounded up to 32), computes its slice
+ * of y, and the slices are all-gathered over NVLink so that every rank holds
+ * the full y. */
+typedef struct q35k_shard q35k_shard;
+typedef struct q35k_sharded_weight q35k_sharded_weight;
+#define Q35K_GATHER_NCCL 0 /* NCCL all-gather (any group) */
+#define Q35K_GATHER_PEER 1 /* peer copies over NVLink (all ranks in one process) */
+#define Q35K_NCCL_ID_BYTES 128
+
+/* One process driving `ndev` GPUs (NCCL communicators from ncclCommInitAll). */
+int q35k_shard_create(int ndev, const int* devices, q35k_shard** out);
+/* One process per GPU: rank `rank` of `nranks` on `device`; every rank
+ * passes the same id, made by one of them with q35k_nccl_unique_id and
+ * shared by the caller's own means. */
+int q35k_nccl_unique_id(void* id_out /* Q35K_NCCL_ID_BYTES */);
+int q35k_shard_create_rank(int nranks, int rank, const void* nccl_id, int device, q35k_shard** out);
+int q35k_shard_destroy(q35k_shard* s);
+const char* q35k_shard_last_error(const q35k_shard* s);
+int q35k_shard_info(const q35k_shard* s, int* nranks, int* first_rank, int* local_devices);
+int q35k_shard_sync(q35k_shard* s);
+/* Upload the local ranks' rows of a full GGUF weight (n_out rows, host). */
+int q35k_shard_weight_upload(q35k_shard* s, int ggml_type, const void* blocks, int n_in, int n_out,
+                             q35k_sharded_weight** out);
+int q35k_shard_weight_free(q35k_shard* s, q35k_sharded_weight* w);
+/* y = x @ W^T with x replicated on every local device (d_x[i]) and the full
+ * y [tokens][n_out] written to every local device (d_y[i]); asynchronous on
+ * the contexts' streams (q35k_shard_sync waits). */
+int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const float* const* d_x, float* const* d_y,
+                          int tokens, int gather_mode);
+/* Host pointers, synchronous: x [tokens][n_in] in, full y out. */
+int q35k_shard_matmul(q35k_shard* s, const q35k_sharded_weight* w, const float* x, float* y, int tokens,
+                      int gather_mode);
+
 /* ---- Allocation-free decode matmul --------------------------------------
  *
  * No counterpart in the reference.  For callers that must not have a library

@@ -265,7 +265,8 @@ static int gemv_chunk(const q35k_weight* w) { return gemv_max_tokens(w->nb); }
 // Launch the GEMV for `tokens` rows of planar Q8_K (in chunks of
 // gemv_chunk(w) rows) already on the device.
 int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl,
-                   const float* d_x) {
+                   const float* d_x, int ldy) {
+    if (ldy <= 0) ldy = w->n_out;
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, chunk, num_sms);
@@ -282,8 +283,8 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
         } else {
             a.q8 = d_q8 + (size_t)(t0 / chunk) * chunk_stride;
         }
-        a.y = d_y + (size_t)t0 * w->n_out;
-        a.ldy = w->n_out;
+        a.y = d_y + (size_t)t0 * ldy;
+        a.ldy = ldy;
         a.n_out = w->n_out;
         a.nb = w->nb;
         a.tokens = std::min(chunk, tokens - t0);
@@ -297,7 +298,8 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
     return Q35K_OK;
 }
 
-int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s) {
+int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy) {
+    if (ldy <= 0) ldy = w->n_out;
     const TcGemmPlan p = plan_tc_gemm(w->nb, w->n_pad, tokens, num_sms);
     int rc;
     if ((rc = ensure_dev(&d_xq, &xq_cap, p.xq_bytes, false)) != Q35K_OK) return rc;
@@ -313,6 +315,7 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     a.scale = w->scale;
     a.xd = d_xd;
     a.y = d_y;
+    a.ldy = ldy;
     a.ws = d_gws;
     a.counters = d_gcnt;
     a.err = d_err;
@@ -327,6 +330,21 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     e = launch_tc_gemm(a, d_xq, d_xe, w->n_in, s, true);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
     return Q35K_OK;
+}
+
+int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s) {
+    // Prefill: the tensor-core GEMM.
+    if (w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens) return gemm(w, d_x, d_y, tokens, s, ldy);
+    const int chunk = gemv_chunk(w);
+    if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
+    // Decode: the GEMV quantizes its own slices of x (one kernel per call).
+    if (tokens <= chunk && gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, num_sms))
+        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy);
+    int rc;
+    if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK) return rc;
+    cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s);
+    if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
+    return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy);
 }
 
 static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, const void* y, int tokens) {
@@ -371,19 +389,7 @@ int q35k_matmul_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* 
     if (rc) return rc;
     if ((rc = check_alignment(c, d_x, 16, d_y, 4)) != Q35K_OK) return rc;
     cudaSetDevice(c->device);
-    cudaStream_t s = pick(c, stream);
-    // Prefill: the tensor-core GEMM.
-    if (w->type == Q35K_TYPE_Q4_K && tokens >= c->gemm_min_tokens) return c->gemm(w, d_x, d_y, tokens, s);
-    const int chunk = gemv_chunk(w);
-    if (chunk <= 0) return c->fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
-    // Decode: the GEMV quantizes its own slices of x (one kernel per call).
-    if (tokens <= chunk && gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, c->num_sms))
-        return c->gemv(w, nullptr, d_y, tokens, s, true, d_x);
-    if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK)
-        return rc;
-    cudaError_t e = launch_quantize_q8k(d_x, c->d_q8, w->n_in, tokens, chunk, s);
-    if (e != cudaSuccess) return c->cuda_fail(e, "Q8_K quantize launch");
-    return c->gemv(w, c->d_q8, d_y, tokens, s);
+    return c->matmul_into(w, d_x, d_y, w->n_out, tokens, pick(c, stream));
 }
 
 int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int tokens) {

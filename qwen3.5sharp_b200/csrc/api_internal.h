@@ -86,7 +86,10 @@ struct q35k_ctx {
     // `pdl`: launch with programmatic stream serialization (the GEMV streams
     // weights before the preceding kernel finishes; its Q8_K reads wait).
     int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true,
-             const float* d_x = nullptr);
+             const float* d_x = nullptr, int ldy = 0);
     // Tensor-core prefill GEMM (Q4_K): quantize x, then the GEMM.
-    int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s);
+    int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0);
+    // y[tokens][ldy] (columns below n_out) = x @ W^T on device pointers: the
+    // dispatch behind q35k_matmul_dev (ldy = n_out) and the sharded calls.
+    int matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s);
 };

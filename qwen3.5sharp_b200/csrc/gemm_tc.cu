@@ -33,16 +33,18 @@
 // adds the pieces in CTA order: results are bit-identical run to run.
 //
 // Warp roles (640 threads, one CTA per SM):
-//   warp 0      TMA: Xq (4 boxes of 64 K x 128 tokens, 128-byte swizzle) and
-//               Xe (16 x 128, 32-byte swizzle) per unit into one of 3 stages
+//   warp 0      TMA: Xq, half a super-block (2 boxes of 64 K x 128 tokens,
+//               128-byte swizzle) per stage
 //   warp 1      TMEM allocation and the MMA issue (one thread)
-//   warps 4-11  weight producers: the A operand of each half super-block,
-//               in turn, in one of 3 TMEM buffers (64 value columns + 8 min
-//               columns); two warps per TMEM lane quadrant
+//   warp 2      bulk copies: weight tiles + metadata + Xe (16 x 128, 32-byte
+//               swizzle) per unit; the drain scales per unit
+//   warps 4-11  weight producers, two groups: group h builds the A operand
+//               of half h of every super-block (64 value columns in TMEM,
+//               the 16-column min term in shared memory)
 //   warps 12-19 drains: per super-block, accumulator -> registers, scaled by
 //               the Q8_K and weight scales; then the tile's output
 // TMEM: accumulators at columns 0 and 128 (double-buffered per super-block),
-// A buffers of 64 value columns at 256 + 64 i and 8 min columns at 448 + 8 i.  Every mbarrier wait is bounded in time; on expiry
+// A buffers of 64 value columns at 256 + 64 i.  Every mbarrier wait is bounded in time; on expiry
 // the CTA sets the device error word, stops issuing work, waits (bounded) for
 // its own copies and MMAs in flight, frees TMEM and exits.
 #include <cuda.h>
@@ -76,29 +78,38 @@ constexpr int X_STAGES = 3;
 constexpr int X_BOX_BYTES = 64 * 2 * TN;           // 16 KB
 constexpr int X_STAGE_BYTES = 2 * X_BOX_BYTES;     // 32 KB
 // Weight ring, one stage per unit: the unit's block-sum operand Xe (16 x 128
-// fp16, 32-byte swizzle), the four 32-row weight tiles (4 x 4608 B), their
-// GEMM metadata (4 x 1536 B), the drain scales s (4 x 128 B) and the 128
-// token scales d8.  Released by the producers and the drains.
-constexpr int W_STAGES = 4;
+// fp16, 32-byte swizzle), the four 32-row weight tiles (4 x 4608 B) and their
+// GEMM metadata (4 x 1536 B).  Released by the producers and the MMA.
+constexpr int W_STAGES = 3;
 constexpr int Q4K_TILE = 32 * 144;                 // one 32-row tile of the uploaded layout
 constexpr int EXT_BOX_BYTES = 16 * 2 * TN;         // 4096
 constexpr int W_EXT_OFF = 0;                       // 1024-aligned (swizzled TMA destination)
 constexpr int W_TILE_OFF = EXT_BOX_BYTES;
 constexpr int W_META_OFF = W_TILE_OFF + 4 * Q4K_TILE;
-constexpr int W_S_OFF = W_META_OFF + 4 * Q4K_META_TILE;
-constexpr int W_DR_OFF = W_S_OFF + 4 * 32 * 4;
-constexpr int W_STAGE_BYTES = W_DR_OFF + TN * 4;   // 29696 (29 KB)
+constexpr int W_STAGE_BYTES = W_META_OFF + 4 * Q4K_META_TILE;  // 28672 (28 KB)
 static_assert(W_STAGE_BYTES % 1024 == 0, "weight stage alignment");
+// Drain ring, one stage per unit: the drain scales s of the 128 rows and the
+// 128 token scales d8.  Released by the drains.
+constexpr int D_STAGES = 4;
+constexpr int D_STAGE_BYTES = 2 * 128 * 4;
+// A operand: 4 TMEM buffers of 64 value columns (one half super-block each;
+// buffers 2 p + h belong to producer group h) and, for the min term, 4 shared
+// memory tiles of 128 rows x 16 fp16 (32-byte swizzle, read by a
+// shared-memory MMA).
+constexpr int A_BUFS = 4;
+constexpr int E_TILE_BYTES = 128 * 32;
 constexpr int X_RING_BYTES = X_STAGES * X_STAGE_BYTES;
 constexpr int W_RING_BYTES = W_STAGES * W_STAGE_BYTES;
-constexpr int A_BUFS = 3;
-// TMEM: accumulators at columns 0 and 128; A buffers of 64 value columns at
-// 256 + 64 i; their 8 min columns at 448 + 8 i.
-constexpr int A_COL0 = 256, E_COL0 = 448;
+constexpr int E_RING_BYTES = A_BUFS * E_TILE_BYTES;
+constexpr int D_RING_BYTES = D_STAGES * D_STAGE_BYTES;
+// TMEM: accumulators at columns 0 and 128; A buffers at 256 + 64 i.
+constexpr int A_COL0 = 256;
 constexpr int TMEM_COLS = 512;
-constexpr int NUM_BARS = 2 * X_STAGES + 3 * W_STAGES + 2 * A_BUFS + 4 + 1;
-constexpr size_t SMEM_BYTES = 1024 + (size_t)X_RING_BYTES + W_RING_BYTES + 256;
-static_assert(NUM_BARS * 8 + 8 <= 256, "barrier area");
+constexpr int NUM_BARS = 2 * X_STAGES + 3 * W_STAGES + 2 * D_STAGES + 2 * A_BUFS + 4 + 1;
+constexpr int BAR_BYTES = 512;
+constexpr size_t SMEM_BYTES =
+    1024 + (size_t)X_RING_BYTES + W_RING_BYTES + E_RING_BYTES + D_RING_BYTES + BAR_BYTES;
+static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
@@ -339,14 +350,18 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* xring = smem;
-    uint8_t* wring = smem + X_RING_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + X_RING_BYTES + W_RING_BYTES);
+    uint8_t* wring = xring + X_RING_BYTES;
+    uint8_t* ering = wring + W_RING_BYTES;
+    uint8_t* dring = ering + E_RING_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(dring + D_RING_BYTES);
     uint64_t* x_full = bars;                      // [X_STAGES] activation half stage landed
     uint64_t* x_empty = x_full + X_STAGES;        // [X_STAGES] its MMAs completed
-    uint64_t* w_full = x_empty + X_STAGES;        // [W_STAGES] weight tiles landed
-    uint64_t* e_full = w_full + W_STAGES;         // [W_STAGES] Xe + d8 landed
-    uint64_t* w_empty = e_full + W_STAGES;        // [W_STAGES] producers and drains done with it
-    uint64_t* a_full = w_empty + W_STAGES;        // [A_BUFS] TMEM A operand written
+    uint64_t* w_full = x_empty + X_STAGES;        // [W_STAGES] weight tiles + metadata landed
+    uint64_t* e_full = w_full + W_STAGES;         // [W_STAGES] Xe landed
+    uint64_t* w_empty = e_full + W_STAGES;        // [W_STAGES] producers read it, its MMAs completed
+    uint64_t* d_full = w_empty + W_STAGES;        // [D_STAGES] drain scales landed
+    uint64_t* d_empty = d_full + D_STAGES;        // [D_STAGES] drains done with them
+    uint64_t* a_full = d_empty + D_STAGES;        // [A_BUFS] A operand written (TMEM + min tile)
     uint64_t* a_empty = a_full + A_BUFS;          // [A_BUFS] its MMAs completed
     uint64_t* acc_full = a_empty + A_BUFS;        // [2]
     uint64_t* acc_empty = acc_full + 2;           // [2]
@@ -371,10 +386,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         for (int i = 0; i < W_STAGES; i++) {
             mbar_init(w_full + i, 1);
             mbar_init(e_full + i, 1);
-            mbar_init(w_empty + i, 16);  // 8 producer warps + 8 drain warps
+            mbar_init(w_empty + i, 9);  // 8 producer warps + the MMA's commit
+        }
+        for (int i = 0; i < D_STAGES; i++) {
+            mbar_init(d_full + i, 1);
+            mbar_init(d_empty + i, NUM_DRAIN);
         }
         for (int i = 0; i < A_BUFS; i++) {
-            mbar_init(a_full + i, 8);
+            mbar_init(a_full + i, 4);  // the 4 warps of the producer group
             mbar_init(a_empty + i, 1);
         }
         for (int i = 0; i < 2; i++) {
@@ -406,54 +425,59 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             p.init(u0, nb, a.tiles_t);
             for (int f = 0; f < n; f++) {
                 if (f > 0 && (f & 1) == 0) p.next(nb, a.tiles_t);
-                const int b = p.b, tt = p.tt;
                 const int xs = f % X_STAGES;
                 if (!wait_bar(x_empty + xs, ((uint32_t)(f / X_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
                 mbar_arrive_expect_tx(x_full + xs, X_STAGE_BYTES);
                 uint8_t* dst = xring + xs * X_STAGE_BYTES;
-                const int k0 = b * QK + 128 * (f & 1);
-                tma_load_2d(dst, &tm_q, k0, tt * TN, x_full + xs);
-                tma_load_2d(dst + X_BOX_BYTES, &tm_q, k0 + 64, tt * TN, x_full + xs);
+                const int k0 = p.b * QK + 128 * (f & 1);
+                tma_load_2d(dst, &tm_q, k0, p.tt * TN, x_full + xs);
+                tma_load_2d(dst + X_BOX_BYTES, &tm_q, k0 + 64, p.tt * TN, x_full + xs);
                 issued = f + 1;
             }
             for (int f = (issued > X_STAGES ? issued - X_STAGES : 0); f < issued; f++)
                 wait_inflight(x_full + (f % X_STAGES), (uint32_t)(f / X_STAGES) & 1u, a.err);
         } else if (warp == WARP_WTMA && lane == 0) {
-            // ---------------- weight tiles, Xe and d8 ----------------
+            // ---------------- weight tiles, metadata, Xe; drain scales ----------------
             bool dep_done = false;
-            int issued = 0;
+            int issued_w = 0, issued_d = 0;
             UnitPos p;
             p.init(u0, nb, a.tiles_t);
             for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
                 const int b = p.b, tw = p.tw, tt = p.tt;
+                int valid = 0;
+                for (int q = 0; q < 4; q++) valid += (tw * 4 + q < n_groups) ? 1 : 0;
                 const int ws = i % W_STAGES;
                 if (!wait_bar(w_empty + ws, ((uint32_t)(i / W_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
                 uint8_t* dst = wring + ws * W_STAGE_BYTES;
-                int valid = 0;
-                for (int q = 0; q < 4; q++) valid += (tw * 4 + q < n_groups) ? 1 : 0;
-                mbar_arrive_expect_tx(w_full + ws, (uint32_t)(valid * (Q4K_TILE + Q4K_META_TILE + 128)));
-                for (int q = 0; q < 4; q++) {
-                    const int g = tw * 4 + q;
-                    if (g >= n_groups) continue;
-                    const size_t tile = (size_t)g * nb + b;
+                mbar_arrive_expect_tx(w_full + ws, (uint32_t)(valid * (Q4K_TILE + Q4K_META_TILE)));
+                for (int q = 0; q < valid; q++) {
+                    const size_t tile = (size_t)(tw * 4 + q) * nb + b;
                     bulk_g2s(dst + W_TILE_OFF + q * Q4K_TILE, a.tiles + tile * Q4K_TILE, Q4K_TILE, w_full + ws);
                     bulk_g2s(dst + W_META_OFF + q * Q4K_META_TILE, a.meta + tile * Q4K_META_TILE, Q4K_META_TILE,
                              w_full + ws);
-                    bulk_g2s(dst + W_S_OFF + q * 128, a.scale + tile * 32, 128, w_full + ws);
                 }
                 if (!dep_done) {
                     griddep_wait();  // Xe and d8 come from the preparation kernel
                     dep_done = true;
                 }
-                mbar_arrive_expect_tx(e_full + ws, EXT_BOX_BYTES + TN * 4);
+                mbar_arrive_expect_tx(e_full + ws, EXT_BOX_BYTES);
                 tma_load_2d(dst + W_EXT_OFF, &tm_e, b * 16, tt * TN, e_full + ws);
-                bulk_g2s(dst + W_DR_OFF, a.xd + (size_t)b * a.m_pad + tt * TN, TN * 4, e_full + ws);
-                issued = i + 1;
+                issued_w = i + 1;
+                const int ds = i % D_STAGES;
+                if (!wait_bar(d_empty + ds, ((uint32_t)(i / D_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
+                uint8_t* dd = dring + ds * D_STAGE_BYTES;
+                mbar_arrive_expect_tx(d_full + ds, (uint32_t)(valid * 128 + TN * 4));
+                for (int q = 0; q < valid; q++)
+                    bulk_g2s(dd + q * 128, a.scale + ((size_t)(tw * 4 + q) * nb + b) * 32, 128, d_full + ds);
+                bulk_g2s(dd + 512, a.xd + (size_t)b * a.m_pad + tt * TN, TN * 4, d_full + ds);
+                issued_d = i + 1;
             }
-            for (int i = (issued > W_STAGES ? issued - W_STAGES : 0); i < issued; i++) {
+            for (int i = (issued_w > W_STAGES ? issued_w - W_STAGES : 0); i < issued_w; i++) {
                 wait_inflight(w_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
                 wait_inflight(e_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
             }
+            for (int i = (issued_d > D_STAGES ? issued_d - D_STAGES : 0); i < issued_d; i++)
+                wait_inflight(d_full + (i % D_STAGES), (uint32_t)(i / D_STAGES) & 1u, a.err);
         } else if (warp == WARP_MMA && lane == 0) {
             // ---------------- MMA issue ----------------
             const uint32_t idesc = tc_idesc_f16_f32(TM, TN);
@@ -463,13 +487,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 if (!wait_bar(acc_empty + accb, ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err, abort_flag)) break;
                 if (!wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
                 const uint32_t d_tmem = tmem + (uint32_t)(accb * TN);
-                const uint32_t ext_addr = smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF);
+                const uint64_t bext = tc_smem_desc(smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF), 256, 6);
                 bool ok = true;
                 for (int h = 0; h < 2; h++) {
                     const int f = 2 * i + h;
-                    const int xs = f % X_STAGES, ab = f % A_BUFS;
+                    const int xs = f % X_STAGES;
+                    const int ab = 2 * (i & 1) + h;
                     if (!wait_bar(x_full + xs, (uint32_t)(f / X_STAGES) & 1u, a.err, abort_flag) ||
-                        !wait_bar(a_full + ab, (uint32_t)(f / A_BUFS) & 1u, a.err, abort_flag)) {
+                        !wait_bar(a_full + ab, (uint32_t)(i >> 1) & 1u, a.err, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -481,12 +506,13 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                         const uint64_t desc = tc_smem_desc(x_addr + (t >> 2) * X_BOX_BYTES + (t & 3) * 32, 1024, 2);
                         tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, desc, idesc, (h | t) != 0 ? 1u : 0u);
                     }
-                    tc_mma_f16_ts(d_tmem, tmem + (uint32_t)(E_COL0 + 8 * ab), tc_smem_desc(ext_addr, 256, 6), idesc,
-                                  1u);
+                    // the min term: 16 K from shared memory (A) against Xe
+                    tc_mma_f16_ss(d_tmem, tc_smem_desc(smem_u32(ering + ab * E_TILE_BYTES), 256, 6), bext, idesc, 1u);
                     tc_commit(a_empty + ab);
                     tc_commit(x_empty + xs);
                 }
                 if (!ok) break;
+                tc_commit(w_empty + ws);
                 tc_commit(acc_full + accb);
             }
             // Every MMA issued by this thread completes before TMEM is freed.
@@ -496,106 +522,90 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     } else if (warp < WARP_DRAIN0) {
         setmaxnreg_dec<REGS_PROD>();
         // ---------------- weight producers ----------------
-        // Every A buffer fill (one half super-block, in order) is built by all
-        // eight producer warps: warp (q, part) writes the 32 value columns of
-        // 64-value chunk 2h + part for lanes 32q..32q+31, and 4 of the 8 min
-        // columns.  Each warp waits on every barrier phase in turn.  The
-        // stores of fill f complete while fill f + 1 is being decoded; fill f
-        // is published (a_full) once they have.
-        const int q = warp & 3;                     // TMEM lane quadrant = 32-row group within the tile
-        const int part = (warp - WARP_PROD0) >> 2;  // which 64-value chunk of each half
+        // Group h (4 warps, one per TMEM lane quadrant q) builds the A
+        // operand of half h of every super-block: the 64 value columns of
+        // rows 32q..32q+31 in TMEM buffer 2 (i & 1) + h, and the min-term tile
+        // (high part for h = 0, low part for h = 1) in shared memory.  Each
+        // group owns its two buffers, so each barrier has one waiting group.
+        const int h = (warp - WARP_PROD0) >> 2;
+        const int q = warp & 3;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-        // Per unit: this lane's fp16 sub-block scales alpha * sc_j (8 halves).
-        uint32_t sa[4];
-        int pending = -1;  // fill whose TMEM stores are in flight
-        const int n_fills = 2 * n_units;
+        const int r = 32 * q + lane;  // row of the tile
         UnitPos p;
         p.init(u0, nb, a.tiles_t);
-        for (int f = 0; f < n_fills; f++) {
-            const int i = f >> 1, h = f & 1;
-            if (f > 0 && h == 0) p.next(nb, a.tiles_t);
-            const int tw = p.tw;
-            const bool valid = tw * 4 + q < n_groups;
-            const int ws = i % W_STAGES, ab = f % A_BUFS;
+        for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
+            const bool valid = p.tw * 4 + q < n_groups;
+            const int ws = i % W_STAGES, ab = 2 * (i & 1) + h;
+            if (!warp_wait_bar(w_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag, lane)) break;
             const uint8_t* stage = wring + ws * W_STAGE_BYTES;
             const uint8_t* tile = stage + W_TILE_OFF + q * Q4K_TILE + lane * 16;
             const uint8_t* mt = stage + W_META_OFF + q * Q4K_META_TILE + lane * 16;
-            if (h == 0) {
-                if (!warp_wait_bar(w_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag, lane)) break;
-                const uint4 v = valid ? *reinterpret_cast<const uint4*>(mt) : make_uint4(0, 0, 0, 0);
-                sa[0] = v.x;
-                sa[1] = v.y;
-                sa[2] = v.z;
-                sa[3] = v.w;
-            }
-            if (!warp_wait_bar(a_empty + ab, ((uint32_t)(f / A_BUFS) & 1u) ^ 1u, a.err, abort_flag, lane)) break;
-            tc_fence_after();
-            // This lane's row: the two 16-byte chunks of qs holding 64-value
-            // chunk c = 2h + part (tile chunks 1 + 2c, 2 + 2c), and the min
-            // column parts of sub-blocks 4 part .. 4 part + 3 (high half for
-            // h = 0, low half for h = 1).
-            const int c = 2 * h + part;
-            uint4 wa = make_uint4(0, 0, 0, 0), wb = wa, em = wa;
+            uint4 sa = make_uint4(0, 0, 0, 0), em = sa, w0 = sa, w1 = sa, w2 = sa, w3 = sa;
             if (valid) {
-                wa = *reinterpret_cast<const uint4*>(tile + (1 + 2 * c) * 512);
-                wb = *reinterpret_cast<const uint4*>(tile + (2 + 2 * c) * 512);
+                sa = *reinterpret_cast<const uint4*>(mt);
                 em = *reinterpret_cast<const uint4*>(mt + (1 + h) * 512);
+                // 64-value chunks c = 2h, 2h + 1 (tile chunks 1 + 4h .. 4 + 4h)
+                w0 = *reinterpret_cast<const uint4*>(tile + (1 + 4 * h) * 512);
+                w1 = *reinterpret_cast<const uint4*>(tile + (2 + 4 * h) * 512);
+                w2 = *reinterpret_cast<const uint4*>(tile + (3 + 4 * h) * 512);
+                w3 = *reinterpret_cast<const uint4*>(tile + (4 + 4 * h) * 512);
             }
-            if (h == 1) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(w_empty + ws);  // this warp is done with the unit's tiles
+            __syncwarp();
+            if (lane == 0) mbar_arrive(w_empty + ws);  // this warp is done with the stage
+            if (!warp_wait_bar(a_empty + ab, ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err, abort_flag, lane)) break;
+            tc_fence_after();
+            // Min-term tile: row r holds 16 fp16 (both halves of pair j are
+            // the value of sub-block j), 32-byte swizzle: 16-byte chunk c of
+            // row r at (r / 8) * 256 + (r % 8) * 32 + ((c ^ ((r >> 2) & 1)) * 16).
+            {
+                uint8_t* et = ering + ab * E_TILE_BYTES + (r >> 3) * 256 + (r & 7) * 32;
+                const int sw = (r >> 2) & 1;
+                const uint4 c0 = make_uint4(__byte_perm(em.x, 0u, 0x1010), __byte_perm(em.x, 0u, 0x3232),
+                                            __byte_perm(em.y, 0u, 0x1010), __byte_perm(em.y, 0u, 0x3232));
+                const uint4 c1 = make_uint4(__byte_perm(em.z, 0u, 0x1010), __byte_perm(em.z, 0u, 0x3232),
+                                            __byte_perm(em.w, 0u, 0x1010), __byte_perm(em.w, 0u, 0x3232));
+                *reinterpret_cast<uint4*>(et + (sw << 4)) = c0;
+                *reinterpret_cast<uint4*>(et + ((sw ^ 1) << 4)) = c1;
             }
-            // fp16 scales of sub-blocks 2c (low nibbles) and 2c + 1 (high
-            // nibbles): word c of sa holds both.
-            const uint32_t sw = c == 0 ? sa[0] : c == 1 ? sa[1] : c == 2 ? sa[2] : sa[3];
-            const uint32_t s_lo = __byte_perm(sw, 0u, 0x1010), s_hi = __byte_perm(sw, 0u, 0x3232);
-            // Low nibbles become fp16 1024 + q; high nibbles, masked in place,
-            // fp16 1024 + 16 q.  (1024 + q) s - 1024 s and (1024 + 16 q) s/16
-            // - 64 s are q s exactly.
-            const uint32_t n_lo = hmul2_bits(s_lo, 0xE400E400u);   // -1024 s
-            const uint32_t s_h16 = hmul2_bits(s_hi, 0x2C002C00u);  // s / 16
-            const uint32_t n_hi = hmul2_bits(s_hi, 0xD400D400u);   // -64 s
-            const uint32_t W[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-            uint32_t v[32];
+            const uint32_t a_col = tmem + lane_base + (uint32_t)(A_COL0 + 64 * ab);
 #pragma unroll
-            for (int w = 0; w < 8; w++) {
-                // bytes l = 4w..4w+3: low nibbles are values 64c+l, high nibbles
-                // 64c+32+l.  One fp16 pair takes the nibbles of bytes 0 and 2,
-                // the other those of bytes 1 and 3: K order 0, 2, 1, 3, as in Xq.
-                const uint32_t w8 = W[w] >> 8;
-                const uint32_t l02 = (W[w] & 0x000F000Fu) | 0x64006400u;
-                const uint32_t l13 = (w8 & 0x000F000Fu) | 0x64006400u;
-                const uint32_t h02 = (W[w] & 0x00F000F0u) | 0x64006400u;
-                const uint32_t h13 = (w8 & 0x00F000F0u) | 0x64006400u;
-                v[2 * w] = hfma2_bits(l02, s_lo, n_lo);
-                v[2 * w + 1] = hfma2_bits(l13, s_lo, n_lo);
-                v[16 + 2 * w] = hfma2_bits(h02, s_h16, n_hi);
-                v[16 + 2 * w + 1] = hfma2_bits(h13, s_h16, n_hi);
+            for (int cc = 0; cc < 2; cc++) {
+                // fp16 scales of sub-blocks 2c (low nibbles) and 2c + 1 (high
+                // nibbles), c = 2h + cc: word c of sa holds both.
+                const uint32_t sw = (h == 0) ? (cc == 0 ? sa.x : sa.y) : (cc == 0 ? sa.z : sa.w);
+                const uint32_t s_lo = __byte_perm(sw, 0u, 0x1010), s_hi = __byte_perm(sw, 0u, 0x3232);
+                // Low nibbles become fp16 1024 + q; high nibbles, masked in
+                // place, fp16 1024 + 16 q.  (1024 + q) s - 1024 s and
+                // (1024 + 16 q) s/16 - 64 s are q s exactly.
+                const uint32_t n_lo = hmul2_bits(s_lo, 0xE400E400u);   // -1024 s
+                const uint32_t s_h16 = hmul2_bits(s_hi, 0x2C002C00u);  // s / 16
+                const uint32_t n_hi = hmul2_bits(s_hi, 0xD400D400u);   // -64 s
+                const uint4 wa = cc ? w2 : w0, wb = cc ? w3 : w1;
+                const uint32_t W[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                uint32_t v[32];
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    // bytes l = 4w..4w+3: low nibbles are values 64c+l, high
+                    // nibbles 64c+32+l.  One fp16 pair takes the nibbles of bytes
+                    // 0 and 2, the other those of bytes 1 and 3: K order 0, 2,
+                    // 1, 3, as in Xq.
+                    const uint32_t w8 = W[w] >> 8;
+                    const uint32_t l02 = (W[w] & 0x000F000Fu) | 0x64006400u;
+                    const uint32_t l13 = (w8 & 0x000F000Fu) | 0x64006400u;
+                    const uint32_t h02 = (W[w] & 0x00F000F0u) | 0x64006400u;
+                    const uint32_t h13 = (w8 & 0x00F000F0u) | 0x64006400u;
+                    v[2 * w] = hfma2_bits(l02, s_lo, n_lo);
+                    v[2 * w + 1] = hfma2_bits(l13, s_lo, n_lo);
+                    v[16 + 2 * w] = hfma2_bits(h02, s_h16, n_hi);
+                    v[16 + 2 * w + 1] = hfma2_bits(h13, s_h16, n_hi);
+                }
+                tmem_st32(a_col + 32 * cc, v);
             }
-            // min columns 4 part + k: both fp16 halves of the column hold the
-            // value of sub-block 4 part + k (block sums 2j and 2j + 1)
-            const uint32_t ew0 = part ? em.z : em.x, ew1 = part ? em.w : em.y;
-            uint32_t e[4];
-            e[0] = __byte_perm(ew0, 0u, 0x1010);
-            e[1] = __byte_perm(ew0, 0u, 0x3232);
-            e[2] = __byte_perm(ew1, 0u, 0x1010);
-            e[3] = __byte_perm(ew1, 0u, 0x3232);
-
-            if (pending >= 0) {
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(a_full + pending % A_BUFS);
-            }
-            tmem_st32(tmem + lane_base + (uint32_t)(A_COL0 + 64 * ab + 32 * part), v);
-            tmem_st4(tmem + lane_base + (uint32_t)(E_COL0 + 8 * ab + 4 * part), e);
-            pending = f;
-        }
-        if (pending >= 0) {
             tmem_st_wait();
+            fence_proxy_async_smem();  // the min-term tile is read by the tensor core
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(a_full + pending % A_BUFS);
+            if (lane == 0) mbar_arrive(a_full + ab);
         }
     } else {
         setmaxnreg_inc<REGS_DRAIN>();
@@ -619,19 +629,17 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             const int g = tw * 4 + q;
             const int row = g * 32 + lane;
-            const int ws = i % W_STAGES;
-            const uint32_t wph = (uint32_t)(i / W_STAGES) & 1u;
+            const int ds = i % D_STAGES;
             const int accb = i & 1;
-            if (!warp_wait_bar(acc_full + accb, (uint32_t)(i >> 1) & 1u, a.err, abort_flag, lane) ||
-                !warp_wait_bar(w_full + ws, wph, a.err, abort_flag, lane) ||
-                !warp_wait_bar(e_full + ws, wph, a.err, abort_flag, lane))
+            if (!warp_wait_bar(d_full + ds, (uint32_t)(i / D_STAGES) & 1u, a.err, abort_flag, lane) ||
+                !warp_wait_bar(acc_full + accb, (uint32_t)(i >> 1) & 1u, a.err, abort_flag, lane))
                 break;
             tc_fence_after();
+            const uint8_t* dstage = dring + ds * D_STAGE_BYTES;
             // Weight scale of this lane's row and the 64 token scales of this
-            // warp's half, from the unit's stage (then released).
-            const uint8_t* st = wring + ws * W_STAGE_BYTES;
-            const float s = (g < n_groups) ? reinterpret_cast<const float*>(st + W_S_OFF)[q * 32 + lane] : 0.f;
-            const float* dr = reinterpret_cast<const float*>(st + W_DR_OFF) + th * 64;
+            // warp's half, from the unit's drain stage.
+            const float s = (g < n_groups) ? reinterpret_cast<const float*>(dstage)[q * 32 + lane] : 0.f;
+            const float* dr = reinterpret_cast<const float*>(dstage + 512) + th * 64;
             const float2 ss = make_float2(s, s);
             uint32_t r0[32], r1[32];
             tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64), r0);
@@ -644,12 +652,12 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             for (int j = 0; j < 64; j += 4) {
                 // out += (d8 * s) * T, two tokens per packed instruction
                 const float4 d4 = *reinterpret_cast<const float4*>(dr + j);
-                const uint32_t* r = j < 32 ? r0 + j : r1 + (j - 32);
+                const uint32_t* rr = j < 32 ? r0 + j : r1 + (j - 32);
                 const float2 c0 = __fmul2_rn(make_float2(d4.x, d4.y), ss);
                 const float2 c1 = __fmul2_rn(make_float2(d4.z, d4.w), ss);
-                const float2 o0 = __ffma2_rn(c0, make_float2(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                const float2 o0 = __ffma2_rn(c0, make_float2(__uint_as_float(rr[0]), __uint_as_float(rr[1])),
                                              make_float2(out[j], out[j + 1]));
-                const float2 o1 = __ffma2_rn(c1, make_float2(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                const float2 o1 = __ffma2_rn(c1, make_float2(__uint_as_float(rr[2]), __uint_as_float(rr[3])),
                                              make_float2(out[j + 2], out[j + 3]));
                 out[j] = o0.x;
                 out[j + 1] = o0.y;
@@ -657,7 +665,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 out[j + 3] = o1.y;
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(w_empty + ws);  // done with the unit's scales
+            if (lane == 0) mbar_arrive(d_empty + ds);  // done with the unit's scales
 
             if (b != nb - 1 && i != n_units - 1) continue;  // the tile's segment goes on
             const int tok0 = tt * TN + th * 64;
@@ -666,7 +674,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 if (row < a.n_out) {
 #pragma unroll
                     for (int j = 0; j < 64; j++)
-                        if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.n_out + row] = out[j];
+                        if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.ldy + row] = out[j];
                 }
                 continue;
             }
@@ -697,17 +705,17 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             if (!is_last) continue;
             __threadfence();
             for (int cta = first; cta <= last; cta++) {
-                const float* p = piece(cta);
+                const float* pc = piece(cta);
 #pragma unroll
                 for (int j = 0; j < 64; j++) {
-                    const float v = __ldcg(p + j * TM);
+                    const float v = __ldcg(pc + j * TM);
                     out[j] = (cta == first) ? v : out[j] + v;
                 }
             }
             if (row < a.n_out) {
 #pragma unroll
                 for (int j = 0; j < 64; j++)
-                    if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.n_out + row] = out[j];
+                    if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.ldy + row] = out[j];
             }
         }
     }

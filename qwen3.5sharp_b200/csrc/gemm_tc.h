@@ -12,7 +12,8 @@ struct TcGemmArgs {
     const uint8_t* meta;   // their GEMM metadata (q4k_meta_kernel)
     const float* scale;    // the drain scale s of every (row, super-block)
     const float* xd;       // Q8_K block scales [nb][m_pad]
-    float* y;              // [tokens][n_out]
+    float* y;              // [tokens][ldy], columns below n_out written
+    int ldy;
     float* ws;             // partial tiles: [grid][2][128 tokens][128 rows]
     int* counters;         // [tiles][8] arrival counters, zero between launches
     unsigned* err;         // device error word

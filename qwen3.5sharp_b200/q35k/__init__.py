@@ -222,6 +222,113 @@ class Weight:
         return sz.value
 
 
+# ---------------------------------------------------------------------------
+# Row-sharded matmul over several GPUs (q35k_shard_*).
+# ---------------------------------------------------------------------------
+
+GATHER_NCCL, GATHER_PEER = _lib.GATHER_NCCL, _lib.GATHER_PEER
+
+
+def shard_rows(n_out: int, nranks: int) -> int:
+    """Rows per rank: an equal share rounded up to the 32-row tile (the C
+    library's rule; the last rank may hold fewer)."""
+    return ((n_out + nranks - 1) // nranks + 31) // 32 * 32
+
+
+def shard_range(n_out: int, nranks: int, rank: int) -> tuple[int, int]:
+    n = shard_rows(n_out, nranks)
+    r0 = min(n_out, rank * n)
+    return r0, min(n_out, r0 + n)
+
+
+def nccl_unique_id() -> bytes:
+    """An NCCL unique id for q35k_shard_create_rank (share it between ranks)."""
+    L = _lib.load()
+    buf = ctypes.create_string_buffer(_lib.NCCL_ID_BYTES)
+    rc = L.q35k_nccl_unique_id(buf)
+    if rc != _lib.OK:
+        _raise(rc, L.q35k_last_error(None).decode())
+    return buf.raw
+
+
+class Shard:
+    """A group of GPUs sharing row-sharded weights.
+
+    Shard(devices=[0, 1, ...]) drives all of them from this process;
+    Shard(nranks=N, rank=r, nccl_id=id, device=d) is this process's rank of a
+    one-process-per-GPU group.
+    """
+
+    def __init__(self, devices=None, *, nranks=None, rank=None, nccl_id=None, device=None):
+        self.L = _lib.load()
+        h = ctypes.c_void_p()
+        if devices is not None:
+            devs = (ctypes.c_int * len(devices))(*devices)
+            rc = self.L.q35k_shard_create(len(devices), devs, ctypes.byref(h))
+        else:
+            idbuf = ctypes.create_string_buffer(nccl_id, _lib.NCCL_ID_BYTES) if nccl_id is not None else None
+            rc = self.L.q35k_shard_create_rank(nranks, rank, idbuf, device, ctypes.byref(h))
+        if rc != _lib.OK:
+            _raise(rc, self.L.q35k_last_error(None).decode())
+        self.h = h
+        n, r0, loc = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        self.L.q35k_shard_info(self.h, ctypes.byref(n), ctypes.byref(r0), ctypes.byref(loc))
+        self.nranks, self.first_rank, self.local_devices = n.value, r0.value, loc.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.q35k_shard_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int):
+        if rc != _lib.OK:
+            _raise(rc, self.L.q35k_shard_last_error(self.h).decode())
+
+    def upload(self, qtype: int, blocks: np.ndarray, n_in: int, n_out: int) -> "ShardedWeight":
+        blocks = _u8(blocks)
+        h = ctypes.c_void_p()
+        self._check(self.L.q35k_shard_weight_upload(self.h, qtype, blocks.ctypes.data, n_in, n_out, ctypes.byref(h)))
+        return ShardedWeight(self, h, qtype, n_in, n_out)
+
+    def matmul(self, w: "ShardedWeight", x: np.ndarray, tokens: int | None = None, gather: int = GATHER_NCCL):
+        x = _f32(x)
+        tokens = tokens if tokens is not None else x.size // w.n_in
+        y = np.empty((tokens, w.n_out), dtype=np.float32)
+        self._check(self.L.q35k_shard_matmul(self.h, w.h, x.ctypes.data, y.ctypes.data, tokens, gather))
+        return y
+
+    def matmul_dev(self, w: "ShardedWeight", d_xs, d_ys, tokens: int, gather: int = GATHER_NCCL):
+        n = len(d_xs)
+        xs = (ctypes.c_void_p * n)(*[_dev_ptr(t) for t in d_xs])
+        ys = (ctypes.c_void_p * n)(*[_dev_ptr(t) for t in d_ys])
+        self._check(self.L.q35k_shard_matmul_dev(self.h, w.h, xs, ys, tokens, gather))
+
+    def sync(self):
+        self._check(self.L.q35k_shard_sync(self.h))
+
+
+class ShardedWeight:
+    def __init__(self, shard: Shard, h, qtype: int, n_in: int, n_out: int):
+        self.shard, self.h, self.qtype, self.n_in, self.n_out = shard, h, qtype, n_in, n_out
+
+    def free(self):
+        if getattr(self, "h", None) and self.shard.h:
+            self.shard.L.q35k_shard_weight_free(self.shard.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 _tls = threading.local()
 
 

@@ -14,6 +14,8 @@ PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "libq35k.so")
 
 OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL = 0, 1, 2, 3, 4, 5, 6
+GATHER_NCCL, GATHER_PEER = 0, 1
+NCCL_ID_BYTES = 128
 
 # Symbols declared in include/q35k.h, with their ctypes signatures.
 _vp, _i32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
@@ -36,6 +38,17 @@ SIGNATURES = {
     "q35k_quantize_q8k_dev": ([_vp, _vp, _vp, _i32, _i32, _vp], _i32),
     "q35k_dequantize": ([_vp, _i32, _vp, _vp, _i32, _i32], _i32),
     "q35k_dequantize_dev": ([_vp, _i32, _vp, _vp, _i32, _i32, _vp], _i32),
+    "q35k_shard_create": ([_i32, ctypes.POINTER(_i32), _pp], _i32),
+    "q35k_nccl_unique_id": ([_vp], _i32),
+    "q35k_shard_create_rank": ([_i32, _i32, _vp, _i32, _pp], _i32),
+    "q35k_shard_destroy": ([_vp], _i32),
+    "q35k_shard_last_error": ([_vp], ctypes.c_char_p),
+    "q35k_shard_info": ([_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32)], _i32),
+    "q35k_shard_sync": ([_vp], _i32),
+    "q35k_shard_weight_upload": ([_vp, _i32, _vp, _i32, _i32, _pp], _i32),
+    "q35k_shard_weight_free": ([_vp, _vp], _i32),
+    "q35k_shard_matmul_dev": ([_vp, _vp, _pp, _pp, _i32, _i32], _i32),
+    "q35k_shard_matmul": ([_vp, _vp, _vp, _vp, _i32, _i32], _i32),
     "q35k_matmul_static_dev": ([_vp, _vp, _vp, _i32, _vp], _i32),
 }
 

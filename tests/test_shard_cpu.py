@@ -1,0 +1,94 @@
+"""Host-side logic of the row-sharded matmul, on CPU.
+
+The row split (q35k.shard_rows / shard_range, the same rule as the C library)
+must cover every output row exactly once on 32-row tile boundaries, and
+gathering the ranks' slices must reassemble the full y.  The exchange is
+exercised with world_size-2 torch.distributed (gloo) ranks, each computing its
+slice with the CPU oracle, as the GPU ranks do with the kernels.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import q35k
+from q35k import synth
+from q35k.synth import Q4_K, Q6_K
+
+
+@pytest.mark.parametrize("nranks", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("n_out", [1, 31, 32, 33, 100, 2560, 9728, 27648, 151936])
+def test_shard_ranges_cover_rows(n_out, nranks):
+    n = q35k.shard_rows(n_out, nranks)
+    assert n % 32 == 0 and n >= 32
+    covered = []
+    for r in range(nranks):
+        r0, r1 = q35k.shard_range(n_out, nranks, r)
+        assert 0 <= r0 <= r1 <= n_out
+        if r1 > r0:
+            assert r0 % 32 == 0  # a non-empty shard starts on a tile boundary
+        assert r1 - r0 <= n
+        covered.extend(range(r0, r1))
+    assert covered == list(range(n_out))
+
+
+def _gather_layout(slices, tokens, n_shard, n_out):
+    """Reassembly of the gathered [rank][tokens][n_shard] slots into y, as the
+    library's gather_permute_kernel does."""
+    g = np.zeros((len(slices), tokens, n_shard), np.float32)
+    for r, sl in enumerate(slices):
+        g[r, :, : sl.shape[1]] = sl
+    y = np.empty((tokens, n_out), np.float32)
+    for c in range(n_out):
+        y[:, c] = g[c // n_shard, :, c % n_shard]
+    return y
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, qt, k, n, m, out_path):
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        w = synth.kquant_blocks(qt, n, k, seed=7)
+        x = synth.activations(m, k, seed=8)
+        r0, r1 = q35k.shard_range(n, world, rank)
+        n_shard = q35k.shard_rows(n, world)
+        mine = np.zeros((m, n_shard), np.float32)
+        if r1 > r0:
+            mine[:, : r1 - r0] = oracle.Weight(qt, w[r0:r1], k, r1 - r0).matmul(x, threads=1)
+        # the exchange: every rank receives every rank's [tokens][n_shard] slot
+        parts = [torch.zeros((m, n_shard)) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(mine))
+        y = _gather_layout([p.numpy() for p in parts], m, n_shard, n)
+        if rank == 0:
+            np.save(out_path, y)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("qt,k,n,m", [(Q4_K, 512, 300, 1), (Q6_K, 768, 129, 3), (Q4_K, 256, 64, 2)])
+def test_gloo_two_ranks_reassemble_full_output(tmp_path, oracle_mod, qt, k, n, m):
+    torch = pytest.importorskip("torch")
+    import torch.multiprocessing as mp
+
+    out = str(tmp_path / "y.npy")
+    port = _free_port()
+    mp.spawn(_rank_main, args=(2, port, qt, k, n, m, out), nprocs=2, join=True)
+    y = np.load(out)
+    w = synth.kquant_blocks(qt, n, k, seed=7)
+    x = synth.activations(m, k, seed=8)
+    ref = oracle_mod.Weight(qt, w, k, n).matmul(x, threads=1)
+    # each row's dot product does not depend on the other rows
+    err = np.abs(y.astype(np.float64) - ref).max() / np.abs(ref).max()
+    assert err <= 1e-6
