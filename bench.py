@@ -202,12 +202,14 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     peaks, peak_kind = load_peaks()
     qt, M, K, N = CFG["qtype"], CFG["m"], CFG["k"], CFG["n"]
-    assert N % world == 0
-    rows = N // world
-    r0 = rank * rows
+    # Rows of this rank: the library's equal-share split (q35k_shard_*).
+    r0, r1 = q35k.shard_range(N, world, rank)
+    rows = r1 - r0
     w = synth.kquant_blocks(qt, rows, K, seed=CFG["seed_w"], row_start=r0)
     x = synth.activations(M, K, seed=CFG["seed_x"])
 
+    # The rank's own slice on a plain context: the GEMV kernel timed alone
+    # (roofline), and the whole step at N = 1.
     ctx = q35k.Context(local)
     W = ctx.upload(qt, w, K, rows)
     # One explicit stream for our kernels, the CUDA events and NCCL.
@@ -215,21 +217,41 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
     dx = torch.from_numpy(x).cuda()
-    dy_full = torch.empty((world, M, rows), dtype=torch.float32, device="cuda")
-    dy_local = torch.empty((M, rows), dtype=torch.float32, device="cuda") if world > 1 else dy_full[0]
+    dy_full = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    dy_local = torch.empty((M, rows), dtype=torch.float32, device="cuda")
+    group = SW = None
+    if world > 1:
+        # One process per GPU: rank 0 makes the NCCL id, torch.distributed
+        # carries it to the others; the library's group does the rest.
+        idt = torch.zeros(q35k._lib.NCCL_ID_BYTES, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(q35k.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(idt, 0)
+        group = q35k.Shard(nranks=world, rank=rank, nccl_id=bytes(idt.cpu().numpy().tobytes()), device=local)
+        # q35k_shard_weight_upload takes the full matrix and keeps this rank's
+        # rows; hand it a view whose rows r0..r1 are this rank's blocks.
+        w_view = np.zeros((N, w.shape[1]), dtype=np.uint8)
+        w_view[r0:r1] = w
+        SW = group.upload(qt, w_view, K, N)
+        del w_view
 
     def step(ev=None):
-        # One pass of the hot path: q35k_matmul_dev (Q8_K quantization of x
-        # fused into the GEMV at M=1), then the all-gather of the logits.
+        # One pass of the hot path: N = 1, q35k_matmul_dev (Q8_K quantization
+        # of x fused into the GEMV at M = 1); N > 1, q35k_shard_matmul_dev (the
+        # rank's GEMV, then the NCCL all-gather of the logits).
         if ev:
             ev[0].record(stream)
-        ctx.matmul_dev(W, dx, dy_local, M, sh)
+        if world == 1:
+            ctx.matmul_dev(W, dx, dy_full, M, sh)
+        else:
+            group.matmul_dev(SW, [dx], [dy_full], M, q35k.GATHER_NCCL, streams=[sh])
         if ev:
             ev[1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(dy_full, dy_local)
-        if ev:
-            ev[2].record(stream)
+
+    def kernel_only(ev):
+        ev[0].record(stream)
+        ctx.matmul_dev(W, dx, dy_local, M, sh)
+        ev[1].record(stream)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -240,7 +262,7 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -252,8 +274,13 @@ def run_ours(args):
     torch.cuda.synchronize()
     clk = clocks.stop()
     total_ms = start.elapsed_time(end)
-    gemv_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    gather_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    # The rank's GEMV kernel timed alone (untimed for the headline).
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        kernel_only(kev[i])
+    torch.cuda.synchronize()
+    gemv_ms = [e[0].elapsed_time(e[1]) for e in kev]
     ms_step = total_ms / args.steps
     if world > 1:
         t = torch.tensor([ms_step], device="cuda")
@@ -279,7 +306,7 @@ def run_ours(args):
                "api": "q35k_matmul (host pointers, synchronous)"}
     else:
         xh = torch.from_numpy(x).pin_memory()
-        yh = torch.empty((world, M, rows), dtype=torch.float32).pin_memory()
+        yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
         for _ in range(3):
             dx.copy_(xh, non_blocking=True)
             step()
@@ -299,7 +326,7 @@ def run_ours(args):
         e2e_ms = float(t.item())
         e2e = {"value": nbytes_total / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
                "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": e2e_ms,
-               "api": "pinned H2D of x + q35k_matmul_dev + NCCL all-gather + D2H of y"}
+               "api": "pinned H2D of x + q35k_shard_matmul_dev (GEMV + NCCL all-gather) + D2H of y"}
 
     gemv_avg = sum(gemv_ms) / len(gemv_ms)
     achieved = nbytes_local / (gemv_avg / 1e3) / 1e9
@@ -334,9 +361,10 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": M,
                        "k": K, "n": N, "rows_per_gpu": rows, "l2": "inputs > L2 (319 MB of weights)",
-                       "parallelism": f"row-sharded N/{world} + NCCL all-gather" if world > 1 else "single GPU"},
+                       "parallelism": (f"row-sharded N/{world} + NCCL all-gather (q35k_shard_matmul_dev)"
+                                       if world > 1 else "single GPU")},
             "frac_of_nominal_8tbs": value / NOMINAL_HBM_GBS,
-            "gemv_ms": gemv_avg, "allgather_ms": sum(gather_ms) / len(gather_ms) if world > 1 else 0.0,
+            "gemv_ms": gemv_avg, "step_ms_events": sum(step_ms) / len(step_ms),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step, "also": extra,
         }
@@ -344,11 +372,14 @@ def run_ours(args):
     W.free()
     ctx.close()
     if world > 1:
+        SW.free()
+        group.close()
         dist.barrier()
         dist.destroy_process_group()
 
 
-OUR_KERNELS = ("gemv_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel")
+OUR_KERNELS = ("gemv_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel",
+               "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel")
 
 
 def count_launches(torch, step):

@@ -129,7 +129,7 @@ int q35k_dequantize_dev(q35k_ctx* ctx, int ggml_type, const void* d_blocks, floa
  * The reference splits output rows between the workers of its CpuThreadPool
  * (Kernels/MulMatQ4K.cs:31-36, Kernels/CpuThreadPool.cs:46-92); here a group
  * of GPUs ("ranks") each holds rows [r * n_shard, (r + 1) * n_shard) of a
- * weight (n_shard = ceil(n_out / ranks) rounded up to 32), computes its slice
+ * weight (n_shard = ceil(n_out / ranks); the last rank may hold fewer), computes its slice
  * of y, and the slices are all-gathered over NVLink so that every rank holds
  * the full y. */
 typedef struct q35k_shard q35k_shard;
@@ -155,9 +155,10 @@ int q35k_shard_weight_upload(q35k_shard* s, int ggml_type, const void* blocks, i
 int q35k_shard_weight_free(q35k_shard* s, q35k_sharded_weight* w);
 /* y = x @ W^T with x replicated on every local device (d_x[i]) and the full
  * y [tokens][n_out] written to every local device (d_y[i]); asynchronous on
- * the contexts' streams (q35k_shard_sync waits). */
+ * streams[i] (cudaStream_t of local device i; NULL array or entry = the
+ * group's own streams, which q35k_shard_sync waits for). */
 int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const float* const* d_x, float* const* d_y,
-                          int tokens, int gather_mode);
+                          int tokens, int gather_mode, void* const* streams);
 /* Host pointers, synchronous: x [tokens][n_in] in, full y out. */
 int q35k_shard_matmul(q35k_shard* s, const q35k_sharded_weight* w, const float* x, float* y, int tokens,
                       int gather_mode);

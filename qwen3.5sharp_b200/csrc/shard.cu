@@ -75,9 +75,10 @@ const NcclApi& nccl() {
     return api;
 }
 
-// Rows per rank: an equal share rounded up to the 32-row tile, so that every
-// rank's rows start on a tile boundary (the last rank may hold fewer).
-int shard_rows(int n_out, int nranks) { return ((n_out + nranks - 1) / nranks + 31) / 32 * 32; }
+// Rows per rank: an equal share (the last rank may hold fewer).  Every rank
+// lays out its own rows in tiles, so a shard may start at any row; when the
+// ranks hold equal shares a single-token y is gathered in place.
+int shard_rows(int n_out, int nranks) { return (n_out + nranks - 1) / nranks; }
 
 // y[t][r * n_shard + j] = g[r][t][j] for the columns below n_out.
 __global__ void gather_permute_kernel(const float* __restrict__ g, float* __restrict__ y, int nranks, int tokens,
@@ -287,8 +288,11 @@ int q35k_shard_weight_free(q35k_shard* s, q35k_sharded_weight* w) {
 }
 
 int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const float* const* d_x, float* const* d_y,
-                          int tokens, int gather_mode) {
+                          int tokens, int gather_mode, void* const* streams) {
     if (!s || !w || !d_x || !d_y || tokens <= 0) return Q35K_EINVAL;
+    auto stream_of = [&](int i) -> cudaStream_t {
+        return (streams && streams[i]) ? static_cast<cudaStream_t>(streams[i]) : s->ctxs[i]->stream;
+    };
     if (gather_mode != Q35K_GATHER_NCCL && gather_mode != Q35K_GATHER_PEER)
         return s->fail(Q35K_EINVAL, "gather_mode must be Q35K_GATHER_NCCL or Q35K_GATHER_PEER");
     const int nloc = (int)s->devices.size();
@@ -323,15 +327,15 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
         if (multi && gather_mode == Q35K_GATHER_PEER) {
             // Peers may still read this buffer from the previous call.
             for (int j = 0; j < nloc; j++)
-                if (j != i && s->used[j]) cudaStreamWaitEvent(c->stream, s->free_ev[j], 0);
+                if (j != i && s->used[j]) cudaStreamWaitEvent(stream_of(i), s->free_ev[j], 0);
         }
         if (w->parts[i]) {
             // Slot layout [tokens][n_shard]; this rank's rows fill the first
             // columns (the last rank may hold fewer).
-            const int rc = c->matmul_into(w->parts[i], d_x[i], mine, w->n_shard, tokens, c->stream);
+            const int rc = c->matmul_into(w->parts[i], d_x[i], mine, w->n_shard, tokens, stream_of(i));
             if (rc != Q35K_OK) return s->fail(rc, c->err);
         } else {
-            cudaMemsetAsync(mine, 0, slot * sizeof(float), c->stream);
+            cudaMemsetAsync(mine, 0, slot * sizeof(float), stream_of(i));
         }
     }
     if (multi) {
@@ -342,7 +346,7 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
                 cudaSetDevice(s->devices[i]);
                 float* g = direct ? d_y[i] : s->gbuf[i];
                 const ncclResult_t r = n.AllGather(g + (size_t)(s->first_rank + i) * slot, g, slot, ncclFloat32,
-                                                   s->comms[i], s->ctxs[i]->stream);
+                                                   s->comms[i], stream_of(i));
                 if (r != ncclSuccess) {
                     n.GroupEnd();
                     return s->nccl_fail(r, "ncclAllGather");
@@ -360,15 +364,15 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
                     if (j == i) continue;
                     float* dst = (direct ? d_y[j] : s->gbuf[j]) + (size_t)i * slot;
                     const cudaError_t e = cudaMemcpyPeerAsync(dst, s->devices[j], src, s->devices[i],
-                                                              slot * sizeof(float), s->ctxs[i]->stream);
+                                                              slot * sizeof(float), stream_of(i));
                     if (e != cudaSuccess) return s->fail(Q35K_ECUDA, std::string("peer copy: ") + cudaGetErrorString(e));
                 }
-                cudaEventRecord(s->done[i], s->ctxs[i]->stream);
+                cudaEventRecord(s->done[i], stream_of(i));
             }
             for (int j = 0; j < nloc; j++) {
                 cudaSetDevice(s->devices[j]);
                 for (int i = 0; i < nloc; i++)
-                    if (i != j) cudaStreamWaitEvent(s->ctxs[j]->stream, s->done[i], 0);
+                    if (i != j) cudaStreamWaitEvent(stream_of(j), s->done[i], 0);
             }
         }
     }
@@ -377,7 +381,7 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
             cudaSetDevice(s->devices[i]);
             const long long total = (long long)tokens * w->n_out;
             const int grid = (int)std::min<long long>((total + 255) / 256, 4096);
-            gather_permute_kernel<<<grid, 256, 0, s->ctxs[i]->stream>>>(s->gbuf[i], d_y[i], s->nranks, tokens,
+            gather_permute_kernel<<<grid, 256, 0, stream_of(i)>>>(s->gbuf[i], d_y[i], s->nranks, tokens,
                                                                        w->n_shard, w->n_out);
             const cudaError_t e = cudaGetLastError();
             if (e != cudaSuccess) return s->fail(Q35K_ECUDA, std::string("gather permute: ") + cudaGetErrorString(e));
@@ -386,7 +390,7 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
     if (multi && gather_mode == Q35K_GATHER_PEER) {
         for (int i = 0; i < nloc; i++) {
             cudaSetDevice(s->devices[i]);
-            cudaEventRecord(s->free_ev[i], s->ctxs[i]->stream);
+            cudaEventRecord(s->free_ev[i], stream_of(i));
             s->used[i] = 1;
         }
     }
@@ -430,7 +434,7 @@ int q35k_shard_matmul(q35k_shard* s, const q35k_sharded_weight* w, const float* 
         if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return s->fail(rc, c->err);
         dy[i] = c->d_y;
     }
-    int rc = q35k_shard_matmul_dev(s, w, dx.data(), dy.data(), tokens, gather_mode);
+    int rc = q35k_shard_matmul_dev(s, w, dx.data(), dy.data(), tokens, gather_mode, nullptr);
     if (rc != Q35K_OK) return rc;
     q35k_ctx* c0 = s->ctxs[0];
     cudaSetDevice(s->devices[0]);

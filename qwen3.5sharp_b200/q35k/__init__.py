@@ -230,9 +230,9 @@ GATHER_NCCL, GATHER_PEER = _lib.GATHER_NCCL, _lib.GATHER_PEER
 
 
 def shard_rows(n_out: int, nranks: int) -> int:
-    """Rows per rank: an equal share rounded up to the 32-row tile (the C
-    library's rule; the last rank may hold fewer)."""
-    return ((n_out + nranks - 1) // nranks + 31) // 32 * 32
+    """Rows per rank: an equal share (the C library's rule; the last rank may
+    hold fewer)."""
+    return (n_out + nranks - 1) // nranks
 
 
 def shard_range(n_out: int, nranks: int, rank: int) -> tuple[int, int]:
@@ -303,11 +303,16 @@ class Shard:
         self._check(self.L.q35k_shard_matmul(self.h, w.h, x.ctypes.data, y.ctypes.data, tokens, gather))
         return y
 
-    def matmul_dev(self, w: "ShardedWeight", d_xs, d_ys, tokens: int, gather: int = GATHER_NCCL):
+    def matmul_dev(self, w: "ShardedWeight", d_xs, d_ys, tokens: int, gather: int = GATHER_NCCL, streams=None):
+        """streams: one cudaStream_t (int or torch stream) per local device,
+        or None for the group's own streams."""
         n = len(d_xs)
         xs = (ctypes.c_void_p * n)(*[_dev_ptr(t) for t in d_xs])
         ys = (ctypes.c_void_p * n)(*[_dev_ptr(t) for t in d_ys])
-        self._check(self.L.q35k_shard_matmul_dev(self.h, w.h, xs, ys, tokens, gather))
+        ss = None
+        if streams is not None:
+            ss = (ctypes.c_void_p * n)(*[getattr(t, "cuda_stream", t) for t in streams])
+        self._check(self.L.q35k_shard_matmul_dev(self.h, w.h, xs, ys, tokens, gather, ss))
 
     def sync(self):
         self._check(self.L.q35k_shard_sync(self.h))

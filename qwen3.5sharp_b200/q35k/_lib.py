@@ -47,7 +47,7 @@ SIGNATURES = {
     "q35k_shard_sync": ([_vp], _i32),
     "q35k_shard_weight_upload": ([_vp, _i32, _vp, _i32, _i32, _pp], _i32),
     "q35k_shard_weight_free": ([_vp, _vp], _i32),
-    "q35k_shard_matmul_dev": ([_vp, _vp, _pp, _pp, _i32, _i32], _i32),
+    "q35k_shard_matmul_dev": ([_vp, _vp, _pp, _pp, _i32, _i32, _pp], _i32),
     "q35k_shard_matmul": ([_vp, _vp, _vp, _vp, _i32, _i32], _i32),
     "q35k_matmul_static_dev": ([_vp, _vp, _vp, _i32, _vp], _i32),
 }

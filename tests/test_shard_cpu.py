@@ -22,13 +22,11 @@ from q35k.synth import Q4_K, Q6_K
 @pytest.mark.parametrize("n_out", [1, 31, 32, 33, 100, 2560, 9728, 27648, 151936])
 def test_shard_ranges_cover_rows(n_out, nranks):
     n = q35k.shard_rows(n_out, nranks)
-    assert n % 32 == 0 and n >= 32
+    assert n * nranks >= n_out and (n - 1) * nranks < n_out  # an equal share
     covered = []
     for r in range(nranks):
         r0, r1 = q35k.shard_range(n_out, nranks, r)
         assert 0 <= r0 <= r1 <= n_out
-        if r1 > r0:
-            assert r0 % 32 == 0  # a non-empty shard starts on a tile boundary
         assert r1 - r0 <= n
         covered.extend(range(r0, r1))
     assert covered == list(range(n_out))
