@@ -492,6 +492,39 @@ def gemm_configs(ctx, torch, synth, peaks):
     return out
 
 
+# Configurations runnable alone under a profiler: (qtype, M, K, N, x scale).
+PROFILE_CASES = {
+    "cfg0_q4k_m1": (12, 1, 2560, 9728, 1.0),
+    "cfg1_q6k_m1": (14, 1, 2560, 151936, 1.0),
+    "cfg2_q5k_m8": (13, 8, 9728, 2560, 0.5),
+    "cfg3_q4k_gemm_m512": (12, 512, 2560, 9728, 1.0),
+    "cfg3_q4k_gemm_m64": (12, 64, 2560, 9728, 1.0),
+    "cfg4_q4k_m8_p1": (12, 8, 5120, 27648, 1.0),
+    "cfg4_q4k_gemm_m512_p1": (12, 512, 5120, 27648, 1.0),
+}
+
+
+def run_profile_case(args):
+    """Upload one configuration's weight and run --steps q35k_matmul_dev
+    calls (device pointers, the context's stream), then synchronize: a small,
+    self-contained command for ncu captures."""
+    import torch
+
+    import q35k
+    from q35k import synth
+
+    qt, m, k, n, scale = PROFILE_CASES[args.profile]
+    ctx = q35k.Context(0)
+    W = ctx.upload(qt, synth.kquant_blocks(qt, n, k, seed=1), k, n)
+    dx = torch.from_numpy(synth.activations(m, k, seed=2, scale=scale)).cuda()
+    dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    for _ in range(args.steps):
+        ctx.matmul_dev(W, dx, dy, m, None)
+    ctx.sync()
+    W.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -500,7 +533,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary configs")
+    ap.add_argument("--profile", choices=sorted(PROFILE_CASES),
+                    help="only run --steps q35k_matmul_dev calls of one configuration (for ncu), no timing output")
     args = ap.parse_args()
+    if args.profile:
+        run_profile_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
