@@ -111,6 +111,18 @@ int q35k_matmul_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_x, float
 int q35k_matmul_q8k_dev(q35k_ctx* ctx, const q35k_weight* w, const void* d_q8k, float* d_y, int tokens,
                         void* stream);
 
+/* Arithmetic of the tensor-core prefill GEMM (Q4_K, tokens >= 16).  No
+ * counterpart in the reference, which has one arithmetic:
+ *   Q35K_GEMM_EXACT (default): the reference's -- Q8_K activations, exact
+ *     integer dots per super-block, fp32 scaling per super-block (results
+ *     within fp32 rounding of the reference's);
+ *   Q35K_GEMM_FAST: fp16-rounded dequantized weights times fp16-rounded
+ *     dequantized Q8_K activations, one fp32 accumulator per tile (about
+ *     4e-4 of max |y| from the reference's results); faster. */
+#define Q35K_GEMM_EXACT 0
+#define Q35K_GEMM_FAST 1
+int q35k_set_gemm_mode(q35k_ctx* ctx, int mode);
+
 /* ---- Utilities ---------------------------------------------------------- */
 
 /* Q8K.QuantizeRow (Kernels/Q8K.cs:12-77) on `rows` rows of k floats:

@@ -150,6 +150,7 @@ int q35k_create(int device, q35k_ctx** out) {
         return Q35K_ECUDA;
     }
     if (const char* v = getenv("Q35K_GEMM_MIN_TOKENS")) c->gemm_min_tokens = std::max(1, atoi(v));
+    if (const char* v = getenv("Q35K_GEMM_MODE")) c->gemm_mode = (strcmp(v, "fast") == 0) ? Q35K_GEMM_FAST : Q35K_GEMM_EXACT;
     if ((e = cudaGetLastError()) != cudaSuccess) {
         g_create_error = std::string("kernel configuration: ") + cudaGetErrorString(e);
         delete c;
@@ -170,6 +171,13 @@ int q35k_destroy(q35k_ctx* c) {
 const char* q35k_last_error(const q35k_ctx* c) {
     if (!c) return g_create_error.c_str();
     return c->err.c_str();
+}
+
+int q35k_set_gemm_mode(q35k_ctx* c, int mode) {
+    if (!c) return Q35K_EINVAL;
+    if (mode != Q35K_GEMM_EXACT && mode != Q35K_GEMM_FAST) return c->fail(Q35K_EINVAL, "unknown GEMM mode %d", mode);
+    c->gemm_mode = mode;
+    return Q35K_OK;
 }
 
 int q35k_sync(q35k_ctx* c) {
@@ -307,7 +315,8 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     if ((rc = ensure_dev((void**)&d_xd, &xd_cap, p.xd_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gws, &gws_cap, p.ws_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gcnt, &gcnt_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
-    cudaError_t e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, s);
+    const bool fast = gemm_mode == Q35K_GEMM_FAST;
+    cudaError_t e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, fast, s);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
     TcGemmArgs a{};
     a.tiles = w->tiles;
@@ -327,7 +336,7 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     a.tiles_t = p.tiles_t;
     a.grid = p.grid;
     a.units = p.units;
-    e = launch_tc_gemm(a, d_xq, d_xe, w->n_in, s, true);
+    e = launch_tc_gemm(a, d_xq, d_xe, w->n_in, fast, s, true);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
     return Q35K_OK;
 }

@@ -52,6 +52,9 @@ struct q35k_ctx {
     // Q4_K calls with at least this many tokens run on the tensor cores
     // (environment variable Q35K_GEMM_MIN_TOKENS overrides it at creation).
     int gemm_min_tokens = 16;
+    // Q35K_GEMM_EXACT (default) or Q35K_GEMM_FAST (environment variable
+    // Q35K_GEMM_MODE=fast at creation, or q35k_set_gemm_mode).
+    int gemm_mode = 0;
 
     // Pinned host staging for the synchronous host-pointer calls.
     void* h_in = nullptr;

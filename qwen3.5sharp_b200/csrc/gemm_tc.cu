@@ -62,16 +62,26 @@ namespace q35k {
 namespace tcg {
 
 constexpr int TM = 128;  // weight rows per tile
-constexpr int Q4K_META_TILE = 3 * 512;  // GEMM metadata of one 32-row tile
+constexpr int Q4K_META_TILE = 5 * 512;  // GEMM metadata of one 32-row tile
 constexpr int TN = 128;  // tokens per tile
 // Five warpgroups of four warps; each warpgroup re-sizes its registers with
 // setmaxnreg.  Registers are split between an SM's four sub-partitions, one
 // warp of every warpgroup in each: 5 x 32 x 96 = 15360 <= 16384 at launch,
-// and afterwards 128 x (32 + 72 + 72 + 152 + 152) = 61440 <= 640 x 96.
+// and afterwards 128 x (ctrl + 2 prod + 2 drain) = 61440 = 640 x 96.  The
+// exact mode's drain holds more state (per-super-block scaling), the fast
+// mode's producers more (the fp16 dequantization): each split is the one
+// ptxas fits without spills.
 constexpr int THREADS = 640;
 constexpr int LAUNCH_REGS = 96;
-constexpr int REGS_CTRL = 32, REGS_PROD = 72, REGS_DRAIN = 152;
-constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_WTMA = 2, WARP_PROD0 = 4, WARP_DRAIN0 = 12, NUM_DRAIN = 8;
+template <bool FAST> struct RegSplit {
+    static constexpr int CTRL = 32, PROD = FAST ? 80 : 72, DRAIN = FAST ? 144 : 152;
+    static_assert(CTRL + 2 * PROD + 2 * DRAIN == 5 * LAUNCH_REGS, "split must use the launch registers exactly");
+};
+// Activation halves h = 0, 1 of every unit are loaded by warps WARP_TMA and
+// WARP_TMA2: a warp that issues a TMA copy and then touches shared memory
+// (its next barrier wait) stalls until that copy has landed, so one loader
+// warp keeps one stage in flight at a time and two loaders double the rate.
+constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_WTMA = 2, WARP_TMA2 = 3, WARP_PROD0 = 4, WARP_DRAIN0 = 12, NUM_DRAIN = 8;
 // Activation ring: half super-blocks (128 K x 128 tokens fp16 = two
 // 128-byte-swizzled boxes of 64 K), released by the MMA.
 constexpr int X_STAGES = 3;
@@ -86,7 +96,7 @@ constexpr int EXT_BOX_BYTES = 16 * 2 * TN;         // 4096
 constexpr int W_EXT_OFF = 0;                       // 1024-aligned (swizzled TMA destination)
 constexpr int W_TILE_OFF = EXT_BOX_BYTES;
 constexpr int W_META_OFF = W_TILE_OFF + 4 * Q4K_TILE;
-constexpr int W_STAGE_BYTES = W_META_OFF + 4 * Q4K_META_TILE;  // 28672 (28 KB)
+constexpr int W_STAGE_BYTES = W_META_OFF + 4 * Q4K_META_TILE;  // 32768 (32 KB)
 static_assert(W_STAGE_BYTES % 1024 == 0, "weight stage alignment");
 // Drain ring, one stage per unit: the drain scales s of the 128 rows and the
 // 128 token scales d8.  Released by the drains.
@@ -121,6 +131,7 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 // (token, super-block).  Xq holds each aligned group of four K values in the
 // order 0, 2, 1, 3; the MMA's K order only has to agree between its operands.
 // ---------------------------------------------------------------------------
+template <bool FAST>
 __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, int k, int tokens, int m_pad,
                                                        __half* __restrict__ xq, __half* __restrict__ xe,
                                                        float* __restrict__ xd) {
@@ -131,18 +142,20 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     if (w >= m_pad * nb) return;
     const int r = w / nb, b = w % nb;
     if (r >= tokens) {
-        if (lane == 0) xd[(size_t)b * m_pad + r] = 0.f;
+        if (!FAST && lane == 0) xd[(size_t)b * m_pad + r] = 0.f;
         return;
     }
     int q[8];
     const float d = warp_q8k_values(x + (size_t)r * k + (size_t)b * QK, lane, q);
     __half* row = xq + (size_t)r * k + (size_t)b * QK;
-    // K order within each group of four values: 0, 2, 1, 3 (the order in
-    // which the weight producers pair nibbles; see the decode in the GEMM).
-    const __half2 p0 = __halves2half2(__int2half_rn(q[0]), __int2half_rn(q[2]));
-    const __half2 p1 = __halves2half2(__int2half_rn(q[1]), __int2half_rn(q[3]));
-    const __half2 p2 = __halves2half2(__int2half_rn(q[4]), __int2half_rn(q[6]));
-    const __half2 p3 = __halves2half2(__int2half_rn(q[5]), __int2half_rn(q[7]));
+    // Exact mode: the q values; fast mode: fp16(d q), the dequantized Q8_K
+    // activations.  K order within each group of four values: 0, 2, 1, 3 (the
+    // order in which the weight producers pair nibbles; see the decode).
+    auto hv = [&](int i) { return FAST ? __float2half_rn(d * (float)q[i]) : __int2half_rn(q[i]); };
+    const __half2 p0 = __halves2half2(hv(0), hv(2));
+    const __half2 p1 = __halves2half2(hv(1), hv(3));
+    const __half2 p2 = __halves2half2(hv(4), hv(6));
+    const __half2 p3 = __halves2half2(hv(5), hv(7));
     uint2 v0, v1;
     v0.x = *reinterpret_cast<const uint32_t*>(&p0);
     v0.y = *reinterpret_cast<const uint32_t*>(&p1);
@@ -150,6 +163,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     v1.y = *reinterpret_cast<const uint32_t*>(&p3);
     reinterpret_cast<uint2*>(row)[lane] = v0;        // values 4l..4l+3
     reinterpret_cast<uint2*>(row + 128)[lane] = v1;  // values 128+4l..
+    if (FAST) return;
     int s0, s1;
     warp_q8k_bsums(q, s0, s1);
     if ((lane & 3) == 0) {
@@ -225,6 +239,11 @@ __device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t 
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
+__device__ __forceinline__ uint32_t hadd2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
@@ -248,6 +267,25 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, unsigne
             }
         }
     }
+}
+// Non-blocking test of two barrier phases in one go: both tests issue back
+// to back and the thread waits once for the pair (a barrier test takes ~100
+// cycles under load, and every cycle the MMA thread spends waiting is a
+// bubble in the tensor pipe).
+__device__ __forceinline__ bool test2(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred q0, q1;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q0, [%1], %2;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q1, [%3], %4;\n"
+        "and.pred q0, q0, q1;\n"
+        "selp.u32 %0, 1, 0, q0;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b0)), "r"(p0), "r"(smem_u32(b1)), "r"(p1)
+        : "memory");
+    return ok != 0;
 }
 // Wait for work already in flight (ignores the abort flag, still bounded).
 __device__ __forceinline__ void wait_inflight(uint64_t* bar, uint32_t parity, unsigned* err) {
@@ -306,6 +344,8 @@ __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
 //   chunk 0: fp16 alpha * sc_j, j = 0..7        (the A operand's sub-block scales)
 //   chunk 1: fp16 high part of -beta * m_j, j = 0..7
 //   chunk 2: fp16 low part of -beta * m_j
+//   chunk 3: fp16 d * sc_j                       (fast mode: the dequantized weight
+//   chunk 4: fp16 dmin * m_j                      q * (d sc_j) - dmin m_j in fp16)
 // and the drain's fp32 s of each row in s[(g nb + b) 32 + r] (q4k_block_scale).
 // One thread per (row, super-block).
 // ---------------------------------------------------------------------------
@@ -318,10 +358,11 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
     const size_t tile = (size_t)g * nb + b;
     const uint4 hdr = *reinterpret_cast<const uint4*>(tiles + tile * tcg::Q4K_TILE + r * 16);
     const BlockScale bs = q4k_block_scale(hdr.x);
-    uint32_t sa[4], hi[4], lo[4];
+    const float d = fp16_bits_to_float(hdr.x), dm = fp16_bits_to_float(hdr.x >> 16);
+    uint32_t sa[4], hi[4], lo[4], fs[4], fm[4];
 #pragma unroll
     for (int j = 0; j < 8; j += 2) {
-        uint16_t a2[2], h2[2], l2[2];
+        uint16_t a2[2], h2[2], l2[2], s2[2], m2[2];
 #pragma unroll
         for (int t = 0; t < 2; t++) {
             int sc, m;
@@ -331,18 +372,25 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
             const __half h = __float2half_rn(v);
             h2[t] = __half_as_ushort(h);
             l2[t] = __half_as_ushort(__float2half_rn(v - __half2float(h)));
+            s2[t] = __half_as_ushort(__float2half_rn(d * (float)sc));
+            m2[t] = __half_as_ushort(__float2half_rn(dm * (float)m));
         }
         sa[j / 2] = a2[0] | ((uint32_t)a2[1] << 16);
         hi[j / 2] = h2[0] | ((uint32_t)h2[1] << 16);
         lo[j / 2] = l2[0] | ((uint32_t)l2[1] << 16);
+        fs[j / 2] = s2[0] | ((uint32_t)s2[1] << 16);
+        fm[j / 2] = m2[0] | ((uint32_t)m2[1] << 16);
     }
     uint8_t* mt = meta + tile * tcg::Q4K_META_TILE + r * 16;
     *reinterpret_cast<uint4*>(mt) = make_uint4(sa[0], sa[1], sa[2], sa[3]);
     *reinterpret_cast<uint4*>(mt + 512) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint4*>(mt + 1024) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(mt + 1536) = make_uint4(fs[0], fs[1], fs[2], fs[3]);
+    *reinterpret_cast<uint4*>(mt + 2048) = make_uint4(fm[0], fm[1], fm[2], fm[3]);
     s_out[tile * 32 + r] = bs.s;
 }
 
+template <bool FAST>
 __global__ void __launch_bounds__(tcg::THREADS, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_e,
                        const TcGemmArgs a) {
@@ -354,11 +402,16 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     uint8_t* ering = wring + W_RING_BYTES;
     uint8_t* dring = ering + E_RING_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(dring + D_RING_BYTES);
-    uint64_t* x_full = bars;                      // [X_STAGES] activation half stage landed
-    uint64_t* x_empty = x_full + X_STAGES;        // [X_STAGES] its MMAs completed
-    uint64_t* w_full = x_empty + X_STAGES;        // [W_STAGES] weight tiles + metadata landed
+    // x_full[h][slot] counts the fills of loader h only: fill f of slot f % 3
+    // uses x_full[f & 1][f % 3], phase f / 6, so a barrier's next phase is
+    // always the same loader's next fill.
+    // An activation stage is free once the MMAs of its fill completed, which
+    // the A buffer's barrier of the same fill already tracks (a_empty): the
+    // MMA issues one commit per half super-block.
+    uint64_t* x_full = bars;                      // [2][X_STAGES] activation half stage landed
+    uint64_t* w_full = x_full + 2 * X_STAGES;     // [W_STAGES] weight tiles + metadata landed
     uint64_t* e_full = w_full + W_STAGES;         // [W_STAGES] Xe landed
-    uint64_t* w_empty = e_full + W_STAGES;        // [W_STAGES] producers read it, its MMAs completed
+    uint64_t* w_empty = e_full + W_STAGES;        // [W_STAGES] producers read it (exact: and its MMAs completed)
     uint64_t* d_full = w_empty + W_STAGES;        // [D_STAGES] drain scales landed
     uint64_t* d_empty = d_full + D_STAGES;        // [D_STAGES] drains done with them
     uint64_t* a_full = d_empty + D_STAGES;        // [A_BUFS] A operand written (TMEM + min tile)
@@ -381,12 +434,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < X_STAGES; i++) {
             mbar_init(x_full + i, 1);
-            mbar_init(x_empty + i, 1);
+            mbar_init(x_full + X_STAGES + i, 1);
         }
         for (int i = 0; i < W_STAGES; i++) {
             mbar_init(w_full + i, 1);
             mbar_init(e_full + i, 1);
-            mbar_init(w_empty + i, 9);  // 8 producer warps + the MMA's commit
+            // 8 producer warps (+ the MMA's commit in exact mode, whose
+            // min-term MMA reads the stage's Xe tile)
+            mbar_init(w_empty + i, FAST ? 8 : 9);
         }
         for (int i = 0; i < D_STAGES; i++) {
             mbar_init(d_full + i, 1);
@@ -415,27 +470,37 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 
     const int wg = warp >> 2;
     if (wg == 0) {
-        setmaxnreg_dec<REGS_CTRL>();
-        if (warp == WARP_TMA && lane == 0) {
+        setmaxnreg_dec<RegSplit<FAST>::CTRL>();
+        if ((warp == WARP_TMA || warp == WARP_TMA2) && lane == 0) {
             // ---------------- activation halves ----------------
+            // This warp loads half h of every unit: fills f = 2 i + h.
             griddep_wait();  // Xq comes from the preparation kernel
-            const int n = 2 * n_units;
-            int issued = 0;
+            const int h = warp == WARP_TMA ? 0 : 1;
+            int issued = -1;
             UnitPos p;
             p.init(u0, nb, a.tiles_t);
-            for (int f = 0; f < n; f++) {
-                if (f > 0 && (f & 1) == 0) p.next(nb, a.tiles_t);
+            for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
+                const int f = 2 * i + h;
                 const int xs = f % X_STAGES;
-                if (!wait_bar(x_empty + xs, ((uint32_t)(f / X_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
-                mbar_arrive_expect_tx(x_full + xs, X_STAGE_BYTES);
+                if (f >= X_STAGES) {  // the slot's previous fill g = f - 3 was consumed
+                    const int g = f - X_STAGES;
+                    const int gab = 2 * ((g >> 1) & 1) + (g & 1);
+                    if (!wait_bar(a_empty + gab, (uint32_t)(g >> 2) & 1u, a.err, abort_flag)) break;
+                }
+                uint64_t* full = x_full + h * X_STAGES + xs;
+                mbar_arrive_expect_tx(full, X_STAGE_BYTES);
                 uint8_t* dst = xring + xs * X_STAGE_BYTES;
-                const int k0 = p.b * QK + 128 * (f & 1);
-                tma_load_2d(dst, &tm_q, k0, p.tt * TN, x_full + xs);
-                tma_load_2d(dst + X_BOX_BYTES, &tm_q, k0 + 64, p.tt * TN, x_full + xs);
-                issued = f + 1;
+                const int k0 = p.b * QK + 128 * h;
+                tma_load_2d(dst, &tm_q, k0, p.tt * TN, full);
+                tma_load_2d(dst + X_BOX_BYTES, &tm_q, k0 + 64, p.tt * TN, full);
+                issued = f;
             }
-            for (int f = (issued > X_STAGES ? issued - X_STAGES : 0); f < issued; f++)
-                wait_inflight(x_full + (f % X_STAGES), (uint32_t)(f / X_STAGES) & 1u, a.err);
+            // Every copy this warp issued lands before the CTA exits.  Fill
+            // f - 3 (the other loader's) was consumed before fill f was
+            // issued, so only this warp's last two fills can be in flight.
+            for (int f = issued - 2; f <= issued; f += 2)
+                if (f >= 0)
+                    wait_inflight(x_full + h * X_STAGES + (f % X_STAGES), (uint32_t)(f / (2 * X_STAGES)) & 1u, a.err);
         } else if (warp == WARP_WTMA && lane == 0) {
             // ---------------- weight tiles, metadata, Xe; drain scales ----------------
             bool dep_done = false;
@@ -456,13 +521,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                     bulk_g2s(dst + W_META_OFF + q * Q4K_META_TILE, a.meta + tile * Q4K_META_TILE, Q4K_META_TILE,
                              w_full + ws);
                 }
+                issued_w = i + 1;
+                if constexpr (FAST) continue;  // no min term, no per-super-block scales
                 if (!dep_done) {
                     griddep_wait();  // Xe and d8 come from the preparation kernel
                     dep_done = true;
                 }
                 mbar_arrive_expect_tx(e_full + ws, EXT_BOX_BYTES);
                 tma_load_2d(dst + W_EXT_OFF, &tm_e, b * 16, tt * TN, e_full + ws);
-                issued_w = i + 1;
                 const int ds = i % D_STAGES;
                 if (!wait_bar(d_empty + ds, ((uint32_t)(i / D_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
                 uint8_t* dd = dring + ds * D_STAGE_BYTES;
@@ -474,53 +540,85 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             for (int i = (issued_w > W_STAGES ? issued_w - W_STAGES : 0); i < issued_w; i++) {
                 wait_inflight(w_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
-                wait_inflight(e_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
+                if (!FAST) wait_inflight(e_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
             }
             for (int i = (issued_d > D_STAGES ? issued_d - D_STAGES : 0); i < issued_d; i++)
                 wait_inflight(d_full + (i % D_STAGES), (uint32_t)(i / D_STAGES) & 1u, a.err);
         } else if (warp == WARP_MMA && lane == 0) {
             // ---------------- MMA issue ----------------
+            // Exact mode: one accumulator per unit (drained per super-block).
+            // Fast mode: one accumulator per tile segment (the run of units of
+            // one tile this CTA computes), drained once.
             const uint32_t idesc = tc_idesc_f16_f32(TM, TN);
-            for (int i = 0; i < n_units; i++) {
-                const int accb = i & 1;
+            // Inputs of fill f = 2 i + h: activation stage x_full[h][f % 3]
+            // (phase f / 6) and A buffer 2 (i & 1) + h (phase i / 2).
+            auto x_bar = [&](int f) { return x_full + (f & 1) * X_STAGES + f % X_STAGES; };
+            auto x_par = [&](int f) { return (uint32_t)(f / (2 * X_STAGES)) & 1u; };
+            auto a_bar = [&](int f) { return a_full + 2 * ((f >> 1) & 1) + (f & 1); };
+            auto a_par = [&](int f) { return (uint32_t)(f >> 2) & 1u; };
+            UnitPos p;
+            p.init(u0, nb, a.tiles_t);
+            int seg = 0;
+            // The next half's inputs are tested (without blocking) in the middle
+            // of the current half's MMAs; the thread blocks on them only when
+            // they had not landed by then.
+            bool ready = false;
+            const int n_fills = 2 * n_units;
+            for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
+                const bool seg_start = (i == 0 || p.b == 0), seg_end = (p.b == nb - 1 || i == n_units - 1);
+                const int acc_i = FAST ? seg : i;  // accumulator use
+                const int accb = acc_i & 1;
                 const int ws = i % W_STAGES;
-                if (!wait_bar(acc_empty + accb, ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err, abort_flag)) break;
-                if (!wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
+                if ((!FAST || seg_start) &&
+                    !wait_bar(acc_empty + accb, ((uint32_t)(acc_i >> 1) & 1u) ^ 1u, a.err, abort_flag))
+                    break;
+                if (!FAST && !wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
                 const uint32_t d_tmem = tmem + (uint32_t)(accb * TN);
-                const uint64_t bext = tc_smem_desc(smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF), 256, 6);
                 bool ok = true;
                 for (int h = 0; h < 2; h++) {
                     const int f = 2 * i + h;
-                    const int xs = f % X_STAGES;
-                    const int ab = 2 * (i & 1) + h;
-                    if (!wait_bar(x_full + xs, (uint32_t)(f / X_STAGES) & 1u, a.err, abort_flag) ||
-                        !wait_bar(a_full + ab, (uint32_t)(i >> 1) & 1u, a.err, abort_flag)) {
+                    if (!ready && !test2(x_bar(f), x_par(f), a_bar(f), a_par(f)) &&
+                        !(wait_bar(x_bar(f), x_par(f), a.err, abort_flag) &&
+                          wait_bar(a_bar(f), a_par(f), a.err, abort_flag))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t x_addr = smem_u32(xring + xs * X_STAGE_BYTES);
+                    const int xs = f % X_STAGES;
+                    const int ab = 2 * (i & 1) + h;
+                    // One descriptor per half; each 16-value K step is a
+                    // constant offset of its start address (16-byte units).
+                    const uint64_t xdesc = tc_smem_desc(smem_u32(xring + xs * X_STAGE_BYTES), 1024, 2);
                     const uint32_t a_tmem = tmem + (uint32_t)(A_COL0 + 64 * ab);
+                    const bool fresh = FAST ? (seg_start && h == 0) : (h == 0);
+                    tc_mma_f16_ts(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u);
 #pragma unroll
-                    for (int t = 0; t < 8; t++) {  // 16-value K steps of the half
-                        const uint64_t desc = tc_smem_desc(x_addr + (t >> 2) * X_BOX_BYTES + (t & 3) * 32, 1024, 2);
-                        tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, desc, idesc, (h | t) != 0 ? 1u : 0u);
+                    for (int t = 1; t < 4; t++)  // 16-value K steps of the half
+                        tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, xdesc + (uint64_t)((t * 32) >> 4), idesc, 1u);
+                    ready = f + 1 < n_fills && test2(x_bar(f + 1), x_par(f + 1), a_bar(f + 1), a_par(f + 1));
+#pragma unroll
+                    for (int t = 4; t < 8; t++)
+                        tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, xdesc + (uint64_t)((X_BOX_BYTES + (t - 4) * 32) >> 4),
+                                      idesc, 1u);
+                    if constexpr (!FAST) {
+                        // the min term: 16 K from shared memory (A) against Xe
+                        const uint64_t bext = tc_smem_desc(smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF), 256, 6);
+                        tc_mma_f16_ss(d_tmem, tc_smem_desc(smem_u32(ering + ab * E_TILE_BYTES), 256, 6), bext, idesc,
+                                      1u);
                     }
-                    // the min term: 16 K from shared memory (A) against Xe
-                    tc_mma_f16_ss(d_tmem, tc_smem_desc(smem_u32(ering + ab * E_TILE_BYTES), 256, 6), bext, idesc, 1u);
-                    tc_commit(a_empty + ab);
-                    tc_commit(x_empty + xs);
+                    tc_commit(a_empty + ab);  // frees the A buffer and the activation stage
                 }
                 if (!ok) break;
-                tc_commit(w_empty + ws);
-                tc_commit(acc_full + accb);
+                if (!FAST) tc_commit(w_empty + ws);
+                if (!FAST || seg_end) tc_commit(acc_full + accb);
+                if (seg_end) seg++;
             }
             // Every MMA issued by this thread completes before TMEM is freed.
             tc_commit(mma_done);
             wait_inflight(mma_done, 0, a.err);
         }
     } else if (warp < WARP_DRAIN0) {
-        setmaxnreg_dec<REGS_PROD>();
+        setmaxnreg_dec<RegSplit<FAST>::PROD>();
         // ---------------- weight producers ----------------
         // Group h (4 warps, one per TMEM lane quadrant q) builds the A
         // operand of half h of every super-block: the 64 value columns of
@@ -542,8 +640,9 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             const uint8_t* mt = stage + W_META_OFF + q * Q4K_META_TILE + lane * 16;
             uint4 sa = make_uint4(0, 0, 0, 0), em = sa, w0 = sa, w1 = sa, w2 = sa, w3 = sa;
             if (valid) {
-                sa = *reinterpret_cast<const uint4*>(mt);
-                em = *reinterpret_cast<const uint4*>(mt + (1 + h) * 512);
+                // exact: alpha sc_j and the min-term part; fast: d sc_j and dmin m_j
+                sa = *reinterpret_cast<const uint4*>(mt + (FAST ? 3 : 0) * 512);
+                em = *reinterpret_cast<const uint4*>(mt + (FAST ? 4 : 1 + h) * 512);
                 // 64-value chunks c = 2h, 2h + 1 (tile chunks 1 + 4h .. 4 + 4h)
                 w0 = *reinterpret_cast<const uint4*>(tile + (1 + 4 * h) * 512);
                 w1 = *reinterpret_cast<const uint4*>(tile + (2 + 4 * h) * 512);
@@ -554,10 +653,10 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             if (lane == 0) mbar_arrive(w_empty + ws);  // this warp is done with the stage
             if (!warp_wait_bar(a_empty + ab, ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err, abort_flag, lane)) break;
             tc_fence_after();
-            // Min-term tile: row r holds 16 fp16 (both halves of pair j are
-            // the value of sub-block j), 32-byte swizzle: 16-byte chunk c of
-            // row r at (r / 8) * 256 + (r % 8) * 32 + ((c ^ ((r >> 2) & 1)) * 16).
-            {
+            if constexpr (!FAST) {
+                // Min-term tile: row r holds 16 fp16 (both halves of pair j are
+                // the value of sub-block j), 32-byte swizzle: 16-byte chunk c of
+                // row r at (r / 8) * 256 + (r % 8) * 32 + ((c ^ ((r >> 2) & 1)) * 16).
                 uint8_t* et = ering + ab * E_TILE_BYTES + (r >> 3) * 256 + (r & 7) * 32;
                 const int sw = (r >> 2) & 1;
                 const uint4 c0 = make_uint4(__byte_perm(em.x, 0u, 0x1010), __byte_perm(em.x, 0u, 0x3232),
@@ -571,44 +670,68 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 #pragma unroll
             for (int cc = 0; cc < 2; cc++) {
                 // fp16 scales of sub-blocks 2c (low nibbles) and 2c + 1 (high
-                // nibbles), c = 2h + cc: word c of sa holds both.
+                // nibbles), c = 2h + cc: word c of sa (and em) holds both.
                 const uint32_t sw = (h == 0) ? (cc == 0 ? sa.x : sa.y) : (cc == 0 ? sa.z : sa.w);
                 const uint32_t s_lo = __byte_perm(sw, 0u, 0x1010), s_hi = __byte_perm(sw, 0u, 0x3232);
-                // Low nibbles become fp16 1024 + q; high nibbles, masked in
-                // place, fp16 1024 + 16 q.  (1024 + q) s - 1024 s and
-                // (1024 + 16 q) s/16 - 64 s are q s exactly.
-                const uint32_t n_lo = hmul2_bits(s_lo, 0xE400E400u);   // -1024 s
-                const uint32_t s_h16 = hmul2_bits(s_hi, 0x2C002C00u);  // s / 16
-                const uint32_t n_hi = hmul2_bits(s_hi, 0xD400D400u);   // -64 s
                 const uint4 wa = cc ? w2 : w0, wb = cc ? w3 : w1;
                 const uint32_t W[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
                 uint32_t v[32];
+                if constexpr (FAST) {
+                    // w = q * (d sc) - dmin m, one fp16 rounding: q recovered
+                    // exactly from the magic-number form, then one fma.
+                    const uint32_t mw = (h == 0) ? (cc == 0 ? em.x : em.y) : (cc == 0 ? em.z : em.w);
+                    const uint32_t nm_lo = __byte_perm(mw, 0u, 0x1010) ^ 0x80008000u;  // -dmin m
+                    const uint32_t nm_hi = __byte_perm(mw, 0u, 0x3232) ^ 0x80008000u;
 #pragma unroll
-                for (int w = 0; w < 8; w++) {
-                    // bytes l = 4w..4w+3: low nibbles are values 64c+l, high
-                    // nibbles 64c+32+l.  One fp16 pair takes the nibbles of bytes
-                    // 0 and 2, the other those of bytes 1 and 3: K order 0, 2,
-                    // 1, 3, as in Xq.
-                    const uint32_t w8 = W[w] >> 8;
-                    const uint32_t l02 = (W[w] & 0x000F000Fu) | 0x64006400u;
-                    const uint32_t l13 = (w8 & 0x000F000Fu) | 0x64006400u;
-                    const uint32_t h02 = (W[w] & 0x00F000F0u) | 0x64006400u;
-                    const uint32_t h13 = (w8 & 0x00F000F0u) | 0x64006400u;
-                    v[2 * w] = hfma2_bits(l02, s_lo, n_lo);
-                    v[2 * w + 1] = hfma2_bits(l13, s_lo, n_lo);
-                    v[16 + 2 * w] = hfma2_bits(h02, s_h16, n_hi);
-                    v[16 + 2 * w + 1] = hfma2_bits(h13, s_h16, n_hi);
+                    for (int w = 0; w < 8; w++) {
+                        const uint32_t w8 = W[w] >> 8;
+                        const uint32_t l02 = (W[w] & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t l13 = (w8 & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t h02 = (W[w] & 0x00F000F0u) | 0x64006400u;
+                        const uint32_t h13 = (w8 & 0x00F000F0u) | 0x64006400u;
+                        // (1024 + q) - 1024 = q; (1024 + 16 q) / 16 - 64 = q
+                        const uint32_t q02 = hadd2_bits(l02, 0xE400E400u), q13 = hadd2_bits(l13, 0xE400E400u);
+                        const uint32_t p02 = hfma2_bits(h02, 0x2C002C00u, 0xD400D400u);
+                        const uint32_t p13 = hfma2_bits(h13, 0x2C002C00u, 0xD400D400u);
+                        v[2 * w] = hfma2_bits(q02, s_lo, nm_lo);
+                        v[2 * w + 1] = hfma2_bits(q13, s_lo, nm_lo);
+                        v[16 + 2 * w] = hfma2_bits(p02, s_hi, nm_hi);
+                        v[16 + 2 * w + 1] = hfma2_bits(p13, s_hi, nm_hi);
+                    }
+                } else {
+                    // Low nibbles become fp16 1024 + q; high nibbles, masked in
+                    // place, fp16 1024 + 16 q.  (1024 + q) s - 1024 s and
+                    // (1024 + 16 q) s/16 - 64 s are q s exactly.
+                    const uint32_t n_lo = hmul2_bits(s_lo, 0xE400E400u);   // -1024 s
+                    const uint32_t s_h16 = hmul2_bits(s_hi, 0x2C002C00u);  // s / 16
+                    const uint32_t n_hi = hmul2_bits(s_hi, 0xD400D400u);   // -64 s
+#pragma unroll
+                    for (int w = 0; w < 8; w++) {
+                        // bytes l = 4w..4w+3: low nibbles are values 64c+l, high
+                        // nibbles 64c+32+l.  One fp16 pair takes the nibbles of
+                        // bytes 0 and 2, the other those of bytes 1 and 3: K order
+                        // 0, 2, 1, 3, as in Xq.
+                        const uint32_t w8 = W[w] >> 8;
+                        const uint32_t l02 = (W[w] & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t l13 = (w8 & 0x000F000Fu) | 0x64006400u;
+                        const uint32_t h02 = (W[w] & 0x00F000F0u) | 0x64006400u;
+                        const uint32_t h13 = (w8 & 0x00F000F0u) | 0x64006400u;
+                        v[2 * w] = hfma2_bits(l02, s_lo, n_lo);
+                        v[2 * w + 1] = hfma2_bits(l13, s_lo, n_lo);
+                        v[16 + 2 * w] = hfma2_bits(h02, s_h16, n_hi);
+                        v[16 + 2 * w + 1] = hfma2_bits(h13, s_h16, n_hi);
+                    }
                 }
                 tmem_st32(a_col + 32 * cc, v);
             }
             tmem_st_wait();
-            fence_proxy_async_smem();  // the min-term tile is read by the tensor core
+            if (!FAST) fence_proxy_async_smem();  // the min-term tile is read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(a_full + ab);
         }
     } else {
-        setmaxnreg_inc<REGS_DRAIN>();
+        setmaxnreg_inc<RegSplit<FAST>::DRAIN>();
         // ---------------- drains ----------------
         const int dw = warp - WARP_DRAIN0;
         const int q = warp & 3;    // lane quadrant = 32 weight rows of the tile
@@ -617,7 +740,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         float out[64];
 #pragma unroll
         for (int j = 0; j < 64; j++) out[j] = 0.f;
-        int seg_b0 = 0;
+        int seg_b0 = 0, seg = 0;
         UnitPos p;
         p.init(u0, nb, a.tiles_t);
         for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
@@ -629,6 +752,26 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             const int g = tw * 4 + q;
             const int row = g * 32 + lane;
+            if constexpr (FAST) {
+                // One accumulator per tile segment: read it once, at the end.
+                if (b != nb - 1 && i != n_units - 1) continue;
+                const int accb = seg & 1;
+                if (!warp_wait_bar(acc_full + accb, (uint32_t)(seg >> 1) & 1u, a.err, abort_flag, lane)) break;
+                seg++;
+                tc_fence_after();
+                uint32_t r0[32], r1[32];
+                tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64), r0);
+                tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64 + 32), r1);
+                tmem_ld_wait2(r0, r1);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty + accb);
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    out[j] = __uint_as_float(r0[j]);
+                    out[32 + j] = __uint_as_float(r1[j]);
+                }
+            } else {
             const int ds = i % D_STAGES;
             const int accb = i & 1;
             if (!warp_wait_bar(d_full + ds, (uint32_t)(i / D_STAGES) & 1u, a.err, abort_flag, lane) ||
@@ -666,6 +809,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(d_empty + ds);  // done with the unit's scales
+            }
 
             if (b != nb - 1 && i != n_units - 1) continue;  // the tile's segment goes on
             const int tok0 = tt * TN + th * 64;
@@ -793,34 +937,45 @@ bool encode_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
 
 cudaError_t configure_tc_gemm() {
     // The warpgroups' setmaxnreg split draws on the registers the CTA is
-    // launched with: the kernel must have been compiled to exactly
+    // launched with: each kernel must have been compiled to exactly
     // LAUNCH_REGS per thread, or a larger request would never be granted.
-    cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, gemm_q4k_tc_kernel);
-    if (e != cudaSuccess) return e;
-    if (fa.numRegs != tcg::LAUNCH_REGS || fa.maxThreadsPerBlock < tcg::THREADS) return cudaErrorInvalidConfiguration;
-    return cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)tcg::SMEM_BYTES);
+    for (const void* fn : {(const void*)gemm_q4k_tc_kernel<false>, (const void*)gemm_q4k_tc_kernel<true>}) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+        if (e != cudaSuccess) return e;
+        if (fa.numRegs != tcg::LAUNCH_REGS || fa.maxThreadsPerBlock < tcg::THREADS) return cudaErrorInvalidConfiguration;
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcg::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
-cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd,
+cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd, bool fast,
                              cudaStream_t s) {
     const int nb = k / QK;
     const long long warps = (long long)m_pad * nb;
     const int grid = (int)((warps + 7) / 8);
-    gemm_prep_kernel<<<grid, 256, 0, s>>>(x, k, tokens, m_pad, static_cast<__half*>(xq), static_cast<__half*>(xe),
-                                          xd);
+    if (fast)
+        gemm_prep_kernel<true><<<grid, 256, 0, s>>>(x, k, tokens, m_pad, static_cast<__half*>(xq), nullptr, nullptr);
+    else
+        gemm_prep_kernel<false><<<grid, 256, 0, s>>>(x, k, tokens, m_pad, static_cast<__half*>(xq),
+                                                     static_cast<__half*>(xe), xd);
     return cudaGetLastError();
 }
 
-cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* xe, int k, cudaStream_t s, bool pdl) {
+cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* xe, int k, bool fast, cudaStream_t s,
+                           bool pdl) {
     CUtensorMap tq, te;
     const int nb = k / QK;
     if (!encode_2d_f16(&tq, xq, (uint64_t)k, (uint64_t)args.tokens, (uint64_t)k * 2, 64, tcg::TN,
-                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d_f16(&te, xe, (uint64_t)nb * 16, (uint64_t)args.tokens, (uint64_t)nb * 32, 16, tcg::TN,
-                       CU_TENSOR_MAP_SWIZZLE_32B))
+                       CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
+    if (fast) {
+        te = tq;  // unused in fast mode
+    } else if (!encode_2d_f16(&te, xe, (uint64_t)nb * 16, (uint64_t)args.tokens, (uint64_t)nb * 32, 16, tcg::TN,
+                              CU_TENSOR_MAP_SWIZZLE_32B)) {
+        return cudaErrorInvalidValue;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(args.grid);
     cfg.blockDim = dim3(tcg::THREADS);
@@ -831,7 +986,8 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* x
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel, tq, te, args);
+    return fast ? cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true>, tq, te, args)
+                : cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false>, tq, te, args);
 }
 
 }  // namespace q35k

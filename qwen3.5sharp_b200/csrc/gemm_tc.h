@@ -33,11 +33,16 @@ size_t q4k_meta_bytes(int nb, int n_pad);
 size_t q4k_scale_bytes(int nb, int n_pad);
 cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad, cudaStream_t s);
 cudaError_t configure_tc_gemm();
-// Q8_K quantization of x [tokens][k] into the GEMM's operands: Xq [tokens][k]
-// fp16 q values, Xe [tokens][k/256*16] fp16 block sums, Xd [k/256][m_pad] d.
-cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd,
+// Q8_K quantization of x [tokens][k] into the GEMM's operands.  Exact mode:
+// Xq [tokens][k] fp16 q values, Xe [tokens][k/256*16] fp16 block sums,
+// Xd [k/256][m_pad] d.  Fast mode: Xq = fp16(d q) only.
+cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd, bool fast,
                              cudaStream_t s);
 // The GEMM; `pdl` lets it start while the preparation kernel finishes.
-cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* xe, int k, cudaStream_t s, bool pdl);
+// Exact mode forms the reference's integer dots and scales them per
+// super-block; fast mode multiplies fp16-rounded dequantized weights and
+// activations with one fp32 accumulator per tile.
+cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* xe, int k, bool fast, cudaStream_t s,
+                           bool pdl);
 
 }  // namespace q35k

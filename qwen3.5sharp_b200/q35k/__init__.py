@@ -138,6 +138,10 @@ class Context:
     def sync(self):
         self._check(self.L.q35k_sync(self.h))
 
+    def set_gemm_mode(self, mode: int):
+        """q35k.GEMM_EXACT (default) or q35k.GEMM_FAST (see include/q35k.h)."""
+        self._check(self.L.q35k_set_gemm_mode(self.h, mode))
+
     def upload(self, qtype: int, blocks: np.ndarray, n_in: int, n_out: int) -> "Weight":
         blocks = _u8(blocks)
         nb = n_in // QK if n_in > 0 else 0
@@ -227,6 +231,7 @@ class Weight:
 # ---------------------------------------------------------------------------
 
 GATHER_NCCL, GATHER_PEER = _lib.GATHER_NCCL, _lib.GATHER_PEER
+GEMM_EXACT, GEMM_FAST = _lib.GEMM_EXACT, _lib.GEMM_FAST
 
 
 def shard_rows(n_out: int, nranks: int) -> int:

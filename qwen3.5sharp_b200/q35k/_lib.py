@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libq35k.so")
 
 OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL = 0, 1, 2, 3, 4, 5, 6
 GATHER_NCCL, GATHER_PEER = 0, 1
+GEMM_EXACT, GEMM_FAST = 0, 1
 NCCL_ID_BYTES = 128
 
 # Symbols declared in include/q35k.h, with their ctypes signatures.
@@ -49,6 +50,7 @@ SIGNATURES = {
     "q35k_shard_weight_free": ([_vp, _vp], _i32),
     "q35k_shard_matmul_dev": ([_vp, _vp, _pp, _pp, _i32, _i32, _pp], _i32),
     "q35k_shard_matmul": ([_vp, _vp, _vp, _vp, _i32, _i32], _i32),
+    "q35k_set_gemm_mode": ([_vp, _i32], _i32),
     "q35k_matmul_static_dev": ([_vp, _vp, _vp, _i32, _vp], _i32),
 }
 

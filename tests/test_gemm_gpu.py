@@ -157,3 +157,55 @@ def test_gemm_device_pointer_path(ctx):
     assert (dy.cpu().numpy() == ctx.matmul(W, x)).all()
     ctx.sync()
     W.free()
+
+
+# ---------------------------------------------------------------------------
+# Fast mode (q35k_set_gemm_mode(Q35K_GEMM_FAST)): fp16-rounded dequantized
+# weights and activations, one accumulator per tile.  Its own bar is the
+# contract's 1e-3; the design lands near 4e-4.
+# ---------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def fast_ctx():
+    c = q35k.Context(0)
+    c.set_gemm_mode(q35k.GEMM_FAST)
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("k,n,m", [(2560, 9728, 512), (5120, 27648, 512), (256, 128, 16), (512, 100, 17),
+                                   (2560, 9728, 129), (5120, 384, 300), (1024, 4096, 1000)])
+def test_fast_mode_within_tolerance(fast_ctx, oracle_mod, k, n, m):
+    w = synth.kquant_blocks(Q4_K, n, k, seed=n + m)
+    x = synth.activations(m, k, seed=k + m)
+    W = fast_ctx.upload(Q4_K, w, k, n)
+    y = fast_ctx.matmul(W, x)
+    ref = oracle_mod.Weight(Q4_K, w, k, n).matmul(x, threads=THREADS)
+    err = rel_err(y, ref)
+    print(f"fast m={m} k={k} n={n}: max|y-r|/max|r| = {err:.3e}")
+    assert np.isfinite(y).all()
+    assert err <= TOL
+    W.free()
+
+
+def test_fast_mode_edge_blocks(fast_ctx, oracle_mod):
+    k, n, m = 1792, 300, 96
+    w = _edge_blocks(n, k, seed=11)
+    x = synth.activations(m, k, seed=12, scale=3.0)
+    x[5] = 0.0
+    W = fast_ctx.upload(Q4_K, w, k, n)
+    y = fast_ctx.matmul(W, x)
+    ref = oracle_mod.Weight(Q4_K, w, k, n).matmul(x, threads=THREADS)
+    assert rel_err(y, ref) <= TOL
+    W.free()
+
+
+def test_fast_mode_is_deterministic(fast_ctx):
+    k, n, m = 2560, 9728, 300
+    w = synth.kquant_blocks(Q4_K, n, k, seed=5)
+    x = synth.activations(m, k, seed=6)
+    W = fast_ctx.upload(Q4_K, w, k, n)
+    first = fast_ctx.matmul(W, x)
+    for _ in range(3):
+        assert (fast_ctx.matmul(W, x) == first).all()
+    W.free()
