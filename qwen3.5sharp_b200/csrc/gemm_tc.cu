@@ -268,6 +268,12 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, unsigne
         }
     }
 }
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Non-blocking test of two barrier phases in one go: both tests issue back
 // to back and the thread waits once for the pair (a barrier test takes ~100
 // cycles under load, and every cycle the MMA thread spends waiting is a
@@ -287,6 +293,61 @@ __device__ __forceinline__ bool test2(uint64_t* b0, uint32_t p0, uint64_t* b1, u
         : "memory");
     return ok != 0;
 }
+// One half super-block of the fast mode in a single instruction block: the
+// eight 16-K MMAs (A in TMEM columns a_tmem + 8 t; B at the activation stage's
+// descriptor, K steps t = 0..3 in the first 64-K box and 4..7 in the second,
+// 16-byte units 2 t and 1024 + 2 (t - 4)), the commit of `done`, and two
+// non-blocking tests of the next half's input barriers.  The tests are issued
+// before the MMAs and their result read after the commit, so their latency
+// (~100 cycles under the kernel's shared-memory load) overlaps MMA issue
+// instead of leaving the tensor pipe idle.
+__device__ __forceinline__ bool mma_half_polled(uint32_t d_tmem, uint32_t a_tmem, uint64_t xdesc, uint32_t idesc,
+                                                uint32_t accumulate, uint64_t* done, uint64_t* nb0, uint32_t np0,
+                                                uint64_t* nb1, uint32_t np1) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred q0, q1, pa, pt;\n"
+        ".reg .b64 bd;\n"
+        ".reg .b32 at;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q0, [%8], %9;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q1, [%10], %11;\n"
+        "setp.ne.b32 pa, %5, 0;\n"
+        "setp.eq.b32 pt, %6, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, {%6, %6, %6, %6}, pa;\n"
+        "add.u32 at, %2, 8;\n"
+        "add.u64 bd, %3, 2;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 16;\n"
+        "add.u64 bd, %3, 4;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 24;\n"
+        "add.u64 bd, %3, 6;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 32;\n"
+        "add.u64 bd, %3, 1024;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 40;\n"
+        "add.u64 bd, %3, 1026;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 48;\n"
+        "add.u64 bd, %3, 1028;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 56;\n"
+        "add.u64 bd, %3, 1030;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n"
+        "and.pred q0, q0, q1;\n"
+        "selp.u32 %0, 1, 0, q0;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(d_tmem), "r"(a_tmem), "l"(xdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(smem_u32(done)),
+          "r"(smem_u32(nb0)), "r"(np0), "r"(smem_u32(nb1)), "r"(np1)
+        : "memory");
+    return ok != 0;
+}
+static_assert(tcg::X_BOX_BYTES == 16384, "mma_half_polled hard-codes the second box at 16-byte unit 1024");
+
 // Wait for work already in flight (ignores the abort flag, still bounded).
 __device__ __forceinline__ void wait_inflight(uint64_t* bar, uint32_t parity, unsigned* err) {
     const uint64_t start = globaltimer_ns();
@@ -591,6 +652,15 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                     const uint64_t xdesc = tc_smem_desc(smem_u32(xring + xs * X_STAGE_BYTES), 1024, 2);
                     const uint32_t a_tmem = tmem + (uint32_t)(A_COL0 + 64 * ab);
                     const bool fresh = FAST ? (seg_start && h == 0) : (h == 0);
+                    if constexpr (FAST) {
+                        // The last fill polls its own (landed) barriers: the
+                        // result is not used.
+                        const int fn = f + 1 < n_fills ? f + 1 : f;
+                        ready = mma_half_polled(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u, a_empty + ab, x_bar(fn),
+                                                x_par(fn), a_bar(fn), a_par(fn)) &&
+                                f + 1 < n_fills;
+                        continue;
+                    }
                     tc_mma_f16_ts(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u);
 #pragma unroll
                     for (int t = 1; t < 4; t++)  // 16-value K steps of the half
@@ -822,11 +892,54 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 }
                 continue;
             }
-            // A piece of a tile shared with neighbouring CTAs: publish it; the
-            // last of the covering CTAs to arrive adds the pieces in CTA order.
+            // A piece of a tile shared with neighbouring CTAs.
             const long long tu0 = (long long)t * nb;
             const int first = cta_of_unit(tu0, U, G), last = cta_of_unit(tu0 + nb - 1, U, G);
             const int me = blockIdx.x;
+            int* const ctr = a.counters + (size_t)t * NUM_DRAIN + dw;
+            if (last == first + 1) {
+                // Two pieces.  CTA `last` computes its piece first (the start of
+                // its range): it stores the piece into y and raises the tile's
+                // flag.  CTA `first` computes its piece last (the end of its
+                // range) and adds it onto y once the flag is up.  Each output is
+                // one addition of the two pieces, whatever the timing.
+                if (me == last) {
+                    if (row < a.n_out) {
+#pragma unroll
+                        for (int j = 0; j < 64; j++)
+                            if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.ldy + row] = out[j];
+                    }
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) atomicExch(ctr, 1);
+                } else {
+                    int up = 0;
+                    if (lane == 0) {
+                        const uint64_t start = globaltimer_ns();
+                        for (uint32_t it = 0;; ++it) {
+                            if (ld_acquire_gpu(ctr) == 1) {
+                                up = 1;
+                                break;
+                            }
+                            if ((it & 63u) == 63u && globaltimer_ns() - start > WAIT_LIMIT_NS) {
+                                atomicOr(a.err, DEV_ERR_TIMEOUT);
+                                break;
+                            }
+                        }
+                    }
+                    up = __shfl_sync(0xffffffffu, up, 0);
+                    if (!up) continue;
+                    if (row < a.n_out) {
+#pragma unroll
+                        for (int j = 0; j < 64; j++)
+                            if (tok0 + j < a.tokens) atomicAdd(a.y + (size_t)(tok0 + j) * a.ldy + row, out[j]);
+                    }
+                    if (lane == 0) *ctr = 0;  // ready for the next launch
+                }
+                continue;
+            }
+            // Three or more pieces: publish this one; the last of the covering
+            // CTAs to arrive adds the pieces in CTA order.
             const int local = (th * 64) * TM + q * 32 + lane;  // token-major piece of this warp
             // Slot 0 holds a CTA's first tile, slot 1 its last one.
             auto piece = [&](int cta) -> float* {
@@ -840,7 +953,6 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             __syncwarp();
             int is_last = 0;
             if (lane == 0) {
-                int* ctr = a.counters + (size_t)t * NUM_DRAIN + dw;
                 const int old = atomicAdd(ctr, 1);
                 is_last = (old == last - first) ? 1 : 0;
                 if (is_last) *ctr = 0;  // ready for the next launch
