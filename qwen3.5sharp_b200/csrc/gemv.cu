@@ -28,9 +28,11 @@
 namespace q35k {
 
 constexpr int GEMV_MAX_TOKENS = 8;
-constexpr int GEMV_MAX_WARPS = 10;
+constexpr int GEMV_MAX_WARPS = 20;        // one warp per tile of a whole-row unit
+constexpr int GEMV_SPLIT_WARPS = 10;      // warps of a split-K unit
 constexpr int GEMV_FUSED_MAX_TOKENS = 2;  // token counts with a fused-quantize variant
-constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per work unit (target)
+constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per split-K work unit (target)
+constexpr int GEMV_ROW_BYTES = 96 * 1024;   // largest whole-row unit
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
 
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -98,6 +100,10 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             bulk_g2s(q8s + qs_bytes + d_bytes, a.q8 + pl.bs + (size_t)b0 * M * 32, bs_bytes, &bars[kr]);
         }
     }
+    // The next kernel in the stream may start streaming its own weights on
+    // SMs this grid frees; it reads activations and writes results only
+    // after its own griddepcontrol.wait, i.e. after this grid completed.
+    asm volatile("griddepcontrol.launch_dependents;");
     const Q8Smem q8{reinterpret_cast<const int8_t*>(q8s), reinterpret_cast<const float*>(q8s + qs_bytes),
                     reinterpret_cast<const int16_t*>(q8s + qs_bytes + d_bytes), M, pl.rows4};
     bool ok = true;
@@ -179,18 +185,28 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     const int m = std::min(std::max(tokens, 1), GEMV_MAX_TOKENS);
     p.groups = (n_out + TILE_ROWS - 1) / TILE_ROWS;
     p.n_pad = p.groups * TILE_ROWS;
-    // Units of up to ~GEMV_UNIT_BYTES (a whole row group when it fits: no
-    // split-K fix-up at all, and a unit's tiles are decoded in parallel by
-    // its warps); split K further only while there are fewer units than SMs.
-    int u = std::max(1, std::min(nb, GEMV_UNIT_BYTES / tile));
-    int splits = (nb + u - 1) / u;
-    while (splits < nb && (long)p.groups * splits < num_sms) splits++;
-    u = (nb + splits - 1) / splits;
+    // A whole row group per CTA, one warp per tile, when it is at most
+    // GEMV_MAX_WARPS tiles and GEMV_ROW_BYTES and there are enough row
+    // groups to fill the SMs: no split-K fix-up, and every tile decoded in
+    // parallel.  Otherwise units of up to ~GEMV_UNIT_BYTES over
+    // GEMV_SPLIT_WARPS warps; split K further only while there are fewer
+    // units than SMs.
+    int u, max_warps;
+    if (nb <= GEMV_MAX_WARPS && nb * tile <= GEMV_ROW_BYTES && p.groups >= num_sms) {
+        u = nb;
+        max_warps = GEMV_MAX_WARPS;
+    } else {
+        u = std::max(1, std::min(nb, GEMV_UNIT_BYTES / tile));
+        int splits = (nb + u - 1) / u;
+        while (splits < nb && (long)p.groups * splits < num_sms) splits++;
+        u = (nb + splits - 1) / splits;
+        max_warps = GEMV_SPLIT_WARPS;
+    }
     // The activations of one unit must fit next to its tiles.
-    while (u > 1 && gemv_smem_layout(tile, u, m, std::min(u, GEMV_MAX_WARPS)).total > GEMV_SMEM_LIMIT) u--;
+    while (u > 1 && gemv_smem_layout(tile, u, m, std::min(u, max_warps)).total > GEMV_SMEM_LIMIT) u--;
     p.unit_blocks = u;
     p.splits = (nb + u - 1) / u;
-    p.warps = std::min(u, GEMV_MAX_WARPS);
+    p.warps = std::min(u, max_warps);
     p.grid = p.groups * p.splits;
     p.smem_bytes = (size_t)gemv_smem_layout(tile, u, m, p.warps).total;
     p.partial_bytes = p.splits > 1 ? (size_t)p.groups * p.splits * GEMV_MAX_TOKENS * 32 * sizeof(float) : 0;
