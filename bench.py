@@ -449,14 +449,29 @@ def secondary_configs(ctx, torch, np, synth, peaks):
 
 def gemm_configs(ctx, torch, synth, peaks):
     """Tensor-core prefill GEMM (Q4_K, M = 512): BASELINE config 3 and config
-    4 at M = 512 on one GPU.  Device time per q35k_matmul_dev call (Q8_K
-    preparation kernel + GEMM kernel), CUDA-graph replay; the weights (14 and
-    80 MB) sit in L2 after the first call, as in any compute-bound GEMM.
-    TFLOP/s = 2 M N K / time against the measured dense bf16 peak."""
+    4 at M = 512 on one GPU, in both GEMM modes (exact: every product formed
+    from the reference's integers, error ~1e-6; fast: fp16-rounded dequantized
+    operands, error ~4e-4, within the 1e-3 bar).  Device time per
+    q35k_matmul_dev call (Q8_K preparation kernel + GEMM kernel), CUDA-graph
+    replay; the weights (14 and 80 MB) sit in L2 after the first call, as in
+    any compute-bound GEMM.  TFLOP/s = 2 M N K / time against the measured
+    dense bf16 peak."""
+    import q35k
+
+    out = {}
+    for mode, suffix in ((q35k.GEMM_EXACT, ""), (q35k.GEMM_FAST, "_fast")):
+        ctx.set_gemm_mode(mode)
+        out.update(_gemm_lines(ctx, torch, synth, peaks, suffix, "exact" if mode == q35k.GEMM_EXACT else "fast"))
+    ctx.set_gemm_mode(q35k.GEMM_EXACT)
+    return out
+
+
+def _gemm_lines(ctx, torch, synth, peaks, suffix, mode_name):
     out = {}
     stream = torch.cuda.current_stream()
     bf16_peak = peaks.get("bf16_tflops")
     for name, m, k, n in (("cfg3_q4k_gemm_m512", 512, 2560, 9728), ("cfg4_q4k_gemm_m512_p1", 512, 5120, 27648)):
+        name = name + suffix
         w = synth.kquant_blocks(synth.Q4_K, n, k, seed=1)
         x = synth.activations(m, k, seed=2)
         W = ctx.upload(synth.Q4_K, w, k, n)
@@ -482,7 +497,7 @@ def gemm_configs(ctx, torch, synth, peaks):
         torch.cuda.synchronize()
         ms = a.elapsed_time(b) / (reps * calls)
         tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
-        out[name] = {"call_ms": ms, "TFLOP/s": tflops,
+        out[name] = {"call_ms": ms, "TFLOP/s": tflops, "gemm_mode": mode_name,
                      "frac_measured_bf16": (tflops / bf16_peak) if bf16_peak else None,
                      "peak_kind": "measured dense bf16 (MEASURED_PEAKS.json bf16_tflops)",
                      "kernels": "gemm_prep_kernel + gemm_q4k_tc_kernel (tcgen05, TMEM, TMA)",
@@ -492,15 +507,19 @@ def gemm_configs(ctx, torch, synth, peaks):
     return out
 
 
-# Configurations runnable alone under a profiler: (qtype, M, K, N, x scale).
+# Configurations runnable alone under a profiler: (qtype, M, K, N, x scale,
+# GEMM mode).
 PROFILE_CASES = {
-    "cfg0_q4k_m1": (12, 1, 2560, 9728, 1.0),
-    "cfg1_q6k_m1": (14, 1, 2560, 151936, 1.0),
-    "cfg2_q5k_m8": (13, 8, 9728, 2560, 0.5),
-    "cfg3_q4k_gemm_m512": (12, 512, 2560, 9728, 1.0),
-    "cfg3_q4k_gemm_m64": (12, 64, 2560, 9728, 1.0),
-    "cfg4_q4k_m8_p1": (12, 8, 5120, 27648, 1.0),
-    "cfg4_q4k_gemm_m512_p1": (12, 512, 5120, 27648, 1.0),
+    "cfg0_q4k_m1": (12, 1, 2560, 9728, 1.0, 0),
+    "cfg1_q6k_m1": (14, 1, 2560, 151936, 1.0, 0),
+    "cfg2_q5k_m8": (13, 8, 9728, 2560, 0.5, 0),
+    "cfg3_q4k_gemm_m512": (12, 512, 2560, 9728, 1.0, 0),
+    "cfg3_q4k_gemm_m512_fast": (12, 512, 2560, 9728, 1.0, 1),
+    "cfg3_q4k_gemm_m64": (12, 64, 2560, 9728, 1.0, 0),
+    "cfg4_q4k_m1_p1": (12, 1, 5120, 27648, 1.0, 0),
+    "cfg4_q4k_m8_p1": (12, 8, 5120, 27648, 1.0, 0),
+    "cfg4_q4k_gemm_m512_p1": (12, 512, 5120, 27648, 1.0, 0),
+    "cfg4_q4k_gemm_m512_p1_fast": (12, 512, 5120, 27648, 1.0, 1),
 }
 
 
@@ -513,8 +532,9 @@ def run_profile_case(args):
     import q35k
     from q35k import synth
 
-    qt, m, k, n, scale = PROFILE_CASES[args.profile]
+    qt, m, k, n, scale, mode = PROFILE_CASES[args.profile]
     ctx = q35k.Context(0)
+    ctx.set_gemm_mode(mode)
     W = ctx.upload(qt, synth.kquant_blocks(qt, n, k, seed=1), k, n)
     dx = torch.from_numpy(synth.activations(m, k, seed=2, scale=scale)).cuda()
     dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
