@@ -7,8 +7,9 @@ Workload: the Q6_K vocab-head GEMV, M=1, K=2560,
 N=151936 -- 319 MB of quantized weights, larger than L2, so every timed step
 streams the weights from HBM.  A step is one pass of the hot path: Q8_K
 quantization of x then the GEMV.  At N>1 GPUs the rows are sharded N/P per
-rank and the fp32 logits are all-gathered over NVLink (NCCL); total work is
-fixed (strong scaling).  Time is measured on the device with CUDA events,
+rank and the fp32 logits are all-gathered over NVLink -- fused into the GEMV
+(each rank stores its slice into every peer's buffer and raises a flag there;
+default) or by NCCL (--gather nccl); total work is fixed (strong scaling).  Time is measured on the device with CUDA events,
 max over ranks.
 
 `--impl reference` times the reference's CPU implementation of the same
@@ -191,6 +192,9 @@ def run_ours(args):
 
     rank, world, local = dist_env()
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    gather_mode = q35k.GATHER_FUSED if args.gather == "fused" else q35k.GATHER_NCCL
+    gather_desc = ("fused into the GEMV (NVLink stores into every peer + bounded flag wait)" if args.gather == "fused"
+                   else "NCCL all-gather")
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -238,13 +242,15 @@ def run_ours(args):
     def step(ev=None):
         # One pass of the hot path: N = 1, q35k_matmul_dev (Q8_K quantization
         # of x fused into the GEMV at M = 1); N > 1, q35k_shard_matmul_dev (the
-        # rank's GEMV, then the NCCL all-gather of the logits).
+        # rank's GEMV, then the gather of the logits: fused into the GEMV --
+        # NVLink stores into every peer plus a bounded flag wait -- or NCCL's
+        # all-gather with --gather nccl).
         if ev:
             ev[0].record(stream)
         if world == 1:
             ctx.matmul_dev(W, dx, dy_full, M, sh)
         else:
-            group.matmul_dev(SW, [dx], [dy_full], M, q35k.GATHER_NCCL, streams=[sh])
+            group.matmul_dev(SW, [dx], [dy_full], M, gather_mode, streams=[sh])
         if ev:
             ev[1].record(stream)
 
@@ -262,18 +268,27 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # K steps back to back (nothing between them on the stream, so each
+    # step's GEMV may start streaming weights under the previous step's tail,
+    # as in a model's decode loop), one event pair around them.
     start.record(stream)
     for i in range(args.steps):
-        step(evs[i])
+        step()
     end.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
     total_ms = start.elapsed_time(end)
+    # Per-step event times, untimed pass (events between steps serialise them).
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        step(evs[i])
+    torch.cuda.synchronize()
     step_ms = [e[0].elapsed_time(e[1]) for e in evs]
     # The rank's GEMV kernel timed alone (untimed for the headline).
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
@@ -326,7 +341,7 @@ def run_ours(args):
         e2e_ms = float(t.item())
         e2e = {"value": nbytes_total / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
                "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": e2e_ms,
-               "api": "pinned H2D of x + q35k_shard_matmul_dev (GEMV + NCCL all-gather) + D2H of y"}
+               "api": f"pinned H2D of x + q35k_shard_matmul_dev (GEMV, gather {gather_desc}) + D2H of y"}
 
     gemv_avg = sum(gemv_ms) / len(gemv_ms)
     achieved = nbytes_local / (gemv_avg / 1e3) / 1e9
@@ -361,7 +376,7 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": M,
                        "k": K, "n": N, "rows_per_gpu": rows, "l2": "inputs > L2 (319 MB of weights)",
-                       "parallelism": (f"row-sharded N/{world} + NCCL all-gather (q35k_shard_matmul_dev)"
+                       "parallelism": (f"row-sharded N/{world}, gather {gather_desc} (q35k_shard_matmul_dev)"
                                        if world > 1 else "single GPU")},
             "frac_of_nominal_8tbs": value / NOMINAL_HBM_GBS,
             "gemv_ms": gemv_avg, "step_ms_events": sum(step_ms) / len(step_ms),
@@ -379,7 +394,8 @@ def run_ours(args):
 
 
 OUR_KERNELS = ("gemv_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel",
-               "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel")
+               "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel", "wait_peer_flags_kernel",
+               "signal_peers_kernel")
 
 
 def count_launches(torch, step):
@@ -553,6 +569,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary configs")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: how the ranks' output slices are all-gathered")
     ap.add_argument("--profile", choices=sorted(PROFILE_CASES),
                     help="only run --steps q35k_matmul_dev calls of one configuration (for ncu), no timing output")
     args = ap.parse_args()

@@ -148,6 +148,12 @@ typedef struct q35k_shard q35k_shard;
 typedef struct q35k_sharded_weight q35k_sharded_weight;
 #define Q35K_GATHER_NCCL 0 /* NCCL all-gather (any group) */
 #define Q35K_GATHER_PEER 1 /* peer copies over NVLink (all ranks in one process) */
+/* Fused into the decode GEMV: each rank stores its slice straight into every
+ * peer's buffer over NVLink and raises a flag there; a bounded wait replaces
+ * the collective.  Calls of at most Q35K_STATIC_MAX_TOKENS tokens and groups
+ * of at most 8 ranks; other calls fall back to the NCCL gather (the peer
+ * copies in a process without NCCL).  Calls of one group must not overlap. */
+#define Q35K_GATHER_FUSED 2
 #define Q35K_NCCL_ID_BYTES 128
 
 /* One process driving `ndev` GPUs (NCCL communicators from ncclCommInitAll). */

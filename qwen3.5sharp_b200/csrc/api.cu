@@ -273,7 +273,7 @@ static int gemv_chunk(const q35k_weight* w) { return gemv_max_tokens(w->nb); }
 // Launch the GEMV for `tokens` rows of planar Q8_K (in chunks of
 // gemv_chunk(w) rows) already on the device.
 int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl,
-                   const float* d_x, int ldy) {
+                   const float* d_x, int ldy, const q35k::GemvPeers* peers) {
     if (ldy <= 0) ldy = w->n_out;
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
@@ -300,6 +300,7 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
         a.counters = d_counters;
         a.err = d_err;
         a.num_sms = num_sms;
+        if (peers) a.peers = *peers;  // one launch: tokens <= chunk (checked by the caller)
         cudaError_t e = launch_gemv(w->type, a, s, pdl && t0 == 0);
         if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
     }
@@ -341,19 +342,22 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     return Q35K_OK;
 }
 
-int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s) {
-    // Prefill: the tensor-core GEMM.
-    if (w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens) return gemm(w, d_x, d_y, tokens, s, ldy);
+int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s,
+                          const q35k::GemvPeers* peers) {
     const int chunk = gemv_chunk(w);
+    if (peers && (chunk <= 0 || tokens > chunk))
+        return fail(Q35K_ENOTSUP, "the fused all-gather takes decode calls of at most %d tokens", chunk);
+    // Prefill: the tensor-core GEMM.
+    if (!peers && w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens) return gemm(w, d_x, d_y, tokens, s, ldy);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     // Decode: the GEMV quantizes its own slices of x (one kernel per call).
     if (tokens <= chunk && gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, num_sms))
-        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy);
+        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy, peers);
     int rc;
     if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK) return rc;
     cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s);
     if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
-    return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy);
+    return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy, peers);
 }
 
 static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, const void* y, int tokens) {

@@ -8,6 +8,10 @@
 
 #include <string>
 
+namespace q35k {
+struct GemvPeers;  // kernels.h
+}
+
 struct q35k_weight {
     int type = 0, n_in = 0, n_out = 0, nb = 0, n_pad = 0, device = 0;
     uint8_t* tiles = nullptr;  // 32-row chunk-major tiles (device_common.cuh)
@@ -88,11 +92,15 @@ struct q35k_ctx {
     int on_device_error(unsigned word);
     // `pdl`: launch with programmatic stream serialization (the GEMV streams
     // weights before the preceding kernel finishes; its Q8_K reads wait).
+    // `peers`: fused all-gather of a sharded decode call (kernels.h).
     int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true,
-             const float* d_x = nullptr, int ldy = 0);
+             const float* d_x = nullptr, int ldy = 0, const q35k::GemvPeers* peers = nullptr);
     // Tensor-core prefill GEMM (Q4_K): quantize x, then the GEMM.
     int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0);
     // y[tokens][ldy] (columns below n_out) = x @ W^T on device pointers: the
     // dispatch behind q35k_matmul_dev (ldy = n_out) and the sharded calls.
-    int matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s);
+    // With `peers` (sharded calls, fused all-gather) the call must take the
+    // decode GEMV: tokens <= 8, else Q35K_ENOTSUP.
+    int matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s,
+                    const q35k::GemvPeers* peers = nullptr);
 };

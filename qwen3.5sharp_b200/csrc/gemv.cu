@@ -148,7 +148,10 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
         if (p.splits == 1) {
             if (row < a.n_out)
 #pragma unroll
-                for (int m = 0; m < M; m++) a.y[(size_t)m * a.ldy + row] = v[m];
+                for (int m = 0; m < M; m++) {
+                    a.y[(size_t)m * a.ldy + row] = v[m];
+                    for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * a.ldy + row] = v[m];
+                }
         } else {
             // Publish this K-range's piece; the last piece to arrive sums all
             // pieces in K order and resets the row group's counter.
@@ -166,7 +169,10 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
                 for (int m = 0; m < M; m++) {
                     float sum = 0.f;
                     for (int k = 0; k < p.splits; k++) sum += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
-                    if (row < a.n_out) a.y[(size_t)m * a.ldy + row] = sum;
+                    if (row < a.n_out) {
+                        a.y[(size_t)m * a.ldy + row] = sum;
+                        for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * a.ldy + row] = sum;
+                    }
                 }
                 if (lane == 0) a.counters[g] = 0;
             }

@@ -24,6 +24,16 @@ cudaError_t launch_dequantize(int type, const uint8_t* blocks, float* y, int k, 
 cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tiles, int nb, int n_out,
                                 int n_pad, cudaStream_t s);
 
+// Fused all-gather of a row-sharded decode call (csrc/shard.cu): besides its
+// own y, the GEMV stores every output value at the same offset in each peer's
+// gather buffer (NVLink stores through IPC or peer pointers).  The kernel that
+// follows it in the stream publishes the stores (flags).  n == 0: off.
+constexpr int GEMV_MAX_PEERS = 7;
+struct GemvPeers {
+    float* y[GEMV_MAX_PEERS];  // this rank's slice in peer k's gather buffer
+    int n;
+};
+
 struct GemvArgs {
     const uint8_t* tiles;  // uploaded weight tiles
     const uint8_t* q8;     // planar Q8_K of `tokens` rows (16-byte aligned), or
@@ -36,6 +46,7 @@ struct GemvArgs {
     int* counters;      // one arrival counter per row group, zero between calls
     unsigned* err;      // device error word
     int num_sms;
+    GemvPeers peers;    // fused all-gather (peers.n == 0: off)
 };
 
 // Launch plan of the GEMV: one CTA per (row group, run of unit_blocks

@@ -10,10 +10,23 @@
 //   * q35k_shard_create_rank: one process per GPU (ncclCommInitRank with an
 //     id from q35k_nccl_unique_id shared by the caller).
 // NCCL is loaded at run time (libnccl.so.2); without it only the peer-copy
-// gather of a single-process group is available.
+// and fused gathers of a single-process group are available.
+//
+// Fused gather (Q35K_GATHER_FUSED, decode calls of at most 8 tokens): every
+// rank owns a "symmetric" buffer -- a header of one flag per rank, then two
+// gather areas [nranks][tokens][n_shard] used on alternate calls -- that every
+// other rank can store into (CUDA IPC mappings exchanged once over NCCL, or
+// peer pointers in one process).  The GEMV stores each output row into its
+// own area and into every peer's.  A one-thread kernel after it publishes the
+// stores (system fence, then this rank's flag -- the call's sequence number
+// -- in every peer) and waits, bounded, for the peers' flags; then the area
+// is permuted into y.  Alternate areas keep a peer's next call from
+// overwriting a slice this rank is still reading: that call's stores come
+// after the peer saw this rank's flag for the call in between.
 #include "../../include/q35k.h"
 #include "api_internal.h"
 #include "device_common.cuh"
+#include "kernels.h"
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -22,6 +35,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <new>
 #include <string>
@@ -81,13 +95,54 @@ const NcclApi& nccl() {
 int shard_rows(int n_out, int nranks) { return (n_out + nranks - 1) / nranks; }
 
 // y[t][r * n_shard + j] = g[r][t][j] for the columns below n_out.
+// Launched with programmatic dependent launch in the fused gather: the next
+// call's GEMV may start streaming its weights at once (it reads x and stores
+// into the other gather areas only after its own griddepcontrol.wait), and
+// this kernel reads the gather area only after the kernel before it (the
+// flag wait) has completed.
 __global__ void gather_permute_kernel(const float* __restrict__ g, float* __restrict__ y, int nranks, int tokens,
                                       int n_shard, int n_out) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const long long total = (long long)tokens * n_out;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
         const int t = (int)(i / n_out), c = (int)(i % n_out);
         const int r = c / n_shard, j = c - r * n_shard;
         y[i] = g[((size_t)r * tokens + t) * n_shard + j];
+    }
+}
+
+// Symmetric buffer header: flag of rank r at u32 index r; the gather areas
+// start at SYM_HDR.
+constexpr size_t SYM_HDR = 256;
+constexpr int SYM_MAX_RANKS = 32;
+
+// After this rank's GEMV (earlier in the stream, so its stores into the peers'
+// buffers have been performed when this kernel starts): publish them with a
+// system-scope release of this rank's flag in every peer, then wait, bounded,
+// until every other rank's flag here reached `epoch`.
+struct PeerFlags {
+    unsigned* flag[GEMV_MAX_PEERS];  // this rank's flag slot in peer k's buffer
+    int n;
+};
+__global__ void signal_wait_kernel(PeerFlags pf, const unsigned* mine, int nranks, int me, unsigned epoch,
+                                   unsigned* err) {
+    // Launched with programmatic dependent launch: publish only after this
+    // rank's GEMV (the kernel before) has completed and its stores landed.
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __threadfence_system();
+    for (int k = 0; k < pf.n; k++) st_release_sys(pf.flag[k], epoch);
+    for (int j = 0; j < nranks; j++) {
+        if (j == me) continue;
+        const uint64_t start = globaltimer_ns();
+        for (uint32_t it = 0;; ++it) {
+            if ((int)(ld_acquire_sys(mine + j) - epoch) >= 0) break;
+            if ((it & 63u) == 63u && globaltimer_ns() - start > 2000000000ull) {
+                atomicOr(err, DEV_ERR_TIMEOUT);
+                return;
+            }
+        }
     }
 }
 
@@ -107,6 +162,14 @@ struct q35k_shard {
     std::vector<cudaEvent_t> done;     // per local device: its slice is in every peer's gather buffer
     std::vector<cudaEvent_t> free_ev;  // per local device: its gather buffer has been read out
     std::vector<char> used;
+    // Fused gather: per local device its symmetric buffer, and every rank's
+    // buffer as that device addresses it ([local][rank]; opened through IPC
+    // where sym_ipc is set).
+    std::vector<uint8_t*> sym;
+    std::vector<std::vector<uint8_t*>> sym_view;
+    std::vector<std::vector<char>> sym_ipc;
+    size_t sym_area = 0;  // bytes of one gather area
+    unsigned epoch = 0;   // sequence number of fused calls
     std::string err;
 
     int fail(int code, const std::string& msg) {
@@ -123,7 +186,26 @@ struct q35k_sharded_weight {
     std::vector<q35k_weight*> parts;  // per local device: its rows
 };
 
+// Close this process's IPC views of peers' symmetric buffers and free its own.
+static void free_sym(q35k_shard* s) {
+    for (size_t i = 0; i < s->sym.size(); i++) {
+        cudaSetDevice(s->devices[i]);
+        for (size_t j = 0; j < s->sym_view[i].size(); j++)
+            if (s->sym_ipc[i][j] && s->sym_view[i][j]) cudaIpcCloseMemHandle(s->sym_view[i][j]);
+        if (s->sym[i]) cudaFree(s->sym[i]);
+    }
+    s->sym.clear();
+    s->sym_view.clear();
+    s->sym_ipc.clear();
+    s->sym_area = 0;
+}
+
 static void destroy_shard(q35k_shard* s) {
+    for (size_t i = 0; i < s->devices.size(); i++) {
+        cudaSetDevice(s->devices[i]);
+        cudaDeviceSynchronize();
+    }
+    free_sym(s);
     for (size_t i = 0; i < s->devices.size(); i++) {
         cudaSetDevice(s->devices[i]);
         cudaDeviceSynchronize();
@@ -155,6 +237,184 @@ static int init_local(q35k_shard* s) {
     s->used.assign(s->devices.size(), 0);
     s->gbuf.assign(s->devices.size(), nullptr);
     s->gcap.assign(s->devices.size(), 0);
+    return Q35K_OK;
+}
+
+// One process per GPU: all-gather `bytes` host bytes from every rank (NCCL
+// on the group's stream, through a device staging buffer); also a barrier.
+static int allgather_host(q35k_shard* s, const void* mine, void* all, size_t bytes) {
+    cudaSetDevice(s->devices[0]);
+    uint8_t* d = nullptr;
+    if (cudaMalloc(&d, bytes * s->nranks) != cudaSuccess) {
+        cudaGetLastError();
+        return s->fail(Q35K_ENOMEM, "staging buffer for the handle exchange");
+    }
+    cudaStream_t st = s->ctxs[0]->stream;
+    int rc = Q35K_OK;
+    if (cudaMemcpyAsync(d + bytes * s->first_rank, mine, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        rc = s->fail(Q35K_ECUDA, "handle exchange copy");
+    } else {
+        const ncclResult_t r = nccl().AllGather(d + bytes * s->first_rank, d, bytes, ncclUint8, s->comms[0], st);
+        if (r != ncclSuccess) rc = s->nccl_fail(r, "ncclAllGather (handle exchange)");
+        else if (cudaMemcpyAsync(all, d, bytes * s->nranks, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                 cudaStreamSynchronize(st) != cudaSuccess)
+            rc = s->fail(Q35K_ECUDA, "handle exchange copy back");
+    }
+    cudaFree(d);
+    return rc;
+}
+
+// Collective: make every rank's symmetric buffer hold gather areas of at
+// least `area` bytes, and map every peer's buffer.
+static int ensure_sym(q35k_shard* s, size_t area) {
+    if (!s->sym.empty() && area <= s->sym_area) return Q35K_OK;
+    const int nloc = (int)s->devices.size();
+    const bool one_process = nloc == s->nranks;
+    if (!one_process && (s->comms.empty() || nloc != 1))
+        return s->fail(Q35K_ENOTSUP, "the fused gather of a rank group needs NCCL for its handle exchange");
+    if (s->nranks > SYM_MAX_RANKS) return s->fail(Q35K_ENOTSUP, "too many ranks for the fused gather");
+    // Every store into the old buffers has landed: this rank's last fused call
+    // waited for all peers' flags, which they raise after their stores.
+    for (int i = 0; i < nloc; i++) {
+        cudaSetDevice(s->devices[i]);
+        if (cudaDeviceSynchronize() != cudaSuccess) return s->fail(Q35K_ECUDA, "synchronize before the gather buffers grow");
+    }
+    if (!s->sym.empty() && !one_process) {
+        // Peers close their views of the old buffers before any rank frees its own.
+        for (size_t j = 0; j < s->sym_view[0].size(); j++)
+            if (s->sym_ipc[0][j] && s->sym_view[0][j]) cudaIpcCloseMemHandle(s->sym_view[0][j]);
+        s->sym_ipc[0].assign(s->nranks, 0);
+        char dummy = 0;
+        std::vector<char> all(s->nranks);
+        const int rc = allgather_host(s, &dummy, all.data(), 1);
+        if (rc != Q35K_OK) return rc;
+    }
+    free_sym(s);
+    const size_t bytes = SYM_HDR + 2 * area;
+    s->sym.assign(nloc, nullptr);
+    s->sym_view.assign(nloc, std::vector<uint8_t*>(s->nranks, nullptr));
+    s->sym_ipc.assign(nloc, std::vector<char>(s->nranks, 0));
+    for (int i = 0; i < nloc; i++) {
+        cudaSetDevice(s->devices[i]);
+        if (cudaMalloc(&s->sym[i], bytes) != cudaSuccess || cudaMemset(s->sym[i], 0, bytes) != cudaSuccess ||
+            cudaDeviceSynchronize() != cudaSuccess) {
+            cudaGetLastError();
+            free_sym(s);
+            return s->fail(Q35K_ENOMEM, "symmetric gather buffer allocation failed");
+        }
+    }
+    if (one_process) {
+        for (int i = 0; i < nloc; i++) {
+            cudaSetDevice(s->devices[i]);
+            for (int j = 0; j < nloc; j++) {
+                s->sym_view[i][j] = s->sym[j];
+                if (j == i) continue;
+                int can = 0;
+                cudaDeviceCanAccessPeer(&can, s->devices[i], s->devices[j]);
+                if (!can) {
+                    free_sym(s);
+                    return s->fail(Q35K_ENOTSUP, "devices without peer access: no fused gather");
+                }
+                const cudaError_t e = cudaDeviceEnablePeerAccess(s->devices[j], 0);
+                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+                    free_sym(s);
+                    return s->fail(Q35K_ECUDA, std::string("peer access: ") + cudaGetErrorString(e));
+                }
+                cudaGetLastError();
+            }
+        }
+    } else {
+        cudaSetDevice(s->devices[0]);
+        cudaIpcMemHandle_t h;
+        if (cudaIpcGetMemHandle(&h, s->sym[0]) != cudaSuccess) {
+            cudaGetLastError();
+            free_sym(s);
+            return s->fail(Q35K_ECUDA, "cudaIpcGetMemHandle failed");
+        }
+        std::vector<cudaIpcMemHandle_t> all(s->nranks);
+        int rc = allgather_host(s, &h, all.data(), sizeof h);
+        if (rc != Q35K_OK) {
+            free_sym(s);
+            return rc;
+        }
+        for (int j = 0; j < s->nranks; j++) {
+            if (j == s->first_rank) {
+                s->sym_view[0][j] = s->sym[0];
+                continue;
+            }
+            void* v = nullptr;
+            const cudaError_t e = cudaIpcOpenMemHandle(&v, all[j], cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                free_sym(s);
+                return s->fail(Q35K_ECUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+            }
+            s->sym_view[0][j] = static_cast<uint8_t*>(v);
+            s->sym_ipc[0][j] = 1;
+        }
+        // Every rank has zeroed its buffer before any peer can store into it:
+        // the exchange above completed on all ranks first.
+    }
+    s->sym_area = area;
+    return Q35K_OK;
+}
+
+// Launch with programmatic stream serialization (the kernel starts while the
+// previous one drains and orders itself with griddepcontrol.wait).
+template <typename... P, typename... A>
+static cudaError_t launch_pdl(void (*kernel)(P...), int grid, int block, cudaStream_t st, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)block);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<P>(args)...);
+}
+
+// The fused-gather call (see the file comment); multi-rank groups only.
+static int shard_matmul_fused(q35k_shard* s, const q35k_sharded_weight* w, const float* const* d_x,
+                              float* const* d_y, int tokens, const std::function<cudaStream_t(int)>& stream_of) {
+    const int nloc = (int)s->devices.size();
+    const size_t slot = (size_t)tokens * w->n_shard;
+    // Areas sized for the largest decode call of this weight (8 tokens), so
+    // that the collective growth happens once.
+    const size_t area = (size_t)s->nranks * 8 * w->n_shard * sizeof(float);
+    int rc = ensure_sym(s, area);
+    if (rc != Q35K_OK) return rc;
+    const unsigned ep = ++s->epoch;
+    const size_t half = (ep & 1) ? s->sym_area : 0;  // alternate gather areas
+    for (int i = 0; i < nloc; i++) {
+        q35k_ctx* c = s->ctxs[i];
+        cudaSetDevice(s->devices[i]);
+        const int rank = s->first_rank + i;
+        GemvPeers pr{};
+        PeerFlags pf{};
+        for (int j = 0; j < s->nranks; j++) {
+            if (j == rank) continue;
+            uint8_t* v = s->sym_view[i][j];
+            pr.y[pr.n++] = reinterpret_cast<float*>(v + SYM_HDR + half) + (size_t)rank * slot;
+            pf.flag[pf.n++] = reinterpret_cast<unsigned*>(v) + rank;
+        }
+        float* mine = reinterpret_cast<float*>(s->sym[i] + SYM_HDR + half) + (size_t)rank * slot;
+        if (w->parts[i]) {
+            rc = c->matmul_into(w->parts[i], d_x[i], mine, w->n_shard, tokens, stream_of(i), &pr);
+            if (rc != Q35K_OK) return s->fail(rc, c->err);
+        }
+        cudaError_t e = launch_pdl(signal_wait_kernel, 1, 1, stream_of(i), pf,
+                                   reinterpret_cast<const unsigned*>(s->sym[i]), s->nranks, rank, ep, c->d_err);
+        const long long total = (long long)tokens * w->n_out;
+        const int grid = (int)std::min<long long>((total + 255) / 256, 4096);
+        if (e == cudaSuccess)
+            e = launch_pdl(gather_permute_kernel, grid, 256, stream_of(i),
+                           reinterpret_cast<const float*>(s->sym[i] + SYM_HDR + half), d_y[i], s->nranks, tokens,
+                           w->n_shard, w->n_out);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) return s->fail(Q35K_ECUDA, std::string("fused gather: ") + cudaGetErrorString(e));
+    }
     return Q35K_OK;
 }
 
@@ -293,10 +553,18 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
     auto stream_of = [&](int i) -> cudaStream_t {
         return (streams && streams[i]) ? static_cast<cudaStream_t>(streams[i]) : s->ctxs[i]->stream;
     };
-    if (gather_mode != Q35K_GATHER_NCCL && gather_mode != Q35K_GATHER_PEER)
-        return s->fail(Q35K_EINVAL, "gather_mode must be Q35K_GATHER_NCCL or Q35K_GATHER_PEER");
+    if (gather_mode != Q35K_GATHER_NCCL && gather_mode != Q35K_GATHER_PEER && gather_mode != Q35K_GATHER_FUSED)
+        return s->fail(Q35K_EINVAL, "gather_mode must be Q35K_GATHER_NCCL, Q35K_GATHER_PEER or Q35K_GATHER_FUSED");
     const int nloc = (int)s->devices.size();
     const bool multi = s->nranks > 1;
+    if (gather_mode == Q35K_GATHER_FUSED) {
+        if (multi && tokens <= Q35K_STATIC_MAX_TOKENS && s->nranks - 1 <= GEMV_MAX_PEERS)
+            return shard_matmul_fused(s, w, d_x, d_y, tokens, stream_of);
+        // Prefill-sized calls (and single-rank groups) take the other gathers.
+        gather_mode = (nloc == s->nranks || s->comms.empty()) ? Q35K_GATHER_PEER : Q35K_GATHER_NCCL;
+        if (multi && gather_mode == Q35K_GATHER_PEER && nloc != s->nranks)
+            return s->fail(Q35K_ENOTSUP, "no NCCL for this rank group's gather");
+    }
     if (multi && gather_mode == Q35K_GATHER_NCCL && s->comms.empty())
         return s->fail(Q35K_ENOTSUP, std::string("NCCL gather unavailable: ") + nccl().why);
     if (multi && gather_mode == Q35K_GATHER_PEER && nloc != s->nranks)

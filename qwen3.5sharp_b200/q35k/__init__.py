@@ -230,7 +230,7 @@ class Weight:
 # Row-sharded matmul over several GPUs (q35k_shard_*).
 # ---------------------------------------------------------------------------
 
-GATHER_NCCL, GATHER_PEER = _lib.GATHER_NCCL, _lib.GATHER_PEER
+GATHER_NCCL, GATHER_PEER, GATHER_FUSED = _lib.GATHER_NCCL, _lib.GATHER_PEER, _lib.GATHER_FUSED
 GEMM_EXACT, GEMM_FAST = _lib.GEMM_EXACT, _lib.GEMM_FAST
 
 

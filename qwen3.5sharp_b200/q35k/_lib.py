@@ -14,7 +14,7 @@ PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "libq35k.so")
 
 OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL = 0, 1, 2, 3, 4, 5, 6
-GATHER_NCCL, GATHER_PEER = 0, 1
+GATHER_NCCL, GATHER_PEER, GATHER_FUSED = 0, 1, 2
 GEMM_EXACT, GEMM_FAST = 0, 1
 NCCL_ID_BYTES = 128
 

@@ -32,7 +32,7 @@ def _ngpus():
 
 @pytest.mark.parametrize("qt,k,n,m", [(Q4_K, 2560, 9728, 1), (Q6_K, 2560, 1000, 3), (Q5_K, 1024, 500, 8),
                                       (Q4_K, 2560, 2048, 64)])
-@pytest.mark.parametrize("mode", [q35k.GATHER_NCCL, q35k.GATHER_PEER])
+@pytest.mark.parametrize("mode", [q35k.GATHER_NCCL, q35k.GATHER_PEER, q35k.GATHER_FUSED])
 def test_one_device_group_matches_single_gpu(ctx, qt, k, n, m, mode):
     w = synth.kquant_blocks(qt, n, k, seed=n + m)
     x = synth.activations(m, k, seed=m)
@@ -80,7 +80,7 @@ def test_shard_device_pointer_path(ctx):
 @pytest.mark.parametrize("ndev", [2, 4, 8])
 @pytest.mark.parametrize("qt,k,n,m", [(Q4_K, 5120, 27648, 1), (Q4_K, 5120, 27648, 8), (Q6_K, 2560, 151936, 1),
                                       (Q4_K, 2560, 9728, 512), (Q5_K, 1024, 1000, 3)])
-@pytest.mark.parametrize("mode", [q35k.GATHER_NCCL, q35k.GATHER_PEER])
+@pytest.mark.parametrize("mode", [q35k.GATHER_NCCL, q35k.GATHER_PEER, q35k.GATHER_FUSED])
 def test_multi_gpu_group(ctx, oracle_mod, ndev, qt, k, n, m, mode):
     if _ngpus() < ndev:
         pytest.skip(f"needs {ndev} GPUs")
@@ -100,20 +100,23 @@ def test_multi_gpu_group(ctx, oracle_mod, ndev, qt, k, n, m, mode):
     sh.close()
 
 
-def _rank_proc(rank, nranks, nccl_id, qt, k, n, m, q):
+def _rank_proc(rank, nranks, nccl_id, qt, k, n, m, mode, q):
     import q35k as Q
 
     sh = Q.Shard(nranks=nranks, rank=rank, nccl_id=nccl_id, device=rank)
     w = synth.kquant_blocks(qt, n, k, seed=1)
     x = synth.activations(m, k, seed=2)
     sw = sh.upload(qt, w, k, n)
-    y = sh.matmul(sw, x)
-    q.put((rank, y))
+    y = sh.matmul(sw, x, gather=mode)
+    # repeated calls alternate the fused gather's buffers and sequence numbers
+    same = all((sh.matmul(sw, x, gather=mode) == y).all() for _ in range(3))
+    q.put((rank, y, same))
     sw.free()
     sh.close()
 
 
-def test_process_per_gpu_group(ctx):
+@pytest.mark.parametrize("mode", [q35k.GATHER_NCCL, q35k.GATHER_FUSED])
+def test_process_per_gpu_group(ctx, mode):
     if _ngpus() < 2:
         pytest.skip("needs 2 GPUs")
     import multiprocessing as mp
@@ -122,10 +125,12 @@ def test_process_per_gpu_group(ctx):
     nid = q35k.nccl_unique_id()
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
-    procs = [mpc.Process(target=_rank_proc, args=(r, 2, nid, qt, k, n, m, q)) for r in range(2)]
+    procs = [mpc.Process(target=_rank_proc, args=(r, 2, nid, qt, k, n, m, mode, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in procs)
+    got = [q.get(timeout=300) for _ in procs]
+    res = {r: y for r, y, _ in got}
+    assert all(same for _, _, same in got)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
