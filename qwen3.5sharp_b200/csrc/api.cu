@@ -309,14 +309,14 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
 
 int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy) {
     if (ldy <= 0) ldy = w->n_out;
-    const TcGemmPlan p = plan_tc_gemm(w->nb, w->n_pad, tokens, num_sms);
+    const bool fast = gemm_mode == Q35K_GEMM_FAST;
+    const TcGemmPlan p = plan_tc_gemm(w->nb, w->n_pad, tokens, num_sms, tc_gemm_tile_tokens(fast, tokens));
     int rc;
     if ((rc = ensure_dev(&d_xq, &xq_cap, p.xq_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev(&d_xe, &xe_cap, p.xe_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_xd, &xd_cap, p.xd_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gws, &gws_cap, p.ws_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gcnt, &gcnt_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
-    const bool fast = gemm_mode == Q35K_GEMM_FAST;
     cudaError_t e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, fast, s);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
     TcGemmArgs a{};
@@ -337,6 +337,7 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     a.tiles_t = p.tiles_t;
     a.grid = p.grid;
     a.units = p.units;
+    a.tn = p.tn;
     e = launch_tc_gemm(a, d_xq, d_xe, w->n_in, fast, s, true);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
     return Q35K_OK;

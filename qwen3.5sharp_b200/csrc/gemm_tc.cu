@@ -123,6 +123,50 @@ static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
+// Geometry of one kernel instance.  TN = 128 (both modes) is the layout
+// above.  TN = 256 (fast mode, 512 or more tokens): each MMA covers 256
+// tokens, so every A operand the producers build and every control step of
+// the MMA thread serves twice the work.  Its activation halves are 64 KB (two
+// boxes of 64 K x 256 tokens), two stages; two weight stages without the Xe
+// tile; one 256-column accumulator (the A buffers keep columns 256..511), so
+// the next tile segment starts once the drains have read the last one.
+template <bool FAST, int TNX> struct Geo {
+    static_assert(TNX == 128 || (FAST && TNX == 256), "tile width");
+    static constexpr int TN = TNX;
+    static constexpr int X_STAGES = TNX == 128 ? 3 : 2;
+    static constexpr int X_BOX_BYTES = 64 * 2 * TN;
+    static constexpr int X_STAGE_BYTES = 2 * X_BOX_BYTES;
+    // Fills on one activation barrier (x_full[f & 1][f % X_STAGES]) recur
+    // every lcm(2, X_STAGES) fills.
+    static constexpr int X_PHASE_FILLS = X_STAGES % 2 ? 2 * X_STAGES : X_STAGES;
+    static constexpr int W_STAGES = TNX == 128 ? 3 : 2;
+    static constexpr int EXT_BOX_BYTES = TNX == 128 ? 16 * 2 * TN : 0;
+    static constexpr int W_EXT_OFF = 0;
+    static constexpr int W_TILE_OFF = EXT_BOX_BYTES;
+    static constexpr int W_META_OFF = W_TILE_OFF + 4 * Q4K_TILE;
+    static constexpr int W_STAGE_BYTES = (W_META_OFF + 4 * Q4K_META_TILE + 1023) / 1024 * 1024;
+    static constexpr int D_STAGES = 4;
+    static constexpr int D_STAGE_BYTES = 2 * 128 * 4;
+    static constexpr int A_BUFS = 4;
+    static constexpr int E_TILE_BYTES = 128 * 32;
+    static constexpr int X_RING_BYTES = X_STAGES * X_STAGE_BYTES;
+    static constexpr int W_RING_BYTES = W_STAGES * W_STAGE_BYTES;
+    static constexpr int E_RING_BYTES = TNX == 128 ? A_BUFS * E_TILE_BYTES : 0;
+    static constexpr int D_RING_BYTES = TNX == 128 ? D_STAGES * D_STAGE_BYTES : 0;
+    static constexpr int ACC_BUFS = 256 / TN;  // accumulators at columns 0 (and 128)
+    static constexpr int A_COL0 = 256;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int PASSES = TN / 128;    // 64-token passes of one drain warp
+    static constexpr int NUM_BARS = 3 * X_STAGES + 3 * W_STAGES + 2 * D_STAGES + 2 * A_BUFS + 4 + 1;
+    static constexpr size_t SMEM_BYTES =
+        1024 + (size_t)X_RING_BYTES + W_RING_BYTES + E_RING_BYTES + D_RING_BYTES + BAR_BYTES;
+    static_assert(NUM_BARS * 8 + 8 <= BAR_BYTES, "barrier area");
+    static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+    static_assert(W_STAGE_BYTES % 1024 == 0 && X_BOX_BYTES % 1024 == 0, "stage alignment");
+};
+static_assert(Geo<false, 128>::SMEM_BYTES == SMEM_BYTES && Geo<false, 128>::W_STAGE_BYTES == W_STAGE_BYTES,
+              "TN = 128 keeps the layout above");
+
 }  // namespace tcg
 
 // ---------------------------------------------------------------------------
@@ -296,11 +340,12 @@ __device__ __forceinline__ bool test2(uint64_t* b0, uint32_t p0, uint64_t* b1, u
 // One half super-block of the fast mode in a single instruction block: the
 // eight 16-K MMAs (A in TMEM columns a_tmem + 8 t; B at the activation stage's
 // descriptor, K steps t = 0..3 in the first 64-K box and 4..7 in the second,
-// 16-byte units 2 t and 1024 + 2 (t - 4)), the commit of `done`, and two
+// 16-byte units 2 t and BOX16 + 2 (t - 4)), the commit of `done`, and two
 // non-blocking tests of the next half's input barriers.  The tests are issued
 // before the MMAs and their result read after the commit, so their latency
 // (~100 cycles under the kernel's shared-memory load) overlaps MMA issue
 // instead of leaving the tensor pipe idle.
+template <int BOX16>  // the second 64-K box of the stage, in 16-byte units
 __device__ __forceinline__ bool mma_half_polled(uint32_t d_tmem, uint32_t a_tmem, uint64_t xdesc, uint32_t idesc,
                                                 uint32_t accumulate, uint64_t* done, uint64_t* nb0, uint32_t np0,
                                                 uint64_t* nb1, uint32_t np1) {
@@ -325,16 +370,16 @@ __device__ __forceinline__ bool mma_half_polled(uint32_t d_tmem, uint32_t a_tmem
         "add.u64 bd, %3, 6;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
         "add.u32 at, %2, 32;\n"
-        "add.u64 bd, %3, 1024;\n"
+        "add.u64 bd, %3, %12;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
         "add.u32 at, %2, 40;\n"
-        "add.u64 bd, %3, 1026;\n"
+        "add.u64 bd, %3, %13;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
         "add.u32 at, %2, 48;\n"
-        "add.u64 bd, %3, 1028;\n"
+        "add.u64 bd, %3, %14;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
         "add.u32 at, %2, 56;\n"
-        "add.u64 bd, %3, 1030;\n"
+        "add.u64 bd, %3, %15;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n"
         "and.pred q0, q0, q1;\n"
@@ -342,11 +387,11 @@ __device__ __forceinline__ bool mma_half_polled(uint32_t d_tmem, uint32_t a_tmem
         "}\n"
         : "=r"(ok)
         : "r"(d_tmem), "r"(a_tmem), "l"(xdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(smem_u32(done)),
-          "r"(smem_u32(nb0)), "r"(np0), "r"(smem_u32(nb1)), "r"(np1)
+          "r"(smem_u32(nb0)), "r"(np0), "r"(smem_u32(nb1)), "r"(np1), "n"(BOX16), "n"(BOX16 + 2), "n"(BOX16 + 4),
+          "n"(BOX16 + 6)
         : "memory");
     return ok != 0;
 }
-static_assert(tcg::X_BOX_BYTES == 16384, "mma_half_polled hard-codes the second box at 16-byte unit 1024");
 
 // Wait for work already in flight (ignores the abort flag, still bounded).
 __device__ __forceinline__ void wait_inflight(uint64_t* bar, uint32_t parity, unsigned* err) {
@@ -451,11 +496,21 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
     s_out[tile * 32 + r] = bs.s;
 }
 
-template <bool FAST>
+template <bool FAST, int TNX>
 __global__ void __launch_bounds__(tcg::THREADS, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_e,
                        const TcGemmArgs a) {
     using namespace tcg;
+    using GG = Geo<FAST, TNX>;
+    constexpr int TN = GG::TN, X_STAGES = GG::X_STAGES, X_BOX_BYTES = GG::X_BOX_BYTES;
+    constexpr int X_STAGE_BYTES = GG::X_STAGE_BYTES, X_PHASE_FILLS = GG::X_PHASE_FILLS;
+    constexpr int W_STAGES = GG::W_STAGES, EXT_BOX_BYTES = GG::EXT_BOX_BYTES, W_EXT_OFF = GG::W_EXT_OFF;
+    constexpr int W_TILE_OFF = GG::W_TILE_OFF, W_META_OFF = GG::W_META_OFF, W_STAGE_BYTES = GG::W_STAGE_BYTES;
+    constexpr int D_STAGES = GG::D_STAGES, D_STAGE_BYTES = GG::D_STAGE_BYTES;
+    constexpr int A_BUFS = GG::A_BUFS, E_TILE_BYTES = GG::E_TILE_BYTES;
+    constexpr int X_RING_BYTES = GG::X_RING_BYTES, W_RING_BYTES = GG::W_RING_BYTES;
+    constexpr int E_RING_BYTES = GG::E_RING_BYTES, D_RING_BYTES = GG::D_RING_BYTES;
+    constexpr int ACC_BUFS = GG::ACC_BUFS, A_COL0 = GG::A_COL0, TMEM_COLS = GG::TMEM_COLS, PASSES = GG::PASSES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* xring = smem;
@@ -463,9 +518,9 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     uint8_t* ering = wring + W_RING_BYTES;
     uint8_t* dring = ering + E_RING_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(dring + D_RING_BYTES);
-    // x_full[h][slot] counts the fills of loader h only: fill f of slot f % 3
-    // uses x_full[f & 1][f % 3], phase f / 6, so a barrier's next phase is
-    // always the same loader's next fill.
+    // x_full[h][slot] counts the fills of loader h only: fill f of slot
+    // f % X_STAGES uses x_full[f & 1][f % X_STAGES], phase f / X_PHASE_FILLS,
+    // so a barrier's next phase is always the same loader's next fill.
     // An activation stage is free once the MMAs of its fill completed, which
     // the A buffer's barrier of the same fill already tracks (a_empty): the
     // MMA issues one commit per half super-block.
@@ -543,7 +598,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
                 const int f = 2 * i + h;
                 const int xs = f % X_STAGES;
-                if (f >= X_STAGES) {  // the slot's previous fill g = f - 3 was consumed
+                if (f >= X_STAGES) {  // the slot's previous fill g = f - X_STAGES was consumed
                     const int g = f - X_STAGES;
                     const int gab = 2 * ((g >> 1) & 1) + (g & 1);
                     if (!wait_bar(a_empty + gab, (uint32_t)(g >> 2) & 1u, a.err, abort_flag)) break;
@@ -557,11 +612,13 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 issued = f;
             }
             // Every copy this warp issued lands before the CTA exits.  Fill
-            // f - 3 (the other loader's) was consumed before fill f was
-            // issued, so only this warp's last two fills can be in flight.
-            for (int f = issued - 2; f <= issued; f += 2)
+            // f - X_STAGES was consumed before fill f was issued: with three
+            // stages (the other loader's fill) this warp's last two fills can
+            // be in flight, with two stages (its own) only its last.
+            constexpr int BACK = X_STAGES % 2 ? 2 : 0;
+            for (int f = issued - BACK; f <= issued; f += 2)
                 if (f >= 0)
-                    wait_inflight(x_full + h * X_STAGES + (f % X_STAGES), (uint32_t)(f / (2 * X_STAGES)) & 1u, a.err);
+                    wait_inflight(x_full + h * X_STAGES + (f % X_STAGES), (uint32_t)(f / X_PHASE_FILLS) & 1u, a.err);
         } else if (warp == WARP_WTMA && lane == 0) {
             // ---------------- weight tiles, metadata, Xe; drain scales ----------------
             bool dep_done = false;
@@ -611,10 +668,10 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             // Fast mode: one accumulator per tile segment (the run of units of
             // one tile this CTA computes), drained once.
             const uint32_t idesc = tc_idesc_f16_f32(TM, TN);
-            // Inputs of fill f = 2 i + h: activation stage x_full[h][f % 3]
-            // (phase f / 6) and A buffer 2 (i & 1) + h (phase i / 2).
+            // Inputs of fill f = 2 i + h: activation stage x_full[h][f % X_STAGES]
+            // (phase f / X_PHASE_FILLS) and A buffer 2 (i & 1) + h (phase i / 2).
             auto x_bar = [&](int f) { return x_full + (f & 1) * X_STAGES + f % X_STAGES; };
-            auto x_par = [&](int f) { return (uint32_t)(f / (2 * X_STAGES)) & 1u; };
+            auto x_par = [&](int f) { return (uint32_t)(f / X_PHASE_FILLS) & 1u; };
             auto a_bar = [&](int f) { return a_full + 2 * ((f >> 1) & 1) + (f & 1); };
             auto a_par = [&](int f) { return (uint32_t)(f >> 2) & 1u; };
             UnitPos p;
@@ -628,10 +685,10 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
                 const bool seg_start = (i == 0 || p.b == 0), seg_end = (p.b == nb - 1 || i == n_units - 1);
                 const int acc_i = FAST ? seg : i;  // accumulator use
-                const int accb = acc_i & 1;
+                const int accb = acc_i % ACC_BUFS;
                 const int ws = i % W_STAGES;
                 if ((!FAST || seg_start) &&
-                    !wait_bar(acc_empty + accb, ((uint32_t)(acc_i >> 1) & 1u) ^ 1u, a.err, abort_flag))
+                    !wait_bar(acc_empty + accb, ((uint32_t)(acc_i / ACC_BUFS) & 1u) ^ 1u, a.err, abort_flag))
                     break;
                 if (!FAST && !wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
                 const uint32_t d_tmem = tmem + (uint32_t)(accb * TN);
@@ -656,8 +713,9 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                         // The last fill polls its own (landed) barriers: the
                         // result is not used.
                         const int fn = f + 1 < n_fills ? f + 1 : f;
-                        ready = mma_half_polled(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u, a_empty + ab, x_bar(fn),
-                                                x_par(fn), a_bar(fn), a_par(fn)) &&
+                        ready = mma_half_polled<X_BOX_BYTES / 16>(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u,
+                                                                  a_empty + ab, x_bar(fn), x_par(fn), a_bar(fn),
+                                                                  a_par(fn)) &&
                                 f + 1 < n_fills;
                         continue;
                     }
@@ -805,7 +863,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         // ---------------- drains ----------------
         const int dw = warp - WARP_DRAIN0;
         const int q = warp & 3;    // lane quadrant = 32 weight rows of the tile
-        const int th = dw >> 2;    // 64-token half of the tile
+        const int th = dw >> 2;    // token half of the tile (TN / 2 tokens)
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         float out[64];
 #pragma unroll
@@ -822,26 +880,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             const int g = tw * 4 + q;
             const int row = g * 32 + lane;
-            if constexpr (FAST) {
-                // One accumulator per tile segment: read it once, at the end.
-                if (b != nb - 1 && i != n_units - 1) continue;
-                const int accb = seg & 1;
-                if (!warp_wait_bar(acc_full + accb, (uint32_t)(seg >> 1) & 1u, a.err, abort_flag, lane)) break;
-                seg++;
-                tc_fence_after();
-                uint32_t r0[32], r1[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64), r0);
-                tmem_ld32(tmem + lane_base + (uint32_t)(accb * TN + th * 64 + 32), r1);
-                tmem_ld_wait2(r0, r1);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(acc_empty + accb);
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    out[j] = __uint_as_float(r0[j]);
-                    out[32 + j] = __uint_as_float(r1[j]);
-                }
-            } else {
+            if constexpr (!FAST) {
             const int ds = i % D_STAGES;
             const int accb = i & 1;
             if (!warp_wait_bar(d_full + ds, (uint32_t)(i / D_STAGES) & 1u, a.err, abort_flag, lane) ||
@@ -882,7 +921,35 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
 
             if (b != nb - 1 && i != n_units - 1) continue;  // the tile's segment goes on
-            const int tok0 = tt * TN + th * 64;
+            int accb = 0;
+            if constexpr (FAST) {
+                // One accumulator per tile segment: read it once, at the end.
+                accb = seg % ACC_BUFS;
+                if (!warp_wait_bar(acc_full + accb, (uint32_t)(seg / ACC_BUFS) & 1u, a.err, abort_flag, lane)) break;
+                seg++;
+                tc_fence_after();
+            }
+            // This warp's tokens of the tile: TN / 2 from th * TN / 2, in
+            // passes of 64 (one pass for 128-token tiles).
+            for (int pp = 0; pp < PASSES; pp++) {
+            if constexpr (FAST) {
+                const uint32_t col = (uint32_t)(accb * TN + th * (TN / 2) + pp * 64);
+                uint32_t r0[32], r1[32];
+                tmem_ld32(tmem + lane_base + col, r0);
+                tmem_ld32(tmem + lane_base + col + 32, r1);
+                tmem_ld_wait2(r0, r1);
+                if (pp == PASSES - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acc_empty + accb);  // all of it read
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    out[j] = __uint_as_float(r0[j]);
+                    out[32 + j] = __uint_as_float(r1[j]);
+                }
+            }
+            const int tok0 = tt * TN + th * (TN / 2) + pp * 64;
             if (seg_b0 == 0 && b == nb - 1) {
                 // This CTA computed the whole tile.
                 if (row < a.n_out) {
@@ -896,7 +963,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             const long long tu0 = (long long)t * nb;
             const int first = cta_of_unit(tu0, U, G), last = cta_of_unit(tu0 + nb - 1, U, G);
             const int me = blockIdx.x;
-            int* const ctr = a.counters + (size_t)t * NUM_DRAIN + dw;
+            int* const ctr = a.counters + ((size_t)t * NUM_DRAIN + dw) * PASSES + pp;
             if (last == first + 1) {
                 // Two pieces.  CTA `last` computes its piece first (the start of
                 // its range): it stores the piece into y and raises the tile's
@@ -940,7 +1007,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             // Three or more pieces: publish this one; the last of the covering
             // CTAs to arrive adds the pieces in CTA order.
-            const int local = (th * 64) * TM + q * 32 + lane;  // token-major piece of this warp
+            const int local = (th * (TN / 2) + pp * 64) * TM + q * 32 + lane;  // token-major piece of this warp
             // Slot 0 holds a CTA's first tile, slot 1 its last one.
             auto piece = [&](int cta) -> float* {
                 const long long cu0 = (long long)cta * U / G;
@@ -973,6 +1040,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 for (int j = 0; j < 64; j++)
                     if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.ldy + row] = out[j];
             }
+            }  // passes
         }
     }
 
@@ -997,20 +1065,23 @@ cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, i
     return cudaGetLastError();
 }
 
-TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms) {
+int tc_gemm_tile_tokens(bool fast, int tokens) { return (fast && tokens >= 512) ? 256 : 128; }
+
+TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms, int tn) {
     TcGemmPlan p{};
-    p.m_pad = (tokens + tcg::TN - 1) / tcg::TN * tcg::TN;
+    p.tn = tn == 256 ? 256 : 128;
+    p.m_pad = (tokens + p.tn - 1) / p.tn * p.tn;
     p.tiles_w = (n_pad + tcg::TM - 1) / tcg::TM;
-    p.tiles_t = p.m_pad / tcg::TN;
+    p.tiles_t = p.m_pad / p.tn;
     p.tiles = p.tiles_w * p.tiles_t;
     p.units = (long long)p.tiles * nb;
     p.grid = (int)(p.units < num_sms ? p.units : num_sms);
     p.xq_bytes = (size_t)p.m_pad * nb * QK * 2;
     p.xe_bytes = (size_t)p.m_pad * nb * 16 * 2;
     p.xd_bytes = (size_t)p.m_pad * nb * 4;
-    p.ws_bytes = (size_t)p.grid * 2 * tcg::TM * tcg::TN * 4;
-    p.counters = (size_t)p.tiles * tcg::NUM_DRAIN;
-    p.smem_bytes = tcg::SMEM_BYTES;
+    p.ws_bytes = (size_t)p.grid * 2 * tcg::TM * p.tn * 4;
+    p.counters = (size_t)p.tiles * tcg::NUM_DRAIN * (p.tn / 128);
+    p.smem_bytes = p.tn == 256 ? tcg::Geo<true, 256>::SMEM_BYTES : tcg::Geo<false, 128>::SMEM_BYTES;
     return p;
 }
 
@@ -1051,12 +1122,18 @@ cudaError_t configure_tc_gemm() {
     // The warpgroups' setmaxnreg split draws on the registers the CTA is
     // launched with: each kernel must have been compiled to exactly
     // LAUNCH_REGS per thread, or a larger request would never be granted.
-    for (const void* fn : {(const void*)gemm_q4k_tc_kernel<false>, (const void*)gemm_q4k_tc_kernel<true>}) {
+    const struct {
+        const void* fn;
+        size_t smem;
+    } kernels[] = {{(const void*)gemm_q4k_tc_kernel<false, 128>, tcg::Geo<false, 128>::SMEM_BYTES},
+                   {(const void*)gemm_q4k_tc_kernel<true, 128>, tcg::Geo<true, 128>::SMEM_BYTES},
+                   {(const void*)gemm_q4k_tc_kernel<true, 256>, tcg::Geo<true, 256>::SMEM_BYTES}};
+    for (const auto& k : kernels) {
         cudaFuncAttributes fa;
-        cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+        cudaError_t e = cudaFuncGetAttributes(&fa, k.fn);
         if (e != cudaSuccess) return e;
         if (fa.numRegs != tcg::LAUNCH_REGS || fa.maxThreadsPerBlock < tcg::THREADS) return cudaErrorInvalidConfiguration;
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcg::SMEM_BYTES);
+        e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -1079,7 +1156,9 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* x
                            bool pdl) {
     CUtensorMap tq, te;
     const int nb = k / QK;
-    if (!encode_2d_f16(&tq, xq, (uint64_t)k, (uint64_t)args.tokens, (uint64_t)k * 2, 64, tcg::TN,
+    const bool wide = fast && args.tn == 256;
+    if (args.tn != 128 && !wide) return cudaErrorInvalidValue;
+    if (!encode_2d_f16(&tq, xq, (uint64_t)k, (uint64_t)args.tokens, (uint64_t)k * 2, 64, (uint32_t)args.tn,
                        CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     if (fast) {
@@ -1091,15 +1170,16 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* x
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(args.grid);
     cfg.blockDim = dim3(tcg::THREADS);
-    cfg.dynamicSmemBytes = tcg::SMEM_BYTES;
+    cfg.dynamicSmemBytes = wide ? tcg::Geo<true, 256>::SMEM_BYTES : tcg::Geo<false, 128>::SMEM_BYTES;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return fast ? cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true>, tq, te, args)
-                : cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false>, tq, te, args);
+    if (wide) return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 256>, tq, te, args);
+    return fast ? cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 128>, tq, te, args)
+                : cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false, 128>, tq, te, args);
 }
 
 }  // namespace q35k

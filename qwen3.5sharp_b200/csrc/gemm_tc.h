@@ -14,20 +14,25 @@ struct TcGemmArgs {
     const float* xd;       // Q8_K block scales [nb][m_pad]
     float* y;              // [tokens][ldy], columns below n_out written
     int ldy;
-    float* ws;             // partial tiles: [grid][2][128 tokens][128 rows]
-    int* counters;         // [tiles][8] arrival counters, zero between launches
+    float* ws;             // partial tiles: [grid][2][tn tokens][128 rows]
+    int* counters;         // [tiles][8][tn / 128] arrival counters, zero between launches
     unsigned* err;         // device error word
     int n_out, n_pad, tokens, m_pad, nb, tiles_t, grid;
     long long units;       // tiles * nb
+    int tn;                // tokens per tile: 128, or 256 (fast mode, 256+ tokens)
 };
 
 struct TcGemmPlan {
-    int m_pad, tiles_w, tiles_t, tiles, grid;
+    int tn, m_pad, tiles_w, tiles_t, tiles, grid;
     long long units;
     size_t xq_bytes, xe_bytes, xd_bytes, ws_bytes, counters, smem_bytes;
 };
 
-TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms);
+// Tokens per tile: 256 for fast-mode calls of at least 512 tokens (twice the
+// work per MMA instruction and per dequantized weight tile; fewer tokens would
+// leave too few tiles to share among the SMs), else 128.
+int tc_gemm_tile_tokens(bool fast, int tokens);
+TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms, int tn);
 // GEMM metadata of an uploaded Q4_K weight: sizes and the kernel that fills it.
 size_t q4k_meta_bytes(int nb, int n_pad);
 size_t q4k_scale_bytes(int nb, int n_pad);

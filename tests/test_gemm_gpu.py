@@ -200,8 +200,9 @@ def test_fast_mode_edge_blocks(fast_ctx, oracle_mod):
     W.free()
 
 
-def test_fast_mode_is_deterministic(fast_ctx):
-    k, n, m = 2560, 9728, 300
+@pytest.mark.parametrize("m", [300, 700])  # 128- and 256-token tiles
+def test_fast_mode_is_deterministic(fast_ctx, m):
+    k, n = 2560, 9728
     w = synth.kquant_blocks(Q4_K, n, k, seed=5)
     x = synth.activations(m, k, seed=6)
     W = fast_ctx.upload(Q4_K, w, k, n)
@@ -209,3 +210,17 @@ def test_fast_mode_is_deterministic(fast_ctx):
     for _ in range(3):
         assert (fast_ctx.matmul(W, x) == first).all()
     W.free()
+
+
+def test_fast_mode_wide_tiles_match_narrow(fast_ctx, oracle_mod):
+    """512+ tokens run on 256-token tiles: against the oracle, ragged
+    tokens (not a multiple of 256) and a K run shared by several CTAs."""
+    for k, n, m in [(2560, 1000, 513), (5120, 640, 777)]:
+        w = synth.kquant_blocks(Q4_K, n, k, seed=m)
+        x = synth.activations(m, k, seed=m + 1)
+        W = fast_ctx.upload(Q4_K, w, k, n)
+        y = fast_ctx.matmul(W, x)
+        ref = oracle_mod.Weight(Q4_K, w, k, n).matmul(x, threads=THREADS)
+        assert np.isfinite(y).all()
+        assert rel_err(y, ref) <= TOL
+        W.free()
