@@ -111,6 +111,17 @@ int q35k_matmul_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_x, float
 int q35k_matmul_q8k_dev(q35k_ctx* ctx, const q35k_weight* w, const void* d_q8k, float* d_y, int tokens,
                         void* stream);
 
+/* Vocab head + ArgMax (Qwen35Sharp.Cli/Program.cs:127-140, after the logits
+ * of Qwen35Model.cs:280-290): idx[t] = the first row holding the largest
+ * logit of token t (strict '>' scan from row 0; a NaN at row 0 keeps row 0,
+ * later NaNs are never taken), computed in the GEMV's epilogue so the logits
+ * need not be written (d_y may be NULL; if given, the logits are written too).
+ * Runs the decode GEMV for any token count.  The host variant is synchronous
+ * and writes no logits. */
+int q35k_matmul_argmax(q35k_ctx* ctx, const q35k_weight* w, const float* x, int* idx, int tokens);
+int q35k_matmul_argmax_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_x, float* d_y, int* d_idx, int tokens,
+                           void* stream);
+
 /* Arithmetic of the tensor-core prefill GEMM (Q4_K, tokens >= 16).  No
  * counterpart in the reference, which has one arithmetic:
  *   Q35K_GEMM_EXACT (default): the reference's -- Q8_K activations, exact

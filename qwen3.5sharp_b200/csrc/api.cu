@@ -273,7 +273,7 @@ static int gemv_chunk(const q35k_weight* w) { return gemv_max_tokens(w->nb); }
 // Launch the GEMV for `tokens` rows of planar Q8_K (in chunks of
 // gemv_chunk(w) rows) already on the device.
 int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl,
-                   const float* d_x, int ldy, const q35k::GemvPeers* peers) {
+                   const float* d_x, int ldy, const q35k::GemvPeers* peers, unsigned long long* argmax) {
     if (ldy <= 0) ldy = w->n_out;
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
@@ -291,7 +291,8 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
         } else {
             a.q8 = d_q8 + (size_t)(t0 / chunk) * chunk_stride;
         }
-        a.y = d_y + (size_t)t0 * ldy;
+        a.y = d_y ? d_y + (size_t)t0 * ldy : nullptr;
+        a.argmax = argmax ? argmax + t0 : nullptr;
         a.ldy = ldy;
         a.n_out = w->n_out;
         a.nb = w->nb;
@@ -344,21 +345,22 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
 }
 
 int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s,
-                          const q35k::GemvPeers* peers) {
+                          const q35k::GemvPeers* peers, unsigned long long* argmax) {
     const int chunk = gemv_chunk(w);
     if (peers && (chunk <= 0 || tokens > chunk))
         return fail(Q35K_ENOTSUP, "the fused all-gather takes decode calls of at most %d tokens", chunk);
-    // Prefill: the tensor-core GEMM.
-    if (!peers && w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens) return gemm(w, d_x, d_y, tokens, s, ldy);
+    // Prefill: the tensor-core GEMM (the fused gather and argmax are GEMV epilogues).
+    if (!peers && !argmax && w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens)
+        return gemm(w, d_x, d_y, tokens, s, ldy);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     // Decode: the GEMV quantizes its own slices of x (one kernel per call).
     if (tokens <= chunk && gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, num_sms))
-        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy, peers);
+        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy, peers, argmax);
     int rc;
     if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK) return rc;
     cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s);
     if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
-    return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy, peers);
+    return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy, peers, argmax);
 }
 
 static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, const void* y, int tokens) {
@@ -427,6 +429,49 @@ int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int
     if (e != cudaSuccess) return c->cuda_fail(e, "matmul");
     if (*h_err) return c->on_device_error(*h_err);
     std::memcpy(y, c->h_out, out_bytes);
+    return Q35K_OK;
+}
+
+int q35k_matmul_argmax_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, float* d_y, int* d_idx, int tokens,
+                           void* stream) {
+    int rc = check_matmul_args(c, w, d_x, d_idx, tokens);
+    if (rc) return rc;
+    if ((rc = check_alignment(c, d_x, 16, d_y, 4)) != Q35K_OK) return rc;
+    cudaSetDevice(c->device);
+    const cudaStream_t s = pick(c, stream);
+    if ((rc = c->ensure_dev((void**)&c->d_amax, &c->amax_cap, (size_t)tokens * sizeof(unsigned long long), false)) !=
+        Q35K_OK)
+        return rc;
+    cudaError_t e = cudaMemsetAsync(c->d_amax, 0, (size_t)tokens * sizeof(unsigned long long), s);
+    if (e != cudaSuccess) return c->cuda_fail(e, "argmax key reset");
+    if ((rc = c->matmul_into(w, d_x, d_y, w->n_out, tokens, s, nullptr, c->d_amax)) != Q35K_OK) return rc;
+    e = launch_argmax_index(c->d_amax, d_idx, tokens, s);
+    if (e != cudaSuccess) return c->cuda_fail(e, "argmax index launch");
+    return Q35K_OK;
+}
+
+int q35k_matmul_argmax(q35k_ctx* c, const q35k_weight* w, const float* x, int* idx, int tokens) {
+    int rc = check_matmul_args(c, w, x, idx, tokens);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)tokens * w->n_in * sizeof(float);
+    const size_t out_bytes = (size_t)tokens * sizeof(int);
+    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
+    std::memcpy(c->h_in, x, in_bytes);
+    cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of x");
+    int* d_idx = reinterpret_cast<int*>(c->d_y);
+    if ((rc = q35k_matmul_argmax_dev(c, w, c->d_x, nullptr, d_idx, tokens, c->stream)) != Q35K_OK) return rc;
+    unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
+    e = cudaMemcpyAsync(c->h_out, d_idx, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "matmul_argmax");
+    if (*h_err) return c->on_device_error(*h_err);
+    std::memcpy(idx, c->h_out, out_bytes);
     return Q35K_OK;
 }
 

@@ -79,6 +79,7 @@ struct q35k_ctx {
         if (d_xd) cudaFree(d_xd);
         if (d_gws) cudaFree(d_gws);
         if (d_gcnt) cudaFree(d_gcnt);
+        if (d_amax) cudaFree(d_amax);
         if (h_in) cudaFreeHost(h_in);
         if (h_out) cudaFreeHost(h_out);
         if (stream) cudaStreamDestroy(stream);
@@ -93,8 +94,10 @@ struct q35k_ctx {
     // `pdl`: launch with programmatic stream serialization (the GEMV streams
     // weights before the preceding kernel finishes; its Q8_K reads wait).
     // `peers`: fused all-gather of a sharded decode call (kernels.h).
+    // `argmax`: fused argmax keys per token (kernels.h); d_y may then be null.
     int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true,
-             const float* d_x = nullptr, int ldy = 0, const q35k::GemvPeers* peers = nullptr);
+             const float* d_x = nullptr, int ldy = 0, const q35k::GemvPeers* peers = nullptr,
+             unsigned long long* argmax = nullptr);
     // Tensor-core prefill GEMM (Q4_K): quantize x, then the GEMM.
     int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0);
     // y[tokens][ldy] (columns below n_out) = x @ W^T on device pointers: the
@@ -102,5 +105,7 @@ struct q35k_ctx {
     // With `peers` (sharded calls, fused all-gather) the call must take the
     // decode GEMV: tokens <= 8, else Q35K_ENOTSUP.
     int matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s,
-                    const q35k::GemvPeers* peers = nullptr);
+                    const q35k::GemvPeers* peers = nullptr, unsigned long long* argmax = nullptr);
+    unsigned long long* d_amax = nullptr;  // fused-argmax keys
+    size_t amax_cap = 0;
 };

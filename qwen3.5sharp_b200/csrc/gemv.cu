@@ -58,6 +58,32 @@ __host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int units
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Order-preserving key of (logit, row) for the fused argmax: the largest key
+// is the reference's ArgMax (Qwen35Sharp.Cli/Program.cs:127-140) -- the first
+// row holding the largest logit under a strict '>' scan from row 0.  -0 and +0
+// compare equal; a NaN at row 0 keeps row 0 (the scan's start value), a NaN
+// elsewhere is never taken.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    uint32_t o;
+    if (v != v) {
+        o = row == 0 ? 0xffffffffu : 0u;
+    } else {
+        const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+        o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    }
+    return ((unsigned long long)o << 32) | (0xffffffffu - (uint32_t)row);
+}
+
+// Warp-wide max of a 64-bit key; lane 0 folds it into *dst.
+__device__ __forceinline__ void warp_argmax_commit(unsigned long long key, unsigned long long* dst, int lane) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+    }
+    if (lane == 0) atomicMax(dst, key);
+}
+
 // FUSED: quantize this CTA's K-range of the fp32 activations (a.x) to Q8_K in
 // shared memory (q8k_quant.cuh, the same bytes as the standalone quantizer)
 // while the weight tiles are in flight, instead of staging planar Q8_K from
@@ -146,12 +172,16 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             for (int w = 1; w < W; w++) v[m] += red[(w * M + m) * 32 + lane];
         }
         if (p.splits == 1) {
-            if (row < a.n_out)
+            if (row < a.n_out && a.y)
 #pragma unroll
                 for (int m = 0; m < M; m++) {
                     a.y[(size_t)m * a.ldy + row] = v[m];
                     for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * a.ldy + row] = v[m];
                 }
+            if (a.argmax)
+#pragma unroll
+                for (int m = 0; m < M; m++)
+                    warp_argmax_commit(row < a.n_out ? argmax_key(v[m], row) : 0ull, a.argmax + m, lane);
         } else {
             // Publish this K-range's piece; the last piece to arrive sums all
             // pieces in K order and resets the row group's counter.
@@ -169,10 +199,11 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
                 for (int m = 0; m < M; m++) {
                     float sum = 0.f;
                     for (int k = 0; k < p.splits; k++) sum += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
-                    if (row < a.n_out) {
+                    if (row < a.n_out && a.y) {
                         a.y[(size_t)m * a.ldy + row] = sum;
                         for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * a.ldy + row] = sum;
                     }
+                    if (a.argmax) warp_argmax_commit(row < a.n_out ? argmax_key(sum, row) : 0ull, a.argmax + m, lane);
                 }
                 if (lane == 0) a.counters[g] = 0;
             }
@@ -297,6 +328,17 @@ bool gemv_fuses_quantize(int type, int nb, int n_out, int tokens, int num_sms) {
     const GemvPlan p = plan_gemv(type, nb, n_out, tokens, num_sms);
     // Each warp quantizes at most two super-blocks of the unit's K-range.
     return tokens * p.unit_blocks <= 2 * p.warps;
+}
+
+// Row index of each token's fused-argmax key.
+__global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys, int* __restrict__ idx, int tokens) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < tokens) idx[t] = (int)(0xffffffffu - (uint32_t)(keys[t] & 0xffffffffull));
+}
+
+cudaError_t launch_argmax_index(const unsigned long long* keys, int* idx, int tokens, cudaStream_t s) {
+    argmax_index_kernel<<<(tokens + 127) / 128, 128, 0, s>>>(keys, idx, tokens);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl) {

@@ -47,6 +47,10 @@ struct GemvArgs {
     unsigned* err;      // device error word
     int num_sms;
     GemvPeers peers;    // fused all-gather (peers.n == 0: off)
+    // Fused argmax (vocab head): per token the 64-bit max of argmax_key(logit,
+    // row) over all rows, combined with atomicMax; nullptr: off.  y may then
+    // be nullptr (logits not written).
+    unsigned long long* argmax;
 };
 
 // Launch plan of the GEMV: one CTA per (row group, run of unit_blocks
@@ -62,6 +66,8 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms);
 // row is too long to stage one token's activations).
 int gemv_max_tokens(int nb);
 cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl);
+// idx[t] = the row of keys[t] (fused argmax, see GemvArgs::argmax).
+cudaError_t launch_argmax_index(const unsigned long long* keys, int* idx, int tokens, cudaStream_t s);
 // Whether the GEMV for this shape quantizes its own activations (small
 // slices per CTA: decode) instead of reading planar Q8_K.
 bool gemv_fuses_quantize(int type, int nb, int n_out, int tokens, int num_sms);

@@ -161,6 +161,17 @@ class Context:
         self._check(self.L.q35k_matmul(self.h, w.h, x.ctypes.data, y.ctypes.data, tokens))
         return y
 
+    def matmul_argmax(self, w: "Weight", x: np.ndarray, tokens: int | None = None) -> np.ndarray:
+        """Vocab head + ArgMax (q35k_matmul_argmax): per token the first row
+        holding the largest logit, without writing the logits."""
+        x = _f32(x)
+        tokens = x.size // w.n_in if tokens is None else tokens
+        if x.size < tokens * w.n_in:
+            raise ArgumentException("input is smaller than tokens * nIn")
+        idx = np.empty(tokens, dtype=np.int32)
+        self._check(self.L.q35k_matmul_argmax(self.h, w.h, x.ctypes.data, idx.ctypes.data, tokens))
+        return idx
+
     def matmul_q8k(self, w: "Weight", q8: np.ndarray, tokens: int) -> np.ndarray:
         q8 = _u8(q8)
         if q8.size < tokens * (w.n_in // QK) * Q8K_BYTES:
@@ -189,6 +200,11 @@ class Context:
     #    a cudaStream_t int, or None for the context's own stream) --
     def matmul_dev(self, w: "Weight", d_x, d_y, tokens: int, stream=None):
         self._check(self.L.q35k_matmul_dev(self.h, w.h, _dev_ptr(d_x), _dev_ptr(d_y), tokens, _stream(stream)))
+
+    def matmul_argmax_dev(self, w: "Weight", d_x, d_y, d_idx, tokens: int, stream=None):
+        """d_y may be None (logits not written); d_idx: int32[tokens]."""
+        self._check(self.L.q35k_matmul_argmax_dev(self.h, w.h, _dev_ptr(d_x), _dev_ptr(d_y) if d_y is not None else None,
+                                                  _dev_ptr(d_idx), tokens, _stream(stream)))
 
     def matmul_q8k_dev(self, w: "Weight", d_q8, d_y, tokens: int, stream=None):
         self._check(self.L.q35k_matmul_q8k_dev(self.h, w.h, _dev_ptr(d_q8), _dev_ptr(d_y), tokens, _stream(stream)))

@@ -34,6 +34,8 @@ SIGNATURES = {
     "q35k_matmul": ([_vp, _vp, _vp, _vp, _i32], _i32),
     "q35k_matmul_q8k": ([_vp, _vp, _vp, _vp, _i32], _i32),
     "q35k_matmul_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
+    "q35k_matmul_argmax": ([_vp, _vp, _vp, _vp, _i32], _i32),
+    "q35k_matmul_argmax_dev": ([_vp, _vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_matmul_q8k_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_quantize_q8k": ([_vp, _vp, _vp, _i32, _i32], _i32),
     "q35k_quantize_q8k_dev": ([_vp, _vp, _vp, _i32, _i32, _vp], _i32),
