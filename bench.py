@@ -460,8 +460,70 @@ def secondary_configs(ctx, torch, np, synth, peaks):
         for W in Ws:
             W.free()
     out.update(argmax_config(ctx, torch, synth, peaks))
+    out.update(ffn_decode_config(ctx, torch, synth, peaks))
     out.update(gemm_configs(ctx, torch, synth, peaks))
     return out
+
+
+def ffn_decode_config(ctx, torch, synth, peaks):
+    """One decode FFN at cfg0/cfg3's dimensions (hidden 2560, ffn 9728, Q4_K):
+    gate and up from one quantization of x in one GEMV launch
+    (q35k_matmul_shared_dev), then ffn_down on silu(gate) * up with the
+    product formed in its quantization (q35k_matmul_silu_dev); against gate
+    and up as two separate calls.  Eight layers' weights (336 MB > L2) cycled
+    in a CUDA graph."""
+    qt, m, hid, ffn, layers = 12, 1, 2560, 9728, 8
+    stream = torch.cuda.current_stream()
+    L = []
+    for i in range(layers):
+        L.append((ctx.upload(qt, synth.kquant_blocks(qt, ffn, hid, seed=3 * i + 1), hid, ffn),
+                  ctx.upload(qt, synth.kquant_blocks(qt, ffn, hid, seed=3 * i + 2), hid, ffn),
+                  ctx.upload(qt, synth.kquant_blocks(qt, hid, ffn, seed=3 * i + 3), ffn, hid)))
+    dx = torch.from_numpy(synth.activations(m, hid, seed=5)).cuda()
+    dg = torch.empty((m, ffn), dtype=torch.float32, device="cuda")
+    du = torch.empty((m, ffn), dtype=torch.float32, device="cuda")
+    dd = torch.empty((m, hid), dtype=torch.float32, device="cuda")
+
+    def shared(cs):
+        for g, u, d in L:
+            ctx.matmul_shared_dev([g, u], dx, [dg, du], m, cs)
+            ctx.matmul_silu_dev(d, dg, du, dd, m, cs)
+
+    def separate(cs):
+        for g, u, d in L:
+            ctx.matmul_dev(g, dx, dg, m, cs)
+            ctx.matmul_dev(u, dx, du, m, cs)
+            ctx.matmul_silu_dev(d, dg, du, dd, m, cs)
+
+    res = {}
+    nbytes = sum(synth.algorithmic_bytes(qt, m, hid, ffn) for _ in range(2)) + synth.algorithmic_bytes(qt, m, ffn, hid)
+    for name, fn in (("shared", shared), ("separate", separate)):
+        fn(stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn(torch.cuda.current_stream())
+        graph.replay()
+        torch.cuda.synchronize()
+        reps = 50
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / (reps * layers)
+        res[name] = (ms, nbytes / (ms / 1e3) / 1e9)
+        del graph
+    for t in L:
+        for W in t:
+            W.free()
+    ms, gbs = res["shared"]
+    return {"cfg3_q4k_m1_ffn_decode": {
+        "layer_ms": ms, "GB/s": gbs, "frac_measured_hbm": gbs / peaks["hbm_gbs"],
+        "separate_gate_up_layer_ms": res["separate"][0], "separate_GB/s": res["separate"][1],
+        "timing": f"gate+up (one shared GEMV launch) + silu-fused ffn_down per layer, CUDA-graph replay over "
+                  f"{layers} layers (336 MB of weights > L2)"}}
 
 
 def argmax_config(ctx, torch, synth, peaks):

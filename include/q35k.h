@@ -122,6 +122,32 @@ int q35k_matmul_argmax(q35k_ctx* ctx, const q35k_weight* w, const float* x, int*
 int q35k_matmul_argmax_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_x, float* d_y, int* d_idx, int tokens,
                            void* stream);
 
+/* Up to Q35K_MAX_SHARED weights with the same nIn applied to one input, with
+ * one quantization of it: ys[i] [tokens][nOut_i] = x @ ws[i]^T.  Replaces
+ * MulMatPanel.QuantizeAndGemm (Kernels/MulMatPanel.cs:27-54, up to three
+ * panel GEMMs on one Q8_Kx4 panel) and the decode pattern of one
+ * Q8K.QuantizeRow feeding GemvPrequant per weight: DecodeGateUp
+ * (Model/Qwen35Model.Decode.cs:254-265, ffn_gate / ffn_up) and DecodeAttention
+ * (Model/Qwen35Model.Decode.cs:286-292, attn_q / attn_k / attn_v).  Decode
+ * weights of one type run in one GEMV launch.  ws and ys are host arrays of
+ * `count` entries (ys of device pointers in the _dev variant). */
+#define Q35K_MAX_SHARED 4
+int q35k_matmul_shared(q35k_ctx* ctx, const q35k_weight* const* ws, int count, const float* x, float* const* ys,
+                       int tokens);
+int q35k_matmul_shared_dev(q35k_ctx* ctx, const q35k_weight* const* ws, int count, const float* d_x,
+                           float* const* d_ys, int tokens, void* stream);
+
+/* ffn_down on SiLU(gate) * up: y = (silu(gate) . up) @ W^T, gate and up
+ * [tokens][nIn], silu(g) = g / (1 + exp(-g)).  The product is formed inside
+ * the Q8_K quantization of the call (no intermediate written).  Replaces
+ * MulMatPanel.SiluQuantizeAndGemm (Kernels/MulMatPanel.cs:57-79, with
+ * QuantizeQ8Kx4.Quantize4x8Silu, Kernels/QuantizeQ8Kx4.cs:24-35) and the
+ * decode sequence Ops.SiLUMul (Model/Ops.cs:624-675) + DecodeLinear(ffn_down)
+ * (Model/Qwen35Model.Decode.cs:248-249). */
+int q35k_matmul_silu(q35k_ctx* ctx, const q35k_weight* w, const float* gate, const float* up, float* y, int tokens);
+int q35k_matmul_silu_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_gate, const float* d_up, float* d_y,
+                         int tokens, void* stream);
+
 /* Arithmetic of the tensor-core prefill GEMM (Q4_K, tokens >= 16).  No
  * counterpart in the reference, which has one arithmetic:
  *   Q35K_GEMM_EXACT (default): the reference's -- Q8_K activations, exact

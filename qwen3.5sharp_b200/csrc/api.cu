@@ -273,11 +273,28 @@ static int gemv_chunk(const q35k_weight* w) { return gemv_max_tokens(w->nb); }
 // Launch the GEMV for `tokens` rows of planar Q8_K (in chunks of
 // gemv_chunk(w) rows) already on the device.
 int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl,
-                   const float* d_x, int ldy, const q35k::GemvPeers* peers, unsigned long long* argmax) {
+                   const float* d_x, int ldy, const q35k::GemvPeers* peers, unsigned long long* argmax,
+                   const float* d_up, const q35k_weight* const* more_w, float* const* more_y, int n_more) {
     if (ldy <= 0) ldy = w->n_out;
     const int chunk = gemv_chunk(w);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
-    const GemvPlan p = plan_gemv(w->type, w->nb, w->n_out, chunk, num_sms);
+    if (n_more < 0 || n_more > GEMV_MAX_MATS - 1) return fail(Q35K_EINVAL, "too many weights for one GEMV launch");
+    GemvMats more{};
+    int groups = (w->n_out + TILE_ROWS - 1) / TILE_ROWS;
+    for (int k = 0; k < n_more; k++) {
+        const q35k_weight* m = more_w[k];
+        if (m->type != w->type || m->nb != w->nb) return fail(Q35K_EINVAL, "weights of one GEMV launch differ in type or nIn");
+        more.tiles[k] = m->tiles;
+        more.n_out[k] = m->n_out;
+        more.ldy[k] = m->n_out;
+        more.g0[k] = groups;
+        groups += (m->n_out + TILE_ROWS - 1) / TILE_ROWS;
+    }
+    more.n = n_more;
+    GemvArgs probe{};
+    probe.n_out = w->n_out;
+    probe.more = more;
+    const GemvPlan p = plan_gemv(w->type, w->nb, gemv_plan_rows(probe), chunk, num_sms);
     int rc;
     if ((rc = ensure_dev((void**)&d_partial, &partial_cap, p.partial_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_counters, &counters_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
@@ -293,6 +310,9 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
         }
         a.y = d_y ? d_y + (size_t)t0 * ldy : nullptr;
         a.argmax = argmax ? argmax + t0 : nullptr;
+        a.up = d_x && d_up ? d_up + (size_t)t0 * w->n_in : nullptr;
+        a.more = more;
+        for (int k = 0; k < n_more; k++) a.more.y[k] = more_y[k] + (size_t)t0 * more.ldy[k];
         a.ldy = ldy;
         a.n_out = w->n_out;
         a.nb = w->nb;
@@ -308,7 +328,8 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
     return Q35K_OK;
 }
 
-int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy) {
+int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy,
+                   const float* d_up, bool prep) {
     if (ldy <= 0) ldy = w->n_out;
     const bool fast = gemm_mode == Q35K_GEMM_FAST;
     const TcGemmPlan p = plan_tc_gemm(w->nb, w->n_pad, tokens, num_sms, tc_gemm_tile_tokens(fast, tokens));
@@ -318,8 +339,11 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     if ((rc = ensure_dev((void**)&d_xd, &xd_cap, p.xd_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gws, &gws_cap, p.ws_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gcnt, &gcnt_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
-    cudaError_t e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, fast, s);
-    if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
+    cudaError_t e;
+    if (prep) {
+        e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, fast, s, d_up);
+        if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
+    }
     TcGemmArgs a{};
     a.tiles = w->tiles;
     a.meta = w->meta;
@@ -345,22 +369,70 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
 }
 
 int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s,
-                          const q35k::GemvPeers* peers, unsigned long long* argmax) {
+                          const q35k::GemvPeers* peers, unsigned long long* argmax, const float* d_up) {
     const int chunk = gemv_chunk(w);
     if (peers && (chunk <= 0 || tokens > chunk))
         return fail(Q35K_ENOTSUP, "the fused all-gather takes decode calls of at most %d tokens", chunk);
     // Prefill: the tensor-core GEMM (the fused gather and argmax are GEMV epilogues).
     if (!peers && !argmax && w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens)
-        return gemm(w, d_x, d_y, tokens, s, ldy);
+        return gemm(w, d_x, d_y, tokens, s, ldy, d_up);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     // Decode: the GEMV quantizes its own slices of x (one kernel per call).
     if (tokens <= chunk && gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, num_sms))
-        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy, peers, argmax);
+        return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy, peers, argmax, d_up);
     int rc;
     if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK) return rc;
-    cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s);
+    cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s, d_up);
     if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
     return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy, peers, argmax);
+}
+
+// One input, several weights of one K.  Prefill GEMM weights share one
+// activation preparation; the GEMV weights of each type run in one launch,
+// quantizing their own slices of x (decode) or reading one shared planar
+// Q8_K of x.
+int q35k_ctx::matmul_shared(const q35k_weight* const* ws, int count, const float* d_x, float* const* d_ys, int tokens,
+                            cudaStream_t s) {
+    const q35k_weight* w0 = ws[0];
+    const int chunk = gemv_chunk(w0);
+    bool prepped = false, quantized = false;
+    int rc;
+    for (int i = 0; i < count; i++) {
+        const q35k_weight* w = ws[i];
+        if (w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens) {
+            if ((rc = gemm(w, d_x, d_ys[i], tokens, s, 0, nullptr, !prepped)) != Q35K_OK) return rc;
+            prepped = true;
+        }
+    }
+    if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w0->n_in);
+    static const int types[] = {Q35K_TYPE_Q4_K, Q35K_TYPE_Q5_K, Q35K_TYPE_Q6_K};
+    for (int type : types) {
+        const q35k_weight* lw[GEMV_MAX_MATS];
+        float* ly[GEMV_MAX_MATS];
+        int n = 0, rows = 0;
+        for (int i = 0; i < count; i++) {
+            const q35k_weight* w = ws[i];
+            if (w->type != type || (type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens)) continue;
+            lw[n] = w;
+            ly[n++] = d_ys[i];
+            rows += (w->n_out + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;
+        }
+        if (n == 0) continue;
+        if (tokens <= chunk && gemv_fuses_quantize(type, w0->nb, rows, tokens, num_sms)) {
+            rc = gemv(lw[0], nullptr, ly[0], tokens, s, true, d_x, 0, nullptr, nullptr, nullptr, lw + 1, ly + 1, n - 1);
+        } else {
+            if (!quantized) {
+                if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w0->nb, chunk), false)) != Q35K_OK)
+                    return rc;
+                cudaError_t e = launch_quantize_q8k(d_x, d_q8, w0->n_in, tokens, chunk, s);
+                if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
+                quantized = true;
+            }
+            rc = gemv(lw[0], d_q8, ly[0], tokens, s, true, nullptr, 0, nullptr, nullptr, nullptr, lw + 1, ly + 1, n - 1);
+        }
+        if (rc != Q35K_OK) return rc;
+    }
+    return Q35K_OK;
 }
 
 static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, const void* y, int tokens) {
@@ -472,6 +544,101 @@ int q35k_matmul_argmax(q35k_ctx* c, const q35k_weight* w, const float* x, int* i
     if (e != cudaSuccess) return c->cuda_fail(e, "matmul_argmax");
     if (*h_err) return c->on_device_error(*h_err);
     std::memcpy(idx, c->h_out, out_bytes);
+    return Q35K_OK;
+}
+
+static int check_shared_args(q35k_ctx* c, const q35k_weight* const* ws, int count, const void* x,
+                             const void* const* ys, int tokens) {
+    if (!c) return Q35K_EINVAL;
+    if (!ws || !ys) return c->fail(Q35K_EINVAL, "weight or output array is NULL");
+    if (count < 1 || count > Q35K_MAX_SHARED)
+        return c->fail(Q35K_EINVAL, "count must be 1..%d (got %d)", Q35K_MAX_SHARED, count);
+    for (int i = 0; i < count; i++) {
+        int rc = check_matmul_args(c, ws[i], x, ys[i], tokens);
+        if (rc) return rc;
+        if (ws[i]->n_in != ws[0]->n_in)
+            return c->fail(Q35K_EINVAL, "weights of one shared call differ in nIn (%d vs %d)", ws[i]->n_in, ws[0]->n_in);
+    }
+    return Q35K_OK;
+}
+
+int q35k_matmul_shared_dev(q35k_ctx* c, const q35k_weight* const* ws, int count, const float* d_x, float* const* d_ys,
+                           int tokens, void* stream) {
+    int rc = check_shared_args(c, ws, count, d_x, (const void* const*)d_ys, tokens);
+    if (rc) return rc;
+    for (int i = 0; i < count; i++)
+        if ((rc = check_alignment(c, d_x, 16, d_ys[i], 4)) != Q35K_OK) return rc;
+    cudaSetDevice(c->device);
+    return c->matmul_shared(ws, count, d_x, d_ys, tokens, pick(c, stream));
+}
+
+int q35k_matmul_shared(q35k_ctx* c, const q35k_weight* const* ws, int count, const float* x, float* const* ys,
+                       int tokens) {
+    int rc = check_shared_args(c, ws, count, x, (const void* const*)ys, tokens);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)tokens * ws[0]->n_in * sizeof(float);
+    size_t out_bytes = 0, off[Q35K_MAX_SHARED];
+    for (int i = 0; i < count; i++) {
+        off[i] = out_bytes;
+        out_bytes += ((size_t)tokens * ws[i]->n_out * sizeof(float) + 15) / 16 * 16;
+    }
+    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
+    std::memcpy(c->h_in, x, in_bytes);
+    cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of x");
+    float* d_ys[Q35K_MAX_SHARED];
+    for (int i = 0; i < count; i++) d_ys[i] = (float*)((char*)c->d_y + off[i]);
+    if ((rc = c->matmul_shared(ws, count, c->d_x, d_ys, tokens, c->stream)) != Q35K_OK) return rc;
+    unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
+    e = cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "matmul_shared");
+    if (*h_err) return c->on_device_error(*h_err);
+    for (int i = 0; i < count; i++)
+        std::memcpy(ys[i], (char*)c->h_out + off[i], (size_t)tokens * ws[i]->n_out * sizeof(float));
+    return Q35K_OK;
+}
+
+int q35k_matmul_silu_dev(q35k_ctx* c, const q35k_weight* w, const float* d_gate, const float* d_up, float* d_y,
+                         int tokens, void* stream) {
+    int rc = check_matmul_args(c, w, d_gate, d_y, tokens);
+    if (rc) return rc;
+    if (!d_up) return c->fail(Q35K_EINVAL, "up pointer is NULL");
+    if ((rc = check_alignment(c, d_gate, 16, d_y, 4)) != Q35K_OK) return rc;
+    if ((rc = check_alignment(c, d_up, 16, d_y, 4)) != Q35K_OK) return rc;
+    cudaSetDevice(c->device);
+    return c->matmul_into(w, d_gate, d_y, w->n_out, tokens, pick(c, stream), nullptr, nullptr, d_up);
+}
+
+int q35k_matmul_silu(q35k_ctx* c, const q35k_weight* w, const float* gate, const float* up, float* y, int tokens) {
+    int rc = check_matmul_args(c, w, gate, y, tokens);
+    if (rc) return rc;
+    if (!up) return c->fail(Q35K_EINVAL, "up pointer is NULL");
+    cudaSetDevice(c->device);
+    const size_t in_bytes = (size_t)tokens * w->n_in * sizeof(float);
+    const size_t out_bytes = (size_t)tokens * w->n_out * sizeof(float);
+    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, 2 * in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, 2 * in_bytes)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
+    std::memcpy(c->h_in, gate, in_bytes);
+    std::memcpy((char*)c->h_in + in_bytes, up, in_bytes);
+    cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_in, 2 * in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of gate and up");
+    const float* d_up = (const float*)((const char*)c->d_x + in_bytes);
+    if ((rc = q35k_matmul_silu_dev(c, w, c->d_x, d_up, c->d_y, tokens, c->stream)) != Q35K_OK) return rc;
+    unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
+    e = cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return c->cuda_fail(e, "matmul_silu");
+    if (*h_err) return c->on_device_error(*h_err);
+    std::memcpy(y, c->h_out, out_bytes);
     return Q35K_OK;
 }
 

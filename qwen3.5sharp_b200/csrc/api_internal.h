@@ -95,17 +95,29 @@ struct q35k_ctx {
     // weights before the preceding kernel finishes; its Q8_K reads wait).
     // `peers`: fused all-gather of a sharded decode call (kernels.h).
     // `argmax`: fused argmax keys per token (kernels.h); d_y may then be null.
+    // `d_up`: quantize silu(x) * up (fused quantize or d_q8 == nullptr only).
+    // `more_w` / `more_y`: n_more further weights of w's type and K in the
+    // same launch, outputs [tokens][n_out] each (no peers or argmax then).
     int gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int tokens, cudaStream_t s, bool pdl = true,
              const float* d_x = nullptr, int ldy = 0, const q35k::GemvPeers* peers = nullptr,
-             unsigned long long* argmax = nullptr);
-    // Tensor-core prefill GEMM (Q4_K): quantize x, then the GEMM.
-    int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0);
+             unsigned long long* argmax = nullptr, const float* d_up = nullptr,
+             const q35k_weight* const* more_w = nullptr, float* const* more_y = nullptr, int n_more = 0);
+    // Tensor-core prefill GEMM (Q4_K): quantize x (silu(x) * up with d_up),
+    // then the GEMM.  prep == false: reuse the operands the previous call
+    // prepared from the same x (same K and token count).
+    int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0,
+             const float* d_up = nullptr, bool prep = true);
+    // Several weights of one K on one input (q35k_matmul_shared_dev).
+    int matmul_shared(const q35k_weight* const* ws, int count, const float* d_x, float* const* d_ys, int tokens,
+                      cudaStream_t s);
     // y[tokens][ldy] (columns below n_out) = x @ W^T on device pointers: the
     // dispatch behind q35k_matmul_dev (ldy = n_out) and the sharded calls.
     // With `peers` (sharded calls, fused all-gather) the call must take the
     // decode GEMV: tokens <= 8, else Q35K_ENOTSUP.
+    // With `d_up` the input is silu(x) * up (q35k_matmul_silu_dev).
     int matmul_into(const q35k_weight* w, const float* d_x, float* d_y, int ldy, int tokens, cudaStream_t s,
-                    const q35k::GemvPeers* peers = nullptr, unsigned long long* argmax = nullptr);
+                    const q35k::GemvPeers* peers = nullptr, unsigned long long* argmax = nullptr,
+                    const float* d_up = nullptr);
     unsigned long long* d_amax = nullptr;  // fused-argmax keys
     size_t amax_cap = 0;
 };

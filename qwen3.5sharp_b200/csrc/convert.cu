@@ -36,8 +36,9 @@ __device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int
     return o;
 }
 
-__global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, uint8_t* __restrict__ q8,
-                                                           int nb, int total_blocks, int rows, int chunk) {
+__global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, const float* __restrict__ up,
+                                                           uint8_t* __restrict__ q8, int nb, int total_blocks, int rows,
+                                                           int chunk) {
     // A GEMV launched after this kernel with programmatic stream
     // serialization may start now: it streams weights first and waits on the
     // grid dependency (full completion of this grid) before reading q8.
@@ -46,16 +47,18 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     const int lane = threadIdx.x & 31;
     if (warp >= total_blocks) return;
     const int row = warp / nb, b = warp % nb;
-    warp_quantize_q8k_block(x + (size_t)row * nb * QK + (size_t)b * QK, q8_out(q8, row, b, nb, rows, chunk), lane);
+    const size_t off = (size_t)row * nb * QK + (size_t)b * QK;
+    warp_quantize_q8k_block(x + off, q8_out(q8, row, b, nb, rows, chunk), lane, up ? up + off : nullptr);
 }
 
-cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s) {
+cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s,
+                                const float* up) {
     const int nb = k / QK;
     const int total = nb * rows;
     if (total == 0) return cudaSuccess;
     const int warps_per_cta = 8;
     const int grid = (total + warps_per_cta - 1) / warps_per_cta;
-    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, q8, nb, total, rows, planar_chunk);
+    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, up, q8, nb, total, rows, planar_chunk);
     return cudaGetLastError();
 }
 

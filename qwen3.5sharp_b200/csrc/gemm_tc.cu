@@ -176,9 +176,9 @@ static_assert(Geo<false, 128>::SMEM_BYTES == SMEM_BYTES && Geo<false, 128>::W_ST
 // order 0, 2, 1, 3; the MMA's K order only has to agree between its operands.
 // ---------------------------------------------------------------------------
 template <bool FAST>
-__global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, int k, int tokens, int m_pad,
-                                                       __half* __restrict__ xq, __half* __restrict__ xe,
-                                                       float* __restrict__ xd) {
+__global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, const float* __restrict__ up,
+                                                       int k, int tokens, int m_pad, __half* __restrict__ xq,
+                                                       __half* __restrict__ xe, float* __restrict__ xd) {
     griddep_launch_dependents();
     const int nb = k / QK;
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
         return;
     }
     int q[8];
-    const float d = warp_q8k_values(x + (size_t)r * k + (size_t)b * QK, lane, q);
+    const size_t off = (size_t)r * k + (size_t)b * QK;
+    const float d = warp_q8k_values(x + off, lane, q, up ? up + off : nullptr);
     __half* row = xq + (size_t)r * k + (size_t)b * QK;
     // Exact mode: the q values; fast mode: fp16(d q), the dequantized Q8_K
     // activations.  K order within each group of four values: 0, 2, 1, 3 (the
@@ -1140,14 +1141,14 @@ cudaError_t configure_tc_gemm() {
 }
 
 cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd, bool fast,
-                             cudaStream_t s) {
+                             cudaStream_t s, const float* up) {
     const int nb = k / QK;
     const long long warps = (long long)m_pad * nb;
     const int grid = (int)((warps + 7) / 8);
     if (fast)
-        gemm_prep_kernel<true><<<grid, 256, 0, s>>>(x, k, tokens, m_pad, static_cast<__half*>(xq), nullptr, nullptr);
+        gemm_prep_kernel<true><<<grid, 256, 0, s>>>(x, up, k, tokens, m_pad, static_cast<__half*>(xq), nullptr, nullptr);
     else
-        gemm_prep_kernel<false><<<grid, 256, 0, s>>>(x, k, tokens, m_pad, static_cast<__half*>(xq),
+        gemm_prep_kernel<false><<<grid, 256, 0, s>>>(x, up, k, tokens, m_pad, static_cast<__half*>(xq),
                                                      static_cast<__half*>(xe), xd);
     return cudaGetLastError();
 }

@@ -40,9 +40,10 @@ cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, i
 cudaError_t configure_tc_gemm();
 // Q8_K quantization of x [tokens][k] into the GEMM's operands.  Exact mode:
 // Xq [tokens][k] fp16 q values, Xe [tokens][k/256*16] fp16 block sums,
-// Xd [k/256][m_pad] d.  Fast mode: Xq = fp16(d q) only.
+// Xd [k/256][m_pad] d.  Fast mode: Xq = fp16(d q) only.  With `up` the rows
+// quantized are silu(x) * up (ffn_down's input).
 cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd, bool fast,
-                             cudaStream_t s);
+                             cudaStream_t s, const float* up = nullptr);
 // The GEMM; `pdl` lets it start while the preparation kernel finishes.
 // Exact mode forms the reference's integer dots and scales them per
 // super-block; fast mode multiplies fp16-rounded dequantized weights and

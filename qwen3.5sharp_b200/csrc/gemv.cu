@@ -100,6 +100,19 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = blockIdx.x / p.splits, s = blockIdx.x % p.splits;
     const int b0 = s * U;
+    // The matrix this row group belongs to (several weights per launch).
+    const uint8_t* wtiles = a.tiles;
+    float* y = a.y;
+    int n_out = a.n_out, ldy = a.ldy, gl = g;
+#pragma unroll
+    for (int k = 0; k < GEMV_MAX_MATS - 1; k++)
+        if (k < a.more.n && g >= a.more.g0[k]) {
+            wtiles = a.more.tiles[k];
+            y = a.more.y[k];
+            n_out = a.more.n_out[k];
+            ldy = a.more.ldy[k];
+            gl = g - a.more.g0[k];
+        }
     const int kr = min(U, nb - b0);
 
     if (tid == 0) {
@@ -112,7 +125,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     const int qs_bytes = kr * M * QK, d_bytes = kr * pl.rows4 * 4, bs_bytes = kr * M * 32;
     if (tid == 0) {
         // Weights first: they do not depend on the preceding kernel.
-        const uint8_t* src = a.tiles + ((size_t)g * nb + b0) * TILE;
+        const uint8_t* src = wtiles + ((size_t)gl * nb + b0) * TILE;
         for (int t = 0; t < kr; t++) {
             mbar_arrive_expect_tx(&bars[t], TILE);
             bulk_g2s(tiles + (size_t)t * TILE, src + (size_t)t * TILE, TILE, &bars[t]);
@@ -141,7 +154,8 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             out.d = reinterpret_cast<uint32_t*>(q8s + qs_bytes) + t * pl.rows4 + m;
             out.qs = reinterpret_cast<uint32_t*>(q8s + (size_t)(t * M + m) * QK);
             out.bs = reinterpret_cast<int16_t*>(q8s + qs_bytes + d_bytes) + (t * M + m) * 16;
-            warp_quantize_q8k_block(a.x + (size_t)m * a.ldx + (size_t)(b0 + t) * QK, out, lane);
+            const size_t off = (size_t)m * a.ldx + (size_t)(b0 + t) * QK;
+            warp_quantize_q8k_block(a.x + off, out, lane, a.up ? a.up + off : nullptr);
         }
         __syncthreads();
     } else {
@@ -164,7 +178,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     __syncthreads();
 
     if (warp == 0) {
-        const int row = g * TILE_ROWS + lane;
+        const int row = gl * TILE_ROWS + lane;
         float v[M];
 #pragma unroll
         for (int m = 0; m < M; m++) {
@@ -172,16 +186,16 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             for (int w = 1; w < W; w++) v[m] += red[(w * M + m) * 32 + lane];
         }
         if (p.splits == 1) {
-            if (row < a.n_out && a.y)
+            if (row < n_out && y)
 #pragma unroll
                 for (int m = 0; m < M; m++) {
-                    a.y[(size_t)m * a.ldy + row] = v[m];
-                    for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * a.ldy + row] = v[m];
+                    y[(size_t)m * ldy + row] = v[m];
+                    for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * ldy + row] = v[m];
                 }
             if (a.argmax)
 #pragma unroll
                 for (int m = 0; m < M; m++)
-                    warp_argmax_commit(row < a.n_out ? argmax_key(v[m], row) : 0ull, a.argmax + m, lane);
+                    warp_argmax_commit(row < n_out ? argmax_key(v[m], row) : 0ull, a.argmax + m, lane);
         } else {
             // Publish this K-range's piece; the last piece to arrive sums all
             // pieces in K order and resets the row group's counter.
@@ -199,11 +213,11 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
                 for (int m = 0; m < M; m++) {
                     float sum = 0.f;
                     for (int k = 0; k < p.splits; k++) sum += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
-                    if (row < a.n_out && a.y) {
-                        a.y[(size_t)m * a.ldy + row] = sum;
-                        for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * a.ldy + row] = sum;
+                    if (row < n_out && y) {
+                        y[(size_t)m * ldy + row] = sum;
+                        for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * ldy + row] = sum;
                     }
-                    if (a.argmax) warp_argmax_commit(row < a.n_out ? argmax_key(sum, row) : 0ull, a.argmax + m, lane);
+                    if (a.argmax) warp_argmax_commit(row < n_out ? argmax_key(sum, row) : 0ull, a.argmax + m, lane);
                 }
                 if (lane == 0) a.counters[g] = 0;
             }
@@ -341,8 +355,15 @@ cudaError_t launch_argmax_index(const unsigned long long* keys, int* idx, int to
     return cudaGetLastError();
 }
 
+int gemv_plan_rows(const GemvArgs& a) {
+    if (a.more.n <= 0) return a.n_out;
+    const int k = a.more.n - 1;
+    return a.more.g0[k] * TILE_ROWS + a.more.n_out[k];
+}
+
 cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl) {
-    const GemvPlan p = plan_gemv(type, a.nb, a.n_out, a.tokens, a.num_sms);
+    if (a.more.n < 0 || a.more.n > GEMV_MAX_MATS - 1) return cudaErrorInvalidValue;
+    const GemvPlan p = plan_gemv(type, a.nb, gemv_plan_rows(a), a.tokens, a.num_sms);
     switch (type) {
     case TYPE_Q4_K: return launch_m<TYPE_Q4_K>(a, p, s, pdl);
     case TYPE_Q5_K: return launch_m<TYPE_Q5_K>(a, p, s, pdl);

@@ -12,7 +12,10 @@ namespace q35k {
 // or the planar layout in chunks of planar_chunk rows.  The kernel lets a
 // dependent kernel launched with programmatic stream serialization start
 // early (that kernel must wait on the grid dependency before reading q8).
-cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s);
+// With `up` (laid out like x) the rows quantized are silu(x) * up (ffn_down's
+// input, QuantizeQ8Kx4.Quantize4x8Silu).
+cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s,
+                                const float* up = nullptr);
 
 // BlockQ8K rows -> planar layout in chunks of `chunk` rows.
 cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s);
@@ -34,6 +37,17 @@ struct GemvPeers {
     int n;
 };
 
+// Further weights of the same type and K sharing one launch and one set of
+// activations (q/k/v, gate/up): matrix k's row groups start at row group
+// g0[k] of the launch; its outputs go to y[k] with row stride ldy[k].
+constexpr int GEMV_MAX_MATS = 4;
+struct GemvMats {
+    const uint8_t* tiles[GEMV_MAX_MATS - 1];
+    float* y[GEMV_MAX_MATS - 1];
+    int n_out[GEMV_MAX_MATS - 1], ldy[GEMV_MAX_MATS - 1], g0[GEMV_MAX_MATS - 1];
+    int n;  // 0: one weight
+};
+
 struct GemvArgs {
     const uint8_t* tiles;  // uploaded weight tiles
     const uint8_t* q8;     // planar Q8_K of `tokens` rows (16-byte aligned), or
@@ -51,7 +65,13 @@ struct GemvArgs {
     // row) over all rows, combined with atomicMax; nullptr: off.  y may then
     // be nullptr (logits not written).
     unsigned long long* argmax;
+    // ffn_down's input (fused quantize only): the GEMV quantizes silu(x) * up,
+    // up laid out like x; nullptr: x itself.
+    const float* up;
+    GemvMats more;  // more weights in this launch (peers and argmax: one weight only)
 };
+// Row count the launch plans for: every matrix's rows, each padded to 32.
+int gemv_plan_rows(const GemvArgs& a);
 
 // Launch plan of the GEMV: one CTA per (row group, run of unit_blocks
 // super-blocks); deterministic in (type, nb, n_out, tokens, sms).

@@ -26,9 +26,20 @@ struct Q8Out {
 // The quantization itself: returns d (the same value on every lane) and this
 // lane's eight q values (q[0..3] = values 4l..4l+3, q[4..7] = 128+4l..+3).
 // An all-zero block gives d = 0 and q = 0.  src: 256 floats, 16-byte aligned.
-__device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, int lane, int (&q)[8]) {
-    const float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
-    const float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
+// With `up` (ffn_down's input): the block quantized is silu(src) * up, SiLU
+// as g / (1 + exp(-g)) in fp32 (Ops.SiLUMul, Qwen35Sharp.Model/Ops.cs:624-675).
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+__device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, int lane, int (&q)[8],
+                                                 const float* __restrict__ up = nullptr) {
+    float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
+    float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
+    if (up) {
+        const float4 u0 = __ldg(reinterpret_cast<const float4*>(up) + lane);
+        const float4 u1 = __ldg(reinterpret_cast<const float4*>(up + 128) + lane);
+        v0 = make_float4(silu_mul(v0.x, u0.x), silu_mul(v0.y, u0.y), silu_mul(v0.z, u0.z), silu_mul(v0.w, u0.w));
+        v1 = make_float4(silu_mul(v1.x, u1.x), silu_mul(v1.y, u1.y), silu_mul(v1.z, u1.z), silu_mul(v1.w, u1.w));
+    }
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 
     float amax = 0.f;
@@ -83,9 +94,10 @@ __device__ __forceinline__ void warp_q8k_bsums(const int (&q)[8], int& s0, int& 
 }
 
 // src: 256 floats, 16-byte aligned.  Writes d, qs, bsums through `out`.
-__device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict__ src, const Q8Out& out, int lane) {
+__device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict__ src, const Q8Out& out, int lane,
+                                                        const float* __restrict__ up = nullptr) {
     int q[8];
-    const float d = warp_q8k_values(src, lane, q);
+    const float d = warp_q8k_values(src, lane, q, up);
     if (lane == 0) *out.d = __float_as_uint(d);
     const uint32_t w0 =
         (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);

@@ -172,6 +172,32 @@ class Context:
         self._check(self.L.q35k_matmul_argmax(self.h, w.h, x.ctypes.data, idx.ctypes.data, tokens))
         return idx
 
+    def matmul_shared(self, ws: list, x: np.ndarray, tokens: int | None = None) -> list:
+        """Several weights with the same nIn on one input, one quantization of
+        it (q35k_matmul_shared; MulMatPanel.QuantizeAndGemm): [x @ W^T for W in ws]."""
+        if not ws or len(ws) > MAX_SHARED:
+            raise ArgumentException(f"1..{MAX_SHARED} weights per shared call")
+        x = _f32(x)
+        n_in = ws[0].n_in
+        tokens = x.size // n_in if tokens is None else tokens
+        if x.size < tokens * n_in:
+            raise ArgumentException("input is smaller than tokens * nIn")
+        ys = [np.empty((tokens, w.n_out), dtype=np.float32) for w in ws]
+        wa = (ctypes.c_void_p * len(ws))(*[w.h for w in ws])
+        ya = (ctypes.c_void_p * len(ws))(*[y.ctypes.data for y in ys])
+        self._check(self.L.q35k_matmul_shared(self.h, wa, len(ws), x.ctypes.data, ya, tokens))
+        return ys
+
+    def matmul_silu(self, w: "Weight", gate: np.ndarray, up: np.ndarray, tokens: int | None = None) -> np.ndarray:
+        """ffn_down on SiLU(gate) * up (q35k_matmul_silu; MulMatPanel.SiluQuantizeAndGemm)."""
+        gate, up = _f32(gate), _f32(up)
+        tokens = gate.size // w.n_in if tokens is None else tokens
+        if gate.size < tokens * w.n_in or up.size < tokens * w.n_in:
+            raise ArgumentException("gate/up is smaller than tokens * nIn")
+        y = np.empty((tokens, w.n_out), dtype=np.float32)
+        self._check(self.L.q35k_matmul_silu(self.h, w.h, gate.ctypes.data, up.ctypes.data, y.ctypes.data, tokens))
+        return y
+
     def matmul_q8k(self, w: "Weight", q8: np.ndarray, tokens: int) -> np.ndarray:
         q8 = _u8(q8)
         if q8.size < tokens * (w.n_in // QK) * Q8K_BYTES:
@@ -205,6 +231,15 @@ class Context:
         """d_y may be None (logits not written); d_idx: int32[tokens]."""
         self._check(self.L.q35k_matmul_argmax_dev(self.h, w.h, _dev_ptr(d_x), _dev_ptr(d_y) if d_y is not None else None,
                                                   _dev_ptr(d_idx), tokens, _stream(stream)))
+
+    def matmul_shared_dev(self, ws: list, d_x, d_ys: list, tokens: int, stream=None):
+        wa = (ctypes.c_void_p * len(ws))(*[w.h for w in ws])
+        ya = (ctypes.c_void_p * len(d_ys))(*[_dev_ptr(y) for y in d_ys])
+        self._check(self.L.q35k_matmul_shared_dev(self.h, wa, len(ws), _dev_ptr(d_x), ya, tokens, _stream(stream)))
+
+    def matmul_silu_dev(self, w: "Weight", d_gate, d_up, d_y, tokens: int, stream=None):
+        self._check(self.L.q35k_matmul_silu_dev(self.h, w.h, _dev_ptr(d_gate), _dev_ptr(d_up), _dev_ptr(d_y), tokens,
+                                                _stream(stream)))
 
     def matmul_q8k_dev(self, w: "Weight", d_q8, d_y, tokens: int, stream=None):
         self._check(self.L.q35k_matmul_q8k_dev(self.h, w.h, _dev_ptr(d_q8), _dev_ptr(d_y), tokens, _stream(stream)))
@@ -248,6 +283,7 @@ class Weight:
 
 GATHER_NCCL, GATHER_PEER, GATHER_FUSED = _lib.GATHER_NCCL, _lib.GATHER_PEER, _lib.GATHER_FUSED
 GEMM_EXACT, GEMM_FAST = _lib.GEMM_EXACT, _lib.GEMM_FAST
+MAX_SHARED = _lib.MAX_SHARED
 
 
 def shard_rows(n_out: int, nranks: int) -> int:

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libq35k.so")
 OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL = 0, 1, 2, 3, 4, 5, 6
 GATHER_NCCL, GATHER_PEER, GATHER_FUSED = 0, 1, 2
 GEMM_EXACT, GEMM_FAST = 0, 1
+MAX_SHARED = 4
 NCCL_ID_BYTES = 128
 
 # Symbols declared in include/q35k.h, with their ctypes signatures.
@@ -36,6 +37,10 @@ SIGNATURES = {
     "q35k_matmul_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_matmul_argmax": ([_vp, _vp, _vp, _vp, _i32], _i32),
     "q35k_matmul_argmax_dev": ([_vp, _vp, _vp, _vp, _vp, _i32, _vp], _i32),
+    "q35k_matmul_shared": ([_vp, _pp, _i32, _vp, _pp, _i32], _i32),
+    "q35k_matmul_shared_dev": ([_vp, _pp, _i32, _vp, _pp, _i32, _vp], _i32),
+    "q35k_matmul_silu": ([_vp, _vp, _vp, _vp, _vp, _i32], _i32),
+    "q35k_matmul_silu_dev": ([_vp, _vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_matmul_q8k_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_quantize_q8k": ([_vp, _vp, _vp, _i32, _i32], _i32),
     "q35k_quantize_q8k_dev": ([_vp, _vp, _vp, _i32, _i32, _vp], _i32),
