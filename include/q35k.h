@@ -166,6 +166,12 @@ int q35k_set_gemm_mode(q35k_ctx* ctx, int mode);
  * bit-exact BlockQ8K bytes (rows * k/256 * 292). */
 int q35k_quantize_q8k(q35k_ctx* ctx, const float* x, void* q8k, int k, int rows);
 int q35k_quantize_q8k_dev(q35k_ctx* ctx, const float* d_x, void* d_q8k, int k, int rows, void* stream);
+/* The same on silu(gate) * up, the product formed inside the quantizer:
+ * QuantizeQ8Kx4.Quantize4x8Silu (Kernels/QuantizeQ8Kx4.cs:24-35) in the
+ * BlockQ8K layout (the quantization of q35k_matmul_silu). */
+int q35k_quantize_q8k_silu(q35k_ctx* ctx, const float* gate, const float* up, void* q8k, int k, int rows);
+int q35k_quantize_q8k_silu_dev(q35k_ctx* ctx, const float* d_gate, const float* d_up, void* d_q8k, int k, int rows,
+                               void* stream);
 
 /* Q4K/Q5K/Q6K.DequantizeRow (Kernels/Q4K.cs:35-60, Kernels/Q5K.cs:5-35,
  * Kernels/Q6K.cs:9-39) on `rows` rows of k values: bit-exact fp32. */

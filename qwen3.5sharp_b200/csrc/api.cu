@@ -666,19 +666,21 @@ int q35k_matmul_q8k(q35k_ctx* c, const q35k_weight* w, const void* q8k, float* y
     return Q35K_OK;
 }
 
-int q35k_quantize_q8k_dev(q35k_ctx* c, const float* d_x, void* d_q8k, int k, int rows, void* stream) {
+// Q8_K rows of x, or of silu(x) * up (up != nullptr).
+static int quantize_dev(q35k_ctx* c, const float* d_x, const float* d_up, void* d_q8k, int k, int rows, void* stream) {
     if (!c) return Q35K_EINVAL;
     if (!d_x || !d_q8k) return c->fail(Q35K_EINVAL, "NULL pointer");
     if (k <= 0 || k % QK) return c->fail(Q35K_EINVAL, "k=%d is not a multiple of 256", k);
     if (rows <= 0) return c->fail(Q35K_EINVAL, "rows must be positive");
     int rc = check_alignment(c, d_x, 16, d_q8k, 4);
     if (rc) return rc;
+    if (d_up && (rc = check_alignment(c, d_up, 16, d_q8k, 4)) != Q35K_OK) return rc;
     cudaSetDevice(c->device);
-    cudaError_t e = launch_quantize_q8k(d_x, (uint8_t*)d_q8k, k, rows, 0, pick(c, stream));
+    cudaError_t e = launch_quantize_q8k(d_x, (uint8_t*)d_q8k, k, rows, 0, pick(c, stream), d_up);
     return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "Q8_K quantize launch");
 }
 
-int q35k_quantize_q8k(q35k_ctx* c, const float* x, void* q8k, int k, int rows) {
+static int quantize_host(q35k_ctx* c, const float* x, const float* up, void* q8k, int k, int rows) {
     if (!c) return Q35K_EINVAL;
     if (!x || !q8k) return c->fail(Q35K_EINVAL, "NULL pointer");
     if (k <= 0 || k % QK) return c->fail(Q35K_EINVAL, "k=%d is not a multiple of 256", k);
@@ -686,14 +688,33 @@ int q35k_quantize_q8k(q35k_ctx* c, const float* x, void* q8k, int k, int rows) {
     cudaSetDevice(c->device);
     const size_t in_bytes = (size_t)rows * k * sizeof(float);
     const size_t out_bytes = (size_t)rows * (k / QK) * Q8K_BYTES;
+    const int n_in = up ? 2 : 1;
     int rc;
-    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
+    if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, n_in * in_bytes, false)) != Q35K_OK) return rc;
     if ((rc = c->ensure_dev((void**)&c->d_q8raw, &c->q8raw_cap, out_bytes, false)) != Q35K_OK) return rc;
+    const float* d_up = up ? (const float*)((const char*)c->d_x + in_bytes) : nullptr;
     cudaError_t e = cudaMemcpyAsync(c->d_x, x, in_bytes, cudaMemcpyHostToDevice, c->stream);
-    if (e == cudaSuccess) e = launch_quantize_q8k(c->d_x, c->d_q8raw, k, rows, 0, c->stream);
+    if (e == cudaSuccess && up) e = cudaMemcpyAsync((void*)d_up, up, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_quantize_q8k(c->d_x, c->d_q8raw, k, rows, 0, c->stream, d_up);
     if (e == cudaSuccess) e = cudaMemcpyAsync(q8k, c->d_q8raw, out_bytes, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     return e == cudaSuccess ? Q35K_OK : c->cuda_fail(e, "quantize_q8k");
+}
+
+int q35k_quantize_q8k_dev(q35k_ctx* c, const float* d_x, void* d_q8k, int k, int rows, void* stream) {
+    return quantize_dev(c, d_x, nullptr, d_q8k, k, rows, stream);
+}
+int q35k_quantize_q8k(q35k_ctx* c, const float* x, void* q8k, int k, int rows) {
+    return quantize_host(c, x, nullptr, q8k, k, rows);
+}
+int q35k_quantize_q8k_silu_dev(q35k_ctx* c, const float* d_gate, const float* d_up, void* d_q8k, int k, int rows,
+                               void* stream) {
+    if (c && !d_up) return c->fail(Q35K_EINVAL, "NULL pointer");
+    return quantize_dev(c, d_gate, d_up, d_q8k, k, rows, stream);
+}
+int q35k_quantize_q8k_silu(q35k_ctx* c, const float* gate, const float* up, void* q8k, int k, int rows) {
+    if (c && !up) return c->fail(Q35K_EINVAL, "NULL pointer");
+    return quantize_host(c, gate, up, q8k, k, rows);
 }
 
 int q35k_dequantize_dev(q35k_ctx* c, int type, const void* d_blocks, float* d_y, int k, int rows, void* stream) {

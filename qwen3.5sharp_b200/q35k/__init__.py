@@ -214,6 +214,17 @@ class Context:
         self._check(self.L.q35k_quantize_q8k(self.h, x.ctypes.data, out.ctypes.data, k, rows))
         return out
 
+    def quantize_q8k_silu(self, gate: np.ndarray, up: np.ndarray, k: int | None = None) -> np.ndarray:
+        """BlockQ8K bytes of silu(gate) * up (QuantizeQ8Kx4.Quantize4x8Silu)."""
+        gate, up = _f32(gate), _f32(up)
+        k = gate.shape[-1] if k is None else k
+        rows = gate.size // k
+        if up.size < rows * k:
+            raise ArgumentException("up is smaller than gate")
+        out = np.empty((rows, (k // QK) * Q8K_BYTES), dtype=np.uint8)
+        self._check(self.L.q35k_quantize_q8k_silu(self.h, gate.ctypes.data, up.ctypes.data, out.ctypes.data, k, rows))
+        return out
+
     def dequantize(self, qtype: int, blocks: np.ndarray, k: int, rows: int | None = None) -> np.ndarray:
         blocks = _u8(blocks)
         bb = BLOCK_BYTES.get(qtype, 1)

@@ -44,6 +44,8 @@ SIGNATURES = {
     "q35k_matmul_q8k_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_quantize_q8k": ([_vp, _vp, _vp, _i32, _i32], _i32),
     "q35k_quantize_q8k_dev": ([_vp, _vp, _vp, _i32, _i32, _vp], _i32),
+    "q35k_quantize_q8k_silu": ([_vp, _vp, _vp, _vp, _i32, _i32], _i32),
+    "q35k_quantize_q8k_silu_dev": ([_vp, _vp, _vp, _vp, _i32, _i32, _vp], _i32),
     "q35k_dequantize": ([_vp, _i32, _vp, _vp, _i32, _i32], _i32),
     "q35k_dequantize_dev": ([_vp, _i32, _vp, _vp, _i32, _i32, _vp], _i32),
     "q35k_shard_create": ([_i32, ctypes.POINTER(_i32), _pp], _i32),

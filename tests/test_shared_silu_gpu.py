@@ -141,6 +141,60 @@ def test_silu_agrees_with_the_oracle(ctx, oracle_mod, mode):
         assert rel(y, r) <= TOL, (qt, m, rel(y, r))
 
 
+def q8k_fields(b, k):
+    """(d [rows, nb], qs [rows, nb, 256]) of BlockQ8K bytes."""
+    blocks = b.reshape(-1, k // 256, 292)
+    d = blocks[:, :, :4].copy().view(np.float32)[..., 0]
+    qs = blocks[:, :, 4:260].view(np.int8)
+    return d, qs
+
+
+def test_quantize_silu_matches_silu_then_quantize(ctx, oracle_mod):
+    # The reference's own check of its fused quantizer
+    # (Qwen35Sharp.Tests/FastExpTests.cs:52-81): four rows of 256 with these
+    # inputs, d within 1e-4 and every q equal to quantizing the product.
+    k = 256
+    i = np.arange(4 * k)
+    gate = ((i % 17 - 8) * 0.2).astype(np.float32).reshape(4, k)
+    up = (0.5 + (i % 9) * 0.05).astype(np.float32).reshape(4, k)
+    got = ctx.quantize_q8k_silu(gate, up)
+    exp = oracle_mod.quantize_q8k(silu_mul(gate, up))
+    (dg, qg), (de, qe) = q8k_fields(got, k), q8k_fields(exp, k)
+    assert np.abs(dg - de).max() < 1e-4
+    assert (qg == qe).all()
+    # and against the GPU's own quantizer of a device-formed product
+    (dd, qd) = q8k_fields(ctx.quantize_q8k(device_silu_mul(gate, up)), k)
+    assert np.abs(dg - dd).max() < 1e-4
+    assert (qg == qd).all()
+
+
+def test_quantize_silu_random_rows(ctx, oracle_mod):
+    k, rows = 2560, 6
+    gate = synth.activations(rows, k, seed=21, scale=3.0)
+    up = synth.activations(rows, k, seed=22)
+    (dg, qg) = q8k_fields(ctx.quantize_q8k_silu(gate, up), k)
+    (de, qe) = q8k_fields(oracle_mod.quantize_q8k(silu_mul(gate, up)), k)
+    assert (np.abs(dg - de) <= 1e-6 * np.abs(de)).all()
+    # a product a few ulp from numpy's can land on the other side of a
+    # rounding boundary: one code in thousands at most, by one step
+    diff = qg.astype(np.int32) - qe.astype(np.int32)
+    assert np.abs(diff).max() <= 1 and (diff != 0).mean() < 1e-3
+
+
+@pytest.mark.parametrize("qt,k,n,m", [(Q4_K, 2560, 1024, 1), (Q6_K, 9728, 2560, 1), (Q5_K, 9728, 2560, 5)])
+def test_silu_gemv_quantizes_like_the_standalone_quantizer(ctx, qt, k, n, m):
+    # The GEMV's own (fused) quantization and the quantize kernel give the
+    # same bytes: matmul_silu == matmul_q8k(quantize_q8k_silu) exactly.
+    w = synth.kquant_blocks(qt, n, k, seed=n + 5)
+    g = synth.activations(m, k, seed=31, scale=2.0)
+    u = synth.activations(m, k, seed=32)
+    W = ctx.upload(qt, w, k, n)
+    y = ctx.matmul_silu(W, g, u)
+    r = ctx.matmul_q8k(W, ctx.quantize_q8k_silu(g, u), m)
+    W.free()
+    assert (y == r).all()
+
+
 def test_device_variants(ctx):
     torch = pytest.importorskip("torch")
     k, m = 2560, 2
