@@ -42,6 +42,8 @@ extern "C" {
 #define Q35K_ECUDA 4    /* CUDA runtime error     -> InvalidOperationException */
 #define Q35K_ETIMEOUT 5 /* a bounded device wait expired -> TimeoutException */
 #define Q35K_ENCCL 6    /* NCCL error             -> InvalidOperationException */
+#define Q35K_EDATA 7    /* malformed/truncated GGUF -> InvalidDataException */
+#define Q35K_EIO 8      /* file cannot be opened/mapped -> IOException */
 
 /* GGML tensor type codes (src/Qwen35Sharp.Gguf/GgmlTensorType.cs). */
 #define Q35K_TYPE_Q4_K 12
@@ -252,6 +254,45 @@ int q35k_shard_matmul(q35k_shard* s, const q35k_sharded_weight* w, const float* 
 #define Q35K_STATIC_MAX_TOKENS 8
 #define Q35K_STATIC_SCRATCH_BYTES (8u << 20)
 int q35k_matmul_static_dev(const q35k_weight* w, const float* d_x, float* d_y, int tokens, void* stream);
+
+/* ---- GGUF ingestion ------------------------------------------------------ */
+
+/* A GGUF v2/v3 file, memory-mapped read-only with its metadata and tensor
+ * table parsed at open: Qwen35Sharp.Gguf/GgufFile.cs (constructor :27-60,
+ * Parse :110-172).  Malformed or truncated files give Q35K_EDATA (the
+ * reference's InvalidDataException / EndOfStreamException), versions other
+ * than 2 and 3 Q35K_ENOTSUP, a file that cannot be opened Q35K_EIO; the
+ * message is in q35k_last_error(NULL).  Host only: no GPU is needed. */
+typedef struct q35k_gguf q35k_gguf;
+int q35k_gguf_open(const char* path, q35k_gguf** out);
+int q35k_gguf_close(q35k_gguf* g);
+/* Version, tensor count, general.alignment (default 32) and the file offset
+ * of the aligned data section (GgufFile.DataBase). */
+int q35k_gguf_info(const q35k_gguf* g, int* version, int* n_tensors, uint32_t* alignment, uint64_t* data_offset);
+/* Index of the tensor `name` (the last one of that name), or -1. */
+int q35k_gguf_find(const q35k_gguf* g, const char* name);
+/* Tensor `index` in file order: name (valid until close), ggml type, dim
+ * count and dims (GGUF order, dim 0 innermost; unused dims reported as 1),
+ * offset from the data section (GgufTensorInfo, GgufTensorInfo.cs). */
+int q35k_gguf_tensor(const q35k_gguf* g, int index, const char** name, int* type, int* n_dims, int64_t* dims4,
+                     uint64_t* offset);
+/* Host pointer to `bytes` bytes of tensor `index` in the mapping
+ * (Q35K_EDATA if they run past the end of the file). */
+int q35k_gguf_tensor_data(const q35k_gguf* g, int index, size_t bytes, const void** data);
+/* Metadata scalars (GgufFile.GetInt32/GetUint32/GetFloat32/GetString,
+ * GgufFile.cs:62-99): integers of any width (bool is not an integer), floats
+ * (integers coerced), strings (valid until close); arrays report their
+ * element type and length.  Q35K_EINVAL when the key is missing or of
+ * another kind. */
+int q35k_gguf_get_int(const q35k_gguf* g, const char* key, int64_t* value);
+int q35k_gguf_get_float(const q35k_gguf* g, const char* key, double* value);
+int q35k_gguf_get_string(const q35k_gguf* g, const char* key, const char** value);
+int q35k_gguf_get_array(const q35k_gguf* g, const char* key, int* elem_type, uint64_t* count);
+/* Upload the Q4_K/Q5_K/Q6_K tensor `name` straight from the mapping, as
+ * LoadWeights does for each quantized tensor (Model/Qwen35Model.cs:463-565):
+ * nIn = dims[0], nOut = dims[1]; a stack of matrices (experts) or nIn not a
+ * multiple of 256 gives Q35K_ENOTSUP, another type Q35K_ENOTSUP. */
+int q35k_weight_upload_gguf(q35k_ctx* ctx, const q35k_gguf* g, const char* name, q35k_weight** out);
 
 #ifdef __cplusplus
 }

@@ -2,7 +2,7 @@
 
     python qwen3.5sharp_b200/build.py [--force]
 
-Compiles every csrc/*.cu with nvcc for sm_100a only and links one shared
+Compiles every csrc/*.cu (and the host-only csrc/*.cpp) with nvcc for sm_100a only and links one shared
 library next to this file, so it travels with the source tree.
 """
 
@@ -36,7 +36,7 @@ def nvcc() -> str:
 
 
 def sources() -> list[str]:
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def headers() -> list[str]:

@@ -36,7 +36,8 @@ from .synth import BLOCK_BYTES, Q4_K, Q5_K, Q6_K, Q8K_BYTES, QK
 __all__ = [
     "Context", "Weight", "MulMatQ4K", "Q4K", "Q5K", "Q6K", "Q8K", "default_context",
     "ArgumentException", "NotSupportedException", "InsufficientMemoryException",
-    "InvalidOperationException", "TimeoutException", "Q4_K", "Q5_K", "Q6_K", "QK",
+    "InvalidOperationException", "TimeoutException", "InvalidDataException", "GgufIOException", "GgufFile",
+    "GgufTensorInfo", "Q4_K", "Q5_K", "Q6_K", "QK",
 ]
 
 
@@ -64,6 +65,17 @@ class TimeoutException(Q35KError, TimeoutError):
     code = _lib.ETIMEOUT
 
 
+class InvalidDataException(Q35KError, ValueError):
+    """A malformed or truncated GGUF file (the reference's
+    InvalidDataException / EndOfStreamException)."""
+    code = _lib.EDATA
+
+
+class GgufIOException(Q35KError, OSError):
+    """A GGUF file that cannot be opened or mapped (IOException)."""
+    code = _lib.EIO
+
+
 _EXC = {
     _lib.EINVAL: ArgumentException,
     _lib.ENOTSUP: NotSupportedException,
@@ -71,6 +83,8 @@ _EXC = {
     _lib.ECUDA: InvalidOperationException,
     _lib.ETIMEOUT: TimeoutException,
     _lib.ENCCL: InvalidOperationException,
+    _lib.EDATA: InvalidDataException,
+    _lib.EIO: GgufIOException,
 }
 
 
@@ -150,6 +164,14 @@ class Context:
         h = ctypes.c_void_p()
         self._check(self.L.q35k_weight_upload(self.h, qtype, blocks.ctypes.data, n_in, n_out, ctypes.byref(h)))
         return Weight(self, h, qtype, n_in, n_out)
+
+    def upload_gguf(self, gguf: "GgufFile", name: str) -> "Weight":
+        """Upload a Q4_K/Q5_K/Q6_K tensor straight from a mapped GGUF file
+        (q35k_weight_upload_gguf; LoadWeights, Model/Qwen35Model.cs:463-565)."""
+        h = ctypes.c_void_p()
+        self._check(self.L.q35k_weight_upload_gguf(self.h, gguf.h, name.encode(), ctypes.byref(h)))
+        info = gguf.tensors[name]
+        return Weight(self, h, info.type, int(info.shape[0]), int(info.shape[1]) if len(info.shape) > 1 else 1)
 
     # -- host-pointer calls (synchronous) --
     def matmul(self, w: "Weight", x: np.ndarray, tokens: int | None = None) -> np.ndarray:
@@ -261,6 +283,103 @@ class Context:
     def dequantize_dev(self, qtype: int, d_blocks, d_y, k: int, rows: int, stream=None):
         self._check(self.L.q35k_dequantize_dev(self.h, qtype, _dev_ptr(d_blocks), _dev_ptr(d_y), k, rows,
                                                _stream(stream)))
+
+
+class GgufTensorInfo:
+    """Type, shape (GGUF order, dim 0 innermost) and data-section offset of
+    one tensor (Qwen35Sharp.Gguf/GgufTensorInfo.cs)."""
+
+    def __init__(self, name: str, type: int, shape: tuple, offset: int):
+        self.name, self.type, self.shape, self.offset = name, type, shape, offset
+
+    @property
+    def num_elements(self) -> int:
+        n = 1
+        for d in self.shape:
+            n *= d
+        return n
+
+    def __repr__(self):
+        return f"GgufTensorInfo({self.name!r}, type={self.type}, shape={self.shape}, offset={self.offset})"
+
+
+class GgufFile:
+    """A memory-mapped GGUF v2/v3 file (q35k_gguf_open; Qwen35Sharp.Gguf/
+    GgufFile.cs).  Host only: needs libq35k.so but no GPU."""
+
+    def __init__(self, path: str):
+        self.L = _lib.load()
+        h = ctypes.c_void_p()
+        rc = self.L.q35k_gguf_open(str(path).encode(), ctypes.byref(h))
+        if rc != _lib.OK:
+            _raise(rc, self.L.q35k_last_error(None).decode())
+        self.h = h
+        ver, n, al, off = ctypes.c_int(), ctypes.c_int(), ctypes.c_uint32(), ctypes.c_uint64()
+        self.L.q35k_gguf_info(h, ctypes.byref(ver), ctypes.byref(n), ctypes.byref(al), ctypes.byref(off))
+        self.version, self.alignment, self.data_offset = ver.value, al.value, off.value
+        self.tensors: dict[str, GgufTensorInfo] = {}
+        self._index: dict[str, int] = {}
+        name, ty, nd, off = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int(), ctypes.c_uint64()
+        dims = (ctypes.c_int64 * 4)()
+        for i in range(n.value):
+            self.L.q35k_gguf_tensor(h, i, ctypes.byref(name), ctypes.byref(ty), ctypes.byref(nd), dims,
+                                    ctypes.byref(off))
+            nm = name.value.decode()
+            self.tensors[nm] = GgufTensorInfo(nm, ty.value, tuple(dims[d] for d in range(nd.value)), off.value)
+            self._index[nm] = i
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.q35k_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def data(self, name: str, nbytes: int) -> np.ndarray:
+        """A copy of the first nbytes bytes of tensor `name`."""
+        p = ctypes.c_void_p()
+        rc = self.L.q35k_gguf_tensor_data(self.h, self._index[name], nbytes, ctypes.byref(p))
+        if rc != _lib.OK:
+            _raise(rc, self.L.q35k_last_error(None).decode())
+        return np.ctypeslib.as_array((ctypes.c_uint8 * nbytes).from_address(p.value)).copy() if nbytes else \
+            np.empty(0, np.uint8)
+
+    def get_int(self, key: str, default: int | None = None) -> int:
+        v = ctypes.c_int64()
+        if self.L.q35k_gguf_get_int(self.h, key.encode(), ctypes.byref(v)) != _lib.OK:
+            if default is None:
+                raise KeyError(f"GGUF missing or non-integer key '{key}'")
+            return default
+        return v.value
+
+    def get_float(self, key: str, default: float = 0.0) -> float:
+        v = ctypes.c_double()
+        if self.L.q35k_gguf_get_float(self.h, key.encode(), ctypes.byref(v)) != _lib.OK:
+            return default
+        return v.value
+
+    def get_string(self, key: str, default: str = "") -> str:
+        v = ctypes.c_char_p()
+        if self.L.q35k_gguf_get_string(self.h, key.encode(), ctypes.byref(v)) != _lib.OK:
+            return default
+        return v.value.decode("utf-8", errors="replace")
+
+    def get_array(self, key: str):
+        """(element type, length) of an array value, or None."""
+        t, n = ctypes.c_int(), ctypes.c_uint64()
+        if self.L.q35k_gguf_get_array(self.h, key.encode(), ctypes.byref(t), ctypes.byref(n)) != _lib.OK:
+            return None
+        return t.value, n.value
 
 
 class Weight:

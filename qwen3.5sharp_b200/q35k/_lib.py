@@ -13,7 +13,7 @@ import threading
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "libq35k.so")
 
-OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL = 0, 1, 2, 3, 4, 5, 6
+OK, EINVAL, ENOTSUP, ENOMEM, ECUDA, ETIMEOUT, ENCCL, EDATA, EIO = 0, 1, 2, 3, 4, 5, 6, 7, 8
 GATHER_NCCL, GATHER_PEER, GATHER_FUSED = 0, 1, 2
 GEMM_EXACT, GEMM_FAST = 0, 1
 MAX_SHARED = 4
@@ -61,6 +61,19 @@ SIGNATURES = {
     "q35k_shard_matmul": ([_vp, _vp, _vp, _vp, _i32, _i32], _i32),
     "q35k_set_gemm_mode": ([_vp, _i32], _i32),
     "q35k_matmul_static_dev": ([_vp, _vp, _vp, _i32, _vp], _i32),
+    "q35k_gguf_open": ([ctypes.c_char_p, _pp], _i32),
+    "q35k_gguf_close": ([_vp], _i32),
+    "q35k_gguf_info": ([_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_uint32),
+                        ctypes.POINTER(ctypes.c_uint64)], _i32),
+    "q35k_gguf_find": ([_vp, ctypes.c_char_p], _i32),
+    "q35k_gguf_tensor": ([_vp, _i32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                          ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_uint64)], _i32),
+    "q35k_gguf_tensor_data": ([_vp, _i32, _sz, _pp], _i32),
+    "q35k_gguf_get_int": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)], _i32),
+    "q35k_gguf_get_float": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)], _i32),
+    "q35k_gguf_get_string": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)], _i32),
+    "q35k_gguf_get_array": ([_vp, ctypes.c_char_p, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_uint64)], _i32),
+    "q35k_weight_upload_gguf": ([_vp, _vp, ctypes.c_char_p, _pp], _i32),
 }
 
 _lib = None
