@@ -30,7 +30,13 @@ __device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int
         const Q8Planar pl = q8_planar(mj, nb);
         const size_t blk = (size_t)b * mj + rr;  // block-major
         o.d = reinterpret_cast<uint32_t*>(base + pl.d) + (size_t)b * pl.rows4 + rr;
-        o.qs = reinterpret_cast<uint32_t*>(base + pl.qs + blk * QK);
+        if (mj >= Q8_INTERLEAVE_MIN_ROWS) {
+            // word w of row rr at word w * mj + rr of the block's qs
+            o.qs = reinterpret_cast<uint32_t*>(base + pl.qs + (size_t)b * mj * QK) + rr;
+            o.qs_stride = mj;
+        } else {
+            o.qs = reinterpret_cast<uint32_t*>(base + pl.qs + blk * QK);
+        }
         o.bs = reinterpret_cast<int16_t*>(base + pl.bs + blk * 32);
     }
     return o;
@@ -73,8 +79,8 @@ __global__ void __launch_bounds__(256) q8k_to_planar_kernel(const uint8_t* __res
     const uint32_t* in = reinterpret_cast<const uint32_t*>(src + (size_t)warp * Q8K_BYTES);
     const Q8Out out = q8_out(dst, warp / nb, warp % nb, nb, rows, chunk);
     if (lane == 0) *out.d = __ldg(in);
-    out.qs[lane] = __ldg(in + 1 + lane);
-    out.qs[32 + lane] = __ldg(in + 33 + lane);
+    out.qs[lane * out.qs_stride] = __ldg(in + 1 + lane);
+    out.qs[(32 + lane) * out.qs_stride] = __ldg(in + 33 + lane);
     if (lane < 8) reinterpret_cast<uint32_t*>(out.bs)[lane] = __ldg(in + 65 + lane);
 }
 

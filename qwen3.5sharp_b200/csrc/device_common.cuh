@@ -57,8 +57,12 @@ __host__ __device__ inline int block_bytes(int type) {
 //   to 4) | bsums [nb][rows][16] int16.
 // Tokens are grouped in chunks of `chunk` rows (one GEMV launch each); chunk
 // j starts at j * q8_planar(chunk, nb).bytes and its planes are sized by its
-// own row count.
+// own row count.  In a chunk of Q8_INTERLEAVE_MIN_ROWS or more rows the qs
+// plane is word-interleaved instead, [nb][64][rows] 32-bit words (word w =
+// values 4w..4w+3): the layout in which the tensor-core GEMV (gemv_dot.cuh)
+// reads its B fragments, one conflict-free 32-bit load per lane.
 // ---------------------------------------------------------------------------
+constexpr int Q8_INTERLEAVE_MIN_ROWS = 5;
 struct Q8Planar {
     size_t qs, d, bs, bytes;
     int rows, rows4;

@@ -31,6 +31,9 @@ constexpr int GEMV_MAX_TOKENS = 8;
 constexpr int GEMV_MAX_WARPS = 20;        // one warp per tile of a whole-row unit
 constexpr int GEMV_SPLIT_WARPS = 10;      // warps of a split-K unit
 constexpr int GEMV_FUSED_MAX_TOKENS = 2;  // token counts with a fused-quantize variant
+// The fused quantizer writes the plain planar layout; 5+ tokens take the
+// tensor-core dots over the word-interleaved one.
+static_assert(GEMV_FUSED_MAX_TOKENS < Q8_INTERLEAVE_MIN_ROWS, "fused GEMV layouts");
 constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per split-K work unit (target)
 constexpr int GEMV_ROW_BYTES = 96 * 1024;   // largest whole-row unit
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
@@ -162,19 +165,39 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
         ok = mbar_wait_bounded(&bars[kr], 0, a.err);
     }
 
-    float acc[M];
-#pragma unroll
-    for (int m = 0; m < M; m++) acc[m] = 0.f;
-    for (int t = warp; ok && t < kr; t += W) {
-        if (!mbar_wait_bounded(&bars[t], 0, a.err)) {
-            ok = false;
-            break;
-        }
-        tile_dot<TYPE, M>(tiles + (size_t)t * TILE, lane, q8, t, acc);
-    }
     float* red = reinterpret_cast<float*>(smem + L.red);
+    if constexpr (M >= Q8_INTERLEAVE_MIN_ROWS) {
+        // Tensor-core dots (gemv_dot.cuh); the staged qs plane is word-interleaved.
+        float acc[2][2][2] = {};
+        for (int t = warp; ok && t < kr; t += W) {
+            if (!mbar_wait_bounded(&bars[t], 0, a.err)) {
+                ok = false;
+                break;
+            }
+            tile_dot_mma<TYPE, M>(tiles + (size_t)t * TILE, lane, q8, t, acc);
+        }
+        const int g = lane >> 2, c = lane & 3;
 #pragma unroll
-    for (int m = 0; m < M; m++) red[(warp * M + m) * 32 + lane] = acc[m];
+        for (int hf = 0; hf < 2; hf++)
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+                    if (2 * c + j < M) red[(warp * M + 2 * c + j) * 32 + 16 * hf + 8 * i + g] = acc[hf][i][j];
+    } else {
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; m++) acc[m] = 0.f;
+        for (int t = warp; ok && t < kr; t += W) {
+            if (!mbar_wait_bounded(&bars[t], 0, a.err)) {
+                ok = false;
+                break;
+            }
+            tile_dot<TYPE, M>(tiles + (size_t)t * TILE, lane, q8, t, acc);
+        }
+#pragma unroll
+        for (int m = 0; m < M; m++) red[(warp * M + m) * 32 + lane] = acc[m];
+    }
     __syncthreads();
 
     if (warp == 0) {

@@ -11,6 +11,8 @@
 
 #include "device_common.cuh"
 
+#include <cuda_fp16.h>
+
 namespace q35k {
 
 // dp4a with unsigned a bytes (0..255) and signed b bytes.
@@ -186,6 +188,239 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
         bias = __dp2a_lo(b1.z, (int)s4[3], bias);
         bias = __dp2a_hi(b1.w, (int)s4[3], bias);
         acc[m] = fmaf(d * q8.dx(m, b), (float)(S[m] - 32 * bias), acc[m]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core form for 5..8 tokens (legacy mma.sync: the weights' decode, not
+// the MACs, bounds this HBM-streaming kernel, so the point is fewer
+// instructions per weight, not tcgen05 throughput).  Its cost per tile does
+// not depend on the token count (an mma always spans 8 token columns), while
+// the dp4a form's grows with it: on B200 the two cross between 4 and 5 tokens.  A warp computes its
+// 32-row tile as two m16 halves x 8 token columns.  Lane (g = lane/4,
+// c = lane%4) supplies rows g, g+8 of a half and token g of the B operand:
+//   * integer dots per sub-block: mma m16n8k32 u8 x s8 (Q4_K/Q5_K, 32-value
+//     sub-blocks) or m16n8k16 (Q6_K, 16-value sub-blocks), A = the unpacked
+//     quants, B = Q8_K words read from the word-interleaved planar qs
+//     (device_common.cuh): in every 16-value group the lane takes values
+//     4c..4c+3, so each operand word is one 32-bit load for both sides;
+//   * exact int32 S per (row, token, block) = sum of sc_j x D_j;
+//   * the mins (Q4_K/Q5_K) or the -32 bias (Q6_K) sum_k coef[row][k] *
+//     bsums[token][k] as one m16n8k16 f16 mma per half: coefficients
+//     (<= 63, or |sc| <= 128) and block sums (|bsum| <= 2032) are exact in
+//     fp16 and every partial sum stays below 2^24, so the fp32 result is exact;
+//   * acc += (d*dx)*S - (dmin*dx)*Mn in fp32, as the dp4a form.
+// Result fragment (both mma shapes): D[0] = (row g, token 2c), D[1] = (g,
+// 2c+1), D[2] = (g+8, 2c), D[3] = (g+8, 2c+1).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void imma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void imma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+__device__ __forceinline__ void hmma_k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+// Two small integers (|v| < 2048) as an fp16 pair (exact).
+__device__ __forceinline__ uint32_t half2_of(int lo, int hi) {
+    const __half2 h = __halves2half2(__int2half_rn(lo), __int2half_rn(hi));
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Per-block operands shared by both halves of a tile: the B words of token g
+// (zero for g >= M), its block sums as fp16 pairs for the coefficient mma and
+// the d of tokens 2c, 2c+1.
+template <int M>
+struct MmaB {
+    uint32_t w[16];  // B word of 16-value group s, values 4c..4c+3
+    uint32_t bs0, bs1;
+    float dx0, dx1;
+    __device__ __forceinline__ void load(const Q8Smem& q8, int b, int g, int c) {
+        const uint32_t* qs = reinterpret_cast<const uint32_t*>(q8.qs + (size_t)b * M * QK);
+#pragma unroll
+        for (int s = 0; s < 16; s++) w[s] = g < M ? qs[(4 * s + c) * M + g] : 0u;
+        if (g < M) {
+            const int16_t* bs = q8.bsums(g, b);
+            const uint32_t p0 = *reinterpret_cast<const uint32_t*>(bs + 2 * c);
+            const uint32_t p1 = *reinterpret_cast<const uint32_t*>(bs + 8 + 2 * c);
+            bs0 = half2_of((int)(int16_t)(p0 & 0xffffu), (int)(int16_t)(p0 >> 16));
+            bs1 = half2_of((int)(int16_t)(p1 & 0xffffu), (int)(int16_t)(p1 >> 16));
+        } else {
+            bs0 = bs1 = 0u;
+        }
+        dx0 = 2 * c < M ? q8.dx(2 * c, b) : 0.f;
+        dx1 = 2 * c + 1 < M ? q8.dx(2 * c + 1, b) : 0.f;
+    }
+};
+
+// acc[i][j] (row g + 8i of the half, token 2c + j) += (d_i dx_j) S - (dmin_i dx_j) cf
+// (Q4_K/Q5_K), or (d_i dx_j) (S - 32 cf) with Q6_BIAS (cf = the bias sums).
+template <bool Q6_BIAS>
+__device__ __forceinline__ void mma_epilogue(float (&acc)[2][2], const int (&S)[4], const float (&cf)[4], float d0,
+                                             float d1, float m0, float m1, float dx0, float dx1) {
+    const float dx[2] = {dx0, dx1};
+    const float dd[2] = {d0, d1}, dm[2] = {m0, m1};
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int k = 2 * i + j;
+            if (Q6_BIAS) {
+                acc[i][j] = fmaf(dd[i] * dx[j], (float)(S[k] - 32 * (int)cf[k]), acc[i][j]);
+            } else {
+                acc[i][j] = fmaf(dd[i] * dx[j], (float)S[k], acc[i][j]);
+                acc[i][j] = fmaf(-(dm[i] * dx[j]), cf[k], acc[i][j]);
+            }
+        }
+}
+
+template <int TYPE, int M>
+__device__ __forceinline__ void half_dot_k45(const uint8_t* __restrict__ tile, int r0, int c, const MmaB<M>& B,
+                                             float (&acc)[2][2]) {
+    const int r1 = r0 + 8;
+    const KHeader h0 = unpack_header(*reinterpret_cast<const uint4*>(tile + r0 * 16));
+    const KHeader h1 = unpack_header(*reinterpret_cast<const uint4*>(tile + r1 * 16));
+    constexpr int QS_CHUNK = (TYPE == TYPE_Q5_K) ? 3 : 1;
+    uint32_t qh00 = 0, qh01 = 0, qh10 = 0, qh11 = 0;  // qh bytes 4c.. and 16+4c.. of rows r0, r1
+    if (TYPE == TYPE_Q5_K) {
+        qh00 = *reinterpret_cast<const uint32_t*>(tile + 1 * 512 + r0 * 16 + 4 * c);
+        qh01 = *reinterpret_cast<const uint32_t*>(tile + 2 * 512 + r0 * 16 + 4 * c);
+        qh10 = *reinterpret_cast<const uint32_t*>(tile + 1 * 512 + r1 * 16 + 4 * c);
+        qh11 = *reinterpret_cast<const uint32_t*>(tile + 2 * 512 + r1 * 16 + 4 * c);
+    }
+    int S[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+        // qs bytes 32p + 4c.. (chunk QS_CHUNK + 2p) and 32p + 16 + 4c.. (next chunk)
+        const uint32_t w00 = *reinterpret_cast<const uint32_t*>(tile + (QS_CHUNK + 2 * p) * 512 + r0 * 16 + 4 * c);
+        const uint32_t w01 = *reinterpret_cast<const uint32_t*>(tile + (QS_CHUNK + 2 * p + 1) * 512 + r0 * 16 + 4 * c);
+        const uint32_t w10 = *reinterpret_cast<const uint32_t*>(tile + (QS_CHUNK + 2 * p) * 512 + r1 * 16 + 4 * c);
+        const uint32_t w11 = *reinterpret_cast<const uint32_t*>(tile + (QS_CHUNK + 2 * p + 1) * 512 + r1 * 16 + 4 * c);
+        uint32_t lo00 = w00 & 0x0f0f0f0fu, lo01 = w01 & 0x0f0f0f0fu, lo10 = w10 & 0x0f0f0f0fu, lo11 = w11 & 0x0f0f0f0fu;
+        uint32_t hi00, hi01, hi10, hi11;
+        if (TYPE == TYPE_Q5_K) {
+            lo00 |= ((qh00 >> (2 * p)) & 0x01010101u) << 4;
+            lo01 |= ((qh01 >> (2 * p)) & 0x01010101u) << 4;
+            lo10 |= ((qh10 >> (2 * p)) & 0x01010101u) << 4;
+            lo11 |= ((qh11 >> (2 * p)) & 0x01010101u) << 4;
+            hi00 = ((w00 >> 4) & 0x0f0f0f0fu) | (((qh00 >> (2 * p + 1)) & 0x01010101u) << 4);
+            hi01 = ((w01 >> 4) & 0x0f0f0f0fu) | (((qh01 >> (2 * p + 1)) & 0x01010101u) << 4);
+            hi10 = ((w10 >> 4) & 0x0f0f0f0fu) | (((qh10 >> (2 * p + 1)) & 0x01010101u) << 4);
+            hi11 = ((w11 >> 4) & 0x0f0f0f0fu) | (((qh11 >> (2 * p + 1)) & 0x01010101u) << 4);
+        } else {
+            // high nibbles left in place: 16 x the value, divided out below
+            hi00 = w00 & 0xf0f0f0f0u;
+            hi01 = w01 & 0xf0f0f0f0u;
+            hi10 = w10 & 0xf0f0f0f0u;
+            hi11 = w11 & 0xf0f0f0f0u;
+        }
+        int dl[4], dh[4];
+        imma_k32(dl, lo00, lo10, lo01, lo11, B.w[4 * p], B.w[4 * p + 1]);
+        imma_k32(dh, hi00, hi10, hi01, hi11, B.w[4 * p + 2], B.w[4 * p + 3]);
+        const int sl0 = k_scale(h0, 2 * p), sh0 = k_scale(h0, 2 * p + 1);
+        const int sl1 = k_scale(h1, 2 * p), sh1 = k_scale(h1, 2 * p + 1);
+        if (TYPE == TYPE_Q5_K) {
+            S[0] += sl0 * dl[0] + sh0 * dh[0];
+            S[1] += sl0 * dl[1] + sh0 * dh[1];
+            S[2] += sl1 * dl[2] + sh1 * dh[2];
+            S[3] += sl1 * dl[3] + sh1 * dh[3];
+        } else {
+            // in units of 1/16: |16 S| <= 16 * 256*63*15*127 < 2^31
+            S[0] += 16 * sl0 * dl[0] + sh0 * dh[0];
+            S[1] += 16 * sl0 * dl[1] + sh0 * dh[1];
+            S[2] += 16 * sl1 * dl[2] + sh1 * dh[2];
+            S[3] += 16 * sl1 * dl[3] + sh1 * dh[3];
+        }
+    }
+    if (TYPE != TYPE_Q5_K)
+#pragma unroll
+        for (int k = 0; k < 4; k++) S[k] >>= 4;  // exact: every term is a multiple of 16
+    // Mins: A[row][k] = m_{k/2}; the lane supplies k = 2c, 2c+1 (m_c) and 8+2c, 9+2c (m_{4+c}).
+    const int mc0 = byte_of(h0.mn_lo, c), mc4_0 = byte_of(h0.mn_hi, c);
+    const int mc1 = byte_of(h1.mn_lo, c), mc4_1 = byte_of(h1.mn_hi, c);
+    float mn[4];
+    hmma_k16(mn, half2_of(mc0, mc0), half2_of(mc1, mc1), half2_of(mc4_0, mc4_0), half2_of(mc4_1, mc4_1), B.bs0,
+             B.bs1);
+    mma_epilogue<false>(acc, S, mn, h0.d, h1.d, h0.dmin, h1.dmin, B.dx0, B.dx1);
+}
+
+template <int M>
+__device__ __forceinline__ void half_dot_q6k(const uint8_t* __restrict__ tile, int r0, int c, const MmaB<M>& B,
+                                             float (&acc)[2][2]) {
+    const int r1 = r0 + 8;
+    const float d0 = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(tile + Fmt<TYPE_Q6_K>::D_OFFSET + r0 * 2));
+    const float d1 = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(tile + Fmt<TYPE_Q6_K>::D_OFFSET + r1 * 2));
+    const uint4 sv0 = *reinterpret_cast<const uint4*>(tile + 12 * 512 + r0 * 16);
+    const uint4 sv1 = *reinterpret_cast<const uint4*>(tile + 12 * 512 + r1 * 16);
+    const uint32_t s0[4] = {sv0.x, sv0.y, sv0.z, sv0.w}, s1[4] = {sv1.x, sv1.y, sv1.z, sv1.w};
+    int S[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+#pragma unroll
+        for (int lg = 0; lg < 2; lg++) {
+            uint32_t q[2][4];  // [row][quarter]: values 128h + 32*quarter + 16lg + 4c..+3
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const int r = rr ? r1 : r0;
+                const uint32_t a = *reinterpret_cast<const uint32_t*>(tile + (4 * h + lg) * 512 + r * 16 + 4 * c);
+                const uint32_t bq = *reinterpret_cast<const uint32_t*>(tile + (4 * h + 2 + lg) * 512 + r * 16 + 4 * c);
+                const uint32_t hh = *reinterpret_cast<const uint32_t*>(tile + (8 + 2 * h + lg) * 512 + r * 16 + 4 * c);
+                q[rr][0] = (a & 0x0f0f0f0fu) | ((hh << 4) & 0x30303030u);
+                q[rr][1] = (bq & 0x0f0f0f0fu) | ((hh << 2) & 0x30303030u);
+                q[rr][2] = ((a >> 4) & 0x0f0f0f0fu) | (hh & 0x30303030u);
+                q[rr][3] = ((bq >> 4) & 0x0f0f0f0fu) | ((hh >> 2) & 0x30303030u);
+            }
+#pragma unroll
+            for (int qq = 0; qq < 4; qq++) {
+                const int s = 8 * h + 2 * qq + lg;  // 16-value group
+                int dq[4];
+                imma_k16(dq, q[0][qq], q[1][qq], B.w[s]);
+                const int sc0 = sext_byte(s0[s >> 2], s & 3), sc1 = sext_byte(s1[s >> 2], s & 3);
+                S[0] += sc0 * dq[0];
+                S[1] += sc0 * dq[1];
+                S[2] += sc1 * dq[2];
+                S[3] += sc1 * dq[3];
+            }
+        }
+    }
+    // -32 bias: sum_s sc_s * bsums_s; the lane supplies s = 2c, 2c+1 and 8+2c, 9+2c.
+    const int w0 = c >> 1, b0 = 2 * (c & 1);
+    float bias[4];
+    hmma_k16(bias, half2_of(sext_byte(s0[w0], b0), sext_byte(s0[w0], b0 + 1)),
+             half2_of(sext_byte(s1[w0], b0), sext_byte(s1[w0], b0 + 1)),
+             half2_of(sext_byte(s0[2 + w0], b0), sext_byte(s0[2 + w0], b0 + 1)),
+             half2_of(sext_byte(s1[2 + w0], b0), sext_byte(s1[2 + w0], b0 + 1)), B.bs0, B.bs1);
+    mma_epilogue<true>(acc, S, bias, d0, d1, 0.f, 0.f, B.dx0, B.dx1);
+}
+
+// One 32-row tile (one super-block) for 5..8 tokens; acc[half][i][j] = row
+// 16*half + g + 8i, token 2c + j.
+template <int TYPE, int M>
+__device__ __forceinline__ void tile_dot_mma(const uint8_t* tile, int lane, const Q8Smem& q8, int b,
+                                             float (&acc)[2][2][2]) {
+    const int g = lane >> 2, c = lane & 3;
+    MmaB<M> B;
+    B.load(q8, b, g, c);
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+        if (TYPE == TYPE_Q6_K)
+            half_dot_q6k<M>(tile, 16 * hf + g, c, B, acc[hf]);
+        else
+            half_dot_k45<TYPE, M>(tile, 16 * hf + g, c, B, acc[hf]);
     }
 }
 

@@ -18,9 +18,10 @@
 namespace q35k {
 
 struct Q8Out {
-    uint32_t* d;   // the block's d word
-    uint32_t* qs;  // 64 words of qs
-    int16_t* bs;   // 16 bsums
+    uint32_t* d;        // the block's d word
+    uint32_t* qs;       // 64 words of qs: word w (values 4w..4w+3) at qs[w * qs_stride]
+    int16_t* bs;        // 16 bsums
+    int qs_stride = 1;  // > 1: the words of several rows interleaved (planar chunks of >= 3 rows)
 };
 
 // The quantization itself: returns d (the same value on every lane) and this
@@ -103,8 +104,8 @@ __device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict_
         (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
     const uint32_t w1 =
         (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-    out.qs[lane] = w0;
-    out.qs[32 + lane] = w1;
+    out.qs[lane * out.qs_stride] = w0;
+    out.qs[(32 + lane) * out.qs_stride] = w1;
     int s0, s1;
     warp_q8k_bsums(q, s0, s1);
     if ((lane & 3) == 0) {
