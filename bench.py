@@ -568,22 +568,30 @@ def gemm_configs(ctx, torch, synth, peaks):
     import q35k
 
     out = {}
+    Q4, Q5, Q6 = synth.Q4_K, synth.Q5_K, synth.Q6_K
+    # Q5_K / Q6_K at cfg2's ffn_down shape (K = 9728, N = 2560) with GGUF-like
+    # scales; Q6_K has no exact tensor-core form (its exact-mode prefill is
+    # the GEMV).
+    cases = [("cfg3_q4k_gemm_m512", Q4, 512, 2560, 9728), ("cfg4_q4k_gemm_m512_p1", Q4, 512, 5120, 27648),
+             ("q5k_gemm_m512_k9728_n2560", Q5, 512, 9728, 2560)]
     for mode, suffix in ((q35k.GEMM_EXACT, ""), (q35k.GEMM_FAST, "_fast")):
         ctx.set_gemm_mode(mode)
-        out.update(_gemm_lines(ctx, torch, synth, peaks, suffix, "exact" if mode == q35k.GEMM_EXACT else "fast"))
+        extra = [("q6k_gemm_m512_k9728_n2560", Q6, 512, 9728, 2560)] if mode == q35k.GEMM_FAST else []
+        out.update(_gemm_lines(ctx, torch, synth, peaks, suffix, "exact" if mode == q35k.GEMM_EXACT else "fast",
+                               cases + extra))
     ctx.set_gemm_mode(q35k.GEMM_EXACT)
     return out
 
 
-def _gemm_lines(ctx, torch, synth, peaks, suffix, mode_name):
+def _gemm_lines(ctx, torch, synth, peaks, suffix, mode_name, cases):
     out = {}
     stream = torch.cuda.current_stream()
     bf16_peak = peaks.get("bf16_tflops")
-    for name, m, k, n in (("cfg3_q4k_gemm_m512", 512, 2560, 9728), ("cfg4_q4k_gemm_m512_p1", 512, 5120, 27648)):
+    for name, qt, m, k, n in cases:
         name = name + suffix
-        w = synth.kquant_blocks(synth.Q4_K, n, k, seed=1)
+        w = synth.kquant_blocks(qt, n, k, seed=1, q5_uniform_d=False)
         x = synth.activations(m, k, seed=2)
-        W = ctx.upload(synth.Q4_K, w, k, n)
+        W = ctx.upload(qt, w, k, n)
         dx = torch.from_numpy(x).cuda()
         dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
         for _ in range(3):
@@ -629,6 +637,9 @@ PROFILE_CASES = {
     "cfg4_q4k_m8_p1": (12, 8, 5120, 27648, 1.0, 0),
     "cfg4_q4k_gemm_m512_p1": (12, 512, 5120, 27648, 1.0, 0),
     "cfg4_q4k_gemm_m512_p1_fast": (12, 512, 5120, 27648, 1.0, 1),
+    "q5k_gemm_m512": (13, 512, 9728, 2560, 1.0, 0),
+    "q5k_gemm_m512_fast": (13, 512, 9728, 2560, 1.0, 1),
+    "q6k_gemm_m512_fast": (14, 512, 9728, 2560, 1.0, 1),
 }
 
 
@@ -644,7 +655,8 @@ def run_profile_case(args):
     qt, m, k, n, scale, mode = PROFILE_CASES[args.profile]
     ctx = q35k.Context(0)
     ctx.set_gemm_mode(mode)
-    W = ctx.upload(qt, synth.kquant_blocks(qt, n, k, seed=1), k, n)
+    # GEMM cases: GGUF-like Q5_K scales (the fast mode's fp16 weights need them)
+    W = ctx.upload(qt, synth.kquant_blocks(qt, n, k, seed=1, q5_uniform_d=m < 16), k, n)
     dx = torch.from_numpy(synth.activations(m, k, seed=2, scale=scale)).cuda()
     dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
     for _ in range(args.steps):

@@ -211,16 +211,18 @@ int q35k_weight_upload(q35k_ctx* c, int type, const void* blocks, int n_in, int 
     w->bytes = tile_bytes;
     uint8_t* raw = nullptr;
     cudaError_t e = cudaMalloc(&w->tiles, tile_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&raw, raw_bytes);
+    // The staged GGUF rows, then a word the metadata kernel flags fp16-range trouble in.
+    const size_t flag_off = (raw_bytes + 15) / 16 * 16;
+    if (e == cudaSuccess) e = cudaMalloc(&raw, flag_off + 16);
     if (e != cudaSuccess) {
         cudaGetLastError();
         if (w->tiles) cudaFree(w->tiles);
         delete w;
         return c->fail(Q35K_ENOMEM, "weight upload: cudaMalloc(%zu) failed", tile_bytes + raw_bytes);
     }
-    if (type == Q35K_TYPE_Q4_K) {
+    {
         // The prefill GEMM's per-block metadata, computed once here.
-        const size_t mb = q4k_meta_bytes(nb, n_pad), sb = q4k_scale_bytes(nb, n_pad);
+        const size_t mb = gemm_meta_bytes(type, nb, n_pad), sb = gemm_scale_bytes(type, nb, n_pad);
         if ((e = cudaMalloc(&w->meta, mb + sb)) != cudaSuccess) {
             cudaGetLastError();
             cudaFree(w->tiles);
@@ -228,13 +230,19 @@ int q35k_weight_upload(q35k_ctx* c, int type, const void* blocks, int n_in, int 
             delete w;
             return c->fail(Q35K_ENOMEM, "weight upload: cudaMalloc(%zu) failed", mb + sb);
         }
-        w->scale = reinterpret_cast<float*>(w->meta + mb);
+        w->scale = sb ? reinterpret_cast<float*>(w->meta + mb) : nullptr;
         w->bytes += mb + sb;
     }
     e = cudaMemcpyAsync(raw, blocks, raw_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) e = launch_repack_tiles(type, raw, w->tiles, nb, n_out, n_pad, c->stream);
-    if (e == cudaSuccess && w->meta) e = launch_q4k_meta(w->tiles, w->meta, w->scale, nb, n_pad, c->stream);
+    unsigned* d_unsafe = reinterpret_cast<unsigned*>(raw + flag_off);
+    unsigned unsafe = 0;
+    if (e == cudaSuccess) e = cudaMemsetAsync(d_unsafe, 0, sizeof(unsigned), c->stream);
+    if (e == cudaSuccess)
+        e = launch_gemm_meta(type, w->tiles, w->meta, w->scale, nb, n_pad, d_unsafe, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&unsafe, d_unsafe, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    w->fast_ok = unsafe == 0;
     cudaFree(raw);
     if (e != cudaSuccess) {
         cudaFree(w->tiles);
@@ -328,10 +336,18 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
     return Q35K_OK;
 }
 
+bool q35k_ctx::uses_gemm(const q35k_weight* w, int tokens) const {
+    return tokens >= gemm_min_tokens && tc_gemm_supports(w->type, gemm_fast(w));
+}
+
+// Fast-mode arithmetic for this weight: the mode is fast and its fp16
+// dequantized values stay in range (else the exact form, or the GEMV).
+bool q35k_ctx::gemm_fast(const q35k_weight* w) const { return gemm_mode == Q35K_GEMM_FAST && w->fast_ok; }
+
 int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy,
                    const float* d_up, bool prep) {
     if (ldy <= 0) ldy = w->n_out;
-    const bool fast = gemm_mode == Q35K_GEMM_FAST;
+    const bool fast = gemm_fast(w);
     const TcGemmPlan p = plan_tc_gemm(w->nb, w->n_pad, tokens, num_sms, tc_gemm_tile_tokens(fast, tokens));
     int rc;
     if ((rc = ensure_dev(&d_xq, &xq_cap, p.xq_bytes, false)) != Q35K_OK) return rc;
@@ -363,6 +379,7 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     a.grid = p.grid;
     a.units = p.units;
     a.tn = p.tn;
+    a.type = w->type;
     e = launch_tc_gemm(a, d_xq, d_xe, w->n_in, fast, s, true);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
     return Q35K_OK;
@@ -374,7 +391,7 @@ int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, in
     if (peers && (chunk <= 0 || tokens > chunk))
         return fail(Q35K_ENOTSUP, "the fused all-gather takes decode calls of at most %d tokens", chunk);
     // Prefill: the tensor-core GEMM (the fused gather and argmax are GEMV epilogues).
-    if (!peers && !argmax && w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens)
+    if (!peers && !argmax && uses_gemm(w, tokens))
         return gemm(w, d_x, d_y, tokens, s, ldy, d_up);
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w->n_in);
     // Decode: the GEMV quantizes its own slices of x (one kernel per call).
@@ -395,13 +412,15 @@ int q35k_ctx::matmul_shared(const q35k_weight* const* ws, int count, const float
                             cudaStream_t s) {
     const q35k_weight* w0 = ws[0];
     const int chunk = gemv_chunk(w0);
-    bool prepped = false, quantized = false;
+    int prepped = -1;  // arithmetic of the prepared GEMM operands (0 exact, 1 fast), -1: none
+    bool quantized = false;
     int rc;
     for (int i = 0; i < count; i++) {
         const q35k_weight* w = ws[i];
-        if (w->type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens) {
-            if ((rc = gemm(w, d_x, d_ys[i], tokens, s, 0, nullptr, !prepped)) != Q35K_OK) return rc;
-            prepped = true;
+        if (uses_gemm(w, tokens)) {
+            const int f = gemm_fast(w) ? 1 : 0;
+            if ((rc = gemm(w, d_x, d_ys[i], tokens, s, 0, nullptr, prepped != f)) != Q35K_OK) return rc;
+            prepped = f;
         }
     }
     if (chunk <= 0) return fail(Q35K_ENOTSUP, "nIn=%d is too long for the decode GEMV", w0->n_in);
@@ -412,7 +431,7 @@ int q35k_ctx::matmul_shared(const q35k_weight* const* ws, int count, const float
         int n = 0, rows = 0;
         for (int i = 0; i < count; i++) {
             const q35k_weight* w = ws[i];
-            if (w->type != type || (type == Q35K_TYPE_Q4_K && tokens >= gemm_min_tokens)) continue;
+            if (w->type != type || uses_gemm(w, tokens)) continue;
             lw[n] = w;
             ly[n++] = d_ys[i];
             rows += (w->n_out + TILE_ROWS - 1) / TILE_ROWS * TILE_ROWS;

@@ -15,9 +15,10 @@ struct GemvPeers;  // kernels.h
 struct q35k_weight {
     int type = 0, n_in = 0, n_out = 0, nb = 0, n_pad = 0, device = 0;
     uint8_t* tiles = nullptr;  // 32-row chunk-major tiles (device_common.cuh)
-    uint8_t* meta = nullptr;   // Q4_K: per-block GEMM metadata (gemm_tc.h)
-    float* scale = nullptr;    // Q4_K: per-block drain scales of the GEMM
+    uint8_t* meta = nullptr;   // per-block GEMM metadata (gemm_tc.h)
+    float* scale = nullptr;    // Q4_K / Q5_K: per-block drain scales of the exact GEMM
     size_t bytes = 0;
+    bool fast_ok = true;       // fast-mode fp16 weight values stay in range (launch_gemm_meta)
 };
 
 struct q35k_ctx {
@@ -107,6 +108,10 @@ struct q35k_ctx {
     // prepared from the same x (same K and token count).
     int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0,
              const float* d_up = nullptr, bool prep = true);
+    // Prefill calls that take the tensor-core GEMM: enough tokens and a type
+    // the current mode supports (Q6_K: fast mode only).
+    bool uses_gemm(const q35k_weight* w, int tokens) const;
+    bool gemm_fast(const q35k_weight* w) const;
     // Several weights of one K on one input (q35k_matmul_shared_dev).
     int matmul_shared(const q35k_weight* const* ws, int count, const float* d_x, float* const* d_ys, int tokens,
                       cudaStream_t s);

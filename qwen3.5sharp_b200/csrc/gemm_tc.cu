@@ -63,6 +63,13 @@ namespace tcg {
 
 constexpr int TM = 128;  // weight rows per tile
 constexpr int Q4K_META_TILE = 5 * 512;  // GEMM metadata of one 32-row tile
+// Uploaded 32-row tile and its GEMM metadata per weight type.  Q5_K shares
+// Q4_K's header and so its metadata; Q6_K (fast mode only) keeps d * sc_s of
+// its sixteen 16-value groups, two 512-byte chunks.
+template <int TYPE> struct WFmt {
+    static constexpr int TILE_BYTES = 32 * (TYPE == TYPE_Q4_K ? 144 : TYPE == TYPE_Q5_K ? 176 : 210);
+    static constexpr int META_TILE = TYPE == TYPE_Q6_K ? 2 * 512 : 5 * 512;
+};
 constexpr int TN = 128;  // tokens per tile
 // Five warpgroups of four warps; each warpgroup re-sizes its registers with
 // setmaxnreg.  Registers are split between an SM's four sub-partitions, one
@@ -130,8 +137,10 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 // boxes of 64 K x 256 tokens), two stages; two weight stages without the Xe
 // tile; one 256-column accumulator (the A buffers keep columns 256..511), so
 // the next tile segment starts once the drains have read the last one.
-template <bool FAST, int TNX> struct Geo {
+template <bool FAST, int TNX, int TYPE = TYPE_Q4_K> struct Geo {
     static_assert(TNX == 128 || (FAST && TNX == 256), "tile width");
+    static_assert(TYPE != TYPE_Q6_K || FAST, "Q6_K products sc*(q-32) need 12 bits: no exact fp16 form");
+    static constexpr int TILE_BYTES = WFmt<TYPE>::TILE_BYTES, META_TILE = WFmt<TYPE>::META_TILE;
     static constexpr int TN = TNX;
     static constexpr int X_STAGES = TNX == 128 ? 3 : 2;
     static constexpr int X_BOX_BYTES = 64 * 2 * TN;
@@ -143,8 +152,8 @@ template <bool FAST, int TNX> struct Geo {
     static constexpr int EXT_BOX_BYTES = TNX == 128 ? 16 * 2 * TN : 0;
     static constexpr int W_EXT_OFF = 0;
     static constexpr int W_TILE_OFF = EXT_BOX_BYTES;
-    static constexpr int W_META_OFF = W_TILE_OFF + 4 * Q4K_TILE;
-    static constexpr int W_STAGE_BYTES = (W_META_OFF + 4 * Q4K_META_TILE + 1023) / 1024 * 1024;
+    static constexpr int W_META_OFF = W_TILE_OFF + 4 * TILE_BYTES;
+    static constexpr int W_STAGE_BYTES = (W_META_OFF + 4 * META_TILE + 1023) / 1024 * 1024;
     static constexpr int D_STAGES = 4;
     static constexpr int D_STAGE_BYTES = 2 * 128 * 4;
     static constexpr int A_BUFS = 4;
@@ -456,14 +465,22 @@ __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
 // and the drain's fp32 s of each row in s[(g nb + b) 32 + r] (q4k_block_scale).
 // One thread per (row, super-block).
 // ---------------------------------------------------------------------------
+// Fast-mode weight values q * (d sc) - dmin m are fp16: a block whose values
+// could reach FAST_RANGE_LIMIT (half the fp16 maximum, a margin for the
+// rounding of d sc) sets *unsafe, and the weight's prefill then keeps the
+// exact arithmetic.  GGUF weights have small d; uniform fp16 test patterns
+// do not.
+constexpr float FAST_RANGE_LIMIT = 32768.f;
+
 __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ meta,
-                                                      float* __restrict__ s_out, int n_pad, int nb) {
+                                                      float* __restrict__ s_out, int n_pad, int nb, int tile_bytes,
+                                                      int qmax, unsigned* __restrict__ unsafe) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)n_pad * nb) return;
     const int row = (int)(idx / nb), b = (int)(idx % nb);
     const int g = row >> 5, r = row & 31;
     const size_t tile = (size_t)g * nb + b;
-    const uint4 hdr = *reinterpret_cast<const uint4*>(tiles + tile * tcg::Q4K_TILE + r * 16);
+    const uint4 hdr = *reinterpret_cast<const uint4*>(tiles + tile * tile_bytes + r * 16);  // Q4_K / Q5_K header
     const BlockScale bs = q4k_block_scale(hdr.x);
     const float d = fp16_bits_to_float(hdr.x), dm = fp16_bits_to_float(hdr.x >> 16);
     uint32_t sa[4], hi[4], lo[4], fs[4], fm[4];
@@ -495,14 +512,54 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
     *reinterpret_cast<uint4*>(mt + 1536) = make_uint4(fs[0], fs[1], fs[2], fs[3]);
     *reinterpret_cast<uint4*>(mt + 2048) = make_uint4(fm[0], fm[1], fm[2], fm[3]);
     s_out[tile * 32 + r] = bs.s;
+    float vmax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        int sc, m;
+        q4k_scale_min(j, hdr.y, hdr.z, hdr.w, sc, m);
+        vmax = fmaxf(vmax, fabsf(d) * (float)(sc * qmax) + fabsf(dm) * (float)m);
+    }
+    if (!(vmax < FAST_RANGE_LIMIT)) atomicOr(unsafe, 1u);
 }
 
-template <bool FAST, int TNX>
+// Q6_K metadata (fast mode): fp16 d * sc_s of the 16-value groups s = 0..7
+// (chunk 0) and 8..15 (chunk 1), one 16-byte slot per row as above; the
+// producers form (q - 32) * (d sc_s) with one fp16 rounding.
+__global__ void __launch_bounds__(256) q6k_meta_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ meta,
+                                                      int n_pad, int nb, unsigned* __restrict__ unsafe) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)n_pad * nb) return;
+    const int row = (int)(idx / nb), b = (int)(idx % nb);
+    const int g = row >> 5, r = row & 31;
+    const size_t tile = (size_t)g * nb + b;
+    const uint8_t* t = tiles + tile * tcg::WFmt<TYPE_Q6_K>::TILE_BYTES;
+    const float d = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(t + Fmt<TYPE_Q6_K>::D_OFFSET + r * 2));
+    const uint4 sv = *reinterpret_cast<const uint4*>(t + 12 * 512 + r * 16);
+    const uint32_t sc4[4] = {sv.x, sv.y, sv.z, sv.w};
+    uint32_t ds[8];
+    float vmax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) vmax = fmaxf(vmax, fabsf(d * (float)(int8_t)(sc4[i >> 2] >> (8 * (i & 3)))) * 32.f);
+    if (!(vmax < FAST_RANGE_LIMIT)) atomicOr(unsafe, 1u);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int s0 = 2 * i, s1 = 2 * i + 1;
+        const float v0 = d * (float)(int8_t)(sc4[s0 >> 2] >> (8 * (s0 & 3)));
+        const float v1 = d * (float)(int8_t)(sc4[s1 >> 2] >> (8 * (s1 & 3)));
+        ds[i] = __half_as_ushort(__float2half_rn(v0)) | ((uint32_t)__half_as_ushort(__float2half_rn(v1)) << 16);
+    }
+    uint8_t* mt = meta + tile * tcg::WFmt<TYPE_Q6_K>::META_TILE + r * 16;
+    *reinterpret_cast<uint4*>(mt) = make_uint4(ds[0], ds[1], ds[2], ds[3]);
+    *reinterpret_cast<uint4*>(mt + 512) = make_uint4(ds[4], ds[5], ds[6], ds[7]);
+}
+
+template <bool FAST, int TNX, int TYPE>
 __global__ void __launch_bounds__(tcg::THREADS, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_e,
                        const TcGemmArgs a) {
     using namespace tcg;
-    using GG = Geo<FAST, TNX>;
+    using GG = Geo<FAST, TNX, TYPE>;
+    constexpr int W_TILE = GG::TILE_BYTES, W_META = GG::META_TILE;
     constexpr int TN = GG::TN, X_STAGES = GG::X_STAGES, X_BOX_BYTES = GG::X_BOX_BYTES;
     constexpr int X_STAGE_BYTES = GG::X_STAGE_BYTES, X_PHASE_FILLS = GG::X_PHASE_FILLS;
     constexpr int W_STAGES = GG::W_STAGES, EXT_BOX_BYTES = GG::EXT_BOX_BYTES, W_EXT_OFF = GG::W_EXT_OFF;
@@ -633,11 +690,11 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 const int ws = i % W_STAGES;
                 if (!wait_bar(w_empty + ws, ((uint32_t)(i / W_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
                 uint8_t* dst = wring + ws * W_STAGE_BYTES;
-                mbar_arrive_expect_tx(w_full + ws, (uint32_t)(valid * (Q4K_TILE + Q4K_META_TILE)));
+                mbar_arrive_expect_tx(w_full + ws, (uint32_t)(valid * (W_TILE + W_META)));
                 for (int q = 0; q < valid; q++) {
                     const size_t tile = (size_t)(tw * 4 + q) * nb + b;
-                    bulk_g2s(dst + W_TILE_OFF + q * Q4K_TILE, a.tiles + tile * Q4K_TILE, Q4K_TILE, w_full + ws);
-                    bulk_g2s(dst + W_META_OFF + q * Q4K_META_TILE, a.meta + tile * Q4K_META_TILE, Q4K_META_TILE,
+                    bulk_g2s(dst + W_TILE_OFF + q * W_TILE, a.tiles + tile * W_TILE, W_TILE, w_full + ws);
+                    bulk_g2s(dst + W_META_OFF + q * W_META, a.meta + tile * W_META, W_META,
                              w_full + ws);
                 }
                 issued_w = i + 1;
@@ -765,18 +822,37 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             const int ws = i % W_STAGES, ab = 2 * (i & 1) + h;
             if (!warp_wait_bar(w_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag, lane)) break;
             const uint8_t* stage = wring + ws * W_STAGE_BYTES;
-            const uint8_t* tile = stage + W_TILE_OFF + q * Q4K_TILE + lane * 16;
-            const uint8_t* mt = stage + W_META_OFF + q * Q4K_META_TILE + lane * 16;
+            const uint8_t* tile = stage + W_TILE_OFF + q * W_TILE + lane * 16;
+            const uint8_t* mt = stage + W_META_OFF + q * W_META + lane * 16;
             uint4 sa = make_uint4(0, 0, 0, 0), em = sa, w0 = sa, w1 = sa, w2 = sa, w3 = sa;
+            uint4 x0 = sa, x1 = sa;  // Q5_K / Q6_K high bits
             if (valid) {
-                // exact: alpha sc_j and the min-term part; fast: d sc_j and dmin m_j
-                sa = *reinterpret_cast<const uint4*>(mt + (FAST ? 3 : 0) * 512);
-                em = *reinterpret_cast<const uint4*>(mt + (FAST ? 4 : 1 + h) * 512);
-                // 64-value chunks c = 2h, 2h + 1 (tile chunks 1 + 4h .. 4 + 4h)
-                w0 = *reinterpret_cast<const uint4*>(tile + (1 + 4 * h) * 512);
-                w1 = *reinterpret_cast<const uint4*>(tile + (2 + 4 * h) * 512);
-                w2 = *reinterpret_cast<const uint4*>(tile + (3 + 4 * h) * 512);
-                w3 = *reinterpret_cast<const uint4*>(tile + (4 + 4 * h) * 512);
+                if constexpr (TYPE == TYPE_Q6_K) {
+                    // d sc_s of the half's groups 8h..8h+7; ql bytes 64h..64h+63
+                    // (chunks 4h..4h+3), qh bytes 32h..32h+31 (chunks 8+2h, 9+2h)
+                    sa = *reinterpret_cast<const uint4*>(mt + h * 512);
+                    w0 = *reinterpret_cast<const uint4*>(tile + (4 * h) * 512);
+                    w1 = *reinterpret_cast<const uint4*>(tile + (4 * h + 1) * 512);
+                    w2 = *reinterpret_cast<const uint4*>(tile + (4 * h + 2) * 512);
+                    w3 = *reinterpret_cast<const uint4*>(tile + (4 * h + 3) * 512);
+                    x0 = *reinterpret_cast<const uint4*>(tile + (8 + 2 * h) * 512);
+                    x1 = *reinterpret_cast<const uint4*>(tile + (9 + 2 * h) * 512);
+                } else {
+                    // exact: alpha sc_j and the min-term part; fast: d sc_j and dmin m_j
+                    sa = *reinterpret_cast<const uint4*>(mt + (FAST ? 3 : 0) * 512);
+                    em = *reinterpret_cast<const uint4*>(mt + (FAST ? 4 : 1 + h) * 512);
+                    // 64-value chunks c = 2h, 2h + 1 (tile chunks QS + 4h .. QS + 3 + 4h)
+                    constexpr int QS = TYPE == TYPE_Q5_K ? 3 : 1;
+                    w0 = *reinterpret_cast<const uint4*>(tile + (QS + 4 * h) * 512);
+                    w1 = *reinterpret_cast<const uint4*>(tile + (QS + 1 + 4 * h) * 512);
+                    w2 = *reinterpret_cast<const uint4*>(tile + (QS + 2 + 4 * h) * 512);
+                    w3 = *reinterpret_cast<const uint4*>(tile + (QS + 3 + 4 * h) * 512);
+                    if constexpr (TYPE == TYPE_Q5_K) {
+                        // qh bytes 0..31 (chunks 1, 2): bit c of byte l is value 32c + l's fifth bit
+                        x0 = *reinterpret_cast<const uint4*>(tile + 1 * 512);
+                        x1 = *reinterpret_cast<const uint4*>(tile + 2 * 512);
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(w_empty + ws);  // this warp is done with the stage
@@ -805,7 +881,69 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 const uint4 wa = cc ? w2 : w0, wb = cc ? w3 : w1;
                 const uint32_t W[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
                 uint32_t v[32];
-                if constexpr (FAST) {
+                if constexpr (TYPE == TYPE_Q6_K) {
+                    // cc = 0: q1 = low nibbles of ql bytes l + qh bits 0-1 (values
+                    // 128h + l), q2 = low nibbles of ql bytes 32 + l + qh bits 2-3
+                    // (128h + 32 + l); cc = 1: the high nibbles with qh bits 4-5
+                    // (q3, 128h + 64 + l) and 6-7 (q4, 128h + 96 + l).  fp16
+                    // 1024 + q - 1056 = q - 32 exactly, times d sc_s (one rounding).
+                    const uint32_t A[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    const uint32_t B[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+                    const uint32_t H[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const uint32_t S[4] = {sa.x, sa.y, sa.z, sa.w};
+#pragma unroll
+                    for (int w = 0; w < 8; w++) {
+                        const uint32_t qa = cc ? (((A[w] >> 4) & 0x0F0F0F0Fu) | (H[w] & 0x30303030u))
+                                               : ((A[w] & 0x0F0F0F0Fu) | ((H[w] << 4) & 0x30303030u));
+                        const uint32_t qb = cc ? (((B[w] >> 4) & 0x0F0F0F0Fu) | ((H[w] >> 2) & 0x30303030u))
+                                               : ((B[w] & 0x0F0F0F0Fu) | ((H[w] << 2) & 0x30303030u));
+                        const int ga = 4 * cc + (w >> 2), gb = ga + 2;  // 16-value group within the half
+                        const uint32_t da = __byte_perm(S[ga >> 1], 0u, (ga & 1) ? 0x3232 : 0x1010);
+                        const uint32_t db = __byte_perm(S[gb >> 1], 0u, (gb & 1) ? 0x3232 : 0x1010);
+                        const uint32_t a02 = hadd2_bits((qa & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
+                        const uint32_t a13 = hadd2_bits(((qa >> 8) & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
+                        const uint32_t b02 = hadd2_bits((qb & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
+                        const uint32_t b13 = hadd2_bits(((qb >> 8) & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
+                        v[2 * w] = hmul2_bits(a02, da);
+                        v[2 * w + 1] = hmul2_bits(a13, da);
+                        v[16 + 2 * w] = hmul2_bits(b02, db);
+                        v[16 + 2 * w + 1] = hmul2_bits(b13, db);
+                    }
+                } else if constexpr (TYPE == TYPE_Q5_K) {
+                    // q = nibble + 16 * (bit 2c, or 2c + 1 for the high nibble, of
+                    // qh byte l), c = 2h + cc; fp16 1024 + q is exact (q <= 31).
+                    const uint32_t QH[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    const int c = 2 * h + cc;
+                    uint32_t n_lo, n_hi;
+                    if constexpr (FAST) {
+                        const uint32_t mw = (h == 0) ? (cc == 0 ? em.x : em.y) : (cc == 0 ? em.z : em.w);
+                        n_lo = __byte_perm(mw, 0u, 0x1010) ^ 0x80008000u;  // -dmin m
+                        n_hi = __byte_perm(mw, 0u, 0x3232) ^ 0x80008000u;
+                    } else {
+                        n_lo = hmul2_bits(s_lo, 0xE400E400u);  // -1024 s
+                        n_hi = hmul2_bits(s_hi, 0xE400E400u);
+                    }
+#pragma unroll
+                    for (int w = 0; w < 8; w++) {
+                        const uint32_t lo = (W[w] & 0x0F0F0F0Fu) | (((QH[w] >> (2 * c)) & 0x01010101u) << 4);
+                        const uint32_t hi = ((W[w] >> 4) & 0x0F0F0F0Fu) | (((QH[w] >> (2 * c + 1)) & 0x01010101u) << 4);
+                        const uint32_t l02 = (lo & 0x001F001Fu) | 0x64006400u, l13 = ((lo >> 8) & 0x001F001Fu) | 0x64006400u;
+                        const uint32_t h02 = (hi & 0x001F001Fu) | 0x64006400u, h13 = ((hi >> 8) & 0x001F001Fu) | 0x64006400u;
+                        if constexpr (FAST) {
+                            // w = q * (d sc) - dmin m, one fp16 rounding
+                            v[2 * w] = hfma2_bits(hadd2_bits(l02, 0xE400E400u), s_lo, n_lo);
+                            v[2 * w + 1] = hfma2_bits(hadd2_bits(l13, 0xE400E400u), s_lo, n_lo);
+                            v[16 + 2 * w] = hfma2_bits(hadd2_bits(h02, 0xE400E400u), s_hi, n_hi);
+                            v[16 + 2 * w + 1] = hfma2_bits(hadd2_bits(h13, 0xE400E400u), s_hi, n_hi);
+                        } else {
+                            // (1024 + q) s - 1024 s = q s exactly (q s <= 31 * 63 alpha)
+                            v[2 * w] = hfma2_bits(l02, s_lo, n_lo);
+                            v[2 * w + 1] = hfma2_bits(l13, s_lo, n_lo);
+                            v[16 + 2 * w] = hfma2_bits(h02, s_hi, n_hi);
+                            v[16 + 2 * w + 1] = hfma2_bits(h13, s_hi, n_hi);
+                        }
+                    }
+                } else if constexpr (FAST) {
                     // w = q * (d sc) - dmin m, one fp16 rounding: q recovered
                     // exactly from the magic-number form, then one fma.
                     const uint32_t mw = (h == 0) ? (cc == 0 ? em.x : em.y) : (cc == 0 ? em.z : em.w);
@@ -1056,14 +1194,36 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
-size_t q4k_meta_bytes(int nb, int n_pad) { return (size_t)(n_pad / 32) * nb * tcg::Q4K_META_TILE; }
-size_t q4k_scale_bytes(int nb, int n_pad) { return (size_t)n_pad * nb * sizeof(float); }
+size_t gemm_meta_bytes(int type, int nb, int n_pad) {
+    const int per_tile = type == TYPE_Q6_K ? tcg::WFmt<TYPE_Q6_K>::META_TILE : tcg::Q4K_META_TILE;
+    return (size_t)(n_pad / 32) * nb * per_tile;
+}
+size_t gemm_scale_bytes(int type, int nb, int n_pad) {
+    return type == TYPE_Q6_K ? 0 : (size_t)n_pad * nb * sizeof(float);
+}
 
-cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad, cudaStream_t s) {
+cudaError_t launch_gemm_meta(int type, const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad,
+                             unsigned* unsafe, cudaStream_t s) {
     const long long n = (long long)n_pad * nb;
     if (n == 0) return cudaSuccess;
-    q4k_meta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(tiles, meta, scale, n_pad, nb);
+    const unsigned grid = (unsigned)((n + 255) / 256);
+    switch (type) {
+    case TYPE_Q4_K:
+        q4k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, tcg::WFmt<TYPE_Q4_K>::TILE_BYTES, 15,
+                                             unsafe);
+        break;
+    case TYPE_Q5_K:
+        q4k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, tcg::WFmt<TYPE_Q5_K>::TILE_BYTES, 31,
+                                             unsafe);
+        break;
+    case TYPE_Q6_K: q6k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, n_pad, nb, unsafe); break;
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
+}
+
+bool tc_gemm_supports(int type, bool fast) {
+    return type == TYPE_Q4_K || type == TYPE_Q5_K || (type == TYPE_Q6_K && fast);
 }
 
 int tc_gemm_tile_tokens(bool fast, int tokens) { return (fast && tokens >= 512) ? 256 : 128; }
@@ -1082,7 +1242,6 @@ TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms, int tn) {
     p.xd_bytes = (size_t)p.m_pad * nb * 4;
     p.ws_bytes = (size_t)p.grid * 2 * tcg::TM * p.tn * 4;
     p.counters = (size_t)p.tiles * tcg::NUM_DRAIN * (p.tn / 128);
-    p.smem_bytes = p.tn == 256 ? tcg::Geo<true, 256>::SMEM_BYTES : tcg::Geo<false, 128>::SMEM_BYTES;
     return p;
 }
 
@@ -1123,12 +1282,19 @@ cudaError_t configure_tc_gemm() {
     // The warpgroups' setmaxnreg split draws on the registers the CTA is
     // launched with: each kernel must have been compiled to exactly
     // LAUNCH_REGS per thread, or a larger request would never be granted.
+    using namespace tcg;
     const struct {
         const void* fn;
         size_t smem;
-    } kernels[] = {{(const void*)gemm_q4k_tc_kernel<false, 128>, tcg::Geo<false, 128>::SMEM_BYTES},
-                   {(const void*)gemm_q4k_tc_kernel<true, 128>, tcg::Geo<true, 128>::SMEM_BYTES},
-                   {(const void*)gemm_q4k_tc_kernel<true, 256>, tcg::Geo<true, 256>::SMEM_BYTES}};
+    } kernels[] = {
+        {(const void*)gemm_q4k_tc_kernel<false, 128, TYPE_Q4_K>, Geo<false, 128, TYPE_Q4_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<true, 128, TYPE_Q4_K>, Geo<true, 128, TYPE_Q4_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<true, 256, TYPE_Q4_K>, Geo<true, 256, TYPE_Q4_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<false, 128, TYPE_Q5_K>, Geo<false, 128, TYPE_Q5_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<true, 128, TYPE_Q5_K>, Geo<true, 128, TYPE_Q5_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<true, 256, TYPE_Q5_K>, Geo<true, 256, TYPE_Q5_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<true, 128, TYPE_Q6_K>, Geo<true, 128, TYPE_Q6_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<true, 256, TYPE_Q6_K>, Geo<true, 256, TYPE_Q6_K>::SMEM_BYTES}};
     for (const auto& k : kernels) {
         cudaFuncAttributes fa;
         cudaError_t e = cudaFuncGetAttributes(&fa, k.fn);
@@ -1153,6 +1319,36 @@ cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void*
     return cudaGetLastError();
 }
 
+template <int TYPE>
+static cudaError_t launch_typed(cudaLaunchConfig_t& cfg, const TcGemmArgs& args, const CUtensorMap& tq,
+                                const CUtensorMap& te, bool fast, bool wide) {
+    using namespace tcg;
+    if (wide) {
+        cfg.dynamicSmemBytes = Geo<true, 256, TYPE>::SMEM_BYTES;
+        return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 256, TYPE>, tq, te, args);
+    }
+    if (fast) {
+        cfg.dynamicSmemBytes = Geo<true, 128, TYPE>::SMEM_BYTES;
+        return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 128, TYPE>, tq, te, args);
+    }
+    if constexpr (TYPE == TYPE_Q6_K) {
+        return cudaErrorInvalidValue;
+    } else {
+        cfg.dynamicSmemBytes = Geo<false, 128, TYPE>::SMEM_BYTES;
+        return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false, 128, TYPE>, tq, te, args);
+    }
+}
+
+static cudaError_t launch_tc_instance(cudaLaunchConfig_t& cfg, const TcGemmArgs& args, const CUtensorMap& tq,
+                                      const CUtensorMap& te, bool fast, bool wide) {
+    switch (args.type) {
+    case TYPE_Q4_K: return launch_typed<TYPE_Q4_K>(cfg, args, tq, te, fast, wide);
+    case TYPE_Q5_K: return launch_typed<TYPE_Q5_K>(cfg, args, tq, te, fast, wide);
+    case TYPE_Q6_K: return launch_typed<TYPE_Q6_K>(cfg, args, tq, te, fast, wide);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* xe, int k, bool fast, cudaStream_t s,
                            bool pdl) {
     CUtensorMap tq, te;
@@ -1168,19 +1364,17 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& args, const void* xq, const void* x
                               CU_TENSOR_MAP_SWIZZLE_32B)) {
         return cudaErrorInvalidValue;
     }
+    if (!tc_gemm_supports(args.type, fast)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(args.grid);
     cfg.blockDim = dim3(tcg::THREADS);
-    cfg.dynamicSmemBytes = wide ? tcg::Geo<true, 256>::SMEM_BYTES : tcg::Geo<false, 128>::SMEM_BYTES;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (wide) return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 256>, tq, te, args);
-    return fast ? cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 128>, tq, te, args)
-                : cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false, 128>, tq, te, args);
+    return launch_tc_instance(cfg, args, tq, te, fast, wide);
 }
 
 }  // namespace q35k

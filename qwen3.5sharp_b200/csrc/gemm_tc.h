@@ -8,8 +8,8 @@
 namespace q35k {
 
 struct TcGemmArgs {
-    const uint8_t* tiles;  // uploaded Q4_K weight tiles (32-row chunk-major layout)
-    const uint8_t* meta;   // their GEMM metadata (q4k_meta_kernel)
+    const uint8_t* tiles;  // uploaded weight tiles (32-row chunk-major layout)
+    const uint8_t* meta;   // their GEMM metadata (launch_gemm_meta)
     const float* scale;    // the drain scale s of every (row, super-block)
     const float* xd;       // Q8_K block scales [nb][m_pad]
     float* y;              // [tokens][ldy], columns below n_out written
@@ -20,12 +20,13 @@ struct TcGemmArgs {
     int n_out, n_pad, tokens, m_pad, nb, tiles_t, grid;
     long long units;       // tiles * nb
     int tn;                // tokens per tile: 128, or 256 (fast mode, 256+ tokens)
+    int type;              // TYPE_Q4_K, TYPE_Q5_K, or TYPE_Q6_K (fast mode only)
 };
 
 struct TcGemmPlan {
     int tn, m_pad, tiles_w, tiles_t, tiles, grid;
     long long units;
-    size_t xq_bytes, xe_bytes, xd_bytes, ws_bytes, counters, smem_bytes;
+    size_t xq_bytes, xe_bytes, xd_bytes, ws_bytes, counters;
 };
 
 // Tokens per tile: 256 for fast-mode calls of at least 512 tokens (twice the
@@ -33,10 +34,17 @@ struct TcGemmPlan {
 // leave too few tiles to share among the SMs), else 128.
 int tc_gemm_tile_tokens(bool fast, int tokens);
 TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms, int tn);
-// GEMM metadata of an uploaded Q4_K weight: sizes and the kernel that fills it.
-size_t q4k_meta_bytes(int nb, int n_pad);
-size_t q4k_scale_bytes(int nb, int n_pad);
-cudaError_t launch_q4k_meta(const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad, cudaStream_t s);
+// GEMM metadata of an uploaded weight: sizes and the kernels that fill it
+// (Q6_K has no drain scales: 0 bytes).  *unsafe (zeroed by the caller) is set
+// when a block's fast-mode fp16 weight values could overflow.
+size_t gemm_meta_bytes(int type, int nb, int n_pad);
+size_t gemm_scale_bytes(int type, int nb, int n_pad);
+cudaError_t launch_gemm_meta(int type, const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad,
+                             unsigned* unsafe, cudaStream_t s);
+// Whether the tensor-core GEMM takes this weight type in this mode: Q4_K and
+// Q5_K in both modes, Q6_K in the fast mode (its products sc * (q - 32) have
+// no exact fp16 form).
+bool tc_gemm_supports(int type, bool fast);
 cudaError_t configure_tc_gemm();
 // Q8_K quantization of x [tokens][k] into the GEMM's operands.  Exact mode:
 // Xq [tokens][k] fp16 q values, Xe [tokens][k/256*16] fp16 block sums,
