@@ -512,9 +512,24 @@ int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int
     std::memcpy(c->h_in, x, in_bytes);
     cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of x");
-    if ((rc = q35k_matmul_dev(c, w, c->d_x, c->d_y, tokens, c->stream)) != Q35K_OK) return rc;
+    // Decode calls: the GEMV stores y straight into the pinned staging buffer
+    // (mapped into the device's address space), so its transfer overlaps the
+    // kernel and no copy follows it.  Prefill calls (tensor-core GEMM, whose
+    // tiles would cross the bus piece by piece) copy y back afterwards.
+    float* d_out = c->d_y;
+    bool direct = false;
+    if (!c->uses_gemm(w, tokens)) {
+        void* dp = nullptr;
+        if (cudaHostGetDevicePointer(&dp, c->h_out, 0) == cudaSuccess && dp) {
+            d_out = static_cast<float*>(dp);
+            direct = true;
+        } else {
+            cudaGetLastError();
+        }
+    }
+    if ((rc = q35k_matmul_dev(c, w, c->d_x, d_out, tokens, c->stream)) != Q35K_OK) return rc;
     unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
-    e = cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    e = direct ? cudaSuccess : cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "matmul");

@@ -174,12 +174,20 @@ class Context:
         return Weight(self, h, info.type, int(info.shape[0]), int(info.shape[1]) if len(info.shape) > 1 else 1)
 
     # -- host-pointer calls (synchronous) --
-    def matmul(self, w: "Weight", x: np.ndarray, tokens: int | None = None) -> np.ndarray:
+    def matmul(self, w: "Weight", x: np.ndarray, tokens: int | None = None, out: np.ndarray | None = None) -> np.ndarray:
+        """y = x @ W^T (q35k_matmul).  `out`: a float32 C-contiguous array of
+        at least tokens * nOut values to write into (a caller's persistent
+        output buffer, as the reference writes through `float* output`)."""
         x = _f32(x)
         tokens = x.size // w.n_in if tokens is None else tokens
         if x.size < tokens * w.n_in:
             raise ArgumentException("input is smaller than tokens * nIn")
-        y = np.empty((tokens, w.n_out), dtype=np.float32)
+        if out is None:
+            y = np.empty((tokens, w.n_out), dtype=np.float32)
+        else:
+            if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < tokens * w.n_out:
+                raise ArgumentException("out must be a C-contiguous float32 array of at least tokens * nOut values")
+            y = out
         self._check(self.L.q35k_matmul(self.h, w.h, x.ctypes.data, y.ctypes.data, tokens))
         return y
 

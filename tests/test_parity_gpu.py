@@ -175,3 +175,20 @@ def test_error_behaviour(ctx):
     with pytest.raises(q35k.ArgumentException):
         ctx._check(ctx.L.q35k_matmul(ctx.h, W.h, np.zeros(256, np.float32).ctypes.data,
                                      np.zeros(8, np.float32).ctypes.data, 0))
+
+
+def test_host_call_writes_into_a_persistent_output(ctx):
+    """q35k_matmul with the caller's own output buffer, reused across calls:
+    decode calls have the GEMV store y into the mapped staging buffer, prefill
+    calls copy it back; both give the same bits as a fresh output."""
+    for qt, k, n, m in [(Q6_K, 2560, 5000, 1), (Q4_K, 2560, 3000, 4), (Q4_K, 2560, 1000, 64), (Q5_K, 512, 300, 11)]:
+        w = synth.kquant_blocks(qt, n, k, seed=n)
+        W = ctx.upload(qt, w, k, n)
+        out = np.full((m, n), np.nan, dtype=np.float32)
+        for s in range(3):
+            x = synth.activations(m, k, seed=s)
+            ref = ctx.matmul(W, x)
+            got = ctx.matmul(W, x, out=out)
+            assert got is out
+            assert (out == ref).all()
+        W.free()
