@@ -54,7 +54,8 @@ __host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int units
     L.flags = 8 * (units + 1);
     L.tiles = align_up(L.flags + 16, 128);
     L.q8 = L.tiles + units * tile_bytes;
-    L.red = L.q8 + units * (m * QK + rows4 * 4 + m * 32);
+    // 5+ tokens read their activations from global memory (L2), not staged.
+    L.red = L.q8 + (m >= Q8_INTERLEAVE_MIN_ROWS ? 0 : units * (m * QK + rows4 * 4 + m * 32));
     L.total = L.red + warps * m * 32 * 4;
     return L;
 }
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             mbar_arrive_expect_tx(&bars[t], TILE);
             bulk_g2s(tiles + (size_t)t * TILE, src + (size_t)t * TILE, TILE, &bars[t]);
         }
-        if (!FUSED) {
+        if (!FUSED && M < Q8_INTERLEAVE_MIN_ROWS) {
             // Then the activations, once the producing kernel has completed.
             griddep_wait();
             mbar_arrive_expect_tx(&bars[kr], qs_bytes + d_bytes + bs_bytes);
@@ -146,8 +147,15 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     // SMs this grid frees; it reads activations and writes results only
     // after its own griddepcontrol.wait, i.e. after this grid completed.
     asm volatile("griddepcontrol.launch_dependents;");
-    const Q8Smem q8{reinterpret_cast<const int8_t*>(q8s), reinterpret_cast<const float*>(q8s + qs_bytes),
-                    reinterpret_cast<const int16_t*>(q8s + qs_bytes + d_bytes), M, pl.rows4};
+    // 5+ tokens: the unit's K-range of the planar Q8_K in global memory (each
+    // warp loads its B operand words directly; L2 serves the CTAs of a K-range).
+    constexpr bool Q8_GLOBAL = M >= Q8_INTERLEAVE_MIN_ROWS;
+    const Q8Smem q8 = Q8_GLOBAL
+        ? Q8Smem{reinterpret_cast<const int8_t*>(a.q8 + pl.qs + (size_t)b0 * M * QK),
+                 reinterpret_cast<const float*>(a.q8 + pl.d + (size_t)b0 * pl.rows4 * 4),
+                 reinterpret_cast<const int16_t*>(a.q8 + pl.bs + (size_t)b0 * M * 32), M, pl.rows4}
+        : Q8Smem{reinterpret_cast<const int8_t*>(q8s), reinterpret_cast<const float*>(q8s + qs_bytes),
+                 reinterpret_cast<const int16_t*>(q8s + qs_bytes + d_bytes), M, pl.rows4};
     bool ok = true;
     if (FUSED) {
         griddep_wait();  // x comes from the preceding kernel
@@ -161,6 +169,8 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             warp_quantize_q8k_block(a.x + off, out, lane, a.up ? a.up + off : nullptr);
         }
         __syncthreads();
+    } else if (Q8_GLOBAL) {
+        griddep_wait();  // q8 comes from the preceding kernel
     } else {
         ok = mbar_wait_bounded(&bars[kr], 0, a.err);
     }
@@ -249,7 +259,8 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     if (!ok && tid == 0) {
         // A wait gave up: give the copies in flight a bounded chance to land
         // before the CTA's shared memory is released.
-        for (int t = 0; t < kr + (FUSED ? 0 : 1); t++) mbar_wait_bounded(&bars[t], 0, a.err, 100000000ull);
+        for (int t = 0; t < kr + ((FUSED || Q8_GLOBAL) ? 0 : 1); t++)
+            mbar_wait_bounded(&bars[t], 0, a.err, 100000000ull);
     }
 }
 
