@@ -279,7 +279,9 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     int u, max_warps;
     if (nb <= GEMV_MAX_WARPS && nb * tile <= GEMV_ROW_BYTES && p.groups >= num_sms) {
         u = nb;
-        max_warps = GEMV_MAX_WARPS;
+        // 5+ tokens: 10 warps (two tiles each at 20 tiles), so that two CTAs
+        // share an SM and one's copies overlap the other's decode.
+        max_warps = m >= Q8_INTERLEAVE_MIN_ROWS ? GEMV_SPLIT_WARPS : GEMV_MAX_WARPS;
     } else {
         u = std::max(1, std::min(nb, GEMV_UNIT_BYTES / tile));
         int splits = (nb + u - 1) / u;
