@@ -399,7 +399,7 @@ int q35k_ctx::matmul_into(const q35k_weight* w, const float* d_x, float* d_y, in
         return gemv(w, nullptr, d_y, tokens, s, true, d_x, ldy, peers, argmax, d_up);
     int rc;
     if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK) return rc;
-    cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s, d_up);
+    cudaError_t e = launch_quantize_q8k(d_x, d_q8, w->n_in, tokens, chunk, s, d_up, q8_interleave_min_rows(w->type));
     if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
     return gemv(w, d_q8, d_y, tokens, s, true, nullptr, ldy, peers, argmax);
 }
@@ -413,7 +413,7 @@ int q35k_ctx::matmul_shared(const q35k_weight* const* ws, int count, const float
     const q35k_weight* w0 = ws[0];
     const int chunk = gemv_chunk(w0);
     int prepped = -1;  // arithmetic of the prepared GEMM operands (0 exact, 1 fast), -1: none
-    bool quantized = false;
+    int quantized = 0;  // layout threshold of the planar Q8_K in d_q8 (q8_interleave_min_rows), 0: none
     int rc;
     for (int i = 0; i < count; i++) {
         const q35k_weight* w = ws[i];
@@ -440,12 +440,15 @@ int q35k_ctx::matmul_shared(const q35k_weight* const* ws, int count, const float
         if (tokens <= chunk && gemv_fuses_quantize(type, w0->nb, rows, tokens, num_sms)) {
             rc = gemv(lw[0], nullptr, ly[0], tokens, s, true, d_x, 0, nullptr, nullptr, nullptr, lw + 1, ly + 1, n - 1);
         } else {
-            if (!quantized) {
+            // One quantization serves every type with the same planar layout
+            // (Q4_K and Q5_K; Q6_K interleaves from more tokens).
+            const int ilv = q8_interleave_min_rows(type);
+            if (quantized != ilv) {
                 if ((rc = ensure_dev((void**)&d_q8, &q8_cap, q8_planar_total(tokens, w0->nb, chunk), false)) != Q35K_OK)
                     return rc;
-                cudaError_t e = launch_quantize_q8k(d_x, d_q8, w0->n_in, tokens, chunk, s);
+                cudaError_t e = launch_quantize_q8k(d_x, d_q8, w0->n_in, tokens, chunk, s, nullptr, ilv);
                 if (e != cudaSuccess) return cuda_fail(e, "Q8_K quantize launch");
-                quantized = true;
+                quantized = ilv;
             }
             rc = gemv(lw[0], d_q8, ly[0], tokens, s, true, nullptr, 0, nullptr, nullptr, nullptr, lw + 1, ly + 1, n - 1);
         }
@@ -486,7 +489,8 @@ int q35k_matmul_q8k_dev(q35k_ctx* c, const q35k_weight* w, const void* d_q8k, fl
     // The caller's BlockQ8K rows -> the GEMV's planar layout.
     if ((rc = c->ensure_dev((void**)&c->d_q8, &c->q8_cap, q8_planar_total(tokens, w->nb, chunk), false)) != Q35K_OK)
         return rc;
-    cudaError_t e = launch_q8k_to_planar((const uint8_t*)d_q8k, c->d_q8, w->n_in, tokens, chunk, s);
+    cudaError_t e = launch_q8k_to_planar((const uint8_t*)d_q8k, c->d_q8, w->n_in, tokens, chunk, s,
+                                         q8_interleave_min_rows(w->type));
     if (e != cudaSuccess) return c->cuda_fail(e, "Q8_K repack launch");
     return c->gemv(w, c->d_q8, d_y, tokens, s);
 }

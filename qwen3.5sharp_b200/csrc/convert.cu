@@ -16,7 +16,7 @@ namespace q35k {
 // Output goes either to BlockQ8K blocks (chunk == 0) or to the planar layout
 // (device_common.cuh) in chunks of `chunk` rows.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int rows, int chunk) {
+__device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int rows, int chunk, int ilv_rows) {
     Q8Out o;
     if (chunk == 0) {
         uint8_t* blk = q8 + ((size_t)row * nb + b) * Q8K_BYTES;
@@ -30,7 +30,7 @@ __device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int
         const Q8Planar pl = q8_planar(mj, nb);
         const size_t blk = (size_t)b * mj + rr;  // block-major
         o.d = reinterpret_cast<uint32_t*>(base + pl.d) + (size_t)b * pl.rows4 + rr;
-        if (mj >= Q8_INTERLEAVE_MIN_ROWS) {
+        if (ilv_rows > 0 && mj >= ilv_rows) {
             // word w of row rr at word w * mj + rr of the block's qs
             o.qs = reinterpret_cast<uint32_t*>(base + pl.qs + (size_t)b * mj * QK) + rr;
             o.qs_stride = mj;
@@ -44,7 +44,7 @@ __device__ __forceinline__ Q8Out q8_out(uint8_t* q8, int row, int b, int nb, int
 
 __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restrict__ x, const float* __restrict__ up,
                                                            uint8_t* __restrict__ q8, int nb, int total_blocks, int rows,
-                                                           int chunk) {
+                                                           int chunk, int ilv_rows) {
     // A GEMV launched after this kernel with programmatic stream
     // serialization may start now: it streams weights first and waits on the
     // grid dependency (full completion of this grid) before reading q8.
@@ -54,43 +54,46 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     if (warp >= total_blocks) return;
     const int row = warp / nb, b = warp % nb;
     const size_t off = (size_t)row * nb * QK + (size_t)b * QK;
-    warp_quantize_q8k_block(x + off, q8_out(q8, row, b, nb, rows, chunk), lane, up ? up + off : nullptr);
+    warp_quantize_q8k_block(x + off, q8_out(q8, row, b, nb, rows, chunk, ilv_rows), lane, up ? up + off : nullptr);
 }
 
 cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s,
-                                const float* up) {
+                                const float* up, int ilv_rows) {
     const int nb = k / QK;
     const int total = nb * rows;
     if (total == 0) return cudaSuccess;
     const int warps_per_cta = 8;
     const int grid = (total + warps_per_cta - 1) / warps_per_cta;
-    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, up, q8, nb, total, rows, planar_chunk);
+    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, up, q8, nb, total, rows, planar_chunk, ilv_rows);
     return cudaGetLastError();
 }
 
 // BlockQ8K rows (a caller's pre-quantized activations) -> the planar layout,
 // one warp per block: word 0 = d, 1..64 = qs, 65..72 = bsums.
 __global__ void __launch_bounds__(256) q8k_to_planar_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
-                                                            int nb, int total_blocks, int rows, int chunk) {
+                                                            int nb, int total_blocks, int rows, int chunk,
+                                                            int ilv_rows) {
     asm volatile("griddepcontrol.launch_dependents;");
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= total_blocks) return;
     const uint32_t* in = reinterpret_cast<const uint32_t*>(src + (size_t)warp * Q8K_BYTES);
-    const Q8Out out = q8_out(dst, warp / nb, warp % nb, nb, rows, chunk);
+    const Q8Out out = q8_out(dst, warp / nb, warp % nb, nb, rows, chunk, ilv_rows);
     if (lane == 0) *out.d = __ldg(in);
     out.qs[lane * out.qs_stride] = __ldg(in + 1 + lane);
     out.qs[(32 + lane) * out.qs_stride] = __ldg(in + 33 + lane);
     if (lane < 8) reinterpret_cast<uint32_t*>(out.bs)[lane] = __ldg(in + 65 + lane);
 }
 
-cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s) {
+cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s,
+                                 int ilv_rows) {
     const int nb = k / QK;
     const int total = nb * rows;
     if (total == 0) return cudaSuccess;
     const int warps_per_cta = 8;
     q8k_to_planar_kernel<<<(total + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, 0, s>>>(src, dst, nb,
-                                                                                                      total, rows, chunk);
+                                                                                                      total, rows, chunk,
+                                                                                                      ilv_rows);
     return cudaGetLastError();
 }
 

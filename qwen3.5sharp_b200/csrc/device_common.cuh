@@ -57,12 +57,15 @@ __host__ __device__ inline int block_bytes(int type) {
 //   to 4) | bsums [nb][rows][16] int16.
 // Tokens are grouped in chunks of `chunk` rows (one GEMV launch each); chunk
 // j starts at j * q8_planar(chunk, nb).bytes and its planes are sized by its
-// own row count.  In a chunk of Q8_INTERLEAVE_MIN_ROWS or more rows the qs
-// plane is word-interleaved instead, [nb][64][rows] 32-bit words (word w =
+// own row count.  In a chunk of q8_interleave_min_rows(type) or more rows the
+// qs plane is word-interleaved instead, [nb][64][rows] 32-bit words (word w =
 // values 4w..4w+3): the layout in which the tensor-core GEMV (gemv_dot.cuh)
-// reads its B fragments, one conflict-free 32-bit load per lane.
+// reads its B fragments, one coalesced 32-bit load per lane.  The mma form's
+// cost per tile does not depend on the token count while the dp4a form's
+// grows with it; on B200 the mma form wins from 3 tokens for Q4_K / Q5_K and
+// from 6 for Q6_K (whose dp4a decode is cheaper per token).
 // ---------------------------------------------------------------------------
-constexpr int Q8_INTERLEAVE_MIN_ROWS = 5;
+__host__ __device__ constexpr int q8_interleave_min_rows(int type) { return type == TYPE_Q6_K ? 6 : 3; }
 struct Q8Planar {
     size_t qs, d, bs, bytes;
     int rows, rows4;

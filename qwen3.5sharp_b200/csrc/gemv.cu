@@ -33,7 +33,9 @@ constexpr int GEMV_SPLIT_WARPS = 10;      // warps of a split-K unit
 constexpr int GEMV_FUSED_MAX_TOKENS = 2;  // token counts with a fused-quantize variant
 // The fused quantizer writes the plain planar layout; 5+ tokens take the
 // tensor-core dots over the word-interleaved one.
-static_assert(GEMV_FUSED_MAX_TOKENS < Q8_INTERLEAVE_MIN_ROWS, "fused GEMV layouts");
+static_assert(GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q4_K) &&
+                  GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q6_K),
+              "fused GEMV layouts");
 constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per split-K work unit (target)
 constexpr int GEMV_ROW_BYTES = 96 * 1024;   // largest whole-row unit
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
@@ -47,7 +49,7 @@ struct SmemLayout {
 // Dynamic shared memory of one GEMV CTA (16-byte aligned regions):
 // U+1 mbarriers | flags | U weight tiles | planar Q8_K of U blocks | W*M*32
 // partial sums.
-__host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int units, int m, int warps) {
+__host__ __device__ inline SmemLayout gemv_smem_layout(int type, int tile_bytes, int units, int m, int warps) {
     SmemLayout L;
     const int rows4 = (m + 3) / 4 * 4;
     L.bars = 0;
@@ -55,7 +57,7 @@ __host__ __device__ inline SmemLayout gemv_smem_layout(int tile_bytes, int units
     L.tiles = align_up(L.flags + 16, 128);
     L.q8 = L.tiles + units * tile_bytes;
     // 5+ tokens read their activations from global memory (L2), not staged.
-    L.red = L.q8 + (m >= Q8_INTERLEAVE_MIN_ROWS ? 0 : units * (m * QK + rows4 * 4 + m * 32));
+    L.red = L.q8 + (m >= q8_interleave_min_rows(type) ? 0 : units * (m * QK + rows4 * 4 + m * 32));
     L.total = L.red + warps * m * 32 * 4;
     return L;
 }
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
     const int U = p.unit_blocks, W = p.warps, nb = a.nb;
-    const SmemLayout L = gemv_smem_layout(TILE, U, M, W);
+    const SmemLayout L = gemv_smem_layout(TYPE, TILE, U, M, W);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);  // [0, kr): tiles, [kr]: activations
     uint8_t* tiles = smem + L.tiles;
 
@@ -134,7 +136,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
             mbar_arrive_expect_tx(&bars[t], TILE);
             bulk_g2s(tiles + (size_t)t * TILE, src + (size_t)t * TILE, TILE, &bars[t]);
         }
-        if (!FUSED && M < Q8_INTERLEAVE_MIN_ROWS) {
+        if (!FUSED && M < q8_interleave_min_rows(TYPE)) {
             // Then the activations, once the producing kernel has completed.
             griddep_wait();
             mbar_arrive_expect_tx(&bars[kr], qs_bytes + d_bytes + bs_bytes);
@@ -149,7 +151,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     asm volatile("griddepcontrol.launch_dependents;");
     // 5+ tokens: the unit's K-range of the planar Q8_K in global memory (each
     // warp loads its B operand words directly; L2 serves the CTAs of a K-range).
-    constexpr bool Q8_GLOBAL = M >= Q8_INTERLEAVE_MIN_ROWS;
+    constexpr bool Q8_GLOBAL = M >= q8_interleave_min_rows(TYPE);
     const Q8Smem q8 = Q8_GLOBAL
         ? Q8Smem{reinterpret_cast<const int8_t*>(a.q8 + pl.qs + (size_t)b0 * M * QK),
                  reinterpret_cast<const float*>(a.q8 + pl.d + (size_t)b0 * pl.rows4 * 4),
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     }
 
     float* red = reinterpret_cast<float*>(smem + L.red);
-    if constexpr (M >= Q8_INTERLEAVE_MIN_ROWS) {
+    if constexpr (M >= q8_interleave_min_rows(TYPE)) {
         // Tensor-core dots (gemv_dot.cuh); the staged qs plane is word-interleaved.
         float acc[2][2][2] = {};
         for (int t = warp; ok && t < kr; t += W) {
@@ -281,7 +283,7 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
         u = nb;
         // 5+ tokens: 10 warps (two tiles each at 20 tiles), so that two CTAs
         // share an SM and one's copies overlap the other's decode.
-        max_warps = m >= Q8_INTERLEAVE_MIN_ROWS ? GEMV_SPLIT_WARPS : GEMV_MAX_WARPS;
+        max_warps = m >= q8_interleave_min_rows(type) ? GEMV_SPLIT_WARPS : GEMV_MAX_WARPS;
     } else {
         u = std::max(1, std::min(nb, GEMV_UNIT_BYTES / tile));
         int splits = (nb + u - 1) / u;
@@ -290,12 +292,12 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
         max_warps = GEMV_SPLIT_WARPS;
     }
     // The activations of one unit must fit next to its tiles.
-    while (u > 1 && gemv_smem_layout(tile, u, m, std::min(u, max_warps)).total > GEMV_SMEM_LIMIT) u--;
+    while (u > 1 && gemv_smem_layout(type, tile, u, m, std::min(u, max_warps)).total > GEMV_SMEM_LIMIT) u--;
     p.unit_blocks = u;
     p.splits = (nb + u - 1) / u;
     p.warps = std::min(u, max_warps);
     p.grid = p.groups * p.splits;
-    p.smem_bytes = (size_t)gemv_smem_layout(tile, u, m, p.warps).total;
+    p.smem_bytes = (size_t)gemv_smem_layout(type, tile, u, m, p.warps).total;
     p.partial_bytes = p.splits > 1 ? (size_t)p.groups * p.splits * GEMV_MAX_TOKENS * 32 * sizeof(float) : 0;
     p.counters = (size_t)p.groups;
     p.fits = p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;

@@ -192,11 +192,11 @@ __device__ __forceinline__ void block_dot_q6k(const uint8_t* __restrict__ tile, 
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core form for 5..8 tokens (legacy mma.sync: the weights' decode, not
-// the MACs, bounds this HBM-streaming kernel, so the point is fewer
-// instructions per weight, not tcgen05 throughput).  Its cost per tile does
-// not depend on the token count (an mma always spans 8 token columns), while
-// the dp4a form's grows with it: on B200 the two cross between 4 and 5 tokens.  A warp computes its
+// Tensor-core form for 3..8 tokens (6..8 for Q6_K; q8_interleave_min_rows)
+// (legacy mma.sync: the weights' decode, not the MACs, bounds this
+// HBM-streaming kernel, so the point is fewer instructions per weight, not
+// tcgen05 throughput).  Its cost per tile does not depend on the token count
+// (an mma always spans 8 token columns), while the dp4a form's grows with it.  A warp computes its
 // 32-row tile as two m16 halves x 8 token columns.  Lane (g = lane/4,
 // c = lane%4) supplies rows g, g+8 of a half and token g of the B operand:
 //   * integer dots per sub-block: mma m16n8k32 u8 x s8 (Q4_K/Q5_K, 32-value
@@ -407,7 +407,7 @@ __device__ __forceinline__ void half_dot_q6k(const uint8_t* __restrict__ tile, i
     mma_epilogue<true>(acc, S, bias, d0, d1, 0.f, 0.f, B.dx0, B.dx1);
 }
 
-// One 32-row tile (one super-block) for 5..8 tokens; acc[half][i][j] = row
+// One 32-row tile (one super-block) for 3..8 tokens; acc[half][i][j] = row
 // 16*half + g + 8i, token 2c + j.
 template <int TYPE, int M>
 __device__ __forceinline__ void tile_dot_mma(const uint8_t* tile, int lane, const Q8Smem& q8, int b,

@@ -14,11 +14,14 @@ namespace q35k {
 // early (that kernel must wait on the grid dependency before reading q8).
 // With `up` (laid out like x) the rows quantized are silu(x) * up (ffn_down's
 // input, QuantizeQ8Kx4.Quantize4x8Silu).
+// Planar chunks of ilv_rows or more rows (ilv_rows > 0; see q8_interleave_min_rows)
+// get the word-interleaved qs plane.
 cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, int planar_chunk, cudaStream_t s,
-                                const float* up = nullptr);
+                                const float* up = nullptr, int ilv_rows = 0);
 
 // BlockQ8K rows -> planar layout in chunks of `chunk` rows.
-cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s);
+cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int rows, int chunk, cudaStream_t s,
+                                 int ilv_rows);
 
 // Bit-exact dequantization of `rows` GGUF rows of k values.
 cudaError_t launch_dequantize(int type, const uint8_t* blocks, float* y, int k, int rows, cudaStream_t s);

@@ -125,7 +125,8 @@ extern "C" int q35k_matmul_static_dev(const q35k_weight* w, const float* d_x, fl
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // The array keeps the last call's contents: clear what must start at zero.
     e = cudaMemsetAsync(base, 0, err_bytes + cnt_bytes, s);
-    if (e == cudaSuccess && !fused) e = launch_quantize_q8k(d_x, q8, w->n_in, tokens, tokens, s);
+    if (e == cudaSuccess && !fused)
+        e = launch_quantize_q8k(d_x, q8, w->n_in, tokens, tokens, s, nullptr, q8_interleave_min_rows(w->type));
     if (e == cudaSuccess) {
         GemvArgs a{};
         a.tiles = w->tiles;
