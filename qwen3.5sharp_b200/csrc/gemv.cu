@@ -31,7 +31,7 @@ constexpr int GEMV_MAX_TOKENS = 8;
 constexpr int GEMV_MAX_WARPS = 20;        // one warp per tile of a whole-row unit
 constexpr int GEMV_SPLIT_WARPS = 10;      // warps of a split-K unit
 constexpr int GEMV_FUSED_MAX_TOKENS = 2;  // token counts with a fused-quantize variant
-// The fused quantizer writes the plain planar layout; 5+ tokens take the
+// The fused quantizer writes the plain planar layout; the mma token counts take the
 // tensor-core dots over the word-interleaved one.
 static_assert(GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q4_K) &&
                   GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q6_K),
@@ -56,7 +56,7 @@ __host__ __device__ inline SmemLayout gemv_smem_layout(int type, int tile_bytes,
     L.flags = 8 * (units + 1);
     L.tiles = align_up(L.flags + 16, 128);
     L.q8 = L.tiles + units * tile_bytes;
-    // 5+ tokens read their activations from global memory (L2), not staged.
+    // The mma token counts read their activations from global memory (L2), not staged.
     L.red = L.q8 + (m >= q8_interleave_min_rows(type) ? 0 : units * (m * QK + rows4 * 4 + m * 32));
     L.total = L.red + warps * m * 32 * 4;
     return L;
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     // SMs this grid frees; it reads activations and writes results only
     // after its own griddepcontrol.wait, i.e. after this grid completed.
     asm volatile("griddepcontrol.launch_dependents;");
-    // 5+ tokens: the unit's K-range of the planar Q8_K in global memory (each
+    // mma token counts: the unit's K-range of the planar Q8_K in global memory (each
     // warp loads its B operand words directly; L2 serves the CTAs of a K-range).
     constexpr bool Q8_GLOBAL = M >= q8_interleave_min_rows(TYPE);
     const Q8Smem q8 = Q8_GLOBAL
@@ -281,7 +281,7 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     int u, max_warps;
     if (nb <= GEMV_MAX_WARPS && nb * tile <= GEMV_ROW_BYTES && p.groups >= num_sms) {
         u = nb;
-        // 5+ tokens: 10 warps (two tiles each at 20 tiles), so that two CTAs
+        // mma token counts: 10 warps (two tiles each at 20 tiles), so that two CTAs
         // share an SM and one's copies overlap the other's decode.
         max_warps = m >= q8_interleave_min_rows(type) ? GEMV_SPLIT_WARPS : GEMV_MAX_WARPS;
     } else {
