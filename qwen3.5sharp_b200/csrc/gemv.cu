@@ -180,15 +180,23 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, G
     float* red = reinterpret_cast<float*>(smem + L.red);
     if constexpr (M >= q8_interleave_min_rows(TYPE)) {
         // Tensor-core dots (gemv_dot.cuh); the staged qs plane is word-interleaved.
+        // A warp's B operands come from L2: each tile's are loaded before
+        // its weight tile is awaited, and the next tile's during this one's
+        // decode, so their latency hides behind the weight stream.
         float acc[2][2][2] = {};
+        const int g = lane >> 2, c = lane & 3;
+        MmaB<M> B;
+        if (warp < kr) B.load(q8, warp, g, c);
         for (int t = warp; ok && t < kr; t += W) {
+            MmaB<M> Bn;
+            if (t + W < kr) Bn.load(q8, t + W, g, c);
             if (!mbar_wait_bounded(&bars[t], 0, a.err)) {
                 ok = false;
                 break;
             }
-            tile_dot_mma<TYPE, M>(tiles + (size_t)t * TILE, lane, q8, t, acc);
+            tile_dot_mma<TYPE, M>(tiles + (size_t)t * TILE, lane, B, acc);
+            B = Bn;
         }
-        const int g = lane >> 2, c = lane & 3;
 #pragma unroll
         for (int hf = 0; hf < 2; hf++)
 #pragma unroll

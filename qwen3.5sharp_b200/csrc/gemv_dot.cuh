@@ -410,11 +410,9 @@ __device__ __forceinline__ void half_dot_q6k(const uint8_t* __restrict__ tile, i
 // One 32-row tile (one super-block) for 3..8 tokens; acc[half][i][j] = row
 // 16*half + g + 8i, token 2c + j.
 template <int TYPE, int M>
-__device__ __forceinline__ void tile_dot_mma(const uint8_t* tile, int lane, const Q8Smem& q8, int b,
+__device__ __forceinline__ void tile_dot_mma(const uint8_t* tile, int lane, const MmaB<M>& B,
                                              float (&acc)[2][2][2]) {
     const int g = lane >> 2, c = lane & 3;
-    MmaB<M> B;
-    B.load(q8, b, g, c);
 #pragma unroll
     for (int hf = 0; hf < 2; hf++) {
         if (TYPE == TYPE_Q6_K)
