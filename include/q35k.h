@@ -150,14 +150,17 @@ int q35k_matmul_silu(q35k_ctx* ctx, const q35k_weight* w, const float* gate, con
 int q35k_matmul_silu_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_gate, const float* d_up, float* d_y,
                          int tokens, void* stream);
 
-/* Arithmetic of the tensor-core prefill GEMM (Q4_K, tokens >= 16).  No
+/* Arithmetic of the tensor-core prefill GEMM (tokens >= 16).  No
  * counterpart in the reference, which has one arithmetic:
  *   Q35K_GEMM_EXACT (default): the reference's -- Q8_K activations, exact
- *     integer dots per super-block, fp32 scaling per super-block (results
- *     within fp32 rounding of the reference's);
+ *     products, fp32 scaling per super-block (results within fp32 rounding
+ *     of the reference's).  Q4_K and Q5_K run on the tensor cores; Q6_K
+ *     (whose sc * (q - 32) has no exact fp16 form) runs on the GEMV;
  *   Q35K_GEMM_FAST: fp16-rounded dequantized weights times fp16-rounded
  *     dequantized Q8_K activations, one fp32 accumulator per tile (about
- *     4e-4 of max |y| from the reference's results); faster. */
+ *     4e-4 of max |y| from the reference's results); faster, and Q6_K runs
+ *     on the tensor cores too.  A weight whose fp16 values could overflow
+ *     (flagged at upload) keeps the exact path. */
 #define Q35K_GEMM_EXACT 0
 #define Q35K_GEMM_FAST 1
 int q35k_set_gemm_mode(q35k_ctx* ctx, int mode);
