@@ -398,7 +398,7 @@ def run_ours(args):
 
 OUR_KERNELS = ("gemv_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel",
                "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel", "signal_wait_kernel",
-               "argmax_index_kernel")
+               "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel")
 
 
 def count_launches(torch, step):
