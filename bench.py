@@ -353,7 +353,7 @@ def run_ours(args):
                 "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
-                "kernel": "gemv_kernel<Q6_K,1,fused>", "kernel_ms": gemv_avg,
+                "kernel": "q35k_decode_kernel<Q6_K,1,fused>", "kernel_ms": gemv_avg,
                 "algorithmic_bytes_per_launch": nbytes_local}
 
     launches_per_step = count_launches(torch, step)
@@ -396,7 +396,7 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-OUR_KERNELS = ("gemv_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel",
+OUR_KERNELS = ("q35k_decode_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel",
                "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel", "signal_wait_kernel",
                "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel")
 

@@ -5,8 +5,8 @@
  * Each entry point replaces one reference kernel entry point the model
  * forward pass calls (reference paths are relative to the DracoUnion/
  * Qwen3.5Sharp tree; "Kernels/" = src/Qwen35Sharp.Kernels/, "Model/" =
- * src/Qwen35Sharp.Model/).  The C# binding a maintainer adds is in
- * INTEGRATION.md.
+ * src/Qwen35Sharp.Model/).  The C# P/Invoke declarations a maintainer adds
+ * next to those entry points ship as bindings/Q35k.cs.
  *
  * Conventions (mirroring the reference's, Model/Qwen35Model.Decode.cs:13-112):
  *   - Matrices are row-major: x is [tokens][n_in] fp32, y is [tokens][n_out]
@@ -20,7 +20,7 @@
  *     reference's CpuThreadPool/ScratchArena pair is not re-entrant.
  *   - Every call returns a status; q35k_last_error() describes the last
  *     failure.  The C# shim maps statuses to the exception types the
- *     reference throws.
+ *     reference throws (the comments on the Q35K_E* codes below).
  *   - There is no CPU fallback: a context cannot be created without an
  *     sm_100 device.
  */
@@ -105,6 +105,20 @@ int q35k_matmul(q35k_ctx* ctx, const q35k_weight* w, const float* x, float* y, i
  * (Kernels/MulMatQ4K.cs:28-43), Q5K.GemvPrequant (Kernels/Q5K.cs:97-112),
  * Q6K.GemvPrequant (Kernels/Q6K.cs:415-430). */
 int q35k_matmul_q8k(q35k_ctx* ctx, const q35k_weight* w, const void* q8k, float* y, int tokens);
+
+/* Page-lock a caller's host buffer (cudaHostRegister, mapped and portable) so
+ * that the host-pointer calls use it in place: q35k_matmul copies x straight
+ * from it and -- for decode calls -- has the GEMV store y over the bus
+ * straight into it, instead of staging both through the context's pinned
+ * buffers (one host memcpy of y per call saved).  No counterpart in the
+ * reference, whose model keeps persistent input and output buffers
+ * (NativeBuffer, Kernels/NativeBuffer.cs:5-35; the ScratchArena slots); those
+ * are the buffers to register, once, at load.  Buffers that are already
+ * page-locked (pinned allocations) are used in place without registering.
+ * Unregister before freeing the memory.  Q35K_EINVAL if the range is already
+ * registered, Q35K_ENOMEM if the pages cannot be locked. */
+int q35k_host_register(q35k_ctx* ctx, void* ptr, size_t bytes);
+int q35k_host_unregister(q35k_ctx* ctx, void* ptr);
 
 /* Device-pointer variants of the two calls above, asynchronous on `stream`
  * (a cudaStream_t; NULL = the context's own stream). */
@@ -253,7 +267,11 @@ int q35k_shard_matmul(q35k_shard* s, const q35k_sharded_weight* w, const float* 
  *     calls that overlap on the GPU (other streams, other host threads) race
  *     on the array -- do not issue them.
  *   - A bounded device wait that expires inside this call's kernels is not
- *     reported (use q35k_matmul_dev + q35k_sync to observe those). */
+ *     reported (use q35k_matmul_dev + q35k_sync to observe those).
+ *   - The resolved address belongs to the device's primary context: do not
+ *     reset it (cudaDeviceReset, or a library that resets the primary
+ *     context) between calls, or later calls would write through a stale
+ *     address. */
 #define Q35K_STATIC_MAX_TOKENS 8
 #define Q35K_STATIC_SCRATCH_BYTES (8u << 20)
 int q35k_matmul_static_dev(const q35k_weight* w, const float* d_x, float* d_y, int tokens, void* stream);

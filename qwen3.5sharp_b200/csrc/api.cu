@@ -468,6 +468,29 @@ static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, c
 
 static cudaStream_t pick(q35k_ctx* c, void* stream) { return stream ? (cudaStream_t)stream : c->stream; }
 
+// Device address of a caller's host buffer [p, p + bytes) when it is
+// page-locked and mapped into the device's address space as one contiguous
+// range (registered with q35k_host_register, or allocated pinned by the
+// caller); nullptr for pageable memory.  Host-pointer calls then read x and
+// write y in place instead of staging them through the context's buffers.
+static void* host_alias(const void* p, size_t bytes) {
+    if (!p || bytes == 0) return nullptr;
+    cudaPointerAttributes a0, a1;
+    if (cudaPointerGetAttributes(&a0, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (a0.type != cudaMemoryTypeHost || !a0.devicePointer) return nullptr;
+    const char* last = static_cast<const char*>(p) + bytes - 1;
+    if (cudaPointerGetAttributes(&a1, last) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (a1.type != cudaMemoryTypeHost || static_cast<char*>(a1.devicePointer) != static_cast<char*>(a0.devicePointer) + (bytes - 1))
+        return nullptr;
+    return a0.devicePointer;
+}
+
 // Device buffers handed in by the caller: the quantizer reads x as float4,
 // the GEMV reads Q8_K blocks and writes y as 32-bit words.
 static int check_alignment(q35k_ctx* c, const void* x, size_t x_align, const void* y, size_t y_align) {
@@ -509,36 +532,73 @@ int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int
     cudaSetDevice(c->device);
     const size_t in_bytes = (size_t)tokens * w->n_in * sizeof(float);
     const size_t out_bytes = (size_t)tokens * w->n_out * sizeof(float);
+    // Page-locked caller buffers (q35k_host_register) are used in place: x is
+    // copied straight from it, and y written straight into it.  Pageable ones
+    // go through the context's pinned staging buffers.
+    const bool x_pinned = host_alias(x, in_bytes) != nullptr;
+    float* y_alias = static_cast<float*>(host_alias(y, out_bytes));
     if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
     if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
-    if ((rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
+    if (!x_pinned && (rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
     if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
-    std::memcpy(c->h_in, x, in_bytes);
-    cudaError_t e = cudaMemcpyAsync(c->d_x, c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (!x_pinned) std::memcpy(c->h_in, x, in_bytes);
+    cudaError_t e = cudaMemcpyAsync(c->d_x, x_pinned ? x : c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of x");
-    // Decode calls: the GEMV stores y straight into the pinned staging buffer
-    // (mapped into the device's address space), so its transfer overlaps the
-    // kernel and no copy follows it.  Prefill calls (tensor-core GEMM, whose
-    // tiles would cross the bus piece by piece) copy y back afterwards.
+    // Decode calls: the GEMV stores y over the bus straight into host memory
+    // (the caller's page-locked y, or the mapped staging buffer), so the
+    // transfer overlaps the kernel and no copy follows it.  Prefill calls
+    // (tensor-core GEMM, whose tiles would cross the bus piece by piece) copy
+    // y back afterwards.
     float* d_out = c->d_y;
     bool direct = false;
     if (!c->uses_gemm(w, tokens)) {
-        void* dp = nullptr;
-        if (cudaHostGetDevicePointer(&dp, c->h_out, 0) == cudaSuccess && dp) {
+        void* dp = y_alias;
+        if (!dp && (cudaHostGetDevicePointer(&dp, c->h_out, 0) != cudaSuccess || !dp)) {
+            cudaGetLastError();
+            dp = nullptr;
+        }
+        if (dp) {
             d_out = static_cast<float*>(dp);
             direct = true;
-        } else {
-            cudaGetLastError();
         }
     }
     if ((rc = q35k_matmul_dev(c, w, c->d_x, d_out, tokens, c->stream)) != Q35K_OK) return rc;
     unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
-    e = direct ? cudaSuccess : cudaMemcpyAsync(c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+    float* host_dst = y_alias ? y : static_cast<float*>(c->h_out);
+    e = direct ? cudaSuccess : cudaMemcpyAsync(host_dst, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "matmul");
     if (*h_err) return c->on_device_error(*h_err);
-    std::memcpy(y, c->h_out, out_bytes);
+    if (!y_alias) std::memcpy(y, c->h_out, out_bytes);
+    return Q35K_OK;
+}
+
+int q35k_host_register(q35k_ctx* c, void* p, size_t bytes) {
+    if (!c) return Q35K_EINVAL;
+    if (!p || bytes == 0) return c->fail(Q35K_EINVAL, "host_register: NULL pointer or zero size");
+    cudaSetDevice(c->device);
+    const cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
+    if (e == cudaErrorHostMemoryAlreadyRegistered) {
+        cudaGetLastError();
+        return c->fail(Q35K_EINVAL, "host_register: the range is already page-locked");
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return c->fail(Q35K_ENOMEM, "host_register: cudaHostRegister(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    }
+    return Q35K_OK;
+}
+
+int q35k_host_unregister(q35k_ctx* c, void* p) {
+    if (!c) return Q35K_EINVAL;
+    if (!p) return c->fail(Q35K_EINVAL, "host_unregister: NULL pointer");
+    cudaSetDevice(c->device);
+    const cudaError_t e = cudaHostUnregister(p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return c->fail(Q35K_EINVAL, "host_unregister: %s", cudaGetErrorString(e));
+    }
     return Q35K_OK;
 }
 

@@ -95,7 +95,7 @@ __device__ __forceinline__ void warp_argmax_commit(unsigned long long key, unsig
 // while the weight tiles are in flight, instead of staging planar Q8_K from
 // a.q8 -- one kernel per call, used when that slice is small (decode).
 template <int TYPE, int M, bool FUSED>
-__global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) gemv_kernel(GemvArgs a, GemvPlan p) {
+__global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvArgs a, GemvPlan p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
     const int U = p.unit_blocks, W = p.warps, nb = a.nb;
@@ -324,9 +324,9 @@ int gemv_max_tokens(int nb) {
 // (called once per context).
 template <int TYPE, int M>
 static void configure_typed() {
-    cudaFuncSetAttribute(gemv_kernel<TYPE, M, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+    cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
     if (M <= GEMV_FUSED_MAX_TOKENS)
-        cudaFuncSetAttribute(gemv_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>,
+        cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
 }
 
@@ -363,9 +363,9 @@ static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream
     cfg.numAttrs = pdl ? 1 : 0;
     // The fused variant exists for small token counts only.
     if (a.x != nullptr && M <= GEMV_FUSED_MAX_TOKENS)
-        return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>, a, p);
+        return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>, a, p);
     if (a.x != nullptr) return cudaErrorInvalidValue;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<TYPE, M, false>, a, p);
+    return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, false>, a, p);
 }
 
 template <int TYPE>

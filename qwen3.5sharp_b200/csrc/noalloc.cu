@@ -22,6 +22,10 @@
 //     contents: each call clears the arrival counters it uses before its
 //     kernels run.  Calls that overlap on the GPU (two streams, or two host
 //     threads) race on the array and must not be issued.
+//   * The cached address belongs to the device's primary context: a
+//     cudaDeviceReset (or another library resetting the primary context)
+//     between calls leaves it dangling, so the context must not be reset
+//     while this entry point is in use.
 #include "../../include/q35k.h"
 #include "api_internal.h"
 #include "device_common.cuh"
@@ -100,12 +104,19 @@ extern "C" int q35k_matmul_static_dev(const q35k_weight* w, const float* d_x, fl
     const bool fused = gemv_fuses_quantize(w->type, w->nb, w->n_out, tokens, sms);
 
     // Carve the scratch: error word, counters, partial sums, planar Q8_K.
+    if (!p.fits) {
+        set_thread_error("q35k_matmul_static_dev: the decode GEMV has no shared-memory plan for this shape");
+        return Q35K_ENOTSUP;
+    }
+    // The kernel indexes the split-K partial sums as [groups][splits][tokens][32]
+    // floats (the context path sizes them for 8 tokens, as it reuses them).
     const size_t err_bytes = 256;
     const size_t cnt_bytes = (p.counters * sizeof(int) + 255) / 256 * 256;
-    const size_t part_bytes = (p.partial_bytes + 255) / 256 * 256;
+    const size_t part_raw = p.splits > 1 ? (size_t)p.groups * p.splits * tokens * 32 * sizeof(float) : 0;
+    const size_t part_bytes = (part_raw + 255) / 256 * 256;
     const size_t q8_bytes = fused ? 0 : (q8_planar(tokens, w->nb).bytes + 255) / 256 * 256;
     const size_t need = err_bytes + cnt_bytes + part_bytes + q8_bytes;
-    if (need > NOALLOC_SCRATCH_BYTES || !p.fits) {
+    if (need > NOALLOC_SCRATCH_BYTES) {
         char buf[256];
         snprintf(buf, sizeof buf,
                  "q35k_matmul_static_dev: this shape needs %zu bytes of scratch; the static array holds %zu "

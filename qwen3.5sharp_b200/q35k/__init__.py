@@ -173,6 +173,14 @@ class Context:
         info = gguf.tensors[name]
         return Weight(self, h, info.type, int(info.shape[0]), int(info.shape[1]) if len(info.shape) > 1 else 1)
 
+    def host_register(self, a: np.ndarray):
+        """Page-lock a persistent host array (q35k_host_register) so that the
+        host-pointer calls read and write it in place."""
+        self._check(self.L.q35k_host_register(self.h, a.ctypes.data, a.nbytes))
+
+    def host_unregister(self, a: np.ndarray):
+        self._check(self.L.q35k_host_unregister(self.h, a.ctypes.data))
+
     # -- host-pointer calls (synchronous) --
     def matmul(self, w: "Weight", x: np.ndarray, tokens: int | None = None, out: np.ndarray | None = None) -> np.ndarray:
         """y = x @ W^T (q35k_matmul).  `out`: a float32 C-contiguous array of

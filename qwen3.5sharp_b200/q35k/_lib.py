@@ -35,6 +35,8 @@ SIGNATURES = {
     "q35k_matmul": ([_vp, _vp, _vp, _vp, _i32], _i32),
     "q35k_matmul_q8k": ([_vp, _vp, _vp, _vp, _i32], _i32),
     "q35k_matmul_dev": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
+    "q35k_host_register": ([_vp, _vp, _sz], _i32),
+    "q35k_host_unregister": ([_vp, _vp], _i32),
     "q35k_matmul_argmax": ([_vp, _vp, _vp, _vp, _i32], _i32),
     "q35k_matmul_argmax_dev": ([_vp, _vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_matmul_shared": ([_vp, _pp, _i32, _vp, _pp, _i32], _i32),

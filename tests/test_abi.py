@@ -80,3 +80,17 @@ def test_mirror_argument_errors_without_gpu():
         q35k.MulMatQ4K.Gemv(np.zeros(10, np.uint8), np.zeros(100, np.float32), None, 100, 1)
     with pytest.raises(q35k.ArgumentException):
         q35k.Q8K.QuantizeRow(np.zeros(100, np.float32), None, 100)
+
+
+def test_csharp_binding_covers_the_header():
+    """bindings/Q35k.cs (the P/Invoke shim for src/Qwen35Sharp.Kernels/)
+    declares every entry point of the header, with the header's argument
+    count."""
+    cs = open(os.path.join(ROOT, "bindings", "Q35k.cs")).read()
+    bound = dict(re.findall(r"static partial \S+ (q35k_\w+)\(([^)]*)\)", cs))
+    assert sorted(bound) == declared_functions()
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    for name, args in re.findall(r"\b(q35k_\w+)\s*\(([^)]*)\)", src):
+        n_c = 0 if args.strip() in ("", "void") else args.count(",") + 1
+        n_cs = 0 if not bound[name].strip() else bound[name].count(",") + 1
+        assert n_c == n_cs, (name, n_c, n_cs)
