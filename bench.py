@@ -3,16 +3,24 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: the Q6_K vocab-head GEMV, M=1, K=2560,
-N=151936 -- 319 MB of quantized weights, larger than L2, so every timed step
-streams the weights from HBM.  A step is one pass of the hot path: Q8_K
-quantization of x then the GEMV.  At N>1 GPUs the rows are sharded N/P per
-rank and the fp32 logits are all-gathered over NVLink -- fused into the GEMV
-(each rank stores its slice into every peer's buffer and raises a flag there;
-default) or by NCCL (--gather nccl); total work is fixed (strong scaling).  Time is measured on the device with CUDA events,
-max over ranks.
+Headline workload: the Q6_K vocab-head GEMV, M=1,
+K=2560, N=151936 -- 319 MB of quantized weights, larger than L2, so every
+timed step streams the weights from HBM.  A step is one pass of the hot path:
+Q8_K quantization of x then the GEMV.  At N>1 GPUs the rows are sharded N/P
+per rank and the fp32 logits are all-gathered over NVLink -- fused into the
+GEMV (each rank stores its slice into every peer's buffer and raises a flag
+there; default) or by NCCL (--gather nccl); total work is fixed (strong
+scaling).  Time is measured on the device with CUDA events, max over ranks.
 
-`--impl reference` times the reference's CPU implementation of the same
+Every other configuration of BASELINE.json is measured too and reported in
+`roofline["configs"]` (value, fraction of the measured peak, parity) and, at
+N = 1, `cpu_baseline["configs"]` (the reference's CPU kernels on the same
+inputs): cfg0, cfg2 and cfg4 at M = 1 / 8 (decode GEMV), cfg3 and cfg4 at
+M = 512 (tensor-core GEMM, both arithmetic modes), and at N > 1 the sharded
+cfg4 at M = 1, 8, 512 with its gather.  The same figures are printed as short
+`# cfg` lines before the headline JSON line.
+
+`--impl reference` times the reference's CPU implementation of the headline
 workload (the C restatement of its AVX2 kernels under oracle/, all host
 threads); under torchrun only rank 0 runs it.
 """
@@ -23,6 +31,7 @@ import argparse
 import csv
 import io
 import json
+import mmap
 import os
 import statistics
 import subprocess
@@ -37,6 +46,24 @@ METRIC = "K-quant GEMV HBM GB/s (frac of 8 TB/s); M=512 GEMM TFLOP/s; 1/2/4/8 GP
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 CFG = dict(qtype=14, m=1, k=2560, n=151936, seed_w=1, seed_x=2)
+# The headline config, identical in both arms' JSON lines.
+CONFIG = {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": 1, "k": 2560,
+          "n": 151936, "l2": "inputs > L2 (319 MB of weights)"}
+Q4, Q5, Q6 = 12, 13, 14
+TYPE_NAME = {Q4: "Q4_K", Q5: "Q5_K", Q6: "Q6_K"}
+# Secondary decode configurations (cold weights): name, type, M, K, N, x scale.
+GEMV_CASES = [("cfg0", Q4, 1, 2560, 9728, 1.0), ("cfg2", Q5, 8, 9728, 2560, 0.5),
+              ("cfg4_m1", Q4, 1, 5120, 27648, 1.0), ("cfg4_m8", Q4, 8, 5120, 27648, 1.0)]
+# Prefill GEMM configurations: name, type, M, K, N.  Q5_K / Q6_K at cfg2's
+# ffn_down shape with GGUF-like scales.
+GEMM_CASES = [("cfg3", Q4, 512, 2560, 9728), ("cfg4_m512", Q4, 512, 5120, 27648),
+              ("q5k_m512", Q5, 512, 9728, 2560), ("q6k_m512", Q6, 512, 9728, 2560)]
+# Sharded configuration 4 at every N: name, M (K = 5120, N = 27648, Q4_K).
+SHARD_CASES = [("cfg4_m1", 1), ("cfg4_m8", 8), ("cfg4_m512", 512)]
+CFG4_K, CFG4_N = 5120, 27648
+OUR_KERNELS = ("q35k_decode_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel",
+               "repack_tiles_kernel", "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel",
+               "signal_wait_kernel", "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel")
 
 
 def load_peaks():
@@ -104,7 +131,7 @@ class ClockSampler:
 
 
 def traffic_from_profile():
-    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary."""
+    """Per-launch DRAM bytes of the headline GEMV from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "gemv_q6k_vocab_m1.txt")
     try:
         for line in open(path):
@@ -115,30 +142,88 @@ def traffic_from_profile():
     return None
 
 
-def cpu_baseline(w_blocks, x, budget_s: float = 10.0):
-    """The reference's CPU GEMV (C restatement of its AVX2 kernels, oracle/)
-    on the full workload, with the reference's default worker count
-    (CpuTopology.ChooseWorkerCount) and with all host threads."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
+def rel_err(y, r) -> float:
+    import numpy as np
 
+    y = np.asarray(y, dtype=np.float64)
+    r = np.asarray(r, dtype=np.float64)
+    return float(np.abs(y - r).max() / max(float(np.abs(r).max()), 1e-30))
+
+
+def page_aligned(shape, dtype):
+    """A numpy array on its own anonymous pages (a persistent buffer a caller
+    registers with q35k_host_register without sharing pages with others)."""
+    import numpy as np
+
+    nbytes = int(np.prod(shape)) * np.dtype(dtype).itemsize
+    buf = mmap.mmap(-1, max(nbytes, 1))
+    return np.frombuffer(buf, dtype=dtype, count=int(np.prod(shape))).reshape(shape), buf
+
+
+def count_launches(torch, step):
+    """Kernels of libq35k launched by one step, counted with the CUDA
+    profiler on an untimed step (NCCL and torch kernels excluded)."""
+    return len(kernels_of(torch, step))
+
+
+def kernels_of(torch, step):
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    return [ev.name for ev in prof.events()
+            if any(k in ev.name for k in OUR_KERNELS) and ev.device_type.name == "CUDA"]
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the reference's kernels (the oracle's C restatement) on the box's
+# host cores, timed as the CPU baseline, and used as the checker of the GPU
+# outputs the GPU legs kept.
+# ---------------------------------------------------------------------------
+
+def cpu_leg(jobs, time_it: bool, budget_s: float = 1.0):
+    """jobs: name -> (qtype, blocks, x, gpu_y, rows) where `rows` (None: all)
+    selects the output rows compared; only whole-matrix jobs are timed.
+    Returns (per-config results, host topology)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle
     from q35k import synth
 
     oracle.build()
     topo = oracle.host_topology()
-    W = oracle.Weight(CFG["qtype"], w_blocks, CFG["k"], w_blocks.shape[0])
-    nbytes = synth.algorithmic_bytes(CFG["qtype"], CFG["m"], CFG["k"], w_blocks.shape[0])
+    workers = topo["reference_workers"]
     out = {}
-    for label, threads in (("reference_workers", topo["reference_workers"]), ("all_threads", topo["logical"])):
-        W.matmul(x, threads=threads)  # warm-up (page-in, pool start)
-        n, t0 = 0, time.perf_counter()
-        while True:
-            W.matmul(x, threads=threads)
-            n += 1
-            el = time.perf_counter() - t0
-            if el > budget_s / 2 or n >= 200:
-                break
-        out[label] = dict(value=nbytes / (el / n) / 1e9, cores=threads, calls=n, seconds=el)
+    for name, (qt, w, x, gy, rows) in jobs.items():
+        m, k = x.shape
+        n = w.shape[0]
+        res = {}
+        if rows is not None:
+            W = oracle.Weight(qt, np.ascontiguousarray(w[rows]), k, len(rows))
+            res["err"] = rel_err(gy[:, rows], W.matmul(x, threads=topo["logical"]))
+            out[name] = res
+            continue
+        W = oracle.Weight(qt, w, k, n)
+        res["err"] = rel_err(gy, W.matmul(x, threads=topo["logical"]))
+        if time_it:
+            W.matmul(x, threads=workers)  # warm-up
+            calls, t0 = 0, time.perf_counter()
+            while True:
+                W.matmul(x, threads=workers)
+                calls += 1
+                el = time.perf_counter() - t0
+                if el > budget_s or calls >= 200:
+                    break
+            s = el / calls
+            if m >= 64:
+                res.update(value=2.0 * m * n * k / s / 1e12, unit="TFLOP/s")
+            else:
+                res.update(value=synth.algorithmic_bytes(qt, m, k, n) / s / 1e9, unit="GB/s")
+            res.update(cores=workers, calls=calls, seconds=el)
+        out[name] = res
     return out, topo
 
 
@@ -171,8 +256,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": 1,
-                   "k": 2560, "n": 151936, "l2": "inputs > L2 (319 MB of weights)"},
+        "config": dict(CONFIG),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": "full cfg1 GEMV per step (Q8K.QuantizeRow + Q6K.GemvPrequant over all "
                                    "151936 rows), C restatement of the reference's AVX2 kernels, "
@@ -183,448 +267,512 @@ def run_reference(args):
     print(json.dumps(line))
 
 
-def run_ours(args):
-    import numpy as np
-    import torch
+# ---------------------------------------------------------------------------
+# GPU legs.
+# ---------------------------------------------------------------------------
 
-    import q35k
-    from q35k import synth
+class Bench:
+    def __init__(self, args):
+        import numpy as np
+        import torch
 
-    rank, world, local = dist_env()
-    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
-    gather_mode = q35k.GATHER_FUSED if args.gather == "fused" else q35k.GATHER_NCCL
-    gather_desc = ("fused into the GEMV (NVLink stores into every peer + bounded flag wait)" if args.gather == "fused"
-                   else "NCCL all-gather")
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
+        import q35k
+        from q35k import synth
 
-        import torch.distributed as dist
+        self.args, self.np, self.torch, self.q35k, self.synth = args, np, torch, q35k, synth
+        self.rank, self.world, self.local = dist_env()
+        assert self.world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={self.world}"
+        torch.cuda.set_device(self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    peaks, peak_kind = load_peaks()
-    qt, M, K, N = CFG["qtype"], CFG["m"], CFG["k"], CFG["n"]
-    # Rows of this rank: the library's equal-share split (q35k_shard_*).
-    r0, r1 = q35k.shard_range(N, world, rank)
-    rows = r1 - r0
-    w = synth.kquant_blocks(qt, rows, K, seed=CFG["seed_w"], row_start=r0)
-    x = synth.activations(M, K, seed=CFG["seed_x"])
+            import torch.distributed as dist
 
-    # The rank's own slice on a plain context: the GEMV kernel timed alone
-    # (roofline), and the whole step at N = 1.
-    ctx = q35k.Context(local)
-    W = ctx.upload(qt, w, K, rows)
-    # One explicit stream for our kernels, the CUDA events and NCCL.
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    sh = stream.cuda_stream
-    dx = torch.from_numpy(x).cuda()
-    dy_full = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    dy_local = torch.empty((M, rows), dtype=torch.float32, device="cuda")
-    group = SW = None
-    if world > 1:
-        # One process per GPU: rank 0 makes the NCCL id, torch.distributed
-        # carries it to the others; the library's group does the rest.
-        idt = torch.zeros(q35k._lib.NCCL_ID_BYTES, dtype=torch.uint8, device="cuda")
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+        self.peaks, self.peak_kind = load_peaks()
+        self.ctx = q35k.Context(self.local)
+        self.stream = torch.cuda.Stream()
+        torch.cuda.set_stream(self.stream)
+        self.sh = self.stream.cuda_stream
+        self.group = None
+        if self.world > 1:
+            # One process per GPU: rank 0 makes the NCCL id, torch.distributed
+            # carries it to the others; the library's group does the rest.
+            idt = torch.zeros(q35k._lib.NCCL_ID_BYTES, dtype=torch.uint8, device="cuda")
+            if self.rank == 0:
+                idt.copy_(torch.frombuffer(bytearray(q35k.nccl_unique_id()), dtype=torch.uint8))
+            self.dist.broadcast(idt, 0)
+            self.group = q35k.Shard(nranks=self.world, rank=self.rank, nccl_id=bytes(idt.cpu().numpy().tobytes()),
+                                    device=self.local)
+        self.gather_mode = q35k.GATHER_FUSED if args.gather == "fused" else q35k.GATHER_NCCL
+        self.gather_desc = ("fused into the GEMV (NVLink stores into every peer + bounded flag wait)"
+                            if args.gather == "fused" else "NCCL all-gather")
+        self.cpu_jobs = {}   # name -> inputs and GPU output for the CPU leg
+        self.configs = {}    # name -> per-config result
+
+    # -- helpers --
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def event_pair(self):
+        return (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
+
+    def back_to_back_ms(self, fn, steps: int) -> float:
+        """ms per call of `steps` calls issued back to back between one event
+        pair (max over ranks)."""
+        torch = self.torch
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        a, b = self.event_pair()
+        a.record(self.stream)
+        for _ in range(steps):
+            fn()
+        b.record(self.stream)
+        torch.cuda.synchronize()
+        return self.max_over_ranks(a.elapsed_time(b) / steps)
+
+    def graph_ms(self, issue, calls_per_replay, reps):
+        """ms per call of a CUDA graph of `calls_per_replay` calls replayed
+        `reps` times."""
+        torch = self.torch
+        issue(self.stream)  # warm-up, sizes every scratch buffer before capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            issue(torch.cuda.current_stream())
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = self.event_pair()
+        a.record(self.stream)
+        for _ in range(reps):
+            graph.replay()
+        b.record(self.stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / (reps * calls_per_replay)
+        del graph
+        return ms
+
+    def sharded_weight(self, qt, w_rows, k, n, r0, r1):
+        """q35k_shard_weight_upload takes the full matrix and keeps this rank's
+        rows; hand it a view whose rows r0..r1 are this rank's blocks."""
+        np = self.np
+        full = np.zeros((n, w_rows.shape[1]), dtype=np.uint8)
+        full[r0:r1] = w_rows
+        return self.group.upload(qt, full, k, n)
+
+    def boundary_rows(self, n):
+        """First and last 64 rows of every rank's slice."""
+        rows = []
+        for r in range(self.world):
+            a, b = self.q35k.shard_range(n, self.world, r)
+            rows += list(range(a, min(b, a + 64))) + list(range(max(a, b - 64), b))
+        return sorted(set(rows))
+
+    def parity_vs_single_gpu(self, qt, k, n, x, y_mine, make_full):
+        """Rank 0 runs the full matrix on its GPU alone (q35k_matmul_dev) and
+        broadcasts y; every rank compares its gathered y with it.  Returns the
+        largest relative difference over the ranks and whether every rank's y
+        has the same bits."""
+        np, torch = self.np, self.torch
+        m = x.shape[0]
+        ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        if self.rank == 0:
+            wf = make_full()
+            Wf = self.ctx.upload(qt, wf, k, n)
+            self.ctx.matmul_dev(Wf, torch.from_numpy(x).cuda(), ref, m, self.sh)
+            torch.cuda.synchronize()
+            Wf.free()
+            del wf
+        torch.cuda.synchronize()
+        self.dist.broadcast(ref, 0)
+        torch.cuda.synchronize()
+        r = ref.cpu().numpy()
+        err = rel_err(y_mine, r)
+        differ = 0.0 if np.array_equal(y_mine.view(np.uint32), r.view(np.uint32)) else 1.0
+        t = torch.tensor([err, differ], device="cuda", dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return {"max_rel_err_vs_1gpu": float(t[0].item()), "bit_equal_1gpu": bool(t[1].item() == 0.0)}
+
+    # -- the headline: cfg1 vocab head --
+    def headline(self):
+        torch, q35k, synth, args = self.torch, self.q35k, self.synth, self.args
+        world, rank = self.world, self.rank
+        qt, M, K, N = CFG["qtype"], CFG["m"], CFG["k"], CFG["n"]
+        r0, r1 = q35k.shard_range(N, world, rank)
+        rows = r1 - r0
+        w = synth.kquant_blocks(qt, rows, K, seed=CFG["seed_w"], row_start=r0)
+        x = synth.activations(M, K, seed=CFG["seed_x"])
+        W = self.ctx.upload(qt, w, K, rows)
+        dx = torch.from_numpy(x).cuda()
+        dy_full = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        dy_local = torch.empty((M, rows), dtype=torch.float32, device="cuda")
+        SW = self.sharded_weight(qt, w, K, N, r0, r1) if world > 1 else None
+        ctx, sh = self.ctx, self.sh
+
+        def step():
+            # One pass of the hot path: N = 1, q35k_matmul_dev (Q8_K quantization
+            # of x fused into the GEMV at M = 1); N > 1, q35k_shard_matmul_dev (the
+            # rank's GEMV, then the gather of the logits).
+            if world == 1:
+                ctx.matmul_dev(W, dx, dy_full, M, sh)
+            else:
+                self.group.matmul_dev(SW, [dx], [dy_full], M, self.gather_mode, streams=[sh])
+
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        self.barrier()
+        clocks = ClockSampler(self.local)
+        clocks.start()
+        ms_step = self.back_to_back_ms(step, args.steps)
+        clk = clocks.stop()
+        # Per-step event times (untimed pass: events between steps serialise them).
+        evs = [self.event_pair() for _ in range(args.steps)]
+        self.barrier()
+        for e in evs:
+            e[0].record(self.stream)
+            step()
+            e[1].record(self.stream)
+        torch.cuda.synchronize()
+        step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+        # The rank's GEMV kernel timed alone (the roofline's kernel).
+        kev = [self.event_pair() for _ in range(args.steps)]
+        for e in kev:
+            e[0].record(self.stream)
+            ctx.matmul_dev(W, dx, dy_local, M, sh)
+            e[1].record(self.stream)
+        torch.cuda.synchronize()
+        gemv_ms = sum(e[0].elapsed_time(e[1]) for e in kev) / len(kev)
+
+        nbytes_total = synth.algorithmic_bytes(qt, M, K, N)
+        nbytes_local = synth.algorithmic_bytes(qt, M, K, rows)
+        value = nbytes_total / (ms_step / 1e3) / 1e9
+        launches = count_launches(torch, step)
+
+        # Parity of the gathered logits: at N > 1 against the single-GPU result
+        # of the full matrix on every rank; on rank 0 against the oracle (the
+        # whole matrix at N = 1, the rows around every shard boundary at N > 1).
+        step()
+        torch.cuda.synchronize()
+        y_mine = dy_full.cpu().numpy()
+        self.head_parity = {}
+        if world > 1:
+            self.head_parity = self.parity_vs_single_gpu(
+                qt, K, N, x, y_mine, lambda: synth.kquant_blocks(qt, N, K, seed=CFG["seed_w"]))
         if rank == 0:
-            idt.copy_(torch.frombuffer(bytearray(q35k.nccl_unique_id()), dtype=torch.uint8))
-        dist.broadcast(idt, 0)
-        group = q35k.Shard(nranks=world, rank=rank, nccl_id=bytes(idt.cpu().numpy().tobytes()), device=local)
-        # q35k_shard_weight_upload takes the full matrix and keeps this rank's
-        # rows; hand it a view whose rows r0..r1 are this rank's blocks.
-        w_view = np.zeros((N, w.shape[1]), dtype=np.uint8)
-        w_view[r0:r1] = w
-        SW = group.upload(qt, w_view, K, N)
-        del w_view
+            self.cpu_jobs["cfg1"] = (qt, w if world == 1 else None, x, y_mine,
+                                     None if world == 1 else self.boundary_rows(N))
 
-    def step(ev=None):
-        # One pass of the hot path: N = 1, q35k_matmul_dev (Q8_K quantization
-        # of x fused into the GEMV at M = 1); N > 1, q35k_shard_matmul_dev (the
-        # rank's GEMV, then the gather of the logits: fused into the GEMV --
-        # NVLink stores into every peer plus a bounded flag wait -- or NCCL's
-        # all-gather with --gather nccl).
-        if ev:
-            ev[0].record(stream)
-        if world == 1:
-            ctx.matmul_dev(W, dx, dy_full, M, sh)
-        else:
-            group.matmul_dev(SW, [dx], [dy_full], M, gather_mode, streams=[sh])
-        if ev:
-            ev[1].record(stream)
+        e2e = self.e2e(W, x, dx, dy_full, step, nbytes_total)
+        achieved = nbytes_local / (gemv_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": self.peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / self.peaks["hbm_gbs"], "traffic": traffic_from_profile() if world == 1 else None,
+                    "peak_kind": (f"{self.peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if self.peak_kind == "measured"
+                                  else "fallback"),
+                    "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
+                    "kernel": "q35k_decode_kernel<Q6_K,1,fused>", "kernel_ms": gemv_ms,
+                    "algorithmic_bytes_per_launch": nbytes_local}
+        self.head = dict(value=value, ms_step=ms_step, step_ms=sum(step_ms) / len(step_ms), gemv_ms=gemv_ms,
+                         rows=rows, clocks=clk, launches=launches, roofline=roofline, e2e=e2e)
+        self.head_w = (W, SW)
 
-    def kernel_only(ev):
-        ev[0].record(stream)
-        ctx.matmul_dev(W, dx, dy_local, M, sh)
-        ev[1].record(stream)
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-
-    clocks = ClockSampler(local)
-    clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    # K steps back to back (nothing between them on the stream, so each
-    # step's GEMV may start streaming weights under the previous step's tail,
-    # as in a model's decode loop), one event pair around them.
-    start.record(stream)
-    for i in range(args.steps):
-        step()
-    end.record(stream)
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    total_ms = start.elapsed_time(end)
-    # Per-step event times, untimed pass (events between steps serialise them).
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    for i in range(args.steps):
-        step(evs[i])
-    torch.cuda.synchronize()
-    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    # The rank's GEMV kernel timed alone (untimed for the headline).
-    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
-    for i in range(args.steps):
-        kernel_only(kev[i])
-    torch.cuda.synchronize()
-    gemv_ms = [e[0].elapsed_time(e[1]) for e in kev]
-    ms_step = total_ms / args.steps
-    if world > 1:
-        t = torch.tensor([ms_step], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step = float(t.item())
-
-    nbytes_total = synth.algorithmic_bytes(qt, M, K, N)
-    nbytes_local = synth.algorithmic_bytes(qt, M, K, rows)
-    value = nbytes_total / (ms_step / 1e3) / 1e9
-
-    # End to end through the public host-pointer API (q35k_matmul): x from
-    # host memory, y back to host memory, every step.
-    e2e = None
-    if world == 1:
-        # The caller's output buffer persists across steps, as the reference's
-        # model writes through one float* output of its scratch arena.
-        y_host = np.empty((M, N), dtype=np.float32)
-        for _ in range(3):
-            ctx.matmul(W, x, out=y_host)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            ctx.matmul(W, x, out=y_host)
-        e2e_s = (time.perf_counter() - t0) / args.steps
-        e2e = {"value": nbytes_total / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
-               "d2h_bytes_per_step": int(y_host.nbytes), "ms_per_step": e2e_s * 1e3,
-               "api": "q35k_matmul (host pointers, synchronous)"}
-    else:
+    def e2e(self, W, x, dx, dy_full, step, nbytes_total):
+        """The same metric end to end through the public API: x from host
+        memory and y back to host memory every step."""
+        np, torch, args = self.np, self.torch, self.args
+        M, N = x.shape[0], dy_full.shape[1]
+        if self.world == 1:
+            # The caller's input and output buffers persist across steps (the
+            # reference model's NativeBuffers) and are registered once with
+            # q35k_host_register, so q35k_matmul reads x and writes y in place.
+            x_host, xb = page_aligned(x.shape, np.float32)
+            y_host, yb = page_aligned((M, N), np.float32)
+            x_host[...] = x
+            self.ctx.host_register(x_host)
+            self.ctx.host_register(y_host)
+            try:
+                for _ in range(3):
+                    self.ctx.matmul(W, x_host, out=y_host)
+                t0 = time.perf_counter()
+                for _ in range(args.steps):
+                    self.ctx.matmul(W, x_host, out=y_host)
+                s = (time.perf_counter() - t0) / args.steps
+            finally:
+                self.ctx.host_unregister(x_host)
+                self.ctx.host_unregister(y_host)
+            # The same with pageable buffers (staged through the context).
+            y_page = np.empty((M, N), dtype=np.float32)
+            for _ in range(3):
+                self.ctx.matmul(W, x, out=y_page)
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                self.ctx.matmul(W, x, out=y_page)
+            s_page = (time.perf_counter() - t0) / args.steps
+            return {"value": nbytes_total / s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
+                    "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": s * 1e3,
+                    "api": "q35k_matmul (host pointers, synchronous; x and y registered with q35k_host_register)",
+                    "pageable_ms_per_step": s_page * 1e3}
         xh = torch.from_numpy(x).pin_memory()
         yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            dx.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(dy_full, non_blocking=True)
+
         for _ in range(3):
-            dx.copy_(xh, non_blocking=True)
-            step()
-            yh.copy_(dy_full, non_blocking=True)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            dx.copy_(xh, non_blocking=True)
-            step()
-            yh.copy_(dy_full, non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-        e2e = {"value": nbytes_total / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
-               "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": e2e_ms,
-               "api": f"pinned H2D of x + q35k_shard_matmul_dev (GEMV, gather {gather_desc}) + D2H of y"}
+            e2e_step()
+        ms = self.back_to_back_ms(e2e_step, args.steps)
+        return {"value": nbytes_total / (ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(x.nbytes),
+                "d2h_bytes_per_step": int(M * N * 4), "ms_per_step": ms,
+                "api": f"pinned H2D of x + q35k_shard_matmul_dev (GEMV, gather {self.gather_desc}) + D2H of y"}
 
-    gemv_avg = sum(gemv_ms) / len(gemv_ms)
-    achieved = nbytes_local / (gemv_avg / 1e3) / 1e9
-    traffic = traffic_from_profile() if world == 1 else None
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
-                "kernel": "q35k_decode_kernel<Q6_K,1,fused>", "kernel_ms": gemv_avg,
-                "algorithmic_bytes_per_launch": nbytes_local}
+    # -- secondary configurations at N = 1 --
+    def gemv_configs(self):
+        """Device time per call (Q8_K quantize + GEMV, q35k_matmul_dev).  These
+        weights fit in L2, so each timed run cycles through enough distinct
+        uploaded copies to exceed 3x L2 (every launch streams cold weights from
+        HBM), replayed from a CUDA graph so host launch latency is not in the
+        device time."""
+        torch, synth = self.torch, self.synth
+        l2 = 126 * 2**20
+        for name, qt, m, k, n, scale in GEMV_CASES:
+            w = synth.kquant_blocks(qt, n, k, seed=1)
+            x = synth.activations(m, k, seed=2, scale=scale)
+            copies = max(2, min(64, -(-3 * l2 // w.nbytes)))
+            Ws = [self.ctx.upload(qt, w, k, n) for _ in range(copies)]
+            dx = torch.from_numpy(x).cuda()
+            dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            ms = self.graph_ms(lambda cs: [self.ctx.matmul_dev(W, dx, dy, m, cs) for W in Ws], copies,
+                               max(3, 400 // copies))
+            gbs = synth.algorithmic_bytes(qt, m, k, n) / (ms / 1e3) / 1e9
+            self.configs[name] = {"v": gbs, "u": "GB/s", "frac": gbs / self.peaks["hbm_gbs"], "ms": ms,
+                                  "what": f"{TYPE_NAME[qt]} M={m} K={k} N={n} GEMV, cold weights"}
+            torch.cuda.synchronize()
+            self.cpu_jobs[name] = (qt, w, x, dy.cpu().numpy(), None)
+            for W in Ws:
+                W.free()
 
-    launches_per_step = count_launches(torch, step)
+    def gemm_configs(self):
+        """Tensor-core prefill GEMM at M = 512 in both arithmetic modes (exact:
+        the reference's integer products, the default; fast: fp16-rounded
+        dequantized operands).  Device time per q35k_matmul_dev call (Q8_K
+        preparation + GEMM), CUDA-graph replay; the weights sit in L2 after the
+        first call, as in any compute-bound GEMM.  TFLOP/s = 2 M N K / time."""
+        torch, synth, q35k = self.torch, self.synth, self.q35k
+        peak = self.peaks.get("bf16_tflops")
+        for name, qt, m, k, n in GEMM_CASES:
+            w = synth.kquant_blocks(qt, n, k, seed=1, q5_uniform_d=False)
+            x = synth.activations(m, k, seed=2)
+            W = self.ctx.upload(qt, w, k, n)
+            dx = torch.from_numpy(x).cuda()
+            dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            for mode, suffix in ((q35k.GEMM_EXACT, "_exact"), (q35k.GEMM_FAST, "_fast")):
+                self.ctx.set_gemm_mode(mode)
+                calls = 10
+                ms = self.graph_ms(lambda cs: [self.ctx.matmul_dev(W, dx, dy, m, cs) for _ in range(calls)], calls, 10)
+                tf = 2.0 * m * n * k / (ms / 1e3) / 1e12
+                names = kernels_of(torch, lambda: self.ctx.matmul_dev(W, dx, dy, m, self.sh))
+                path = "tcgen05 GEMM" if any("gemm_q4k_tc_kernel" in s for s in names) else "decode GEMV chunks"
+                self.configs[name + suffix] = {"v": tf, "u": "TFLOP/s", "frac": tf / peak if peak else None, "ms": ms,
+                                               "what": f"{TYPE_NAME[qt]} M={m} K={k} N={n} {path}"}
+                # Checked against the oracle: exact mode on the whole matrix
+                # (timed there as the CPU baseline), fast mode on a row subset.
+                torch.cuda.synchronize()
+                y = dy.cpu().numpy()
+                rows = None if mode == q35k.GEMM_EXACT else list(range(0, n, max(1, n // 256)))
+                self.cpu_jobs[name + suffix] = (qt, w, x, y, rows)
+            self.ctx.set_gemm_mode(q35k.GEMM_EXACT)
+            W.free()
 
-    extra = {}
-    if world == 1 and not args.no_extra:
-        extra = secondary_configs(ctx, torch, np, synth, peaks)
+    def argmax_config(self):
+        """cfg1's vocab head with ArgMax fused into the GEMV epilogue
+        (q35k_matmul_argmax_dev, logits not written), back to back."""
+        torch, synth = self.torch, self.synth
+        W = self.head_w[0]
+        qt, m, k, n = CFG["qtype"], CFG["m"], CFG["k"], CFG["n"]
+        dx = torch.from_numpy(synth.activations(m, k, seed=CFG["seed_x"])).cuda()
+        di = torch.empty(m, dtype=torch.int32, device="cuda")
+        for _ in range(5):
+            self.ctx.matmul_argmax_dev(W, dx, None, di, m, self.sh)
+        ms = self.back_to_back_ms(lambda: self.ctx.matmul_argmax_dev(W, dx, None, di, m, self.sh), 50)
+        gbs = (synth.algorithmic_bytes(qt, m, k, n) - m * n * 4) / (ms / 1e3) / 1e9
+        self.configs["cfg1_argmax"] = {"v": gbs, "u": "GB/s", "frac": gbs / self.peaks["hbm_gbs"], "ms": ms,
+                                       "what": "Q6_K vocab head + fused ArgMax, no logits written"}
 
-    cpu = None
-    if world == 1 and rank == 0 and not args.no_cpu:
-        w_full = w  # world == 1: the full matrix
-        res, topo = cpu_baseline(w_full, x)
-        ref = res["reference_workers"]
-        cpu = {"value": ref["value"], "unit": "GB/s", "cores": ref["cores"], "kind": "port",
-               "sample": f"{ref['calls']} full cfg1 GEMV calls ({ref['seconds']:.1f} s), C restatement of the "
-                         f"reference's AVX2 Q6K.Gemv, reference worker count {ref['cores']}",
-               "all_threads": res["all_threads"], "host": topo}
+    def ffn_config(self):
+        """One decode FFN at cfg3's dimensions (hidden 2560, ffn 9728, Q4_K):
+        gate and up from one quantization of x in one GEMV launch, then
+        ffn_down on silu(gate) * up with the product formed in its
+        quantization.  Eight layers' weights (336 MB > L2) in a CUDA graph."""
+        torch, synth = self.torch, self.synth
+        qt, m, hid, ffn, layers = Q4, 1, 2560, 9728, 8
+        L = []
+        for i in range(layers):
+            L.append((self.ctx.upload(qt, synth.kquant_blocks(qt, ffn, hid, seed=3 * i + 1), hid, ffn),
+                      self.ctx.upload(qt, synth.kquant_blocks(qt, ffn, hid, seed=3 * i + 2), hid, ffn),
+                      self.ctx.upload(qt, synth.kquant_blocks(qt, hid, ffn, seed=3 * i + 3), ffn, hid)))
+        dx = torch.from_numpy(synth.activations(m, hid, seed=5)).cuda()
+        dg = torch.empty((m, ffn), dtype=torch.float32, device="cuda")
+        du = torch.empty((m, ffn), dtype=torch.float32, device="cuda")
+        dd = torch.empty((m, hid), dtype=torch.float32, device="cuda")
 
-    if rank == 0:
+        def layers_fn(cs):
+            for g, u, d in L:
+                self.ctx.matmul_shared_dev([g, u], dx, [dg, du], m, cs)
+                self.ctx.matmul_silu_dev(d, dg, du, dd, m, cs)
+
+        ms = self.graph_ms(layers_fn, layers, 50)
+        nbytes = 2 * synth.algorithmic_bytes(qt, m, hid, ffn) + synth.algorithmic_bytes(qt, m, ffn, hid)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        self.configs["ffn_decode"] = {"v": gbs, "u": "GB/s", "frac": gbs / self.peaks["hbm_gbs"], "ms": ms,
+                                      "what": "Q4_K gate+up (one shared launch) + SiLU-fused down, M=1, per layer"}
+        for t in L:
+            for W in t:
+                W.free()
+
+    # -- the sharded configuration 4 at N > 1 --
+    def shard_configs(self):
+        """cfg4 (Q4_K, K=5120, N=27648) row-sharded over the N GPUs at M = 1,
+        8 (decode GEMV, gather fused into it) and 512 (tensor-core GEMM, then
+        NCCL's all-gather and a permute): device time per call issued back to
+        back, max over ranks; the gathered y checked on every rank against
+        rank 0's single-GPU result, and on rank 0 against the oracle on the
+        rows around every shard boundary."""
+        torch, synth, q35k = self.torch, self.synth, self.q35k
+        qt, k, n = Q4, CFG4_K, CFG4_N
+        r0, r1 = q35k.shard_range(n, self.world, self.rank)
+        w = synth.kquant_blocks(qt, r1 - r0, k, seed=1, row_start=r0)
+        SW = self.sharded_weight(qt, w, k, n, r0, r1)
+        peak_bf16 = self.peaks.get("bf16_tflops")
+        for name, m in SHARD_CASES:
+            x = synth.activations(m, k, seed=2)
+            dx = torch.from_numpy(x).cuda()
+            dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
+
+            def call():
+                self.group.matmul_dev(SW, [dx], [dy], m, self.gather_mode, streams=[self.sh])
+
+            for _ in range(3):
+                call()
+            ms = self.back_to_back_ms(call, 20 if m < 64 else 10)
+            call()
+            torch.cuda.synchronize()
+            y = dy.cpu().numpy()
+            par = self.parity_vs_single_gpu(qt, k, n, x, y, lambda: synth.kquant_blocks(qt, n, k, seed=1))
+            if m >= 64:
+                v, u = 2.0 * m * n * k / (ms / 1e3) / 1e12, "TFLOP/s"
+                frac = v / peak_bf16 if peak_bf16 else None
+                gather = "NCCL all-gather + permute"
+            else:
+                v, u = synth.algorithmic_bytes(qt, m, k, n) / (ms / 1e3) / 1e9, "GB/s"
+                frac = v / self.peaks["hbm_gbs"]
+                gather = "gather fused into the GEMV" if self.gather_mode == q35k.GATHER_FUSED else "NCCL all-gather"
+            self.configs[f"{name}_p{self.world}"] = {
+                "v": v, "u": u, "frac_per_gpu": frac / self.world if frac is not None else None, "ms": ms,
+                "err_1gpu": par["max_rel_err_vs_1gpu"], "bit_eq_1gpu": par["bit_equal_1gpu"],
+                "what": f"Q4_K M={m} K={k} N={n} row-sharded over {self.world} GPUs, {gather}, whole job"}
+            if self.rank == 0:
+                self.cpu_jobs[f"{name}_p{self.world}"] = (qt, None, x, y, self.boundary_rows(n))
+        SW.free()
+
+    def cpu_checks(self):
+        """The CPU leg: at N = 1 the reference's kernels timed on every config
+        (the CPU baseline) and checked against the GPU outputs; at N > 1 the
+        gathered outputs checked on the rows around the shard boundaries."""
+        synth = self.synth
+        jobs, full = {}, {}
+        for name, (qt, w, x, y, rows) in self.cpu_jobs.items():
+            if w is None:
+                # Sharded configs: rank 0 regenerates the full matrix.
+                key = "cfg1" if name == "cfg1" else "cfg4"
+                if key not in full:
+                    full[key] = (synth.kquant_blocks(qt, CFG["n"], CFG["k"], seed=CFG["seed_w"]) if key == "cfg1"
+                                 else synth.kquant_blocks(qt, CFG4_N, CFG4_K, seed=1))
+                w = full[key]
+            jobs[name] = (qt, w, x, y, rows)
+        return cpu_leg(jobs, time_it=self.world == 1)
+
+    def report(self, cpu):
+        h, world = self.head, self.world
+        cpu_line = None
+        if cpu is not None:
+            res, topo = cpu
+            for name, r in res.items():
+                if name in self.configs:
+                    self.configs[name]["err"] = r["err"]
+            if "cfg1" in res:
+                self.head_parity["max_rel_err_vs_oracle"] = res["cfg1"]["err"]
+            if world == 1 and "value" in res.get("cfg1", {}):
+                c1 = res["cfg1"]
+                cpu_line = {"value": c1["value"], "unit": c1["unit"], "cores": c1["cores"], "kind": "port",
+                            "sample": f"{c1['calls']} full cfg1 GEMV calls ({c1['seconds']:.1f} s), C restatement of "
+                                      f"the reference's AVX2 Q6K.Gemv, reference worker count {c1['cores']} "
+                                      f"(CpuTopology.ChooseWorkerCount; {topo['logical']} logical CPUs)",
+                            "configs": {n: {"v": r["value"], "u": r["unit"], "cores": r["cores"], "calls": r["calls"]}
+                                        for n, r in res.items() if "value" in r and n != "cfg1"},
+                            "host": topo}
+        roofline = dict(h["roofline"])
+        roofline["configs"] = self.configs
+        for name, c in self.configs.items():
+            parts = [f"# cfg {name}: {c['v']:.1f} {c['u']}"]
+            if c.get("frac") is not None:
+                parts.append(f"{c['frac']:.3f} of measured peak")
+            if cpu_line and name in cpu_line["configs"]:
+                cc = cpu_line["configs"][name]
+                parts.append(f"cpu {cc['v']:.3g} {cc['u']} ({cc['cores']} cores)")
+            if "err" in c:
+                parts.append(f"err vs oracle {c['err']:.1e}")
+            if "err_1gpu" in c:
+                parts.append(f"err vs 1 GPU {c['err_1gpu']:.1e} bit-equal {c['bit_eq_1gpu']}")
+            print(" | ".join(parts) + f" | {c['what']}")
         line = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "cfg1 Q6_K GEMV M=1 K=2560 N=151936 (vocab head)", "qtype": "Q6_K", "m": M,
-                       "k": K, "n": N, "rows_per_gpu": rows, "l2": "inputs > L2 (319 MB of weights)",
-                       "parallelism": (f"row-sharded N/{world}, gather {gather_desc} (q35k_shard_matmul_dev)"
-                                       if world > 1 else "single GPU")},
-            "frac_of_nominal_8tbs": value / NOMINAL_HBM_GBS,
-            "gemv_ms": gemv_avg, "step_ms_events": sum(step_ms) / len(step_ms),
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-            "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step, "also": extra,
+            "metric": METRIC, "value": h["value"], "unit": "GB/s", "n_gpus": world, "steps": self.args.steps,
+            "warmup": self.args.warmup, "ms_per_step": h["ms_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": dict(CONFIG),
+            "parallelism": (f"row-sharded N/{world} ({h['rows']} rows per GPU), gather {self.gather_desc} "
+                            "(q35k_shard_matmul_dev)" if world > 1 else "single GPU"),
+            "frac_of_nominal_8tbs": h["value"] / NOMINAL_HBM_GBS, "gemv_ms": h["gemv_ms"],
+            "step_ms_events": h["step_ms"], "parity": self.head_parity, "roofline": roofline,
+            "cpu_baseline": cpu_line, "e2e": h["e2e"], "clocks": h["clocks"],
+            "gpu_launches": h["launches"] * self.args.steps, "launches_per_step": h["launches"],
         }
         print(json.dumps(line))
-    W.free()
-    ctx.close()
-    if world > 1:
-        SW.free()
-        group.close()
-        dist.barrier()
-        dist.destroy_process_group()
 
-
-OUR_KERNELS = ("q35k_decode_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel", "repack_tiles_kernel",
-               "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel", "signal_wait_kernel",
-               "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel")
-
-
-def count_launches(torch, step):
-    """Kernels of libq35k launched by one step, counted with the CUDA
-    profiler on an untimed step (NCCL and torch kernels excluded)."""
-    from torch.profiler import ProfilerActivity, profile
-
-    torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        step()
-        torch.cuda.synchronize()
-    n = 0
-    for ev in prof.events():
-        if any(k in ev.name for k in OUR_KERNELS) and ev.device_type.name == "CUDA":
-            n += 1
-    return n
-
-
-def secondary_configs(ctx, torch, np, synth, peaks):
-    """Device time per call (Q8_K quantize + GEMV, q35k_matmul_dev) for the
-    other configs.  They fit in L2, so each timed run cycles through enough
-    distinct uploaded copies of the weights to exceed 3x L2 (every launch
-    streams cold weights from HBM), and the calls are replayed from a CUDA
-    graph so that host launch latency does not enter the device time."""
-    out = {}
-    stream = torch.cuda.current_stream()
-    cases = [("cfg0_q4k_m1", 12, 1, 2560, 9728, 1.0), ("cfg2_q5k_m8", 13, 8, 9728, 2560, 0.5),
-             ("cfg4_q4k_m1_p1", 12, 1, 5120, 27648, 1.0), ("cfg4_q4k_m8_p1", 12, 8, 5120, 27648, 1.0)]
-    l2 = 126 * 2**20
-    for name, qt, m, k, n, scale in cases:
-        w = synth.kquant_blocks(qt, n, k, seed=1)
-        x = synth.activations(m, k, seed=2, scale=scale)
-        copies = max(2, min(64, -(-3 * l2 // w.nbytes)))
-        Ws = [ctx.upload(qt, w, k, n) for _ in range(copies)]
-        dx = torch.from_numpy(x).cuda()
-        dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
-        for W in Ws:  # warm-up, sizes every scratch buffer before capture
-            ctx.matmul_dev(W, dx, dy, m, stream)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            cs = torch.cuda.current_stream()
-            for W in Ws:
-                ctx.matmul_dev(W, dx, dy, m, cs)
-        graph.replay()
-        torch.cuda.synchronize()
-        reps = max(3, 400 // copies)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / (reps * copies)
-        nbytes = synth.algorithmic_bytes(qt, m, k, n)
-        gbs = nbytes / (ms / 1e3) / 1e9
-        out[name] = {"call_ms": ms, "GB/s": gbs, "frac_measured_hbm": gbs / peaks["hbm_gbs"],
-                     "frac_nominal_8tbs": gbs / NOMINAL_HBM_GBS,
-                     "timing": f"quantize+GEMV per call, CUDA-graph replay over {copies} weight copies "
-                               f"({copies * w.nbytes / 2**20:.0f} MiB > 3x L2)"}
-        del graph
-        for W in Ws:
-            W.free()
-    out.update(argmax_config(ctx, torch, synth, peaks))
-    out.update(ffn_decode_config(ctx, torch, synth, peaks))
-    out.update(gemm_configs(ctx, torch, synth, peaks))
-    return out
-
-
-def ffn_decode_config(ctx, torch, synth, peaks):
-    """One decode FFN at cfg0/cfg3's dimensions (hidden 2560, ffn 9728, Q4_K):
-    gate and up from one quantization of x in one GEMV launch
-    (q35k_matmul_shared_dev), then ffn_down on silu(gate) * up with the
-    product formed in its quantization (q35k_matmul_silu_dev); against gate
-    and up as two separate calls.  Eight layers' weights (336 MB > L2) cycled
-    in a CUDA graph."""
-    qt, m, hid, ffn, layers = 12, 1, 2560, 9728, 8
-    stream = torch.cuda.current_stream()
-    L = []
-    for i in range(layers):
-        L.append((ctx.upload(qt, synth.kquant_blocks(qt, ffn, hid, seed=3 * i + 1), hid, ffn),
-                  ctx.upload(qt, synth.kquant_blocks(qt, ffn, hid, seed=3 * i + 2), hid, ffn),
-                  ctx.upload(qt, synth.kquant_blocks(qt, hid, ffn, seed=3 * i + 3), ffn, hid)))
-    dx = torch.from_numpy(synth.activations(m, hid, seed=5)).cuda()
-    dg = torch.empty((m, ffn), dtype=torch.float32, device="cuda")
-    du = torch.empty((m, ffn), dtype=torch.float32, device="cuda")
-    dd = torch.empty((m, hid), dtype=torch.float32, device="cuda")
-
-    def shared(cs):
-        for g, u, d in L:
-            ctx.matmul_shared_dev([g, u], dx, [dg, du], m, cs)
-            ctx.matmul_silu_dev(d, dg, du, dd, m, cs)
-
-    def separate(cs):
-        for g, u, d in L:
-            ctx.matmul_dev(g, dx, dg, m, cs)
-            ctx.matmul_dev(u, dx, du, m, cs)
-            ctx.matmul_silu_dev(d, dg, du, dd, m, cs)
-
-    res = {}
-    nbytes = sum(synth.algorithmic_bytes(qt, m, hid, ffn) for _ in range(2)) + synth.algorithmic_bytes(qt, m, ffn, hid)
-    for name, fn in (("shared", shared), ("separate", separate)):
-        fn(stream)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            fn(torch.cuda.current_stream())
-        graph.replay()
-        torch.cuda.synchronize()
-        reps = 50
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / (reps * layers)
-        res[name] = (ms, nbytes / (ms / 1e3) / 1e9)
-        del graph
-    for t in L:
-        for W in t:
-            W.free()
-    ms, gbs = res["shared"]
-    return {"cfg3_q4k_m1_ffn_decode": {
-        "layer_ms": ms, "GB/s": gbs, "frac_measured_hbm": gbs / peaks["hbm_gbs"],
-        "separate_gate_up_layer_ms": res["separate"][0], "separate_GB/s": res["separate"][1],
-        "timing": f"gate+up (one shared GEMV launch) + silu-fused ffn_down per layer, CUDA-graph replay over "
-                  f"{layers} layers (336 MB of weights > L2)"}}
-
-
-def argmax_config(ctx, torch, synth, peaks):
-    """cfg1's vocab head with the ArgMax fused into the GEMV epilogue
-    (q35k_matmul_argmax_dev, logits not written): back-to-back calls on the
-    same 319 MB weight (> L2), as a decode loop issues them."""
-    qt, m, k, n = 14, 1, 2560, 151936
-    w = synth.kquant_blocks(qt, n, k, seed=1)
-    x = synth.activations(m, k, seed=2)
-    W = ctx.upload(qt, w, k, n)
-    dx = torch.from_numpy(x).cuda()
-    di = torch.empty(m, dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream()
-    for _ in range(5):
-        ctx.matmul_argmax_dev(W, dx, None, di, m, stream)
-    torch.cuda.synchronize()
-    reps = 50
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(reps):
-        ctx.matmul_argmax_dev(W, dx, None, di, m, stream)
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
-    nbytes = synth.algorithmic_bytes(qt, m, k, n) - m * n * 4  # no logits written
-    gbs = nbytes / (ms / 1e3) / 1e9
-    W.free()
-    return {"cfg1_q6k_m1_argmax": {"call_ms": ms, "GB/s": gbs, "frac_measured_hbm": gbs / peaks["hbm_gbs"],
-                                   "timing": f"{reps} back-to-back q35k_matmul_argmax_dev calls (GEMV + argmax "
-                                             f"epilogue + index kernel), CUDA events"}}
-
-
-def gemm_configs(ctx, torch, synth, peaks):
-    """Tensor-core prefill GEMM (Q4_K, M = 512): BASELINE config 3 and config
-    4 at M = 512 on one GPU, in both GEMM modes (exact: every product formed
-    from the reference's integers, error ~1e-6; fast: fp16-rounded dequantized
-    operands, error ~4e-4, within the 1e-3 bar).  Device time per
-    q35k_matmul_dev call (Q8_K preparation kernel + GEMM kernel), CUDA-graph
-    replay; the weights (14 and 80 MB) sit in L2 after the first call, as in
-    any compute-bound GEMM.  TFLOP/s = 2 M N K / time against the measured
-    dense bf16 peak."""
-    import q35k
-
-    out = {}
-    Q4, Q5, Q6 = synth.Q4_K, synth.Q5_K, synth.Q6_K
-    # Q5_K / Q6_K at cfg2's ffn_down shape (K = 9728, N = 2560) with GGUF-like
-    # scales; Q6_K has no exact tensor-core form (its exact-mode prefill is
-    # the GEMV).
-    cases = [("cfg3_q4k_gemm_m512", Q4, 512, 2560, 9728), ("cfg4_q4k_gemm_m512_p1", Q4, 512, 5120, 27648),
-             ("q5k_gemm_m512_k9728_n2560", Q5, 512, 9728, 2560)]
-    for mode, suffix in ((q35k.GEMM_EXACT, ""), (q35k.GEMM_FAST, "_fast")):
-        ctx.set_gemm_mode(mode)
-        extra = [("q6k_gemm_m512_k9728_n2560", Q6, 512, 9728, 2560)] if mode == q35k.GEMM_FAST else []
-        out.update(_gemm_lines(ctx, torch, synth, peaks, suffix, "exact" if mode == q35k.GEMM_EXACT else "fast",
-                               cases + extra))
-    ctx.set_gemm_mode(q35k.GEMM_EXACT)
-    return out
-
-
-def _gemm_lines(ctx, torch, synth, peaks, suffix, mode_name, cases):
-    out = {}
-    stream = torch.cuda.current_stream()
-    bf16_peak = peaks.get("bf16_tflops")
-    for name, qt, m, k, n in cases:
-        name = name + suffix
-        w = synth.kquant_blocks(qt, n, k, seed=1, q5_uniform_d=False)
-        x = synth.activations(m, k, seed=2)
-        W = ctx.upload(qt, w, k, n)
-        dx = torch.from_numpy(x).cuda()
-        dy = torch.empty((m, n), dtype=torch.float32, device="cuda")
-        for _ in range(3):
-            ctx.matmul_dev(W, dx, dy, m, stream)
-        torch.cuda.synchronize()
-        calls = 10
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            cs = torch.cuda.current_stream()
-            for _ in range(calls):
-                ctx.matmul_dev(W, dx, dy, m, cs)
-        graph.replay()
-        torch.cuda.synchronize()
-        reps = 10
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        b.record(stream)
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / (reps * calls)
-        tflops = 2.0 * m * n * k / (ms / 1e3) / 1e12
-        out[name] = {"call_ms": ms, "TFLOP/s": tflops, "gemm_mode": mode_name,
-                     "frac_measured_bf16": (tflops / bf16_peak) if bf16_peak else None,
-                     "peak_kind": "measured dense bf16 (MEASURED_PEAKS.json bf16_tflops)",
-                     "kernels": "gemm_prep_kernel + gemm_q4k_tc_kernel (tcgen05, TMEM, TMA)",
-                     "timing": f"CUDA-graph replay of {calls} calls x {reps}"}
-        del graph
+    def run(self):
+        args = self.args
+        self.headline()
+        if self.world == 1 and not args.no_extra:
+            self.gemv_configs()
+            self.gemm_configs()
+            self.argmax_config()
+            self.ffn_config()
+        if self.world > 1 and not args.no_extra:
+            self.shard_configs()
+        cpu = self.cpu_checks() if self.rank == 0 and not args.no_cpu else None
+        if self.rank == 0:
+            self.report(cpu)
+        W, SW = self.head_w
         W.free()
-    return out
+        if self.world > 1:
+            SW.free()
+            self.group.close()
+        self.ctx.close()
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
 
 
 # Configurations runnable alone under a profiler: (qtype, M, K, N, x scale,
@@ -642,6 +790,7 @@ PROFILE_CASES = {
     "cfg4_q4k_gemm_m512_p1_fast": (12, 512, 5120, 27648, 1.0, 1),
     "q5k_gemm_m512": (13, 512, 9728, 2560, 1.0, 0),
     "q5k_gemm_m512_fast": (13, 512, 9728, 2560, 1.0, 1),
+    "q6k_gemm_m512": (14, 512, 9728, 2560, 1.0, 0),
     "q6k_gemm_m512_fast": (14, 512, 9728, 2560, 1.0, 1),
 }
 
@@ -675,7 +824,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU leg (baselines and oracle checks)")
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary configs")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="N > 1: how the ranks' output slices are all-gathered")
@@ -690,7 +839,7 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     else:
-        run_ours(args)
+        Bench(args).run()
 
 
 if __name__ == "__main__":
