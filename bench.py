@@ -63,7 +63,8 @@ SHARD_CASES = [("cfg4_m1", 1), ("cfg4_m8", 8), ("cfg4_m512", 512)]
 CFG4_K, CFG4_N = 5120, 27648
 OUR_KERNELS = ("q35k_decode_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel",
                "repack_tiles_kernel", "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel",
-               "signal_wait_kernel", "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel")
+               "q35k_shard_gather_kernel", "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel",
+               "q35k_stage_in_kernel", "q35k_err_out_kernel")
 
 
 def load_peaks():
@@ -438,6 +439,38 @@ class Bench:
         clocks.start()
         ms_step = self.back_to_back_ms(step, args.steps)
         clk = clocks.stop()
+        extra = {}
+        if world > 1:
+            # Host time to issue one step (Python + the library call), and the
+            # same steps replayed from a CUDA graph (the call's kernel
+            # arguments do not change from call to call, so it can be captured).
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                step()
+            extra["host_issue_ms_per_step"] = (time.perf_counter() - t0) / args.steps * 1e3
+            torch.cuda.synchronize()
+            self.barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                cs = torch.cuda.current_stream().cuda_stream
+                for _ in range(args.steps):
+                    self.group.matmul_dev(SW, [dx], [dy_full], M, self.gather_mode, streams=[cs])
+            graph.replay()
+            torch.cuda.synchronize()
+            extra["graph_ms_per_step"] = self.back_to_back_ms(graph.replay, 3) / args.steps
+            del graph
+            # Phase breakdown of one isolated call on this rank's GPU.
+            self.barrier()
+            self.group.set_trace(True)
+            step()
+            torch.cuda.synchronize()
+            tr = self.group.trace(0)
+            self.group.set_trace(False)
+            us = lambda a, b: (tr[b] - tr[a]) / 1e3  # noqa: E731
+            extra["phases_us"] = {"gemv": us("gemv_start", "gemv_end"), "publish": us("gemv_end", "flags_published"),
+                                  "peer_wait": us("flags_published", "peers_seen"),
+                                  "copy": us("peers_seen", "gather_end"), "total": us("gemv_start", "gather_end")}
         # Per-step event times (untimed pass: events between steps serialise them).
         evs = [self.event_pair() for _ in range(args.steps)]
         self.barrier()
@@ -485,7 +518,7 @@ class Bench:
                     "kernel": "q35k_decode_kernel<Q6_K,1,fused>", "kernel_ms": gemv_ms,
                     "algorithmic_bytes_per_launch": nbytes_local}
         self.head = dict(value=value, ms_step=ms_step, step_ms=sum(step_ms) / len(step_ms), gemv_ms=gemv_ms,
-                         rows=rows, clocks=clk, launches=launches, roofline=roofline, e2e=e2e)
+                         rows=rows, clocks=clk, launches=launches, roofline=roofline, e2e=e2e, extra=extra)
         self.head_w = (W, SW)
 
     def e2e(self, W, x, dx, dy_full, step, nbytes_total):
@@ -749,6 +782,7 @@ class Bench:
             "cpu_baseline": cpu_line, "e2e": h["e2e"], "clocks": h["clocks"],
             "gpu_launches": h["launches"] * self.args.steps, "launches_per_step": h["launches"],
         }
+        line.update(h["extra"])
         print(json.dumps(line))
 
     def run(self):

@@ -96,6 +96,10 @@ public static unsafe partial class Q35k
                                                                           int gatherMode, nint* streams);
     [LibraryImport(Lib)] public static partial int q35k_shard_matmul(nint shard, nint w, float* x, float* y, int tokens,
                                                                       int gatherMode);
+    [LibraryImport(Lib)] public static partial int q35k_shard_set_wait_limit(nint shard, int milliseconds);
+    [LibraryImport(Lib)] public static partial int q35k_shard_reset(nint shard);
+    [LibraryImport(Lib)] public static partial int q35k_shard_set_trace(nint shard, int on);
+    [LibraryImport(Lib)] public static partial int q35k_shard_trace(nint shard, int local, ulong* out6);
 
     // ---- Decode matmul that allocates no device memory ----
     [LibraryImport(Lib)] public static partial int q35k_matmul_static_dev(nint w, nint dX, nint dY, int tokens, nint stream);

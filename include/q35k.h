@@ -242,6 +242,24 @@ int q35k_shard_matmul_dev(q35k_shard* s, const q35k_sharded_weight* w, const flo
 /* Host pointers, synchronous: x [tokens][n_in] in, full y out. */
 int q35k_shard_matmul(q35k_shard* s, const q35k_sharded_weight* w, const float* x, float* y, int tokens,
                       int gather_mode);
+/* Bound of the fused gather's wait for the peers' flags (default 2000 ms).
+ * A rank that does not take part in a fused call makes the other ranks'
+ * waits run out: their call reports Q35K_ETIMEOUT at q35k_shard_sync (the
+ * reference's synchronous exceptions, Model/Qwen35Model.Decode.cs:18-85,
+ * become a TimeoutException) instead of hanging. */
+int q35k_shard_set_wait_limit(q35k_shard* s, int milliseconds);
+/* Collective: after a Q35K_ETIMEOUT, every rank of the group calls this
+ * before its next call.  It waits for the rank's kernels, clears its error
+ * state and the fused gather's flags and call counters, and (one process per
+ * GPU) returns once every rank has done so. */
+int q35k_shard_reset(q35k_shard* s);
+/* Diagnostics of the fused gather: with tracing on, each fused call records
+ * on every local device the %globaltimer (ns) of six phases -- GEMV first
+ * CTA start, GEMV last CTA end, gather kernel start, flags published, all
+ * peers' flags seen, gather kernel end -- which q35k_shard_trace copies out
+ * for local device `local` (after the call; it synchronizes that device). */
+int q35k_shard_set_trace(q35k_shard* s, int on);
+int q35k_shard_trace(q35k_shard* s, int local, uint64_t* out6);
 
 /* ---- Allocation-free decode matmul --------------------------------------
  *

@@ -14,8 +14,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
+#include <vector>
 
 using namespace q35k;
 
@@ -468,6 +470,18 @@ static int check_matmul_args(q35k_ctx* c, const q35k_weight* w, const void* x, c
 
 static cudaStream_t pick(q35k_ctx* c, void* stream) { return stream ? (cudaStream_t)stream : c->stream; }
 
+// Page-locked host ranges registered with q35k_host_register (process-wide,
+// as the registration is): base, length and device alias.
+namespace {
+struct HostRange {
+    const char* base;
+    size_t bytes;
+    char* dev;
+};
+std::mutex g_ranges_mu;
+std::vector<HostRange> g_ranges;
+}  // namespace
+
 // Device address of a caller's host buffer [p, p + bytes) when it is
 // page-locked and mapped into the device's address space as one contiguous
 // range (registered with q35k_host_register, or allocated pinned by the
@@ -475,14 +489,19 @@ static cudaStream_t pick(q35k_ctx* c, void* stream) { return stream ? (cudaStrea
 // write y in place instead of staging them through the context's buffers.
 static void* host_alias(const void* p, size_t bytes) {
     if (!p || bytes == 0) return nullptr;
+    const char* cp = static_cast<const char*>(p);
+    {
+        std::lock_guard<std::mutex> lock(g_ranges_mu);
+        for (const HostRange& r : g_ranges)
+            if (cp >= r.base && cp + bytes <= r.base + r.bytes) return r.dev + (cp - r.base);
+    }
     cudaPointerAttributes a0, a1;
     if (cudaPointerGetAttributes(&a0, p) != cudaSuccess) {
         cudaGetLastError();
         return nullptr;
     }
     if (a0.type != cudaMemoryTypeHost || !a0.devicePointer) return nullptr;
-    const char* last = static_cast<const char*>(p) + bytes - 1;
-    if (cudaPointerGetAttributes(&a1, last) != cudaSuccess) {
+    if (cudaPointerGetAttributes(&a1, cp + bytes - 1) != cudaSuccess) {
         cudaGetLastError();
         return nullptr;
     }
@@ -490,6 +509,49 @@ static void* host_alias(const void* p, size_t bytes) {
         return nullptr;
     return a0.devicePointer;
 }
+
+// x of a host-pointer decode call crosses the bus in this kernel (mapped host
+// memory -> device) rather than by a copy-engine transfer: the GEMV launched
+// after it with programmatic dependent launch starts streaming its weights
+// while x is still in flight, and reads x only after this grid completed.
+__global__ void q35k_stage_in_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t n) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((((uintptr_t)src | (uintptr_t)dst) & 15) == 0 && n % 4 == 0) {
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (size_t i = i0; i < n / 4; i += stride) d4[i] = s4[i];
+    } else {
+        for (size_t i = i0; i < n; i += stride) dst[i] = src[i];
+    }
+}
+
+// The device error word of a host-pointer call, read out into mapped host
+// memory once the kernels before it have completed (no copy-engine transfer
+// on the call's critical path).
+__global__ void q35k_err_out_kernel(const unsigned* __restrict__ d_err, unsigned* h_err) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    *reinterpret_cast<volatile unsigned*>(h_err) = *reinterpret_cast<const volatile unsigned*>(d_err);
+}
+
+template <typename... P, typename... A>
+static cudaError_t launch_k(void (*kernel)(P...), int grid, int block, cudaStream_t st, bool pdl, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)block);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<P>(args)...);
+}
+
+// Inputs of at most this many bytes go through q35k_stage_in_kernel; larger
+// ones (prefill) through the copy engines.
+constexpr size_t STAGE_KERNEL_MAX_BYTES = 256 * 1024;
 
 // Device buffers handed in by the caller: the quantizer reads x as float4,
 // the GEMV reads Q8_K blocks and writes y as 32-bit words.
@@ -532,41 +594,54 @@ int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int
     cudaSetDevice(c->device);
     const size_t in_bytes = (size_t)tokens * w->n_in * sizeof(float);
     const size_t out_bytes = (size_t)tokens * w->n_out * sizeof(float);
+    const bool gemm = c->uses_gemm(w, tokens);
     // Page-locked caller buffers (q35k_host_register) are used in place: x is
-    // copied straight from it, and y written straight into it.  Pageable ones
-    // go through the context's pinned staging buffers.
-    const bool x_pinned = host_alias(x, in_bytes) != nullptr;
+    // read straight from it and y written straight into it.  Pageable ones go
+    // through the context's pinned staging buffers.
+    const float* x_alias = static_cast<const float*>(host_alias(x, in_bytes));
     float* y_alias = static_cast<float*>(host_alias(y, out_bytes));
     if ((rc = c->ensure_dev((void**)&c->d_x, &c->x_cap, in_bytes, false)) != Q35K_OK) return rc;
-    if ((rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
-    if (!x_pinned && (rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
-    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, out_bytes + 64)) != Q35K_OK) return rc;
-    if (!x_pinned) std::memcpy(c->h_in, x, in_bytes);
-    cudaError_t e = cudaMemcpyAsync(c->d_x, x_pinned ? x : c->h_in, in_bytes, cudaMemcpyHostToDevice, c->stream);
-    if (e != cudaSuccess) return c->cuda_fail(e, "H2D copy of x");
+    if (gemm && (rc = c->ensure_dev((void**)&c->d_y, &c->y_cap, out_bytes, false)) != Q35K_OK) return rc;
+    if (!x_alias && (rc = c->ensure_host(&c->h_in, &c->h_in_cap, in_bytes)) != Q35K_OK) return rc;
+    // Staging for y (pageable callers) and, after it, the mapped error word.
+    const size_t stage_y = y_alias ? 0 : out_bytes;
+    if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, stage_y + 64)) != Q35K_OK) return rc;
+    volatile unsigned* h_err = reinterpret_cast<volatile unsigned*>(static_cast<char*>(c->h_out) + stage_y);
+    *h_err = 0;
+    void* h_out_dev = nullptr;
+    if (cudaHostGetDevicePointer(&h_out_dev, c->h_out, 0) != cudaSuccess || !h_out_dev) {
+        cudaGetLastError();
+        return c->fail(Q35K_ECUDA, "the pinned staging buffer is not mapped into the device's address space");
+    }
+    if (!x_alias) {
+        std::memcpy(c->h_in, x, in_bytes);
+        void* dp = nullptr;
+        if (cudaHostGetDevicePointer(&dp, c->h_in, 0) == cudaSuccess) x_alias = static_cast<const float*>(dp);
+        cudaGetLastError();
+    }
+    cudaError_t e;
+    if (x_alias && in_bytes <= STAGE_KERNEL_MAX_BYTES) {
+        const size_t n = in_bytes / sizeof(float);
+        const int grid = (int)std::min<size_t>((n / 4 + 255) / 256, 16);
+        e = launch_k(q35k_stage_in_kernel, std::max(grid, 1), 256, c->stream, false, x_alias, c->d_x, n);
+    } else {
+        e = cudaMemcpyAsync(c->d_x, x_alias ? x : static_cast<const float*>(c->h_in), in_bytes,
+                            cudaMemcpyHostToDevice, c->stream);
+    }
+    if (e != cudaSuccess) return c->cuda_fail(e, "H2D transfer of x");
     // Decode calls: the GEMV stores y over the bus straight into host memory
     // (the caller's page-locked y, or the mapped staging buffer), so the
     // transfer overlaps the kernel and no copy follows it.  Prefill calls
     // (tensor-core GEMM, whose tiles would cross the bus piece by piece) copy
     // y back afterwards.
     float* d_out = c->d_y;
-    bool direct = false;
-    if (!c->uses_gemm(w, tokens)) {
-        void* dp = y_alias;
-        if (!dp && (cudaHostGetDevicePointer(&dp, c->h_out, 0) != cudaSuccess || !dp)) {
-            cudaGetLastError();
-            dp = nullptr;
-        }
-        if (dp) {
-            d_out = static_cast<float*>(dp);
-            direct = true;
-        }
-    }
+    if (!gemm) d_out = y_alias ? y_alias : static_cast<float*>(h_out_dev);
     if ((rc = q35k_matmul_dev(c, w, c->d_x, d_out, tokens, c->stream)) != Q35K_OK) return rc;
-    unsigned* h_err = (unsigned*)((char*)c->h_out + out_bytes);
-    float* host_dst = y_alias ? y : static_cast<float*>(c->h_out);
-    e = direct ? cudaSuccess : cudaMemcpyAsync(host_dst, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream);
+    e = gemm ? cudaMemcpyAsync(y_alias ? y : c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream)
+             : cudaSuccess;
+    if (e == cudaSuccess)
+        e = launch_k(q35k_err_out_kernel, 1, 1, c->stream, !gemm, (const unsigned*)c->d_err,
+                     reinterpret_cast<unsigned*>(static_cast<char*>(h_out_dev) + stage_y));
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "matmul");
     if (*h_err) return c->on_device_error(*h_err);
@@ -578,7 +653,7 @@ int q35k_host_register(q35k_ctx* c, void* p, size_t bytes) {
     if (!c) return Q35K_EINVAL;
     if (!p || bytes == 0) return c->fail(Q35K_EINVAL, "host_register: NULL pointer or zero size");
     cudaSetDevice(c->device);
-    const cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
+    cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
     if (e == cudaErrorHostMemoryAlreadyRegistered) {
         cudaGetLastError();
         return c->fail(Q35K_EINVAL, "host_register: the range is already page-locked");
@@ -587,6 +662,14 @@ int q35k_host_register(q35k_ctx* c, void* p, size_t bytes) {
         cudaGetLastError();
         return c->fail(Q35K_ENOMEM, "host_register: cudaHostRegister(%zu) failed: %s", bytes, cudaGetErrorString(e));
     }
+    void* dev = nullptr;
+    if ((e = cudaHostGetDevicePointer(&dev, p, 0)) != cudaSuccess || !dev) {
+        cudaGetLastError();
+        cudaHostUnregister(p);
+        return c->fail(Q35K_ECUDA, "host_register: no device address for the range: %s", cudaGetErrorString(e));
+    }
+    std::lock_guard<std::mutex> lock(g_ranges_mu);
+    g_ranges.push_back(HostRange{static_cast<const char*>(p), bytes, static_cast<char*>(dev)});
     return Q35K_OK;
 }
 
@@ -594,6 +677,14 @@ int q35k_host_unregister(q35k_ctx* c, void* p) {
     if (!c) return Q35K_EINVAL;
     if (!p) return c->fail(Q35K_EINVAL, "host_unregister: NULL pointer");
     cudaSetDevice(c->device);
+    {
+        std::lock_guard<std::mutex> lock(g_ranges_mu);
+        for (size_t i = 0; i < g_ranges.size(); i++)
+            if (g_ranges[i].base == p) {
+                g_ranges.erase(g_ranges.begin() + (long)i);
+                break;
+            }
+    }
     const cudaError_t e = cudaHostUnregister(p);
     if (e != cudaSuccess) {
         cudaGetLastError();

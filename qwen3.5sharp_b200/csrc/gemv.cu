@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
     if (tid == 0) {
         for (int t = 0; t <= kr; t++) mbar_init(&bars[t], 1);
         fence_mbar_init();
+        if (a.peers.trace) atomicMin(a.peers.trace, (unsigned long long)globaltimer_ns());
     }
     __syncthreads();
     const Q8Planar pl = q8_planar(M, nb);
@@ -222,6 +223,9 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
 
     if (warp == 0) {
         const int row = gl * TILE_ROWS + lane;
+        // Fused all-gather: this call's gather area in the peers' buffers.
+        const size_t poff = a.peers.n ? (size_t)((*a.peers.seq + 1u) & 1u) * a.peers.half : 0;
+        const int ldp = a.peers.ldp;
         float v[M];
 #pragma unroll
         for (int m = 0; m < M; m++) {
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
 #pragma unroll
                 for (int m = 0; m < M; m++) {
                     y[(size_t)m * ldy + row] = v[m];
-                    for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * ldy + row] = v[m];
+                    for (int k = 0; k < a.peers.n; k++) a.peers.y[k][poff + (size_t)m * ldp + row] = v[m];
                 }
             if (a.argmax)
 #pragma unroll
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
                     for (int k = 0; k < p.splits; k++) sum += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
                     if (row < n_out && y) {
                         y[(size_t)m * ldy + row] = sum;
-                        for (int k = 0; k < a.peers.n; k++) a.peers.y[k][(size_t)m * ldy + row] = sum;
+                        for (int k = 0; k < a.peers.n; k++) a.peers.y[k][poff + (size_t)m * ldp + row] = sum;
                     }
                     if (a.argmax) warp_argmax_commit(row < n_out ? argmax_key(sum, row) : 0ull, a.argmax + m, lane);
                 }
@@ -266,6 +270,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
             }
         }
     }
+    if (a.peers.trace && tid == 0) atomicMax(a.peers.trace + 1, (unsigned long long)globaltimer_ns());
     if (!ok && tid == 0) {
         // A wait gave up: give the copies in flight a bounded chance to land
         // before the CTA's shared memory is released.

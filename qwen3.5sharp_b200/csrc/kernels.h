@@ -31,13 +31,22 @@ cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tile
                                 int n_pad, cudaStream_t s);
 
 // Fused all-gather of a row-sharded decode call (csrc/shard.cu): besides its
-// own y, the GEMV stores every output value at the same offset in each peer's
-// gather buffer (NVLink stores through IPC or peer pointers).  The kernel that
-// follows it in the stream publishes the stores (flags).  n == 0: off.
+// own y, the GEMV stores every output value into each peer's gather area
+// (NVLink stores through IPC or peer pointers), at [token][row] with row
+// stride ldp.  Each buffer holds two areas used on alternate calls: the
+// call's area is half (*seq + 1) & 1, where *seq counts this rank's completed
+// fused calls (device memory, advanced by the gather kernel that follows the
+// GEMV; read after the GEMV's grid-dependency wait).  The gather kernel
+// publishes the stores (flags).  n == 0: off.
 constexpr int GEMV_MAX_PEERS = 7;
 struct GemvPeers {
-    float* y[GEMV_MAX_PEERS];  // this rank's slice in peer k's gather buffer
-    int n;
+    float* y[GEMV_MAX_PEERS];  // this rank's slice in peer k's gather area 0
+    int n, ldp;
+    size_t half;               // floats from gather area 0 to area 1
+    const unsigned* seq;
+    // Optional phase timestamps of the call (%globaltimer, ns): [0] first CTA
+    // start (atomicMin), [1] last CTA end (atomicMax); nullptr: off.
+    unsigned long long* trace;
 };
 
 // Further weights of the same type and K sharing one launch and one set of

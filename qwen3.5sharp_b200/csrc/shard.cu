@@ -13,16 +13,20 @@
 // and fused gathers of a single-process group are available.
 //
 // Fused gather (Q35K_GATHER_FUSED, decode calls of at most 8 tokens): every
-// rank owns a "symmetric" buffer -- a header of one flag per rank, then two
-// gather areas [nranks][tokens][n_shard] used on alternate calls -- that every
-// other rank can store into (CUDA IPC mappings exchanged once over NCCL, or
-// peer pointers in one process).  The GEMV stores each output row into its
-// own area and into every peer's.  A one-thread kernel after it publishes the
-// stores (system fence, then this rank's flag -- the call's sequence number
-// -- in every peer) and waits, bounded, for the peers' flags; then the area
-// is permuted into y.  Alternate areas keep a peer's next call from
-// overwriting a slice this rank is still reading: that call's stores come
-// after the peer saw this rank's flag for the call in between.
+// rank owns a "symmetric" buffer -- a header (one flag per rank, the rank's
+// call counter) and two gather areas [nranks][tokens][n_shard] used on
+// alternate calls -- that every other rank can store into (CUDA IPC mappings
+// exchanged once over NCCL, or peer pointers in one process).  The GEMV
+// writes its rows straight into the caller's y and stores them into every
+// peer's area.  One gather kernel after it publishes the stores (one system
+// fence, then this rank's flag in every peer, one lane per peer), waits --
+// bounded, one lane per peer -- for the peers' flags, and copies the peers'
+// slices from its own area into y.  The call counter lives in device memory
+// and is advanced by that kernel, so a call's kernel arguments do not change
+// from call to call (the call can be captured in a CUDA graph).  Alternate
+// areas keep a peer's next call from overwriting a slice this rank is still
+// reading: that call's stores come after the peer saw this rank's flag for
+// the call in between.
 #include "../../include/q35k.h"
 #include "api_internal.h"
 #include "device_common.cuh"
@@ -112,37 +116,107 @@ __global__ void gather_permute_kernel(const float* __restrict__ g, float* __rest
     }
 }
 
-// Symmetric buffer header: flag of rank r at u32 index r; the gather areas
-// start at SYM_HDR.
+// Symmetric buffer header (u32 words): the flag rank r raised here at [r],
+// this rank's count of completed fused calls at HDR_SEQ, the gather kernel's
+// arrival counter at HDR_DONE, and 64-bit phase timestamps from byte
+// HDR_TRACE (tracing only).  The gather areas start at SYM_HDR.
 constexpr size_t SYM_HDR = 256;
 constexpr int SYM_MAX_RANKS = 32;
+constexpr int HDR_SEQ = 32, HDR_DONE = 33;
+constexpr size_t HDR_TRACE = 192;  // 8 slots of u64
+constexpr int TRACE_SLOTS = 6;
 
-// After this rank's GEMV (earlier in the stream, so its stores into the peers'
-// buffers have been performed when this kernel starts): publish them with a
-// system-scope release of this rank's flag in every peer, then wait, bounded,
-// until every other rank's flag here reached `epoch`.
-struct PeerFlags {
-    unsigned* flag[GEMV_MAX_PEERS];  // this rank's flag slot in peer k's buffer
-    int n;
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+struct GatherArgs {
+    unsigned* flag_out[GEMV_MAX_PEERS];  // this rank's flag in peer k's buffer
+    int peer_rank[GEMV_MAX_PEERS];
+    unsigned* hdr;                       // this rank's buffer header
+    const float* area;                   // this rank's gather area 0, [nranks][tokens][n_shard]
+    float* y;                            // [tokens][ldy]
+    size_t half;                         // floats from area 0 to area 1
+    int n_peers, tokens, n_shard, n_out, ldy;
+    unsigned* err;
+    unsigned long long* trace;           // phase timestamps (nullptr: off)
+    unsigned long long limit_ns;         // bound of the flag wait
 };
-__global__ void signal_wait_kernel(PeerFlags pf, const unsigned* mine, int nranks, int me, unsigned epoch,
-                                   unsigned* err) {
-    // Launched with programmatic dependent launch: publish only after this
-    // rank's GEMV (the kernel before) has completed and its stores landed.
+
+// After this rank's GEMV (the kernel before it, launched with programmatic
+// dependent launch): publish, wait for the peers, copy their slices into y.
+// A flag wait that runs out sets DEV_ERR_TIMEOUT and skips the copy; the
+// host then reports Q35K_ETIMEOUT and the group must be reset
+// (q35k_shard_reset) before its next fused call.
+__global__ void __launch_bounds__(256) q35k_shard_gather_kernel(GatherArgs g) {
     asm volatile("griddepcontrol.launch_dependents;");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    __threadfence_system();
-    for (int k = 0; k < pf.n; k++) st_release_sys(pf.flag[k], epoch);
-    for (int j = 0; j < nranks; j++) {
-        if (j == me) continue;
-        const uint64_t start = globaltimer_ns();
-        for (uint32_t it = 0;; ++it) {
-            if ((int)(ld_acquire_sys(mine + j) - epoch) >= 0) break;
-            if ((it & 63u) == 63u && globaltimer_ns() - start > 2000000000ull) {
-                atomicOr(err, DEV_ERR_TIMEOUT);
-                return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMV completed, its stores performed
+    const unsigned ep = *reinterpret_cast<volatile const unsigned*>(g.hdr + HDR_SEQ) + 1u;
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < 32) {
+        if (blockIdx.x == 0) {
+            if (g.trace && lane == 0) atomicMax(g.trace + 2, (unsigned long long)globaltimer_ns());
+            // One system-scope fence per peer lane, then this rank's flag there:
+            // the GEMV's stores into that peer are ordered before the flag.
+            if (lane < g.n_peers) {
+                __threadfence_system();
+                st_relaxed_sys(g.flag_out[lane], ep);
+            }
+            __syncwarp();
+            if (g.trace && lane == 0) atomicMax(g.trace + 3, (unsigned long long)globaltimer_ns());
+        }
+        // Lane k waits for peer k's flag of this call, bounded in time.
+        int good = 1;
+        if (lane < g.n_peers) {
+            const unsigned* f = g.hdr + g.peer_rank[lane];
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t it = 0;; ++it) {
+                if ((int)(ld_relaxed_sys(f) - ep) >= 0) break;
+                if ((it & 63u) == 63u && globaltimer_ns() - t0 > g.limit_ns) {
+                    atomicOr(g.err, DEV_ERR_TIMEOUT);
+                    good = 0;
+                    break;
+                }
             }
         }
+        good = __all_sync(0xffffffffu, good);
+        // Acquire side: the peers' stores, released with their flags, are
+        // visible to this CTA's reads below.
+        fence_acq_rel_sys();
+        if (lane == 0) s_ok = good;
+    }
+    __syncthreads();
+    if (s_ok) {
+        if (g.trace && tid == 0) atomicMax(g.trace + 4, (unsigned long long)globaltimer_ns());
+        const float* area = g.area + (size_t)(ep & 1u) * g.half;
+        const long long per_peer = (long long)g.tokens * g.n_shard;
+        const long long total = per_peer * g.n_peers;
+        for (long long i = (long long)blockIdx.x * blockDim.x + tid; i < total; i += (long long)gridDim.x * blockDim.x) {
+            const int k = (int)(i / per_peer);
+            const long long rem = i - k * per_peer;
+            const int t = (int)(rem / g.n_shard), j = (int)(rem - (long long)t * g.n_shard);
+            const int r = g.peer_rank[k];
+            const int c = r * g.n_shard + j;
+            if (c < g.n_out) g.y[(size_t)t * g.ldy + c] = area[((size_t)r * g.tokens + t) * g.n_shard + j];
+        }
+    }
+    // The last CTA to finish advances this rank's call counter (read by the
+    // next call's kernels after their grid-dependency wait).
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(g.hdr + HDR_DONE, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile unsigned*>(g.hdr + HDR_DONE) = 0u;
+            *reinterpret_cast<volatile unsigned*>(g.hdr + HDR_SEQ) = ep;
+        }
+        if (g.trace) atomicMax(g.trace + 5, (unsigned long long)globaltimer_ns());
     }
 }
 
@@ -169,7 +243,8 @@ struct q35k_shard {
     std::vector<std::vector<uint8_t*>> sym_view;
     std::vector<std::vector<char>> sym_ipc;
     size_t sym_area = 0;  // bytes of one gather area
-    unsigned epoch = 0;   // sequence number of fused calls
+    unsigned long long wait_limit_ns = 2000000000ull;  // bound of the fused gather's flag wait
+    bool trace = false;   // record phase timestamps of fused calls
     std::string err;
 
     int fail(int code, const std::string& msg) {
@@ -385,33 +460,50 @@ static int shard_matmul_fused(q35k_shard* s, const q35k_sharded_weight* w, const
     const size_t area = (size_t)s->nranks * 8 * w->n_shard * sizeof(float);
     int rc = ensure_sym(s, area);
     if (rc != Q35K_OK) return rc;
-    const unsigned ep = ++s->epoch;
-    const size_t half = (ep & 1) ? s->sym_area : 0;  // alternate gather areas
     for (int i = 0; i < nloc; i++) {
         q35k_ctx* c = s->ctxs[i];
         cudaSetDevice(s->devices[i]);
+        const cudaStream_t st = stream_of(i);
         const int rank = s->first_rank + i;
+        unsigned* hdr = reinterpret_cast<unsigned*>(s->sym[i]);
+        unsigned long long* trace =
+            s->trace ? reinterpret_cast<unsigned long long*>(s->sym[i] + HDR_TRACE) : nullptr;
         GemvPeers pr{};
-        PeerFlags pf{};
+        GatherArgs g{};
         for (int j = 0; j < s->nranks; j++) {
             if (j == rank) continue;
             uint8_t* v = s->sym_view[i][j];
-            pr.y[pr.n++] = reinterpret_cast<float*>(v + SYM_HDR + half) + (size_t)rank * slot;
-            pf.flag[pf.n++] = reinterpret_cast<unsigned*>(v) + rank;
+            pr.y[pr.n++] = reinterpret_cast<float*>(v + SYM_HDR) + (size_t)rank * slot;
+            g.flag_out[g.n_peers] = reinterpret_cast<unsigned*>(v) + rank;
+            g.peer_rank[g.n_peers++] = j;
         }
-        float* mine = reinterpret_cast<float*>(s->sym[i] + SYM_HDR + half) + (size_t)rank * slot;
+        pr.ldp = w->n_shard;
+        pr.half = s->sym_area / sizeof(float);
+        pr.seq = hdr + HDR_SEQ;
+        pr.trace = trace;
+        if (trace) {
+            cudaMemsetAsync(trace, 0xff, sizeof(unsigned long long), st);
+            cudaMemsetAsync(trace + 1, 0, (TRACE_SLOTS - 1) * sizeof(unsigned long long), st);
+        }
         if (w->parts[i]) {
-            rc = c->matmul_into(w->parts[i], d_x[i], mine, w->n_shard, tokens, stream_of(i), &pr);
+            // This rank's rows go straight to their columns of y.
+            rc = c->matmul_into(w->parts[i], d_x[i], d_y[i] + (size_t)rank * w->n_shard, w->n_out, tokens, st, &pr);
             if (rc != Q35K_OK) return s->fail(rc, c->err);
         }
-        cudaError_t e = launch_pdl(signal_wait_kernel, 1, 1, stream_of(i), pf,
-                                   reinterpret_cast<const unsigned*>(s->sym[i]), s->nranks, rank, ep, c->d_err);
-        const long long total = (long long)tokens * w->n_out;
-        const int grid = (int)std::min<long long>((total + 255) / 256, 4096);
-        if (e == cudaSuccess)
-            e = launch_pdl(gather_permute_kernel, grid, 256, stream_of(i),
-                           reinterpret_cast<const float*>(s->sym[i] + SYM_HDR + half), d_y[i], s->nranks, tokens,
-                           w->n_shard, w->n_out);
+        g.hdr = hdr;
+        g.area = reinterpret_cast<const float*>(s->sym[i] + SYM_HDR);
+        g.y = d_y[i];
+        g.half = pr.half;
+        g.tokens = tokens;
+        g.n_shard = w->n_shard;
+        g.n_out = w->n_out;
+        g.ldy = w->n_out;
+        g.err = c->d_err;
+        g.trace = trace;
+        g.limit_ns = s->wait_limit_ns;
+        const long long total = (long long)g.n_peers * slot;
+        const int grid = (int)std::max(1LL, std::min<long long>((total + 2047) / 2048, 148));
+        cudaError_t e = launch_pdl(q35k_shard_gather_kernel, grid, 256, st, g);
         if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) return s->fail(Q35K_ECUDA, std::string("fused gather: ") + cudaGetErrorString(e));
     }
@@ -671,6 +763,68 @@ int q35k_shard_sync(q35k_shard* s) {
         const int rc = q35k_sync(c);
         if (rc != Q35K_OK) return s->fail(rc, q35k_last_error(c));
     }
+    return Q35K_OK;
+}
+
+int q35k_shard_set_wait_limit(q35k_shard* s, int milliseconds) {
+    if (!s) return Q35K_EINVAL;
+    if (milliseconds < 1 || milliseconds > 600000) return s->fail(Q35K_EINVAL, "wait limit must be 1..600000 ms");
+    s->wait_limit_ns = (unsigned long long)milliseconds * 1000000ull;
+    return Q35K_OK;
+}
+
+int q35k_shard_reset(q35k_shard* s) {
+    if (!s) return Q35K_EINVAL;
+    // 1. No kernel of this process is in flight after the synchronization
+    //    (every device wait is bounded).  2. One process per GPU: a barrier,
+    //    so no rank's kernel can still store a flag into this rank's buffer.
+    //    3. The fused gather's flags and call counters restart from zero.
+    //    4. A second barrier: no rank starts its next call before every rank
+    //    has cleared its buffer.
+    const bool multi_process = (int)s->devices.size() != s->nranks && !s->comms.empty();
+    for (size_t i = 0; i < s->devices.size(); i++) {
+        cudaSetDevice(s->devices[i]);
+        cudaDeviceSynchronize();
+        cudaGetLastError();
+    }
+    char mine = 1;
+    std::vector<char> all(s->nranks);
+    if (multi_process) {
+        const int rc = allgather_host(s, &mine, all.data(), 1);
+        if (rc != Q35K_OK) return rc;
+    }
+    for (size_t i = 0; i < s->devices.size(); i++) {
+        cudaSetDevice(s->devices[i]);
+        q35k_ctx* c = s->ctxs[i];
+        if (cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess ||
+            (c->d_counters && cudaMemset(c->d_counters, 0, c->counters_cap) != cudaSuccess) ||
+            (c->d_gcnt && cudaMemset(c->d_gcnt, 0, c->gcnt_cap) != cudaSuccess) ||
+            (i < s->sym.size() && s->sym[i] && cudaMemset(s->sym[i], 0, SYM_HDR) != cudaSuccess) ||
+            cudaDeviceSynchronize() != cudaSuccess)
+            return s->fail(Q35K_ECUDA, "shard reset: clearing the device state failed");
+    }
+    if (multi_process) {
+        const int rc = allgather_host(s, &mine, all.data(), 1);
+        if (rc != Q35K_OK) return rc;
+    }
+    return Q35K_OK;
+}
+
+int q35k_shard_set_trace(q35k_shard* s, int on) {
+    if (!s) return Q35K_EINVAL;
+    s->trace = on != 0;
+    return Q35K_OK;
+}
+
+int q35k_shard_trace(q35k_shard* s, int local, uint64_t* out) {
+    if (!s || !out) return Q35K_EINVAL;
+    if (local < 0 || local >= (int)s->devices.size()) return s->fail(Q35K_EINVAL, "local device index out of range");
+    if (!s->trace || (size_t)local >= s->sym.size() || !s->sym[local])
+        return s->fail(Q35K_EINVAL, "no traced fused call on this group (q35k_shard_set_trace)");
+    cudaSetDevice(s->devices[local]);
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(out, s->sym[local] + HDR_TRACE, TRACE_SLOTS * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return s->fail(Q35K_ECUDA, "reading the trace failed");
     return Q35K_OK;
 }
 

@@ -520,6 +520,26 @@ class Shard:
     def sync(self):
         self._check(self.L.q35k_shard_sync(self.h))
 
+    def set_wait_limit(self, milliseconds: int):
+        """Bound of the fused gather's wait for the peers (q35k_shard_set_wait_limit)."""
+        self._check(self.L.q35k_shard_set_wait_limit(self.h, int(milliseconds)))
+
+    def reset(self):
+        """Collective recovery after a TimeoutException (q35k_shard_reset)."""
+        self._check(self.L.q35k_shard_reset(self.h))
+
+    def set_trace(self, on: bool = True):
+        self._check(self.L.q35k_shard_set_trace(self.h, 1 if on else 0))
+
+    TRACE_PHASES = ("gemv_start", "gemv_end", "gather_start", "flags_published", "peers_seen", "gather_end")
+
+    def trace(self, local: int = 0) -> dict:
+        """Phase timestamps (ns, %globaltimer) of the last fused call on local
+        device `local` (q35k_shard_trace)."""
+        buf = (ctypes.c_uint64 * 6)()
+        self._check(self.L.q35k_shard_trace(self.h, local, buf))
+        return dict(zip(self.TRACE_PHASES, list(buf)))
+
 
 class ShardedWeight:
     def __init__(self, shard: Shard, h, qtype: int, n_in: int, n_out: int):

@@ -61,6 +61,10 @@ SIGNATURES = {
     "q35k_shard_weight_free": ([_vp, _vp], _i32),
     "q35k_shard_matmul_dev": ([_vp, _vp, _pp, _pp, _i32, _i32, _pp], _i32),
     "q35k_shard_matmul": ([_vp, _vp, _vp, _vp, _i32, _i32], _i32),
+    "q35k_shard_set_wait_limit": ([_vp, _i32], _i32),
+    "q35k_shard_reset": ([_vp], _i32),
+    "q35k_shard_set_trace": ([_vp, _i32], _i32),
+    "q35k_shard_trace": ([_vp, _i32, ctypes.POINTER(ctypes.c_uint64)], _i32),
     "q35k_set_gemm_mode": ([_vp, _i32], _i32),
     "q35k_matmul_static_dev": ([_vp, _vp, _vp, _i32, _vp], _i32),
     "q35k_gguf_open": ([ctypes.c_char_p, _pp], _i32),

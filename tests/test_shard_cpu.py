@@ -90,3 +90,105 @@ def test_gloo_two_ranks_reassemble_full_output(tmp_path, oracle_mod, qt, k, n, m
     # each row's dot product does not depend on the other rows
     err = np.abs(y.astype(np.float64) - ref).max() / np.abs(ref).max()
     assert err <= 1e-6
+
+
+# ---------------------------------------------------------------------------
+# The fused gather's protocol and its failure handling, restated on CPU ranks:
+# each rank stores its slice into every peer's alternate area, raises its flag
+# there with its call counter + 1, waits (bounded) for the peers' flags, and
+# advances its counter; a missing rank makes the others' waits run out, and
+# the two-barrier reset (q35k_shard_reset) restarts every counter from zero.
+# The peers' memory is a TCPStore shared by the gloo ranks.
+# ---------------------------------------------------------------------------
+
+class _FusedGatherModel:
+    def __init__(self, store, rank, world, wait_s):
+        self.store, self.rank, self.world, self.wait_s = store, rank, world, wait_s
+        self.seq = 0
+
+    def call(self, my_slice):
+        ep = self.seq + 1
+        half = ep & 1
+        for j in range(self.world):  # the GEMV's stores into every peer's area
+            if j != self.rank:
+                self.store.set(f"area/{j}/{half}/{self.rank}", my_slice.tobytes())
+        for j in range(self.world):  # publish: the flag after the stores
+            if j != self.rank:
+                self.store.set(f"flag/{j}/{self.rank}", str(ep))
+        parts = {self.rank: my_slice}
+        deadline = __import__("time").monotonic() + self.wait_s
+        timed_out = False
+        for j in range(self.world):
+            if j == self.rank:
+                continue
+            key = f"flag/{self.rank}/{j}"
+            while not (self.store.check([key]) and int(self.store.get(key)) >= ep):
+                if __import__("time").monotonic() > deadline:
+                    timed_out = True
+                    break
+            if timed_out:
+                break
+            parts[j] = np.frombuffer(self.store.get(f"area/{self.rank}/{half}/{j}"), dtype=np.float32)
+        self.seq = ep  # the gather kernel advances the counter even when a wait ran out
+        if timed_out:
+            raise TimeoutError("a peer's flag did not arrive")
+        return np.concatenate([parts[j] for j in range(self.world)])
+
+    def reset(self, barrier):
+        barrier()  # nothing of any rank still stores into this rank's buffer
+        for j in range(self.world):
+            self.store.set(f"flag/{self.rank}/{j}", "0")
+        self.seq = 0
+        barrier()  # every buffer is clear before anyone's next call
+
+
+def _protocol_rank(rank, world, port, out_path):
+    import datetime
+
+    import torch.distributed as dist
+
+    import oracle
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        store = dist.TCPStore("127.0.0.1", port + 1, world, rank == 0, timeout=datetime.timedelta(seconds=60))
+        qt, k, n = Q4_K, 512, 256
+        w = synth.kquant_blocks(qt, n, k, seed=21)
+        r0, r1 = q35k.shard_range(n, world, rank)
+        W = oracle.Weight(qt, w[r0:r1], k, r1 - r0)
+        model = _FusedGatherModel(store, rank, world, wait_s=0.3)
+        xs = [synth.activations(1, k, seed=30 + i) for i in range(4)]
+        outs, events = [], []
+        outs.append(model.call(W.matmul(xs[0], threads=1)[0]))
+        if rank == 0:  # call 2: rank 1 leaves between steps
+            try:
+                model.call(W.matmul(xs[1], threads=1)[0])
+                events.append("no timeout")
+            except TimeoutError:
+                events.append("timeout")
+        model.reset(dist.barrier)
+        for x in xs[2:]:
+            outs.append(model.call(W.matmul(x, threads=1)[0]))
+        np.save(out_path.format(rank), np.stack(outs))
+        with open(out_path.format(rank) + ".txt", "w") as f:
+            f.write(",".join(events))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_missing_rank_times_out_and_reset_recovers(tmp_path, oracle_mod):
+    pytest.importorskip("torch")
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    out = str(tmp_path / "y{}.npy")
+    mp.spawn(_protocol_rank, args=(2, port, out), nprocs=2, join=True)
+    assert open(out.format(0) + ".txt").read() == "timeout"
+    qt, k, n = Q4_K, 512, 256
+    w = synth.kquant_blocks(qt, n, k, seed=21)
+    W = oracle_mod.Weight(qt, w, k, n)
+    refs = [W.matmul(synth.activations(1, k, seed=30 + i), threads=1)[0] for i in (0, 2, 3)]
+    for r in range(2):
+        ys = np.load(out.format(r))
+        for y, ref in zip(ys, refs):
+            assert np.array_equal(y, ref)

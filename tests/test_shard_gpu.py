@@ -108,8 +108,16 @@ def _rank_proc(rank, nranks, nccl_id, qt, k, n, m, mode, q):
     x = synth.activations(m, k, seed=2)
     sw = sh.upload(qt, w, k, n)
     y = sh.matmul(sw, x, gather=mode)
-    # repeated calls alternate the fused gather's buffers and sequence numbers
+    # repeated calls alternate the fused gather's buffers and call counters
     same = all((sh.matmul(sw, x, gather=mode) == y).all() for _ in range(3))
+    if mode == Q.GATHER_FUSED:
+        # phase trace of one call: six increasing timestamps on this device
+        sh.set_trace(True)
+        same = same and (sh.matmul(sw, x, gather=mode) == y).all()
+        tr = sh.trace(0)
+        sh.set_trace(False)
+        ph = [tr[k] for k in Q.Shard.TRACE_PHASES]
+        same = same and ph[0] <= ph[1] <= ph[5] and ph[2] <= ph[3] <= ph[5] and ph[4] <= ph[5]
     q.put((rank, y, same))
     sw.free()
     sh.close()
@@ -141,3 +149,80 @@ def test_process_per_gpu_group(ctx, mode):
     W.free()
     for r in range(2):
         assert rel_err(res[r], single.astype(np.float64)) <= 1e-5
+
+
+def _skip_proc(rank, nid, q):
+    """Rank `rank` of a 2-GPU fused-gather group: call 1 on both ranks, call
+    2 on rank 0 only (rank 1 leaves between steps, nothing in flight), then
+    the collective reset and call 3 on both ranks."""
+    import q35k as Q
+
+    try:
+        sh = Q.Shard(nranks=2, rank=rank, nccl_id=nid, device=rank)
+        sh.set_wait_limit(50)
+        qt, k, n = Q4_K, 2560, 4096
+        w = synth.kquant_blocks(qt, n, k, seed=11)
+        sw = sh.upload(qt, w, k, n)
+        x1 = synth.activations(1, k, seed=12)
+        x3 = synth.activations(1, k, seed=13)
+        y1 = sh.matmul(sw, x1, gather=Q.GATHER_FUSED)
+        timed_out = None
+        if rank == 0:
+            try:
+                sh.matmul(sw, x1, gather=Q.GATHER_FUSED)
+                timed_out = False
+            except Q.TimeoutException:
+                timed_out = True
+        sh.reset()
+        y3 = sh.matmul(sw, x3, gather=Q.GATHER_FUSED)
+        y3b = sh.matmul(sw, x3, gather=Q.GATHER_FUSED)
+        q.put((rank, None, timed_out, y1, y3, y3b))
+        sw.free()
+        sh.close()
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e), None, None, None, None))
+
+
+def test_missing_rank_times_out_and_group_recovers(ctx):
+    """Failure detection without a GPU fault: a bounded flag wait (50 ms) runs
+    out because a peer skipped the call; the call reports TimeoutException
+    (Q35K_ETIMEOUT), and after q35k_shard_reset on both ranks the next calls
+    are correct again."""
+    if _ngpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    nid = q35k.nccl_unique_id()
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    procs = [mpc.Process(target=_skip_proc, args=(r, nid, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        r, err, timed_out, y1, y3, y3b = q.get(timeout=300)
+        got[r] = (err, timed_out, y1, y3, y3b)
+    for p in procs:
+        p.join(timeout=120)
+    assert got[0][0] is None and got[1][0] is None, (got[0][0], got[1][0])
+    assert got[0][1] is True
+    qt, k, n = Q4_K, 2560, 4096
+    W = ctx.upload(qt, synth.kquant_blocks(qt, n, k, seed=11), k, n)
+    r1 = ctx.matmul(W, synth.activations(1, k, seed=12))
+    r3 = ctx.matmul(W, synth.activations(1, k, seed=13))
+    W.free()
+    for r in range(2):
+        _, _, y1, y3, y3b = got[r]
+        assert rel_err(y1, r1.astype(np.float64)) <= 1e-5
+        assert rel_err(y3, r3.astype(np.float64)) <= 1e-5
+        assert (y3 == y3b).all()
+
+
+def test_wait_limit_is_validated(ctx):
+    sh = q35k.Shard(devices=[0])
+    with pytest.raises(q35k.ArgumentException):
+        sh.set_wait_limit(0)
+    sh.set_wait_limit(100)
+    sh.reset()
+    sh.close()
