@@ -468,9 +468,11 @@ class Bench:
             tr = self.group.trace(0)
             self.group.set_trace(False)
             us = lambda a, b: (tr[b] - tr[a]) / 1e3  # noqa: E731
-            extra["phases_us"] = {"gemv": us("gemv_start", "gemv_end"), "publish": us("gemv_end", "flags_published"),
-                                  "peer_wait": us("flags_published", "peers_seen"),
-                                  "copy": us("peers_seen", "gather_end"), "total": us("gemv_start", "gather_end")}
+            extra["phases_us"] = {"gemv": us("gemv_start", "gemv_end"),
+                                  "gather_start_after_gemv_start": us("gemv_start", "gather_start"),
+                                  "peers_seen_after_gemv_end": us("gemv_end", "peers_seen"),
+                                  "gemv_done_seen_after_gemv_end": us("gemv_end", "gemv_done_seen"),
+                                  "total": us("gemv_start", "gather_end")}
         # Per-step event times (untimed pass: events between steps serialise them).
         evs = [self.event_pair() for _ in range(args.steps)]
         self.barrier()

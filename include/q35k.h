@@ -255,9 +255,10 @@ int q35k_shard_set_wait_limit(q35k_shard* s, int milliseconds);
 int q35k_shard_reset(q35k_shard* s);
 /* Diagnostics of the fused gather: with tracing on, each fused call records
  * on every local device the %globaltimer (ns) of six phases -- GEMV first
- * CTA start, GEMV last CTA end, gather kernel start, flags published, all
- * peers' flags seen, gather kernel end -- which q35k_shard_trace copies out
- * for local device `local` (after the call; it synchronizes that device). */
+ * CTA start, GEMV last CTA end, gather kernel start, every peer value of the
+ * call arrived, the GEMV's completion seen by the gather kernel, gather
+ * kernel end -- which q35k_shard_trace copies out for local device `local`
+ * (after the call; it synchronizes that device). */
 int q35k_shard_set_trace(q35k_shard* s, int on);
 int q35k_shard_trace(q35k_shard* s, int local, uint64_t* out6);
 

@@ -149,7 +149,11 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
     // The next kernel in the stream may start streaming its own weights on
     // SMs this grid frees; it reads activations and writes results only
     // after its own griddepcontrol.wait, i.e. after this grid completed.
-    asm volatile("griddepcontrol.launch_dependents;");
+    // Fused all-gather: the kernel after this one (the gather) reads the call
+    // counter when it starts, so it may start only once every CTA has passed
+    // the wait for the kernel before (the previous call's gather, which
+    // advanced the counter): the trigger then follows that wait.
+    if (a.peers.n == 0) asm volatile("griddepcontrol.launch_dependents;");
     // mma token counts: the unit's K-range of the planar Q8_K in global memory (each
     // warp loads its B operand words directly; L2 serves the CTAs of a K-range).
     constexpr bool Q8_GLOBAL = M >= q8_interleave_min_rows(TYPE);
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
     } else {
         ok = mbar_wait_bounded(&bars[kr], 0, a.err);
     }
+    if (a.peers.n) asm volatile("griddepcontrol.launch_dependents;");
 
     float* red = reinterpret_cast<float*>(smem + L.red);
     if constexpr (M >= q8_interleave_min_rows(TYPE)) {
@@ -223,9 +228,17 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
 
     if (warp == 0) {
         const int row = gl * TILE_ROWS + lane;
-        // Fused all-gather: this call's gather area in the peers' buffers.
-        const size_t poff = a.peers.n ? (size_t)((*a.peers.seq + 1u) & 1u) * a.peers.half : 0;
+        // Fused all-gather: this call's number and its gather area in the
+        // peers' buffers.  Each value goes out as one 64-bit store of (call
+        // number, value bits), so a peer knows it has arrived without a
+        // fence or a flag.
+        const unsigned ep = a.peers.n ? *a.peers.seq + 1u : 0u;
+        const size_t poff = (size_t)(ep & 1u) * a.peers.half;
         const int ldp = a.peers.ldp;
+        auto to_peers = [&](size_t off, float v) {
+            const unsigned long long word = ((unsigned long long)ep << 32) | __float_as_uint(v);
+            for (int k = 0; k < a.peers.n; k++) st_relaxed_sys_u64(a.peers.y[k] + poff + off, word);
+        };
         float v[M];
 #pragma unroll
         for (int m = 0; m < M; m++) {
@@ -237,7 +250,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
 #pragma unroll
                 for (int m = 0; m < M; m++) {
                     y[(size_t)m * ldy + row] = v[m];
-                    for (int k = 0; k < a.peers.n; k++) a.peers.y[k][poff + (size_t)m * ldp + row] = v[m];
+                    to_peers((size_t)m * ldp + row, v[m]);
                 }
             if (a.argmax)
 #pragma unroll
@@ -262,7 +275,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
                     for (int k = 0; k < p.splits; k++) sum += __ldcg(&part[((size_t)k * M + m) * 32 + lane]);
                     if (row < n_out && y) {
                         y[(size_t)m * ldy + row] = sum;
-                        for (int k = 0; k < a.peers.n; k++) a.peers.y[k][poff + (size_t)m * ldp + row] = sum;
+                        to_peers((size_t)m * ldp + row, sum);
                     }
                     if (a.argmax) warp_argmax_commit(row < n_out ? argmax_key(sum, row) : 0ull, a.argmax + m, lane);
                 }

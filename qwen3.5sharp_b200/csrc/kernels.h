@@ -33,16 +33,16 @@ cudaError_t launch_repack_tiles(int type, const uint8_t* rows_src, uint8_t* tile
 // Fused all-gather of a row-sharded decode call (csrc/shard.cu): besides its
 // own y, the GEMV stores every output value into each peer's gather area
 // (NVLink stores through IPC or peer pointers), at [token][row] with row
-// stride ldp.  Each buffer holds two areas used on alternate calls: the
-// call's area is half (*seq + 1) & 1, where *seq counts this rank's completed
-// fused calls (device memory, advanced by the gather kernel that follows the
-// GEMV; read after the GEMV's grid-dependency wait).  The gather kernel
-// publishes the stores (flags).  n == 0: off.
+// stride ldp, as one 64-bit word (call number << 32 | value bits).  Each
+// buffer holds two areas used on alternate calls: the call's number is
+// *seq + 1 and its area (*seq + 1) & 1, where *seq counts this rank's
+// completed fused calls (device memory, advanced by the gather kernel that
+// follows the GEMV; read after the GEMV's grid-dependency wait).  n == 0: off.
 constexpr int GEMV_MAX_PEERS = 7;
 struct GemvPeers {
-    float* y[GEMV_MAX_PEERS];  // this rank's slice in peer k's gather area 0
+    unsigned long long* y[GEMV_MAX_PEERS];  // this rank's slice in peer k's gather area 0
     int n, ldp;
-    size_t half;               // floats from gather area 0 to area 1
+    size_t half;               // words from gather area 0 to area 1
     const unsigned* seq;
     // Optional phase timestamps of the call (%globaltimer, ns): [0] first CTA
     // start (atomicMin), [1] last CTA end (atomicMax); nullptr: off.

@@ -13,20 +13,22 @@
 // and fused gathers of a single-process group are available.
 //
 // Fused gather (Q35K_GATHER_FUSED, decode calls of at most 8 tokens): every
-// rank owns a "symmetric" buffer -- a header (one flag per rank, the rank's
-// call counter) and two gather areas [nranks][tokens][n_shard] used on
+// rank owns a "symmetric" buffer -- a header (the rank's call counter) and
+// two gather areas [nranks][tokens][n_shard] of 64-bit words used on
 // alternate calls -- that every other rank can store into (CUDA IPC mappings
 // exchanged once over NCCL, or peer pointers in one process).  The GEMV
-// writes its rows straight into the caller's y and stores them into every
-// peer's area.  One gather kernel after it publishes the stores (one system
-// fence, then this rank's flag in every peer, one lane per peer), waits --
-// bounded, one lane per peer -- for the peers' flags, and copies the peers'
-// slices from its own area into y.  The call counter lives in device memory
-// and is advanced by that kernel, so a call's kernel arguments do not change
-// from call to call (the call can be captured in a CUDA graph).  Alternate
-// areas keep a peer's next call from overwriting a slice this rank is still
-// reading: that call's stores come after the peer saw this rank's flag for
-// the call in between.
+// writes its rows straight into the caller's y and stores each of them into
+// every peer's area as one 64-bit word (call number << 32 | value bits), so
+// the receiver knows a value has arrived from the word itself: there is no
+// fence, flag or separate publish step.  The gather kernel after the GEMV
+// starts while the GEMV's last CTAs still run, waits (bounded in time) for
+// each peer word of this call and copies the values into y.  The call
+// counter lives in device memory and is advanced by that kernel once its own
+// GEMV has completed, so a call's kernel arguments do not change from call
+// to call (the call can be captured in a CUDA graph).  Alternate areas keep
+// a peer's next call from overwriting a slice this rank is still reading:
+// that call's stores come after the peer's own gather of the call in
+// between, which needed this rank's words of that call.
 #include "../../include/q35k.h"
 #include "api_internal.h"
 #include "device_common.cuh"
@@ -116,103 +118,76 @@ __global__ void gather_permute_kernel(const float* __restrict__ g, float* __rest
     }
 }
 
-// Symmetric buffer header (u32 words): the flag rank r raised here at [r],
-// this rank's count of completed fused calls at HDR_SEQ, the gather kernel's
-// arrival counter at HDR_DONE, and 64-bit phase timestamps from byte
-// HDR_TRACE (tracing only).  The gather areas start at SYM_HDR.
+// Symmetric buffer header (u32 words): this rank's count of completed fused
+// calls at HDR_SEQ, the gather kernel's arrival counter at HDR_DONE, and
+// 64-bit phase timestamps from byte HDR_TRACE (tracing only).  The gather
+// areas start at SYM_HDR.
 constexpr size_t SYM_HDR = 256;
 constexpr int SYM_MAX_RANKS = 32;
 constexpr int HDR_SEQ = 32, HDR_DONE = 33;
 constexpr size_t HDR_TRACE = 192;  // 8 slots of u64
 constexpr int TRACE_SLOTS = 6;
 
-__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
-    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
 struct GatherArgs {
-    unsigned* flag_out[GEMV_MAX_PEERS];  // this rank's flag in peer k's buffer
     int peer_rank[GEMV_MAX_PEERS];
-    unsigned* hdr;                       // this rank's buffer header
-    const float* area;                   // this rank's gather area 0, [nranks][tokens][n_shard]
-    float* y;                            // [tokens][ldy]
-    size_t half;                         // floats from area 0 to area 1
+    unsigned* hdr;                        // this rank's buffer header
+    const unsigned long long* area;       // this rank's gather area 0, [nranks][tokens][n_shard] words
+    float* y;                             // [tokens][ldy]
+    size_t half;                          // words from area 0 to area 1
     int n_peers, tokens, n_shard, n_out, ldy;
     unsigned* err;
-    unsigned long long* trace;           // phase timestamps (nullptr: off)
-    unsigned long long limit_ns;         // bound of the flag wait
+    unsigned long long* trace;            // phase timestamps (nullptr: off)
+    unsigned long long limit_ns;          // bound of the wait for a peer's words
 };
 
-// After this rank's GEMV (the kernel before it, launched with programmatic
-// dependent launch): publish, wait for the peers, copy their slices into y.
-// A flag wait that runs out sets DEV_ERR_TIMEOUT and skips the copy; the
-// host then reports Q35K_ETIMEOUT and the group must be reset
+// After this rank's GEMV (launched with programmatic dependent launch; it may
+// start while the GEMV's last CTAs run, which is safe because this kernel
+// reads only the peers' words, and because the GEMV lets it start only once
+// the previous call's gather has completed, so the call counter it reads is
+// current).  A wait that runs out sets DEV_ERR_TIMEOUT and skips the rest;
+// the host then reports Q35K_ETIMEOUT and the group must be reset
 // (q35k_shard_reset) before its next fused call.
 __global__ void __launch_bounds__(256) q35k_shard_gather_kernel(GatherArgs g) {
     asm volatile("griddepcontrol.launch_dependents;");
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMV completed, its stores performed
     const unsigned ep = *reinterpret_cast<volatile const unsigned*>(g.hdr + HDR_SEQ) + 1u;
-    __shared__ int s_ok;
-    const int tid = threadIdx.x, lane = tid & 31;
-    if (tid < 32) {
-        if (blockIdx.x == 0) {
-            if (g.trace && lane == 0) atomicMax(g.trace + 2, (unsigned long long)globaltimer_ns());
-            // One system-scope fence per peer lane, then this rank's flag there:
-            // the GEMV's stores into that peer are ordered before the flag.
-            if (lane < g.n_peers) {
-                __threadfence_system();
-                st_relaxed_sys(g.flag_out[lane], ep);
-            }
-            __syncwarp();
-            if (g.trace && lane == 0) atomicMax(g.trace + 3, (unsigned long long)globaltimer_ns());
-        }
-        // Lane k waits for peer k's flag of this call, bounded in time.
-        int good = 1;
-        if (lane < g.n_peers) {
-            const unsigned* f = g.hdr + g.peer_rank[lane];
-            const uint64_t t0 = globaltimer_ns();
-            for (uint32_t it = 0;; ++it) {
-                if ((int)(ld_relaxed_sys(f) - ep) >= 0) break;
-                if ((it & 63u) == 63u && globaltimer_ns() - t0 > g.limit_ns) {
-                    atomicOr(g.err, DEV_ERR_TIMEOUT);
-                    good = 0;
-                    break;
+    const int tid = threadIdx.x;
+    if (g.trace && tid == 0) atomicMin(g.trace + 2, (unsigned long long)globaltimer_ns());
+    const unsigned long long* area = g.area + (size_t)(ep & 1u) * g.half;
+    const int nthreads = gridDim.x * blockDim.x, me = blockIdx.x * blockDim.x + tid;
+    bool good = true;
+    const uint64_t t0 = globaltimer_ns();
+    for (int k = 0; good && k < g.n_peers; k++) {
+        const int r = g.peer_rank[k];
+        const int rows = min(g.n_shard, g.n_out - r * g.n_shard);
+        for (int t = 0; good && t < g.tokens; t++) {
+            const unsigned long long* src = area + ((size_t)r * g.tokens + t) * g.n_shard;
+            float* dst = g.y + (size_t)t * g.ldy + (size_t)r * g.n_shard;
+            for (int j = me; j < rows; j += nthreads) {
+                unsigned long long v = ld_relaxed_sys_u64(src + j);
+                for (uint32_t it = 0; (unsigned)(v >> 32) != ep; ++it) {
+                    if ((it & 63u) == 63u && globaltimer_ns() - t0 > g.limit_ns) {
+                        atomicOr(g.err, DEV_ERR_TIMEOUT);
+                        good = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                    v = ld_relaxed_sys_u64(src + j);
                 }
+                if (!good) break;
+                dst[j] = __uint_as_float((unsigned)v);
             }
         }
-        good = __all_sync(0xffffffffu, good);
-        // Acquire side: the peers' stores, released with their flags, are
-        // visible to this CTA's reads below.
-        fence_acq_rel_sys();
-        if (lane == 0) s_ok = good;
     }
-    __syncthreads();
-    if (s_ok) {
-        if (g.trace && tid == 0) atomicMax(g.trace + 4, (unsigned long long)globaltimer_ns());
-        const float* area = g.area + (size_t)(ep & 1u) * g.half;
-        const long long per_peer = (long long)g.tokens * g.n_shard;
-        const long long total = per_peer * g.n_peers;
-        for (long long i = (long long)blockIdx.x * blockDim.x + tid; i < total; i += (long long)gridDim.x * blockDim.x) {
-            const int k = (int)(i / per_peer);
-            const long long rem = i - k * per_peer;
-            const int t = (int)(rem / g.n_shard), j = (int)(rem - (long long)t * g.n_shard);
-            const int r = g.peer_rank[k];
-            const int c = r * g.n_shard + j;
-            if (c < g.n_out) g.y[(size_t)t * g.ldy + c] = area[((size_t)r * g.tokens + t) * g.n_shard + j];
-        }
-    }
-    // The last CTA to finish advances this rank's call counter (read by the
-    // next call's kernels after their grid-dependency wait).
+    if (g.trace) atomicMax(g.trace + 3, (unsigned long long)globaltimer_ns());
+    // The last CTA to finish advances this rank's call counter -- after this
+    // rank's GEMV has completed (it reads the counter) -- for the next call's
+    // kernels, which read it after their own grid-dependency wait.
     __syncthreads();
     if (tid == 0) {
         __threadfence();
         if (atomicAdd(g.hdr + HDR_DONE, 1u) == gridDim.x - 1) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            if (g.trace) atomicMax(g.trace + 4, (unsigned long long)globaltimer_ns());
             *reinterpret_cast<volatile unsigned*>(g.hdr + HDR_DONE) = 0u;
             *reinterpret_cast<volatile unsigned*>(g.hdr + HDR_SEQ) = ep;
         }
@@ -454,10 +429,10 @@ static cudaError_t launch_pdl(void (*kernel)(P...), int grid, int block, cudaStr
 static int shard_matmul_fused(q35k_shard* s, const q35k_sharded_weight* w, const float* const* d_x,
                               float* const* d_y, int tokens, const std::function<cudaStream_t(int)>& stream_of) {
     const int nloc = (int)s->devices.size();
-    const size_t slot = (size_t)tokens * w->n_shard;
+    const size_t slot = (size_t)tokens * w->n_shard;  // words per rank
     // Areas sized for the largest decode call of this weight (8 tokens), so
     // that the collective growth happens once.
-    const size_t area = (size_t)s->nranks * 8 * w->n_shard * sizeof(float);
+    const size_t area = (size_t)s->nranks * 8 * w->n_shard * sizeof(unsigned long long);
     int rc = ensure_sym(s, area);
     if (rc != Q35K_OK) return rc;
     for (int i = 0; i < nloc; i++) {
@@ -473,17 +448,18 @@ static int shard_matmul_fused(q35k_shard* s, const q35k_sharded_weight* w, const
         for (int j = 0; j < s->nranks; j++) {
             if (j == rank) continue;
             uint8_t* v = s->sym_view[i][j];
-            pr.y[pr.n++] = reinterpret_cast<float*>(v + SYM_HDR) + (size_t)rank * slot;
-            g.flag_out[g.n_peers] = reinterpret_cast<unsigned*>(v) + rank;
+            pr.y[pr.n++] = reinterpret_cast<unsigned long long*>(v + SYM_HDR) + (size_t)rank * slot;
             g.peer_rank[g.n_peers++] = j;
         }
         pr.ldp = w->n_shard;
-        pr.half = s->sym_area / sizeof(float);
+        pr.half = s->sym_area / sizeof(unsigned long long);
         pr.seq = hdr + HDR_SEQ;
         pr.trace = trace;
         if (trace) {
+            // slots 0 and 2 take a minimum, the others a maximum
+            cudaMemsetAsync(trace, 0, TRACE_SLOTS * sizeof(unsigned long long), st);
             cudaMemsetAsync(trace, 0xff, sizeof(unsigned long long), st);
-            cudaMemsetAsync(trace + 1, 0, (TRACE_SLOTS - 1) * sizeof(unsigned long long), st);
+            cudaMemsetAsync(trace + 2, 0xff, sizeof(unsigned long long), st);
         }
         if (w->parts[i]) {
             // This rank's rows go straight to their columns of y.
@@ -491,7 +467,7 @@ static int shard_matmul_fused(q35k_shard* s, const q35k_sharded_weight* w, const
             if (rc != Q35K_OK) return s->fail(rc, c->err);
         }
         g.hdr = hdr;
-        g.area = reinterpret_cast<const float*>(s->sym[i] + SYM_HDR);
+        g.area = reinterpret_cast<const unsigned long long*>(s->sym[i] + SYM_HDR);
         g.y = d_y[i];
         g.half = pr.half;
         g.tokens = tokens;
@@ -502,7 +478,7 @@ static int shard_matmul_fused(q35k_shard* s, const q35k_sharded_weight* w, const
         g.trace = trace;
         g.limit_ns = s->wait_limit_ns;
         const long long total = (long long)g.n_peers * slot;
-        const int grid = (int)std::max(1LL, std::min<long long>((total + 2047) / 2048, 148));
+        const int grid = (int)std::max(1LL, std::min<long long>((total + 1023) / 1024, 148));
         cudaError_t e = launch_pdl(q35k_shard_gather_kernel, grid, 256, st, g);
         if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) return s->fail(Q35K_ECUDA, std::string("fused gather: ") + cudaGetErrorString(e));
@@ -799,7 +775,7 @@ int q35k_shard_reset(q35k_shard* s) {
         if (cudaMemset(c->d_err, 0, sizeof(unsigned)) != cudaSuccess ||
             (c->d_counters && cudaMemset(c->d_counters, 0, c->counters_cap) != cudaSuccess) ||
             (c->d_gcnt && cudaMemset(c->d_gcnt, 0, c->gcnt_cap) != cudaSuccess) ||
-            (i < s->sym.size() && s->sym[i] && cudaMemset(s->sym[i], 0, SYM_HDR) != cudaSuccess) ||
+            (i < s->sym.size() && s->sym[i] && cudaMemset(s->sym[i], 0, SYM_HDR + 2 * s->sym_area) != cudaSuccess) ||
             cudaDeviceSynchronize() != cudaSuccess)
             return s->fail(Q35K_ECUDA, "shard reset: clearing the device state failed");
     }

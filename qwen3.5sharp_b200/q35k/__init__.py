@@ -531,7 +531,7 @@ class Shard:
     def set_trace(self, on: bool = True):
         self._check(self.L.q35k_shard_set_trace(self.h, 1 if on else 0))
 
-    TRACE_PHASES = ("gemv_start", "gemv_end", "gather_start", "flags_published", "peers_seen", "gather_end")
+    TRACE_PHASES = ("gemv_start", "gemv_end", "gather_start", "peers_seen", "gemv_done_seen", "gather_end")
 
     def trace(self, local: int = 0) -> dict:
         """Phase timestamps (ns, %globaltimer) of the last fused call on local

@@ -94,11 +94,12 @@ def test_gloo_two_ranks_reassemble_full_output(tmp_path, oracle_mod, qt, k, n, m
 
 # ---------------------------------------------------------------------------
 # The fused gather's protocol and its failure handling, restated on CPU ranks:
-# each rank stores its slice into every peer's alternate area, raises its flag
-# there with its call counter + 1, waits (bounded) for the peers' flags, and
-# advances its counter; a missing rank makes the others' waits run out, and
-# the two-barrier reset (q35k_shard_reset) restarts every counter from zero.
-# The peers' memory is a TCPStore shared by the gloo ranks.
+# each rank stores its slice into every peer's alternate area as words that
+# carry the call number (its call counter + 1), waits (bounded) until every
+# peer word of this call has arrived in its own area, and advances its
+# counter; a missing rank makes the others' waits run out, and the
+# two-barrier reset (q35k_shard_reset) clears every buffer and counter.  The
+# peers' memory is a TCPStore shared by the gloo ranks.
 # ---------------------------------------------------------------------------
 
 class _FusedGatherModel:
@@ -107,37 +108,43 @@ class _FusedGatherModel:
         self.seq = 0
 
     def call(self, my_slice):
+        import time
+
         ep = self.seq + 1
         half = ep & 1
-        for j in range(self.world):  # the GEMV's stores into every peer's area
+        word = np.concatenate([np.full(my_slice.shape, ep, np.uint32).view(np.float32), my_slice])
+        for j in range(self.world):  # the GEMV's stores into every peer's area: (call number, values)
             if j != self.rank:
-                self.store.set(f"area/{j}/{half}/{self.rank}", my_slice.tobytes())
-        for j in range(self.world):  # publish: the flag after the stores
-            if j != self.rank:
-                self.store.set(f"flag/{j}/{self.rank}", str(ep))
+                self.store.set(f"area/{j}/{half}/{self.rank}", word.tobytes())
         parts = {self.rank: my_slice}
-        deadline = __import__("time").monotonic() + self.wait_s
+        deadline = time.monotonic() + self.wait_s
         timed_out = False
         for j in range(self.world):
             if j == self.rank:
                 continue
-            key = f"flag/{self.rank}/{j}"
-            while not (self.store.check([key]) and int(self.store.get(key)) >= ep):
-                if __import__("time").monotonic() > deadline:
+            key = f"area/{self.rank}/{half}/{j}"
+            while True:
+                if self.store.check([key]):
+                    got = np.frombuffer(self.store.get(key), dtype=np.float32)
+                    n = got.size // 2
+                    if n and (got[:n].view(np.uint32) == ep).all():
+                        parts[j] = got[n:].copy()
+                        break
+                if time.monotonic() > deadline:
                     timed_out = True
                     break
             if timed_out:
                 break
-            parts[j] = np.frombuffer(self.store.get(f"area/{self.rank}/{half}/{j}"), dtype=np.float32)
         self.seq = ep  # the gather kernel advances the counter even when a wait ran out
         if timed_out:
-            raise TimeoutError("a peer's flag did not arrive")
+            raise TimeoutError("a peer's words of this call did not arrive")
         return np.concatenate([parts[j] for j in range(self.world)])
 
     def reset(self, barrier):
         barrier()  # nothing of any rank still stores into this rank's buffer
         for j in range(self.world):
-            self.store.set(f"flag/{self.rank}/{j}", "0")
+            for half in (0, 1):
+                self.store.set(f"area/{self.rank}/{half}/{j}", b"")
         self.seq = 0
         barrier()  # every buffer is clear before anyone's next call
 

@@ -117,7 +117,7 @@ def _rank_proc(rank, nranks, nccl_id, qt, k, n, m, mode, q):
         tr = sh.trace(0)
         sh.set_trace(False)
         ph = [tr[k] for k in Q.Shard.TRACE_PHASES]
-        same = same and ph[0] <= ph[1] <= ph[5] and ph[2] <= ph[3] <= ph[5] and ph[4] <= ph[5]
+        same = same and ph[0] <= ph[1] <= ph[4] <= ph[5] and ph[2] <= ph[3] <= ph[5]
     q.put((rank, y, same))
     sw.free()
     sh.close()
