@@ -168,13 +168,13 @@ int q35k_matmul_silu_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_gat
  * counterpart in the reference, which has one arithmetic:
  *   Q35K_GEMM_EXACT (default): the reference's -- Q8_K activations, exact
  *     products, fp32 scaling per super-block (results within fp32 rounding
- *     of the reference's).  Q4_K and Q5_K run on the tensor cores; Q6_K
- *     (whose sc * (q - 32) has no exact fp16 form) runs on the GEMV;
+ *     of the reference's).  Every type runs on the tensor cores; Q6_K, whose
+ *     sc * (q - 32) needs 12 significant bits, as two exact fp16 parts
+ *     (sc = 16 sh + sl) and two MMAs per K step;
  *   Q35K_GEMM_FAST: fp16-rounded dequantized weights times fp16-rounded
  *     dequantized Q8_K activations, one fp32 accumulator per tile (about
- *     4e-4 of max |y| from the reference's results); faster, and Q6_K runs
- *     on the tensor cores too.  A weight whose fp16 values could overflow
- *     (flagged at upload) keeps the exact path. */
+ *     4e-4 of max |y| from the reference's results); faster.  A weight whose
+ *     fp16 values could overflow (flagged at upload) keeps the exact path. */
 #define Q35K_GEMM_EXACT 0
 #define Q35K_GEMM_FAST 1
 int q35k_set_gemm_mode(q35k_ctx* ctx, int mode);

@@ -109,7 +109,7 @@ struct q35k_ctx {
     int gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy = 0,
              const float* d_up = nullptr, bool prep = true);
     // Prefill calls that take the tensor-core GEMM: enough tokens and a type
-    // the current mode supports (Q6_K: fast mode only).
+    // the current mode supports (every K-quant type in both modes).
     bool uses_gemm(const q35k_weight* w, int tokens) const;
     bool gemm_fast(const q35k_weight* w) const;
     // Several weights of one K on one input (q35k_matmul_shared_dev).

@@ -80,8 +80,10 @@ constexpr int TN = 128;  // tokens per tile
 // ptxas fits without spills.
 constexpr int THREADS = 640;
 constexpr int LAUNCH_REGS = 96;
-template <bool FAST> struct RegSplit {
-    static constexpr int CTRL = 32, PROD = FAST ? 80 : 72, DRAIN = FAST ? 144 : 152;
+template <bool FAST, int TYPE = TYPE_Q4_K> struct RegSplit {
+    // Q6_K's producers hold the most raw words (ql, qh, scales): 80 in both modes.
+    static constexpr bool WIDE_PROD = FAST || TYPE == TYPE_Q6_K;
+    static constexpr int CTRL = 32, PROD = WIDE_PROD ? 80 : 72, DRAIN = WIDE_PROD ? 144 : 152;
     static_assert(CTRL + 2 * PROD + 2 * DRAIN == 5 * LAUNCH_REGS, "split must use the launch registers exactly");
 };
 // Activation halves h = 0, 1 of every unit are loaded by warps WARP_TMA and
@@ -137,9 +139,16 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 // boxes of 64 K x 256 tokens), two stages; two weight stages without the Xe
 // tile; one 256-column accumulator (the A buffers keep columns 256..511), so
 // the next tile segment starts once the drains have read the last one.
+// Q6_K in the exact mode: its products sc * (q - 32) need up to 12
+// significant bits, so each half super-block's A operand is two exact fp16
+// parts, sl * (q - 32) and 16 sh * (q - 32) with sc = 16 sh + sl (sl in
+// [0, 15]), of 64 columns each, multiplied against the same activations and
+// summed in the accumulator: two MMAs per K step, no min term (the -32 is
+// applied to q itself).  Two A buffers of 128 columns then hold one unit.
 template <bool FAST, int TNX, int TYPE = TYPE_Q4_K> struct Geo {
     static_assert(TNX == 128 || (FAST && TNX == 256), "tile width");
-    static_assert(TYPE != TYPE_Q6_K || FAST, "Q6_K products sc*(q-32) need 12 bits: no exact fp16 form");
+    static constexpr bool Q6X = TYPE == TYPE_Q6_K && !FAST;
+    static constexpr bool MIN_TERM = !FAST && TYPE != TYPE_Q6_K;  // the exact mins MMA against Xe
     static constexpr int TILE_BYTES = WFmt<TYPE>::TILE_BYTES, META_TILE = WFmt<TYPE>::META_TILE;
     static constexpr int TN = TNX;
     static constexpr int X_STAGES = TNX == 128 ? 3 : 2;
@@ -149,18 +158,19 @@ template <bool FAST, int TNX, int TYPE = TYPE_Q4_K> struct Geo {
     // every lcm(2, X_STAGES) fills.
     static constexpr int X_PHASE_FILLS = X_STAGES % 2 ? 2 * X_STAGES : X_STAGES;
     static constexpr int W_STAGES = TNX == 128 ? 3 : 2;
-    static constexpr int EXT_BOX_BYTES = TNX == 128 ? 16 * 2 * TN : 0;
+    static constexpr int EXT_BOX_BYTES = (TNX == 128 && !Q6X) ? 16 * 2 * TN : 0;
     static constexpr int W_EXT_OFF = 0;
     static constexpr int W_TILE_OFF = EXT_BOX_BYTES;
     static constexpr int W_META_OFF = W_TILE_OFF + 4 * TILE_BYTES;
     static constexpr int W_STAGE_BYTES = (W_META_OFF + 4 * META_TILE + 1023) / 1024 * 1024;
     static constexpr int D_STAGES = 4;
     static constexpr int D_STAGE_BYTES = 2 * 128 * 4;
-    static constexpr int A_BUFS = 4;
+    static constexpr int A_BUFS = Q6X ? 2 : 4;
+    static constexpr int A_COLS = Q6X ? 128 : 64;  // TMEM columns of one A buffer
     static constexpr int E_TILE_BYTES = 128 * 32;
     static constexpr int X_RING_BYTES = X_STAGES * X_STAGE_BYTES;
     static constexpr int W_RING_BYTES = W_STAGES * W_STAGE_BYTES;
-    static constexpr int E_RING_BYTES = TNX == 128 ? A_BUFS * E_TILE_BYTES : 0;
+    static constexpr int E_RING_BYTES = (TNX == 128 && !Q6X) ? A_BUFS * E_TILE_BYTES : 0;
     static constexpr int D_RING_BYTES = TNX == 128 ? D_STAGES * D_STAGE_BYTES : 0;
     static constexpr int ACC_BUFS = 256 / TN;  // accumulators at columns 0 (and 128)
     static constexpr int A_COL0 = 256;
@@ -298,6 +308,12 @@ __device__ __forceinline__ uint32_t hadd2_bits(uint32_t a, uint32_t b) {
     asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
+// A small integer (|v| <= 2048) as both halves of an fp16 pair (exact).
+__device__ __forceinline__ uint32_t h2_dup(int v) {
+    const uint32_t u = __half_as_ushort(__int2half_rn(v));
+    return u | (u << 16);
+}
+__device__ __forceinline__ int sext_byte(uint32_t w, int k) { return (int)(int8_t)(uint8_t)(w >> (8 * k)); }
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
@@ -399,6 +415,129 @@ __device__ __forceinline__ bool mma_half_polled(uint32_t d_tmem, uint32_t a_tmem
         : "r"(d_tmem), "r"(a_tmem), "l"(xdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(smem_u32(done)),
           "r"(smem_u32(nb0)), "r"(np0), "r"(smem_u32(nb1)), "r"(np1), "n"(BOX16), "n"(BOX16 + 2), "n"(BOX16 + 4),
           "n"(BOX16 + 6)
+        : "memory");
+    return ok != 0;
+}
+
+// One half super-block of the exact Q6_K form in a single instruction block:
+// for each of the eight 16-K steps, the MMAs of both A parts (TMEM columns
+// a_tmem + 8 t and a_tmem + 64 + 8 t) against the step's activations (as in
+// mma_half_polled), the commit of `done`, and the two non-blocking tests of
+// the next half's input barriers.
+template <int BOX16>
+__device__ __forceinline__ bool mma_half_q6x(uint32_t d_tmem, uint32_t a_tmem, uint64_t xdesc, uint32_t idesc,
+                                             uint32_t accumulate, uint64_t* done, uint64_t* nb0, uint32_t np0,
+                                             uint64_t* nb1, uint32_t np1) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred q0, q1, pa, pt;\n"
+        ".reg .b64 bd;\n"
+        ".reg .b32 at;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q0, [%8], %9;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q1, [%10], %11;\n"
+        "setp.ne.b32 pa, %5, 0;\n"
+        "setp.eq.b32 pt, %6, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, {%6, %6, %6, %6}, pa;\n"
+        "add.u32 at, %2, 64;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], %3, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 8;\n"
+        "add.u64 bd, %3, 2;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 72;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 16;\n"
+        "add.u64 bd, %3, 4;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 80;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 24;\n"
+        "add.u64 bd, %3, 6;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 88;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 32;\n"
+        "add.u64 bd, %3, %12;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 96;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 40;\n"
+        "add.u64 bd, %3, %13;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 104;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 48;\n"
+        "add.u64 bd, %3, %14;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 112;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 56;\n"
+        "add.u64 bd, %3, %15;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 120;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n"
+        "and.pred q0, q0, q1;\n"
+        "selp.u32 %0, 1, 0, q0;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(d_tmem), "r"(a_tmem), "l"(xdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(smem_u32(done)),
+          "r"(smem_u32(nb0)), "r"(np0), "r"(smem_u32(nb1)), "r"(np1), "n"(BOX16), "n"(BOX16 + 2), "n"(BOX16 + 4),
+          "n"(BOX16 + 6)
+        : "memory");
+    return ok != 0;
+}
+
+// One half super-block of the exact Q4_K / Q5_K form in a single instruction
+// block: the eight 16-K MMAs (as in mma_half_polled), the min-term MMA (A
+// from the shared-memory tile at adesc_e, B = the block sums at bdesc_e), the
+// commit of `done`, and the two non-blocking tests of the next half's input
+// barriers.
+template <int BOX16>
+__device__ __forceinline__ bool mma_half_exact(uint32_t d_tmem, uint32_t a_tmem, uint64_t xdesc, uint32_t idesc,
+                                               uint32_t accumulate, uint64_t adesc_e, uint64_t bdesc_e, uint64_t* done,
+                                               uint64_t* nb0, uint32_t np0, uint64_t* nb1, uint32_t np1) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred q0, q1, pa, pt;\n"
+        ".reg .b64 bd;\n"
+        ".reg .b32 at;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q0, [%8], %9;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 q1, [%10], %11;\n"
+        "setp.ne.b32 pa, %5, 0;\n"
+        "setp.eq.b32 pt, %6, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, {%6, %6, %6, %6}, pa;\n"
+        "add.u32 at, %2, 8;\n"
+        "add.u64 bd, %3, 2;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 16;\n"
+        "add.u64 bd, %3, 4;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 24;\n"
+        "add.u64 bd, %3, 6;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 32;\n"
+        "add.u64 bd, %3, %12;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 40;\n"
+        "add.u64 bd, %3, %13;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 48;\n"
+        "add.u64 bd, %3, %14;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "add.u32 at, %2, 56;\n"
+        "add.u64 bd, %3, %15;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], [at], bd, %4, {%6, %6, %6, %6}, pt;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %16, %17, %4, {%6, %6, %6, %6}, pt;\n"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n"
+        "and.pred q0, q0, q1;\n"
+        "selp.u32 %0, 1, 0, q0;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(d_tmem), "r"(a_tmem), "l"(xdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(smem_u32(done)),
+          "r"(smem_u32(nb0)), "r"(np0), "r"(smem_u32(nb1)), "r"(np1), "n"(BOX16), "n"(BOX16 + 2), "n"(BOX16 + 4),
+          "n"(BOX16 + 6), "l"(adesc_e), "l"(bdesc_e)
         : "memory");
     return ok != 0;
 }
@@ -522,11 +661,14 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
     if (!(vmax < FAST_RANGE_LIMIT)) atomicOr(unsafe, 1u);
 }
 
-// Q6_K metadata (fast mode): fp16 d * sc_s of the 16-value groups s = 0..7
-// (chunk 0) and 8..15 (chunk 1), one 16-byte slot per row as above; the
-// producers form (q - 32) * (d sc_s) with one fp16 rounding.
+// Q6_K metadata: for the fast mode fp16 d * sc_s of the 16-value groups
+// s = 0..7 (chunk 0) and 8..15 (chunk 1), one 16-byte slot per row as above
+// (the producers form (q - 32) * (d sc_s) with one fp16 rounding); for the
+// exact mode the drain scale d of each row and super-block (the producers
+// read the int8 scales from the tile itself).
 __global__ void __launch_bounds__(256) q6k_meta_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ meta,
-                                                      int n_pad, int nb, unsigned* __restrict__ unsafe) {
+                                                      float* __restrict__ s_out, int n_pad, int nb,
+                                                      unsigned* __restrict__ unsafe) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)n_pad * nb) return;
     const int row = (int)(idx / nb), b = (int)(idx % nb);
@@ -534,6 +676,7 @@ __global__ void __launch_bounds__(256) q6k_meta_kernel(const uint8_t* __restrict
     const size_t tile = (size_t)g * nb + b;
     const uint8_t* t = tiles + tile * tcg::WFmt<TYPE_Q6_K>::TILE_BYTES;
     const float d = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(t + Fmt<TYPE_Q6_K>::D_OFFSET + r * 2));
+    s_out[tile * 32 + r] = d;
     const uint4 sv = *reinterpret_cast<const uint4*>(t + 12 * 512 + r * 16);
     const uint32_t sc4[4] = {sv.x, sv.y, sv.z, sv.w};
     uint32_t ds[8];
@@ -569,6 +712,8 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     constexpr int X_RING_BYTES = GG::X_RING_BYTES, W_RING_BYTES = GG::W_RING_BYTES;
     constexpr int E_RING_BYTES = GG::E_RING_BYTES, D_RING_BYTES = GG::D_RING_BYTES;
     constexpr int ACC_BUFS = GG::ACC_BUFS, A_COL0 = GG::A_COL0, TMEM_COLS = GG::TMEM_COLS, PASSES = GG::PASSES;
+    constexpr int A_COLS = GG::A_COLS;
+    constexpr bool Q6X = GG::Q6X, MIN_TERM = GG::MIN_TERM;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* xring = smem;
@@ -615,7 +760,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             mbar_init(e_full + i, 1);
             // 8 producer warps (+ the MMA's commit in exact mode, whose
             // min-term MMA reads the stage's Xe tile)
-            mbar_init(w_empty + i, FAST ? 8 : 9);
+            mbar_init(w_empty + i, MIN_TERM ? 9 : 8);
         }
         for (int i = 0; i < D_STAGES; i++) {
             mbar_init(d_full + i, 1);
@@ -644,7 +789,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 
     const int wg = warp >> 2;
     if (wg == 0) {
-        setmaxnreg_dec<RegSplit<FAST>::CTRL>();
+        setmaxnreg_dec<RegSplit<FAST, TYPE>::CTRL>();
         if ((warp == WARP_TMA || warp == WARP_TMA2) && lane == 0) {
             // ---------------- activation halves ----------------
             // This warp loads half h of every unit: fills f = 2 i + h.
@@ -658,8 +803,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 const int xs = f % X_STAGES;
                 if (f >= X_STAGES) {  // the slot's previous fill g = f - X_STAGES was consumed
                     const int g = f - X_STAGES;
-                    const int gab = 2 * ((g >> 1) & 1) + (g & 1);
-                    if (!wait_bar(a_empty + gab, (uint32_t)(g >> 2) & 1u, a.err, abort_flag)) break;
+                    if (!wait_bar(a_empty + g % A_BUFS, (uint32_t)(g / A_BUFS) & 1u, a.err, abort_flag)) break;
                 }
                 uint64_t* full = x_full + h * X_STAGES + xs;
                 mbar_arrive_expect_tx(full, X_STAGE_BYTES);
@@ -703,8 +847,10 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                     griddep_wait();  // Xe and d8 come from the preparation kernel
                     dep_done = true;
                 }
-                mbar_arrive_expect_tx(e_full + ws, EXT_BOX_BYTES);
-                tma_load_2d(dst + W_EXT_OFF, &tm_e, b * 16, tt * TN, e_full + ws);
+                if constexpr (MIN_TERM) {
+                    mbar_arrive_expect_tx(e_full + ws, EXT_BOX_BYTES);
+                    tma_load_2d(dst + W_EXT_OFF, &tm_e, b * 16, tt * TN, e_full + ws);
+                }
                 const int ds = i % D_STAGES;
                 if (!wait_bar(d_empty + ds, ((uint32_t)(i / D_STAGES) & 1u) ^ 1u, a.err, abort_flag)) break;
                 uint8_t* dd = dring + ds * D_STAGE_BYTES;
@@ -716,7 +862,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             for (int i = (issued_w > W_STAGES ? issued_w - W_STAGES : 0); i < issued_w; i++) {
                 wait_inflight(w_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
-                if (!FAST) wait_inflight(e_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
+                if (MIN_TERM) wait_inflight(e_full + (i % W_STAGES), (uint32_t)(i / W_STAGES) & 1u, a.err);
             }
             for (int i = (issued_d > D_STAGES ? issued_d - D_STAGES : 0); i < issued_d; i++)
                 wait_inflight(d_full + (i % D_STAGES), (uint32_t)(i / D_STAGES) & 1u, a.err);
@@ -730,8 +876,8 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             // (phase f / X_PHASE_FILLS) and A buffer 2 (i & 1) + h (phase i / 2).
             auto x_bar = [&](int f) { return x_full + (f & 1) * X_STAGES + f % X_STAGES; };
             auto x_par = [&](int f) { return (uint32_t)(f / X_PHASE_FILLS) & 1u; };
-            auto a_bar = [&](int f) { return a_full + 2 * ((f >> 1) & 1) + (f & 1); };
-            auto a_par = [&](int f) { return (uint32_t)(f >> 2) & 1u; };
+            auto a_bar = [&](int f) { return a_full + f % A_BUFS; };
+            auto a_par = [&](int f) { return (uint32_t)(f / A_BUFS) & 1u; };
             UnitPos p;
             p.init(u0, nb, a.tiles_t);
             int seg = 0;
@@ -748,7 +894,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 if ((!FAST || seg_start) &&
                     !wait_bar(acc_empty + accb, ((uint32_t)(acc_i / ACC_BUFS) & 1u) ^ 1u, a.err, abort_flag))
                     break;
-                if (!FAST && !wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
+                if (MIN_TERM && !wait_bar(e_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag)) break;
                 const uint32_t d_tmem = tmem + (uint32_t)(accb * TN);
                 bool ok = true;
                 for (int h = 0; h < 2; h++) {
@@ -761,11 +907,11 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                     }
                     tc_fence_after();
                     const int xs = f % X_STAGES;
-                    const int ab = 2 * (i & 1) + h;
+                    const int ab = f % A_BUFS;
                     // One descriptor per half; each 16-value K step is a
                     // constant offset of its start address (16-byte units).
                     const uint64_t xdesc = tc_smem_desc(smem_u32(xring + xs * X_STAGE_BYTES), 1024, 2);
-                    const uint32_t a_tmem = tmem + (uint32_t)(A_COL0 + 64 * ab);
+                    const uint32_t a_tmem = tmem + (uint32_t)(A_COL0 + A_COLS * ab);
                     const bool fresh = FAST ? (seg_start && h == 0) : (h == 0);
                     if constexpr (FAST) {
                         // The last fill polls its own (landed) barriers: the
@@ -777,25 +923,31 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                                 f + 1 < n_fills;
                         continue;
                     }
-                    tc_mma_f16_ts(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u);
-#pragma unroll
-                    for (int t = 1; t < 4; t++)  // 16-value K steps of the half
-                        tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, xdesc + (uint64_t)((t * 32) >> 4), idesc, 1u);
-                    ready = f + 1 < n_fills && test2(x_bar(f + 1), x_par(f + 1), a_bar(f + 1), a_par(f + 1));
-#pragma unroll
-                    for (int t = 4; t < 8; t++)
-                        tc_mma_f16_ts(d_tmem, a_tmem + 8 * t, xdesc + (uint64_t)((X_BOX_BYTES + (t - 4) * 32) >> 4),
-                                      idesc, 1u);
-                    if constexpr (!FAST) {
-                        // the min term: 16 K from shared memory (A) against Xe
-                        const uint64_t bext = tc_smem_desc(smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF), 256, 6);
-                        tc_mma_f16_ss(d_tmem, tc_smem_desc(smem_u32(ering + ab * E_TILE_BYTES), 256, 6), bext, idesc,
-                                      1u);
+                    if constexpr (Q6X) {
+                        // Two exact parts of the A operand per K step, one B;
+                        // the commit frees the A buffer and the activation stage.
+                        const int fn = f + 1 < n_fills ? f + 1 : f;
+                        ready = mma_half_q6x<X_BOX_BYTES / 16>(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u,
+                                                               a_empty + ab, x_bar(fn), x_par(fn), a_bar(fn),
+                                                               a_par(fn)) &&
+                                f + 1 < n_fills;
+                        continue;
                     }
-                    tc_commit(a_empty + ab);  // frees the A buffer and the activation stage
+                    if constexpr (MIN_TERM) {
+                        // The eight K steps, then the min term: 16 K from shared
+                        // memory (A) against Xe; the commit frees the A buffer
+                        // and the activation stage.
+                        const uint64_t bext = tc_smem_desc(smem_u32(wring + ws * W_STAGE_BYTES + W_EXT_OFF), 256, 6);
+                        const uint64_t aext = tc_smem_desc(smem_u32(ering + ab * E_TILE_BYTES), 256, 6);
+                        const int fn = f + 1 < n_fills ? f + 1 : f;
+                        ready = mma_half_exact<X_BOX_BYTES / 16>(d_tmem, a_tmem, xdesc, idesc, fresh ? 0u : 1u, aext,
+                                                                 bext, a_empty + ab, x_bar(fn), x_par(fn), a_bar(fn),
+                                                                 a_par(fn)) &&
+                                f + 1 < n_fills;
+                    }
                 }
                 if (!ok) break;
-                if (!FAST) tc_commit(w_empty + ws);
+                if (MIN_TERM) tc_commit(w_empty + ws);
                 if (!FAST || seg_end) tc_commit(acc_full + accb);
                 if (seg_end) seg++;
             }
@@ -804,13 +956,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             wait_inflight(mma_done, 0, a.err);
         }
     } else if (warp < WARP_DRAIN0) {
-        setmaxnreg_dec<RegSplit<FAST>::PROD>();
+        setmaxnreg_dec<RegSplit<FAST, TYPE>::PROD>();
         // ---------------- weight producers ----------------
         // Group h (4 warps, one per TMEM lane quadrant q) builds the A
         // operand of half h of every super-block: the 64 value columns of
-        // rows 32q..32q+31 in TMEM buffer 2 (i & 1) + h, and the min-term tile
-        // (high part for h = 0, low part for h = 1) in shared memory.  Each
-        // group owns its two buffers, so each barrier has one waiting group.
+        // rows 32q..32q+31 (Q6_K exact: two parts of 64) in TMEM buffer
+        // (2 i + h) % A_BUFS, and the min-term tile (high part for h = 0, low
+        // part for h = 1) in shared memory.  Each group owns its buffers, so
+        // each barrier has one waiting group.
         const int h = (warp - WARP_PROD0) >> 2;
         const int q = warp & 3;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
@@ -819,7 +972,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         p.init(u0, nb, a.tiles_t);
         for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
             const bool valid = p.tw * 4 + q < n_groups;
-            const int ws = i % W_STAGES, ab = 2 * (i & 1) + h;
+            const int ws = i % W_STAGES, fa = 2 * i + h, ab = fa % A_BUFS;
             if (!warp_wait_bar(w_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag, lane)) break;
             const uint8_t* stage = wring + ws * W_STAGE_BYTES;
             const uint8_t* tile = stage + W_TILE_OFF + q * W_TILE + lane * 16;
@@ -828,9 +981,11 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             uint4 x0 = sa, x1 = sa;  // Q5_K / Q6_K high bits
             if (valid) {
                 if constexpr (TYPE == TYPE_Q6_K) {
-                    // d sc_s of the half's groups 8h..8h+7; ql bytes 64h..64h+63
-                    // (chunks 4h..4h+3), qh bytes 32h..32h+31 (chunks 8+2h, 9+2h)
-                    sa = *reinterpret_cast<const uint4*>(mt + h * 512);
+                    // fast: d sc_s of the half's groups 8h..8h+7 (metadata);
+                    // exact: the 16 int8 scales (tile chunk 12).  ql bytes
+                    // 64h..64h+63 (chunks 4h..4h+3), qh bytes 32h..32h+31
+                    // (chunks 8+2h, 9+2h)
+                    sa = *reinterpret_cast<const uint4*>(Q6X ? tile + 12 * 512 : mt + h * 512);
                     w0 = *reinterpret_cast<const uint4*>(tile + (4 * h) * 512);
                     w1 = *reinterpret_cast<const uint4*>(tile + (4 * h + 1) * 512);
                     w2 = *reinterpret_cast<const uint4*>(tile + (4 * h + 2) * 512);
@@ -856,9 +1011,9 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(w_empty + ws);  // this warp is done with the stage
-            if (!warp_wait_bar(a_empty + ab, ((uint32_t)(i >> 1) & 1u) ^ 1u, a.err, abort_flag, lane)) break;
+            if (!warp_wait_bar(a_empty + ab, ((uint32_t)(fa / A_BUFS) & 1u) ^ 1u, a.err, abort_flag, lane)) break;
             tc_fence_after();
-            if constexpr (!FAST) {
+            if constexpr (MIN_TERM) {
                 // Min-term tile: row r holds 16 fp16 (both halves of pair j are
                 // the value of sub-block j), 32-byte swizzle: 16-byte chunk c of
                 // row r at (r / 8) * 256 + (r % 8) * 32 + ((c ^ ((r >> 2) & 1)) * 16).
@@ -871,7 +1026,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                 *reinterpret_cast<uint4*>(et + (sw << 4)) = c0;
                 *reinterpret_cast<uint4*>(et + ((sw ^ 1) << 4)) = c1;
             }
-            const uint32_t a_col = tmem + lane_base + (uint32_t)(A_COL0 + 64 * ab);
+            const uint32_t a_col = tmem + lane_base + (uint32_t)(A_COL0 + A_COLS * ab);
 #pragma unroll
             for (int cc = 0; cc < 2; cc++) {
                 // fp16 scales of sub-blocks 2c (low nibbles) and 2c + 1 (high
@@ -891,6 +1046,10 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                     const uint32_t B[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
                     const uint32_t H[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                     const uint32_t S[4] = {sa.x, sa.y, sa.z, sa.w};
+                    // Exact mode: part 0 (sl (q - 32)) is stored here, part 1
+                    // (16 sh (q - 32)) by the common store below.
+#pragma unroll 1
+                    for (int part = Q6X ? 0 : 1; part < 2; part++) {
 #pragma unroll
                     for (int w = 0; w < 8; w++) {
                         const uint32_t qa = cc ? (((A[w] >> 4) & 0x0F0F0F0Fu) | (H[w] & 0x30303030u))
@@ -898,8 +1057,20 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                         const uint32_t qb = cc ? (((B[w] >> 4) & 0x0F0F0F0Fu) | ((H[w] >> 2) & 0x30303030u))
                                                : ((B[w] & 0x0F0F0F0Fu) | ((H[w] << 2) & 0x30303030u));
                         const int ga = 4 * cc + (w >> 2), gb = ga + 2;  // 16-value group within the half
-                        const uint32_t da = __byte_perm(S[ga >> 1], 0u, (ga & 1) ? 0x3232 : 0x1010);
-                        const uint32_t db = __byte_perm(S[gb >> 1], 0u, (gb & 1) ? 0x3232 : 0x1010);
+                        uint32_t da, db;
+                        if constexpr (Q6X) {
+                            // sc = 16 sh + sl, sl in [0, 15]: the exact fp16
+                            // factors sl (part 0) and 16 sh = sc - sl (part 1);
+                            // the half's scales are bytes 8h..8h+7 (words 2h, 2h+1)
+                            const uint32_t sw0 = h ? S[2] : S[0], sw1 = h ? S[3] : S[1];
+                            const int sca = sext_byte(ga < 4 ? sw0 : sw1, ga & 3);
+                            const int scb = sext_byte(gb < 4 ? sw0 : sw1, gb & 3);
+                            da = h2_dup(part == 0 ? (sca & 15) : sca - (sca & 15));
+                            db = h2_dup(part == 0 ? (scb & 15) : scb - (scb & 15));
+                        } else {
+                            da = __byte_perm(S[ga >> 1], 0u, (ga & 1) ? 0x3232 : 0x1010);
+                            db = __byte_perm(S[gb >> 1], 0u, (gb & 1) ? 0x3232 : 0x1010);
+                        }
                         const uint32_t a02 = hadd2_bits((qa & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
                         const uint32_t a13 = hadd2_bits(((qa >> 8) & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
                         const uint32_t b02 = hadd2_bits((qb & 0x003F003Fu) | 0x64006400u, 0xE420E420u);
@@ -908,6 +1079,8 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                         v[2 * w + 1] = hmul2_bits(a13, da);
                         v[16 + 2 * w] = hmul2_bits(b02, db);
                         v[16 + 2 * w + 1] = hmul2_bits(b13, db);
+                    }
+                    if (Q6X && part == 0) tmem_st32(a_col + 32 * cc, v);
                     }
                 } else if constexpr (TYPE == TYPE_Q5_K) {
                     // q = nibble + 16 * (bit 2c, or 2c + 1 for the high nibble, of
@@ -989,16 +1162,16 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                         v[16 + 2 * w + 1] = hfma2_bits(h13, s_h16, n_hi);
                     }
                 }
-                tmem_st32(a_col + 32 * cc, v);
+                tmem_st32(a_col + (Q6X ? 64 : 0) + 32 * cc, v);
             }
             tmem_st_wait();
-            if (!FAST) fence_proxy_async_smem();  // the min-term tile is read by the tensor core
+            if (MIN_TERM) fence_proxy_async_smem();  // the min-term tile is read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(a_full + ab);
         }
     } else {
-        setmaxnreg_inc<RegSplit<FAST>::DRAIN>();
+        setmaxnreg_inc<RegSplit<FAST, TYPE>::DRAIN>();
         // ---------------- drains ----------------
         const int dw = warp - WARP_DRAIN0;
         const int q = warp & 3;    // lane quadrant = 32 weight rows of the tile
@@ -1199,7 +1372,8 @@ size_t gemm_meta_bytes(int type, int nb, int n_pad) {
     return (size_t)(n_pad / 32) * nb * per_tile;
 }
 size_t gemm_scale_bytes(int type, int nb, int n_pad) {
-    return type == TYPE_Q6_K ? 0 : (size_t)n_pad * nb * sizeof(float);
+    (void)type;
+    return (size_t)n_pad * nb * sizeof(float);
 }
 
 cudaError_t launch_gemm_meta(int type, const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad,
@@ -1216,14 +1390,15 @@ cudaError_t launch_gemm_meta(int type, const uint8_t* tiles, uint8_t* meta, floa
         q4k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, tcg::WFmt<TYPE_Q5_K>::TILE_BYTES, 31,
                                              unsafe);
         break;
-    case TYPE_Q6_K: q6k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, n_pad, nb, unsafe); break;
+    case TYPE_Q6_K: q6k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, unsafe); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
 bool tc_gemm_supports(int type, bool fast) {
-    return type == TYPE_Q4_K || type == TYPE_Q5_K || (type == TYPE_Q6_K && fast);
+    (void)fast;
+    return type == TYPE_Q4_K || type == TYPE_Q5_K || type == TYPE_Q6_K;
 }
 
 int tc_gemm_tile_tokens(bool fast, int tokens) { return (fast && tokens >= 512) ? 256 : 128; }
@@ -1293,6 +1468,7 @@ cudaError_t configure_tc_gemm() {
         {(const void*)gemm_q4k_tc_kernel<false, 128, TYPE_Q5_K>, Geo<false, 128, TYPE_Q5_K>::SMEM_BYTES},
         {(const void*)gemm_q4k_tc_kernel<true, 128, TYPE_Q5_K>, Geo<true, 128, TYPE_Q5_K>::SMEM_BYTES},
         {(const void*)gemm_q4k_tc_kernel<true, 256, TYPE_Q5_K>, Geo<true, 256, TYPE_Q5_K>::SMEM_BYTES},
+        {(const void*)gemm_q4k_tc_kernel<false, 128, TYPE_Q6_K>, Geo<false, 128, TYPE_Q6_K>::SMEM_BYTES},
         {(const void*)gemm_q4k_tc_kernel<true, 128, TYPE_Q6_K>, Geo<true, 128, TYPE_Q6_K>::SMEM_BYTES},
         {(const void*)gemm_q4k_tc_kernel<true, 256, TYPE_Q6_K>, Geo<true, 256, TYPE_Q6_K>::SMEM_BYTES}};
     for (const auto& k : kernels) {
@@ -1331,12 +1507,8 @@ static cudaError_t launch_typed(cudaLaunchConfig_t& cfg, const TcGemmArgs& args,
         cfg.dynamicSmemBytes = Geo<true, 128, TYPE>::SMEM_BYTES;
         return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<true, 128, TYPE>, tq, te, args);
     }
-    if constexpr (TYPE == TYPE_Q6_K) {
-        return cudaErrorInvalidValue;
-    } else {
-        cfg.dynamicSmemBytes = Geo<false, 128, TYPE>::SMEM_BYTES;
-        return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false, 128, TYPE>, tq, te, args);
-    }
+    cfg.dynamicSmemBytes = Geo<false, 128, TYPE>::SMEM_BYTES;
+    return cudaLaunchKernelEx(&cfg, gemm_q4k_tc_kernel<false, 128, TYPE>, tq, te, args);
 }
 
 static cudaError_t launch_tc_instance(cudaLaunchConfig_t& cfg, const TcGemmArgs& args, const CUtensorMap& tq,

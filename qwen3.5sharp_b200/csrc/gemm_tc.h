@@ -20,7 +20,7 @@ struct TcGemmArgs {
     int n_out, n_pad, tokens, m_pad, nb, tiles_t, grid;
     long long units;       // tiles * nb
     int tn;                // tokens per tile: 128, or 256 (fast mode, 256+ tokens)
-    int type;              // TYPE_Q4_K, TYPE_Q5_K, or TYPE_Q6_K (fast mode only)
+    int type;              // TYPE_Q4_K, TYPE_Q5_K or TYPE_Q6_K
 };
 
 struct TcGemmPlan {
@@ -35,15 +35,15 @@ struct TcGemmPlan {
 int tc_gemm_tile_tokens(bool fast, int tokens);
 TcGemmPlan plan_tc_gemm(int nb, int n_pad, int tokens, int num_sms, int tn);
 // GEMM metadata of an uploaded weight: sizes and the kernels that fill it
-// (Q6_K has no drain scales: 0 bytes).  *unsafe (zeroed by the caller) is set
+// (the exact mode's drain scales).  *unsafe (zeroed by the caller) is set
 // when a block's fast-mode fp16 weight values could overflow.
 size_t gemm_meta_bytes(int type, int nb, int n_pad);
 size_t gemm_scale_bytes(int type, int nb, int n_pad);
 cudaError_t launch_gemm_meta(int type, const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad,
                              unsigned* unsafe, cudaStream_t s);
-// Whether the tensor-core GEMM takes this weight type in this mode: Q4_K and
-// Q5_K in both modes, Q6_K in the fast mode (its products sc * (q - 32) have
-// no exact fp16 form).
+// Whether the tensor-core GEMM takes this weight type in this mode: Q4_K,
+// Q5_K and Q6_K in both modes (Q6_K's exact products sc * (q - 32) as two
+// exact fp16 parts, two MMAs per K step).
 bool tc_gemm_supports(int type, bool fast);
 cudaError_t configure_tc_gemm();
 // Q8_K quantization of x [tokens][k] into the GEMM's operands.  Exact mode:

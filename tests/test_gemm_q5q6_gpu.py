@@ -2,12 +2,14 @@
 oracle (Q5K.Gemm, Kernels/Q5K.cs:114-118, per-token GEMV; Q6K.Gemm,
 Kernels/Q6K.cs:317-353) through the C ABI.
 
-Q5_K runs in both GEMM modes.  Its exact mode uses Q4_K's scheme: the weight
-values alpha * sc_j * q (q <= 31, at most 1953 * alpha) are exact in fp16, so
-the observed error is fp32 rounding (DESIGN_BOUND).  Q6_K runs in the fast
-mode only: its products sc * (q - 32) need up to 12 significant bits and
-have no exact fp16 form, so in the exact mode Q6_K prefill stays on the GEMV,
-bit for bit.  Bar: max|y - r| / max|r| <= 1e-3.
+Both types run in both GEMM modes.  Q5_K's exact mode uses Q4_K's scheme:
+the weight values alpha * sc_j * q (q <= 31, at most 1953 * alpha) are exact
+in fp16, so the observed error is fp32 rounding (DESIGN_BOUND).  Q6_K's
+products sc * (q - 32) need up to 12 significant bits, so its exact mode
+splits every int8 scale as sc = 16 sh + sl (sl in [0, 15]) and multiplies
+the two exact fp16 parts sl (q - 32) and 16 sh (q - 32) against the same
+activations (two MMAs per K step); its error is fp32 rounding as well.
+Bar: max|y - r| / max|r| <= 1e-3, and DESIGN_BOUND for the exact mode.
 """
 
 import os
@@ -144,7 +146,7 @@ def test_q5k_edge_blocks(ctx, fast_ctx, oracle_mod, fast):
 def test_fast_mode_keeps_out_of_range_weights_exact(ctx, fast_ctx, gemv_ctx, oracle_mod):
     """Weights whose fp16 dequantized values could overflow (d up to the fp16
     maximum) are flagged at upload: in the fast mode their prefill keeps the
-    exact GEMM (Q5_K) or the GEMV (Q6_K), bit for bit."""
+    exact GEMM, bit for bit."""
     k, n, m = 2560, 512, 64
     w5 = synth.kquant_blocks(Q5_K, n, k, seed=13)  # uniform fp16 d and dmin
     x = synth.activations(m, k, seed=14)
@@ -157,7 +159,7 @@ def test_fast_mode_keeps_out_of_range_weights_exact(ctx, fast_ctx, gemv_ctx, ora
     w6[0, 0, 208:210] = np.frombuffer(np.float16(1000.0).tobytes(), np.uint8)  # one block with d = 1000
     w6 = w6.reshape(n, -1)
     y6 = run(fast_ctx, Q6_K, w6, x, k, n)
-    assert (y6 == run(gemv_ctx, Q6_K, w6, x, k, n)).all()
+    assert (y6 == run(ctx, Q6_K, w6, x, k, n)).all()
 
 
 def test_q6k_fast_mode_ran_on_the_tensor_cores(fast_ctx, gemv_ctx):
@@ -170,14 +172,60 @@ def test_q6k_fast_mode_ran_on_the_tensor_cores(fast_ctx, gemv_ctx):
     assert not (y == y_gemv).all()  # fp16-rounded operands: not the GEMV's bits
 
 
-def test_q6k_exact_mode_stays_on_the_gemv(ctx, gemv_ctx):
-    k, n, m = 2560, 1000, 64
-    w = synth.kquant_blocks(Q6_K, n, k, seed=5)
-    x = synth.activations(m, k, seed=6)
-    assert (run(ctx, Q6_K, w, x, k, n) == run(gemv_ctx, Q6_K, w, x, k, n)).all()
+@pytest.mark.parametrize("k,n,m", SHAPES)
+def test_q6k_exact(ctx, oracle_mod, gemv_ctx, k, n, m):
+    w = synth.kquant_blocks(Q6_K, n, k, seed=n + m + 1)
+    x = synth.activations(m, k, seed=k + m + 1)
+    y = run(ctx, Q6_K, w, x, k, n)
+    ref = oracle_mod.Weight(Q6_K, w, k, n).matmul(x, threads=THREADS)
+    err = rel_err(y, ref)
+    print(f"Q6_K exact m={m} k={k} n={n}: {err:.3e}")
+    assert np.isfinite(y).all()
+    assert err <= TOL and err <= DESIGN_BOUND
+    if m == 64:
+        # the tensor-core path ran: a different fp32 summation order than the GEMV's
+        assert not (y == run(gemv_ctx, Q6_K, w, x, k, n)).all()
 
 
-@pytest.mark.parametrize("qt,fast", [(Q5_K, False), (Q5_K, True), (Q6_K, True)])
+def _q6k_edge_blocks(n, k, seed):
+    """Q6_K blocks at the ends of every field: d = 0, negative and subnormal
+    d, the full int8 scale range (the reference's format allows -128..127,
+    beyond the synthetic [-32, 31]), every quant at 0 or 63."""
+    w = synth.kquant_blocks(Q6_K, n, k, seed=seed).reshape(n, k // 256, 210)
+    h = lambda v: np.frombuffer(np.float16(v).tobytes(), np.uint8)
+    rng = np.random.default_rng(seed)
+    for r in range(n):
+        for b in range(k // 256):
+            kind = (r * (k // 256) + b) % 6
+            if kind == 0:
+                w[r, b, 208:210] = h(0.0)
+            elif kind == 1:
+                w[r, b, 208:210] = h(-float(rng.random()) * 0.01)
+            elif kind == 2:
+                w[r, b, 208:210] = h(3e-7)                   # subnormal d
+            elif kind == 3:
+                w[r, b, 192:208] = rng.choice(np.array([-128, 127, -1, 0, 15, -16], np.int8), 16).view(np.uint8)
+            elif kind == 4:
+                w[r, b, 0:192] = 0xFF                         # q = 63 everywhere
+                w[r, b, 192:208] = np.int8(-128).view(np.uint8)
+            elif kind == 5:
+                w[r, b, 0:192] = 0x00                         # q = 0 everywhere
+                w[r, b, 192:208] = np.int8(127).view(np.uint8)
+    return w.reshape(n, -1)
+
+
+def test_q6k_exact_edge_blocks(ctx, oracle_mod):
+    k, n, m = 1792, 300, 96
+    w = _q6k_edge_blocks(n, k, seed=17)
+    x = synth.activations(m, k, seed=18, scale=3.0)
+    x[7] = 0.0
+    y = run(ctx, Q6_K, w, x, k, n)
+    ref = oracle_mod.Weight(Q6_K, w, k, n).matmul(x, threads=THREADS)
+    assert np.isfinite(y).all()
+    assert rel_err(y, ref) <= DESIGN_BOUND
+
+
+@pytest.mark.parametrize("qt,fast", [(Q5_K, False), (Q5_K, True), (Q6_K, False), (Q6_K, True)])
 def test_deterministic(ctx, fast_ctx, qt, fast):
     c = fast_ctx if fast else ctx
     k, n, m = 2560, 2048, 600
