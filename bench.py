@@ -422,44 +422,50 @@ class Bench:
         SW = self.sharded_weight(qt, w, K, N, r0, r1) if world > 1 else None
         ctx, sh = self.ctx, self.sh
 
-        def step():
+        def step(stream_handle=None):
             # One pass of the hot path: N = 1, q35k_matmul_dev (Q8_K quantization
             # of x fused into the GEMV at M = 1); N > 1, q35k_shard_matmul_dev (the
             # rank's GEMV, then the gather of the logits).
+            st = sh if stream_handle is None else stream_handle
             if world == 1:
-                ctx.matmul_dev(W, dx, dy_full, M, sh)
+                ctx.matmul_dev(W, dx, dy_full, M, st)
             else:
-                self.group.matmul_dev(SW, [dx], [dy_full], M, self.gather_mode, streams=[sh])
+                self.group.matmul_dev(SW, [dx], [dy_full], M, self.gather_mode, streams=[st])
 
         for _ in range(max(3, args.warmup)):
             step()
         torch.cuda.synchronize()
         self.barrier()
+        # The K timed steps are issued from a CUDA graph captured once (a
+        # decode loop is launch-bound at 8 GPUs, where a step's device time
+        # falls below the host's time to issue it; every call's kernel
+        # arguments are the same from call to call, so the call can be
+        # captured).  The same steps issued as plain launches are reported
+        # beside it.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cs = torch.cuda.current_stream().cuda_stream
+            for _ in range(args.steps):
+                step(cs)
+        graph.replay()
+        torch.cuda.synchronize()
+        self.barrier()
         clocks = ClockSampler(self.local)
         clocks.start()
-        ms_step = self.back_to_back_ms(step, args.steps)
+        ms_step = self.back_to_back_ms(graph.replay, 1) / args.steps
         clk = clocks.stop()
-        extra = {}
+        extra = {"timing": f"{args.steps} steps replayed from one CUDA graph between one pair of CUDA events, "
+                           "max over ranks"}
+        extra["ms_per_step_launches"] = self.back_to_back_ms(step, args.steps)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        extra["host_issue_ms_per_step"] = (time.perf_counter() - t0) / args.steps * 1e3
+        torch.cuda.synchronize()
+        self.barrier()
+        del graph
         if world > 1:
-            # Host time to issue one step (Python + the library call), and the
-            # same steps replayed from a CUDA graph (the call's kernel
-            # arguments do not change from call to call, so it can be captured).
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
-            for _ in range(args.steps):
-                step()
-            extra["host_issue_ms_per_step"] = (time.perf_counter() - t0) / args.steps * 1e3
-            torch.cuda.synchronize()
-            self.barrier()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                cs = torch.cuda.current_stream().cuda_stream
-                for _ in range(args.steps):
-                    self.group.matmul_dev(SW, [dx], [dy_full], M, self.gather_mode, streams=[cs])
-            graph.replay()
-            torch.cuda.synchronize()
-            extra["graph_ms_per_step"] = self.back_to_back_ms(graph.replay, 3) / args.steps
-            del graph
             # Phase breakdown of one isolated call on this rank's GPU.
             self.barrier()
             self.group.set_trace(True)
@@ -702,7 +708,22 @@ class Bench:
 
             for _ in range(3):
                 call()
-            ms = self.back_to_back_ms(call, 20 if m < 64 else 10)
+            if m <= 8:
+                # Decode calls (fused gather): replayed from a CUDA graph, as the
+                # headline steps are.
+                torch.cuda.synchronize()
+                self.barrier()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    cs = torch.cuda.current_stream().cuda_stream
+                    for _ in range(20):
+                        self.group.matmul_dev(SW, [dx], [dy], m, self.gather_mode, streams=[cs])
+                graph.replay()
+                torch.cuda.synchronize()
+                ms = self.back_to_back_ms(graph.replay, 1) / 20
+                del graph
+            else:
+                ms = self.back_to_back_ms(call, 10)
             call()
             torch.cuda.synchronize()
             y = dy.cpu().numpy()
