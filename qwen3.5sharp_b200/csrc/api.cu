@@ -64,6 +64,7 @@ int q35k_ctx::ensure_host(void** p, size_t* cap, size_t bytes) {
     if (*p) cudaFreeHost(*p);
     *p = nullptr;
     *cap = 0;
+    if (p == &h_out) h_out_dev = nullptr;
     size_t want = std::max(bytes, (size_t)4096);
     cudaError_t e = cudaMallocHost(p, want);
     if (e != cudaSuccess) {
@@ -72,6 +73,10 @@ int q35k_ctx::ensure_host(void** p, size_t* cap, size_t bytes) {
         return fail(Q35K_ENOMEM, "cudaMallocHost(%zu) failed: %s", want, cudaGetErrorString(e));
     }
     *cap = want;
+    if (p == &h_out && (cudaHostGetDevicePointer(&h_out_dev, h_out, 0) != cudaSuccess || !h_out_dev)) {
+        cudaGetLastError();
+        h_out_dev = nullptr;
+    }
     return Q35K_OK;
 }
 
@@ -330,6 +335,7 @@ int q35k_ctx::gemv(const q35k_weight* w, const uint8_t* d_q8, float* d_y, int to
         a.partial = d_partial;
         a.counters = d_counters;
         a.err = d_err;
+        a.h_err = call_h_err;
         a.num_sms = num_sms;
         if (peers) a.peers = *peers;  // one launch: tokens <= chunk (checked by the caller)
         cudaError_t e = launch_gemv(w->type, a, s, pdl && t0 == 0);
@@ -608,11 +614,9 @@ int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int
     if ((rc = c->ensure_host(&c->h_out, &c->h_out_cap, stage_y + 64)) != Q35K_OK) return rc;
     volatile unsigned* h_err = reinterpret_cast<volatile unsigned*>(static_cast<char*>(c->h_out) + stage_y);
     *h_err = 0;
-    void* h_out_dev = nullptr;
-    if (cudaHostGetDevicePointer(&h_out_dev, c->h_out, 0) != cudaSuccess || !h_out_dev) {
-        cudaGetLastError();
-        return c->fail(Q35K_ECUDA, "the pinned staging buffer is not mapped into the device's address space");
-    }
+    char* const h_out_dev = static_cast<char*>(c->h_out_dev);
+    if (!h_out_dev) return c->fail(Q35K_ECUDA, "the pinned staging buffer is not mapped into the device's address space");
+    unsigned* const h_err_dev = reinterpret_cast<unsigned*>(h_out_dev + stage_y);
     if (!x_alias) {
         std::memcpy(c->h_in, x, in_bytes);
         void* dp = nullptr;
@@ -635,13 +639,18 @@ int q35k_matmul(q35k_ctx* c, const q35k_weight* w, const float* x, float* y, int
     // (tensor-core GEMM, whose tiles would cross the bus piece by piece) copy
     // y back afterwards.
     float* d_out = c->d_y;
-    if (!gemm) d_out = y_alias ? y_alias : static_cast<float*>(h_out_dev);
-    if ((rc = q35k_matmul_dev(c, w, c->d_x, d_out, tokens, c->stream)) != Q35K_OK) return rc;
+    if (!gemm) d_out = y_alias ? y_alias : reinterpret_cast<float*>(h_out_dev);
+    // Decode calls: the GEMV launches set the mapped error word themselves
+    // when a wait expires; prefill calls read the device word out after the
+    // GEMM and the copy of y.
+    c->call_h_err = gemm ? nullptr : h_err_dev;
+    rc = q35k_matmul_dev(c, w, c->d_x, d_out, tokens, c->stream);
+    c->call_h_err = nullptr;
+    if (rc != Q35K_OK) return rc;
     e = gemm ? cudaMemcpyAsync(y_alias ? y : c->h_out, c->d_y, out_bytes, cudaMemcpyDeviceToHost, c->stream)
              : cudaSuccess;
-    if (e == cudaSuccess)
-        e = launch_k(q35k_err_out_kernel, 1, 1, c->stream, !gemm, (const unsigned*)c->d_err,
-                     reinterpret_cast<unsigned*>(static_cast<char*>(h_out_dev) + stage_y));
+    if (e == cudaSuccess && gemm)
+        e = launch_k(q35k_err_out_kernel, 1, 1, c->stream, false, (const unsigned*)c->d_err, h_err_dev);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return c->cuda_fail(e, "matmul");
     if (*h_err) return c->on_device_error(*h_err);

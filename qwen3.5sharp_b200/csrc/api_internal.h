@@ -66,6 +66,10 @@ struct q35k_ctx {
     size_t h_in_cap = 0;
     void* h_out = nullptr;
     size_t h_out_cap = 0;
+    void* h_out_dev = nullptr;  // h_out's device address (mapped), set when h_out is allocated
+    // While a host-pointer call runs: its mapped host error word, which the
+    // GEMV launches of the call also set (GemvArgs::h_err); nullptr otherwise.
+    unsigned* call_h_err = nullptr;
 
     ~q35k_ctx() {
         if (d_x) cudaFree(d_x);

@@ -36,8 +36,15 @@ constexpr int GEMV_FUSED_MAX_TOKENS = 2;  // token counts with a fused-quantize 
 static_assert(GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q4_K) &&
                   GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q6_K),
               "fused GEMV layouts");
-constexpr int GEMV_UNIT_BYTES = 72 * 1024;  // weight bytes per split-K work unit (target)
-constexpr int GEMV_ROW_BYTES = 96 * 1024;   // largest whole-row unit
+// Unit sizes of the launch plan (compile-time; the defaults are the measured best).
+#ifndef Q35K_GEMV_UNIT_KB
+#define Q35K_GEMV_UNIT_KB 72
+#endif
+#ifndef Q35K_GEMV_ROW_KB
+#define Q35K_GEMV_ROW_KB 96
+#endif
+constexpr int GEMV_UNIT_BYTES = Q35K_GEMV_UNIT_KB * 1024;  // weight bytes per split-K work unit (target)
+constexpr int GEMV_ROW_BYTES = Q35K_GEMV_ROW_KB * 1024;    // largest whole-row unit
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
 
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
@@ -284,6 +291,8 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
         }
     }
     if (a.peers.trace && tid == 0) atomicMax(a.peers.trace + 1, (unsigned long long)globaltimer_ns());
+    // Any warp whose wait gave up reports it to the host-pointer caller too.
+    if (!ok && lane == 0 && a.h_err) *reinterpret_cast<volatile unsigned*>(a.h_err) = DEV_ERR_TIMEOUT;
     if (!ok && tid == 0) {
         // A wait gave up: give the copies in flight a bounded chance to land
         // before the CTA's shared memory is released.

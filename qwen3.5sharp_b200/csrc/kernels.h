@@ -71,6 +71,10 @@ struct GemvArgs {
     float* partial;     // pieces of row groups cut by a CTA boundary
     int* counters;      // one arrival counter per row group, zero between calls
     unsigned* err;      // device error word
+    // Host-pointer calls: a word in mapped host memory that a CTA whose
+    // bounded wait expired also sets (plain store), so the caller learns of it
+    // after synchronizing without reading the device word back; nullptr: off.
+    unsigned* h_err;
     int num_sms;
     GemvPeers peers;    // fused all-gather (peers.n == 0: off)
     // Fused argmax (vocab head): per token the 64-bit max of argmax_key(logit,
