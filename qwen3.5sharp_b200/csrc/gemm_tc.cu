@@ -30,10 +30,7 @@
 // splits the units into equal contiguous ranges (stream-K), so every SM gets
 // the same number of MMAs.  A tile cut by a range boundary is finished by
 // whichever covering CTA arrives last (per drain warp, via a counter), which
-// adds the pieces in CTA order: results are bit-identical run to run.  Each
-// CTA computes the start of its last tile first (UnitOrder), so the pieces of
-// shared tiles are combined early and every CTA ends on whole tiles or on a
-// piece whose partner is long done.
+// adds the pieces in CTA order: results are bit-identical run to run.
 //
 // Warp roles (640 threads, one CTA per SM):
 //   warp 0      TMA: Xq, half a super-block (2 boxes of 64 K x 128 tokens,
@@ -341,6 +338,11 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, unsigne
         }
     }
 }
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // Non-blocking test of two barrier phases in one go: both tests issue back
 // to back and the thread waits once for the pair (a barrier test takes ~100
@@ -582,31 +584,6 @@ struct UnitPos {
     }
 };
 
-// Order in which a CTA processes its unit range [u0, u1): when the range
-// covers more than one tile, the units of its last tile first if that tile is
-// cut at u1 (its start, shared with the next CTA), then [u0, ...) in order.
-// Both pieces of every tile shared by two CTAs are then computed early in
-// their CTAs' timelines, so their combination overlaps the remaining work, and
-// every CTA ends on pieces whose combination it can finish at once.
-struct UnitOrder {
-    int u0, u1, n_tail;
-    __device__ __forceinline__ static UnitOrder make(int u0, int u1, int nb) {
-        UnitOrder o{u0, u1, 0};
-        if (u1 > u0 && u0 / nb != (u1 - 1) / nb && u1 % nb) o.n_tail = u1 % nb;
-        return o;
-    }
-    __device__ __forceinline__ int at(int i) const { return i < n_tail ? u1 - n_tail + i : u0 + (i - n_tail); }
-    // Whether the unit at position i + 1 continues the one at i in K.
-    __device__ __forceinline__ bool contiguous(int i) const { return i + 1 != n_tail; }
-    // Position the cursor on the unit at position i + 1.
-    __device__ __forceinline__ void advance(UnitPos& p, int i, int nb, int tiles_t) const {
-        if (contiguous(i))
-            p.next(nb, tiles_t);
-        else
-            p.init(at(i + 1), nb, tiles_t);
-    }
-};
-
 // CTA whose unit range [c*U/G, (c+1)*U/G) contains unit u.
 __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
     return (int)(((u + 1) * G + U - 1) / U) - 1;
@@ -770,7 +747,6 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
     const int u0 = (int)((long long)blockIdx.x * U / G);
     const int u1 = (int)((long long)(blockIdx.x + 1) * U / G);
     const int n_units = u1 - u0;
-    const UnitOrder ord = UnitOrder::make(u0, u1, a.nb);
     const int nb = a.nb;
     const int n_groups = a.n_pad / 32;
 
@@ -821,8 +797,8 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             const int h = warp == WARP_TMA ? 0 : 1;
             int issued = -1;
             UnitPos p;
-            p.init(ord.at(0), nb, a.tiles_t);
-            for (int i = 0; i < n_units; ord.advance(p, i, nb, a.tiles_t), i++) {
+            p.init(u0, nb, a.tiles_t);
+            for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
                 const int f = 2 * i + h;
                 const int xs = f % X_STAGES;
                 if (f >= X_STAGES) {  // the slot's previous fill g = f - X_STAGES was consumed
@@ -850,8 +826,8 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             bool dep_done = false;
             int issued_w = 0, issued_d = 0;
             UnitPos p;
-            p.init(ord.at(0), nb, a.tiles_t);
-            for (int i = 0; i < n_units; ord.advance(p, i, nb, a.tiles_t), i++) {
+            p.init(u0, nb, a.tiles_t);
+            for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
                 const int b = p.b, tw = p.tw, tt = p.tt;
                 int valid = 0;
                 for (int q = 0; q < 4; q++) valid += (tw * 4 + q < n_groups) ? 1 : 0;
@@ -903,17 +879,15 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             auto a_bar = [&](int f) { return a_full + f % A_BUFS; };
             auto a_par = [&](int f) { return (uint32_t)(f / A_BUFS) & 1u; };
             UnitPos p;
-            p.init(ord.at(0), nb, a.tiles_t);
+            p.init(u0, nb, a.tiles_t);
             int seg = 0;
             // The next half's inputs are tested (without blocking) in the middle
             // of the current half's MMAs; the thread blocks on them only when
             // they had not landed by then.
             bool ready = false;
             const int n_fills = 2 * n_units;
-            for (int i = 0; i < n_units; ord.advance(p, i, nb, a.tiles_t), i++) {
-                // A tile segment: a run of units of one tile that continue in K.
-                const bool seg_start = (i == 0 || p.b == 0 || !ord.contiguous(i - 1));
-                const bool seg_end = (p.b == nb - 1 || i == n_units - 1 || !ord.contiguous(i));
+            for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
+                const bool seg_start = (i == 0 || p.b == 0), seg_end = (p.b == nb - 1 || i == n_units - 1);
                 const int acc_i = FAST ? seg : i;  // accumulator use
                 const int accb = acc_i % ACC_BUFS;
                 const int ws = i % W_STAGES;
@@ -995,8 +969,8 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const int r = 32 * q + lane;  // row of the tile
         UnitPos p;
-        p.init(ord.at(0), nb, a.tiles_t);
-        for (int i = 0; i < n_units; ord.advance(p, i, nb, a.tiles_t), i++) {
+        p.init(u0, nb, a.tiles_t);
+        for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
             const bool valid = p.tw * 4 + q < n_groups;
             const int ws = i % W_STAGES, fa = 2 * i + h, ab = fa % A_BUFS;
             if (!warp_wait_bar(w_full + ws, (uint32_t)(i / W_STAGES) & 1u, a.err, abort_flag, lane)) break;
@@ -1208,10 +1182,10 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         for (int j = 0; j < 64; j++) out[j] = 0.f;
         int seg_b0 = 0, seg = 0;
         UnitPos p;
-        p.init(ord.at(0), nb, a.tiles_t);
-        for (int i = 0; i < n_units; ord.advance(p, i, nb, a.tiles_t), i++) {
+        p.init(u0, nb, a.tiles_t);
+        for (int i = 0; i < n_units; i++, p.next(nb, a.tiles_t)) {
             const int t = p.t, b = p.b, tw = p.tw, tt = p.tt;
-            if (i == 0 || b == 0 || !ord.contiguous(i - 1)) {
+            if (i == 0 || b == 0) {
 #pragma unroll
                 for (int j = 0; j < 64; j++) out[j] = 0.f;
                 seg_b0 = b;
@@ -1258,7 +1232,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             if (lane == 0) mbar_arrive(d_empty + ds);  // done with the unit's scales
             }
 
-            if (b != nb - 1 && i != n_units - 1 && ord.contiguous(i)) continue;  // the tile's segment goes on
+            if (b != nb - 1 && i != n_units - 1) continue;  // the tile's segment goes on
             int accb = 0;
             if constexpr (FAST) {
                 // One accumulator per tile segment: read it once, at the end.
@@ -1302,11 +1276,49 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
             const int first = cta_of_unit(tu0, U, G), last = cta_of_unit(tu0 + nb - 1, U, G);
             const int me = blockIdx.x;
             int* const ctr = a.counters + ((size_t)t * NUM_DRAIN + dw) * PASSES + pp;
-            // Publish this piece; the last of the covering CTAs to arrive adds
-            // the pieces in CTA order (deterministic whatever the timing) and
-            // stores the outputs.  The pieces of a tile shared by two CTAs are
-            // computed early in both CTAs (UnitOrder), so this overlaps their
-            // remaining work.
+            if (last == first + 1) {
+                // Two pieces.  CTA `last` computes its piece first (the start of
+                // its range): it stores the piece into y and raises the tile's
+                // flag.  CTA `first` computes its piece last (the end of its
+                // range) and adds it onto y once the flag is up.  Each output is
+                // one addition of the two pieces, whatever the timing.
+                if (me == last) {
+                    if (row < a.n_out) {
+#pragma unroll
+                        for (int j = 0; j < 64; j++)
+                            if (tok0 + j < a.tokens) a.y[(size_t)(tok0 + j) * a.ldy + row] = out[j];
+                    }
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) atomicExch(ctr, 1);
+                } else {
+                    int up = 0;
+                    if (lane == 0) {
+                        const uint64_t start = globaltimer_ns();
+                        for (uint32_t it = 0;; ++it) {
+                            if (ld_acquire_gpu(ctr) == 1) {
+                                up = 1;
+                                break;
+                            }
+                            if ((it & 63u) == 63u && globaltimer_ns() - start > WAIT_LIMIT_NS) {
+                                atomicOr(a.err, DEV_ERR_TIMEOUT);
+                                break;
+                            }
+                        }
+                    }
+                    up = __shfl_sync(0xffffffffu, up, 0);
+                    if (!up) continue;
+                    if (row < a.n_out) {
+#pragma unroll
+                        for (int j = 0; j < 64; j++)
+                            if (tok0 + j < a.tokens) atomicAdd(a.y + (size_t)(tok0 + j) * a.ldy + row, out[j]);
+                    }
+                    if (lane == 0) *ctr = 0;  // ready for the next launch
+                }
+                continue;
+            }
+            // Three or more pieces: publish this one; the last of the covering
+            // CTAs to arrive adds the pieces in CTA order.
             const int local = (th * (TN / 2) + pp * 64) * TM + q * 32 + lane;  // token-major piece of this warp
             // Slot 0 holds a CTA's first tile, slot 1 its last one.
             auto piece = [&](int cta) -> float* {
