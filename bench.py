@@ -31,7 +31,6 @@ import argparse
 import csv
 import io
 import json
-import mmap
 import os
 import statistics
 import subprocess
@@ -149,16 +148,6 @@ def rel_err(y, r) -> float:
     y = np.asarray(y, dtype=np.float64)
     r = np.asarray(r, dtype=np.float64)
     return float(np.abs(y - r).max() / max(float(np.abs(r).max()), 1e-30))
-
-
-def page_aligned(shape, dtype):
-    """A numpy array on its own anonymous pages (a persistent buffer a caller
-    registers with q35k_host_register without sharing pages with others)."""
-    import numpy as np
-
-    nbytes = int(np.prod(shape)) * np.dtype(dtype).itemsize
-    buf = mmap.mmap(-1, max(nbytes, 1))
-    return np.frombuffer(buf, dtype=dtype, count=int(np.prod(shape))).reshape(shape), buf
 
 
 def count_launches(torch, step):
@@ -557,8 +546,8 @@ class Bench:
             # The caller's input and output buffers persist across steps (the
             # reference model's NativeBuffers) and are registered once with
             # q35k_host_register, so q35k_matmul reads x and writes y in place.
-            x_host, xb = page_aligned(x.shape, np.float32)
-            y_host, yb = page_aligned((M, N), np.float32)
+            x_host = self.q35k.page_aligned_empty(x.shape)
+            y_host = self.q35k.page_aligned_empty((M, N))
             x_host[...] = x
             self.ctx.host_register(x_host)
             self.ctx.host_register(y_host)

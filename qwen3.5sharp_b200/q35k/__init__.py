@@ -37,7 +37,7 @@ __all__ = [
     "Context", "Weight", "MulMatQ4K", "Q4K", "Q5K", "Q6K", "Q8K", "default_context",
     "ArgumentException", "NotSupportedException", "InsufficientMemoryException",
     "InvalidOperationException", "TimeoutException", "InvalidDataException", "GgufIOException", "GgufFile",
-    "GgufTensorInfo", "Q4_K", "Q5_K", "Q6_K", "QK",
+    "GgufTensorInfo", "Q4_K", "Q5_K", "Q6_K", "QK", "page_aligned_empty",
 ]
 
 
@@ -111,6 +111,19 @@ def _stream(stream):
     if hasattr(stream, "cuda_stream"):
         stream = stream.cuda_stream
     return stream if stream != 0 else _CUDA_STREAM_LEGACY
+
+
+def page_aligned_empty(shape, dtype=np.float32) -> np.ndarray:
+    """An uninitialised array on pages of its own (an anonymous mapping), for
+    a persistent buffer to register with Context.host_register: registering
+    page-locks whole pages, so two buffers that share a page cannot both be
+    registered."""
+    import mmap
+
+    n = int(np.prod(shape)) if np.ndim(shape) else int(shape)
+    nbytes = max(n * np.dtype(dtype).itemsize, 1)
+    buf = mmap.mmap(-1, (nbytes + mmap.PAGESIZE - 1) // mmap.PAGESIZE * mmap.PAGESIZE)
+    return np.frombuffer(buf, dtype=dtype, count=n).reshape(shape)
 
 
 def _dev_ptr(t) -> int:

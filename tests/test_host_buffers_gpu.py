@@ -18,8 +18,9 @@ def test_registered_buffers_give_the_same_bits(ctx, qt, m):
     k, n = 2560, 3000
     w = synth.kquant_blocks(qt, n, k, seed=31 + m)
     W = ctx.upload(qt, w, k, n)
-    x_reg = np.empty((m, k), dtype=np.float32)
-    y_reg = np.full((m, n), np.nan, dtype=np.float32)
+    x_reg = q35k.page_aligned_empty((m, k))
+    y_reg = q35k.page_aligned_empty((m, n))
+    y_reg[...] = np.nan
     ctx.host_register(x_reg)
     ctx.host_register(y_reg)
     try:
@@ -37,7 +38,7 @@ def test_registered_buffers_give_the_same_bits(ctx, qt, m):
 
 
 def test_register_twice_is_an_argument_error(ctx):
-    a = np.zeros(4096, dtype=np.float32)
+    a = q35k.page_aligned_empty(4096)
     ctx.host_register(a)
     try:
         with pytest.raises(q35k.ArgumentException):
