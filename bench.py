@@ -63,7 +63,8 @@ CFG4_K, CFG4_N = 5120, 27648
 OUR_KERNELS = ("q35k_decode_kernel", "quantize_q8k_kernel", "q8k_to_planar_kernel", "dequant_kernel",
                "repack_tiles_kernel", "gemm_prep_kernel", "gemm_q4k_tc_kernel", "gather_permute_kernel",
                "q35k_shard_gather_kernel", "argmax_index_kernel", "q4k_meta_kernel", "q6k_meta_kernel",
-               "q35k_stage_in_kernel", "q35k_err_out_kernel")
+               "q35k_stage_in_kernel", "q35k_err_out_kernel", "gemm_prep_fast_kernel", "gemm_token_max_kernel",
+               "fast_row_scale_kernel", "q4k_fast_meta_kernel", "q6k_fast_meta_kernel")
 
 
 def load_peaks():

@@ -172,9 +172,12 @@ int q35k_matmul_silu_dev(q35k_ctx* ctx, const q35k_weight* w, const float* d_gat
  *     sc * (q - 32) needs 12 significant bits, as two exact fp16 parts
  *     (sc = 16 sh + sl) and two MMAs per K step;
  *   Q35K_GEMM_FAST: fp16-rounded dequantized weights times fp16-rounded
- *     dequantized Q8_K activations, one fp32 accumulator per tile (about
- *     4e-4 of max |y| from the reference's results); faster.  A weight whose
- *     fp16 values could overflow (flagged at upload) keeps the exact path. */
+ *     dequantized Q8_K activations, one fp32 accumulator per tile (2-4.5e-4
+ *     of max |y| from the reference's results, whatever the scales: each
+ *     weight row, and each token whose largest |x| is outside [2^-4, 2^15),
+ *     is normalised by a power of two before the rounding); faster.  A
+ *     weight with an infinite or NaN block scale (flagged at upload) keeps
+ *     the exact path. */
 #define Q35K_GEMM_EXACT 0
 #define Q35K_GEMM_FAST 1
 int q35k_set_gemm_mode(q35k_ctx* ctx, int mode);

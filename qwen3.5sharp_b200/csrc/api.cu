@@ -218,7 +218,7 @@ int q35k_weight_upload(q35k_ctx* c, int type, const void* blocks, int n_in, int 
     w->bytes = tile_bytes;
     uint8_t* raw = nullptr;
     cudaError_t e = cudaMalloc(&w->tiles, tile_bytes);
-    // The staged GGUF rows, then a word the metadata kernel flags fp16-range trouble in.
+    // The staged GGUF rows, then a word the metadata kernel flags non-finite block scales in.
     const size_t flag_off = (raw_bytes + 15) / 16 * 16;
     if (e == cudaSuccess) e = cudaMalloc(&raw, flag_off + 16);
     if (e != cudaSuccess) {
@@ -348,8 +348,8 @@ bool q35k_ctx::uses_gemm(const q35k_weight* w, int tokens) const {
     return tokens >= gemm_min_tokens && tc_gemm_supports(w->type, gemm_fast(w));
 }
 
-// Fast-mode arithmetic for this weight: the mode is fast and its fp16
-// dequantized values stay in range (else the exact form, or the GEMV).
+// Fast-mode arithmetic for this weight: the mode is fast and its block
+// scales are finite (else the exact form, or the GEMV).
 bool q35k_ctx::gemm_fast(const q35k_weight* w) const { return gemm_mode == Q35K_GEMM_FAST && w->fast_ok; }
 
 int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int tokens, cudaStream_t s, int ldy,
@@ -363,9 +363,11 @@ int q35k_ctx::gemm(const q35k_weight* w, const float* d_x, float* d_y, int token
     if ((rc = ensure_dev((void**)&d_xd, &xd_cap, p.xd_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gws, &gws_cap, p.ws_bytes, false)) != Q35K_OK) return rc;
     if ((rc = ensure_dev((void**)&d_gcnt, &gcnt_cap, p.counters * sizeof(int), true)) != Q35K_OK) return rc;
+    if (fast && (rc = ensure_dev((void**)&d_tmax, &tmax_cap, (size_t)p.m_pad * sizeof(unsigned), true)) != Q35K_OK)
+        return rc;
     cudaError_t e;
     if (prep) {
-        e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, fast, s, d_up);
+        e = launch_gemm_prep(d_x, w->n_in, tokens, p.m_pad, d_xq, d_xe, d_xd, d_tmax, fast, s, d_up);
         if (e != cudaSuccess) return cuda_fail(e, "GEMM activation launch");
     }
     TcGemmArgs a{};

@@ -18,7 +18,7 @@ struct q35k_weight {
     uint8_t* meta = nullptr;   // per-block GEMM metadata (gemm_tc.h)
     float* scale = nullptr;    // Q4_K / Q5_K: per-block drain scales of the exact GEMM
     size_t bytes = 0;
-    bool fast_ok = true;       // fast-mode fp16 weight values stay in range (launch_gemm_meta)
+    bool fast_ok = true;       // every d and dmin finite: the fast mode may take it (launch_gemm_meta)
 };
 
 struct q35k_ctx {
@@ -54,6 +54,8 @@ struct q35k_ctx {
     size_t gws_cap = 0;
     int* d_gcnt = nullptr;
     size_t gcnt_cap = 0;
+    unsigned* d_tmax = nullptr;  // fast-mode token maxima (zero between calls)
+    size_t tmax_cap = 0;
     // Q4_K calls with at least this many tokens run on the tensor cores
     // (environment variable Q35K_GEMM_MIN_TOKENS overrides it at creation).
     int gemm_min_tokens = 16;
@@ -84,6 +86,7 @@ struct q35k_ctx {
         if (d_xd) cudaFree(d_xd);
         if (d_gws) cudaFree(d_gws);
         if (d_gcnt) cudaFree(d_gcnt);
+        if (d_tmax) cudaFree(d_tmax);
         if (d_amax) cudaFree(d_amax);
         if (h_in) cudaFreeHost(h_in);
         if (h_out) cudaFreeHost(h_out);

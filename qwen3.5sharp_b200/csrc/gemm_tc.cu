@@ -194,7 +194,20 @@ static_assert(Geo<false, 128>::SMEM_BYTES == SMEM_BYTES && Geo<false, 128>::W_ST
 // (token, super-block).  Xq holds each aligned group of four K values in the
 // order 0, 2, 1, 3; the MMA's K order only has to agree between its operands.
 // ---------------------------------------------------------------------------
-template <bool FAST>
+__device__ __forceinline__ void store_xq_group(__half* row, int lane, const __half (&h)[8]) {
+    const __half2 p0 = __halves2half2(h[0], h[2]);
+    const __half2 p1 = __halves2half2(h[1], h[3]);
+    const __half2 p2 = __halves2half2(h[4], h[6]);
+    const __half2 p3 = __halves2half2(h[5], h[7]);
+    uint2 v0, v1;
+    v0.x = *reinterpret_cast<const uint32_t*>(&p0);
+    v0.y = *reinterpret_cast<const uint32_t*>(&p1);
+    v1.x = *reinterpret_cast<const uint32_t*>(&p2);
+    v1.y = *reinterpret_cast<const uint32_t*>(&p3);
+    reinterpret_cast<uint2*>(row)[lane] = v0;        // values 4l..4l+3
+    reinterpret_cast<uint2*>(row + 128)[lane] = v1;  // values 128+4l..
+}
+
 __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict__ x, const float* __restrict__ up,
                                                        int k, int tokens, int m_pad, __half* __restrict__ xq,
                                                        __half* __restrict__ xe, float* __restrict__ xd) {
@@ -205,29 +218,18 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     if (w >= m_pad * nb) return;
     const int r = w / nb, b = w % nb;
     if (r >= tokens) {
-        if (!FAST && lane == 0) xd[(size_t)b * m_pad + r] = 0.f;
+        if (lane == 0) xd[(size_t)b * m_pad + r] = 0.f;
         return;
     }
     int q[8];
     const size_t off = (size_t)r * k + (size_t)b * QK;
     const float d = warp_q8k_values(x + off, lane, q, up ? up + off : nullptr);
-    __half* row = xq + (size_t)r * k + (size_t)b * QK;
-    // Exact mode: the q values; fast mode: fp16(d q), the dequantized Q8_K
-    // activations.  K order within each group of four values: 0, 2, 1, 3 (the
-    // order in which the weight producers pair nibbles; see the decode).
-    auto hv = [&](int i) { return FAST ? __float2half_rn(d * (float)q[i]) : __int2half_rn(q[i]); };
-    const __half2 p0 = __halves2half2(hv(0), hv(2));
-    const __half2 p1 = __halves2half2(hv(1), hv(3));
-    const __half2 p2 = __halves2half2(hv(4), hv(6));
-    const __half2 p3 = __halves2half2(hv(5), hv(7));
-    uint2 v0, v1;
-    v0.x = *reinterpret_cast<const uint32_t*>(&p0);
-    v0.y = *reinterpret_cast<const uint32_t*>(&p1);
-    v1.x = *reinterpret_cast<const uint32_t*>(&p2);
-    v1.y = *reinterpret_cast<const uint32_t*>(&p3);
-    reinterpret_cast<uint2*>(row)[lane] = v0;        // values 4l..4l+3
-    reinterpret_cast<uint2*>(row + 128)[lane] = v1;  // values 128+4l..
-    if (FAST) return;
+    // The q values (exact small integers), in the K order of the weight
+    // producers' nibble pairs.
+    __half h[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) h[i] = __int2half_rn(q[i]);
+    store_xq_group(xq + (size_t)r * k + (size_t)b * QK, lane, h);
     int s0, s1;
     warp_q8k_bsums(q, s0, s1);
     if ((lane & 3) == 0) {
@@ -236,6 +238,109 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
         e[8 + (lane >> 2)] = __int2half_rn(s1);
     }
     if (lane == 0) xd[(size_t)b * m_pad + r] = d;
+}
+
+// Fast mode: Xq = fp16(2^e d q), the Q8_K-dequantized activations of a token
+// times a power of two, and Xs[token] = 2^-e, which the GEMM's drain
+// multiplies its outputs by (exact).  A token whose largest |x| lies in
+// [2^FAST_TOKEN_LO, 2^FAST_TOKEN_HI) keeps e = 0: its fp16 values cannot
+// overflow, and those that fall into the fp16 subnormals carry errors below
+// 2^-21 of the token's largest value.  Any other token gets the e that puts
+// its largest |x| in [2^13, 2^14).
+constexpr int FAST_TOKEN_EXP = 14, FAST_TOKEN_LO = -4, FAST_TOKEN_HI = 15;
+
+__device__ __forceinline__ int fast_token_exp(float tm) {
+    int E = 0;
+    if (tm > 0.f && isfinite(tm)) frexpf(tm, &E);
+    // At most 120, so that 2^e and 2^-e stay normal floats (e >= -114 for
+    // any finite maximum).
+    return (E == 0 || (E > FAST_TOKEN_LO && E <= FAST_TOKEN_HI)) ? 0 : min(FAST_TOKEN_EXP - E, 120);
+}
+
+__device__ __forceinline__ void fast_quantize_store(const float (&v)[8], int lane, float scale,
+                                                    __half* __restrict__ dst) {
+    int q[8];
+    const float d = warp_q8k_quantize(v, lane, q) * scale;
+    __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) h[j] = __float2half_rn(d * (float)q[j]);
+    store_xq_group(dst, lane, h);
+}
+
+__device__ __forceinline__ float warp_abs_max(const float (&v)[8]) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) m = fmaxf(m, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+// Two kernels: gemm_prep_fast_kernel, one warp per (token, super-block),
+// stores the block with e = 0 and records its max |x| in tmax[token] (float
+// bits, atomic max); gemm_token_scale_kernel, its programmatic dependent,
+// writes Xs, clears tmax for the next call, and rewrites the rows of the
+// tokens outside the range.  (A token's maximum is known only once all its
+// blocks are read; storing with e = 0 first costs the common case nothing.)
+__global__ void __launch_bounds__(256) gemm_prep_fast_kernel(const float* __restrict__ x, const float* __restrict__ up,
+                                                            int k, int tokens, __half* __restrict__ xq,
+                                                            unsigned* __restrict__ tmax) {
+    griddep_launch_dependents();
+    const int nb = k / QK;
+    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= tokens * nb) return;
+    const int r = w / nb, b = w % nb;
+    const size_t off = (size_t)r * k + (size_t)b * QK;
+    float v[8];
+    warp_q8k_load(x + off, lane, v, up ? up + off : nullptr);
+    fast_quantize_store(v, lane, 1.f, xq + off);
+    const float m = warp_abs_max(v);
+    if (lane == 0) atomicMax(tmax + r, __float_as_uint(m));  // m >= 0: the bits order as the values
+}
+
+// FAST_SCALE_TOKENS tokens per CTA: few CTAs, so that while they wait for
+// the preparation kernel they keep few SMs from the GEMM that follows.
+constexpr int FAST_SCALE_TOKENS = 64;
+
+__global__ void __launch_bounds__(256) gemm_token_scale_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ up, int k, int tokens,
+                                                              int m_pad, __half* __restrict__ xq,
+                                                              float* __restrict__ xs, unsigned* __restrict__ tmax) {
+    griddep_launch_dependents();
+    __shared__ int rescale[FAST_SCALE_TOKENS];
+    __shared__ float scales[FAST_SCALE_TOKENS];
+    __shared__ int n_rescale;
+    const int r0 = blockIdx.x * FAST_SCALE_TOKENS;
+    if (threadIdx.x == 0) n_rescale = 0;
+    griddep_wait();  // the maxima and the e = 0 rows
+    __syncthreads();
+    if (threadIdx.x < FAST_SCALE_TOKENS && r0 + (int)threadIdx.x < m_pad) {
+        const int r = r0 + threadIdx.x;
+        if (r >= tokens) {
+            xs[r] = 0.f;  // padded token
+        } else {
+            const float tm = __uint_as_float(tmax[r]);
+            tmax[r] = 0u;
+            const int e = fast_token_exp(tm);
+            xs[r] = ldexpf(1.f, -e);
+            if (e) {
+                const int i = atomicAdd(&n_rescale, 1);
+                rescale[i] = r;
+                scales[i] = ldexpf(1.f, e);
+            }
+        }
+    }
+    __syncthreads();
+    // Rows outside the range, one (token, super-block) per warp at a time.
+    const int nb = k / QK, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int u = warp; u < n_rescale * nb; u += blockDim.x >> 5) {
+        const int i = u / nb, b = u % nb;
+        const size_t off = (size_t)rescale[i] * k + (size_t)b * QK;
+        float v[8];
+        warp_q8k_load(x + off, lane, v, up ? up + off : nullptr);
+        fast_quantize_store(v, lane, scales[i], xq + off);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -599,21 +704,33 @@ __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
 //   chunk 0: fp16 alpha * sc_j, j = 0..7        (the A operand's sub-block scales)
 //   chunk 1: fp16 high part of -beta * m_j, j = 0..7
 //   chunk 2: fp16 low part of -beta * m_j
-//   chunk 3: fp16 d * sc_j                       (fast mode: the dequantized weight
-//   chunk 4: fp16 dmin * m_j                      q * (d sc_j) - dmin m_j in fp16)
+//   chunk 3: fp16 2^e d * sc_j                   (fast mode: the dequantized weight
+//   chunk 4: fp16 2^e dmin * m_j                  2^e (q * (d sc_j) - dmin m_j) in fp16)
 // and the drain's fp32 s of each row in s[(g nb + b) 32 + r] (q4k_block_scale).
+//
+// Fast mode normalises every weight row by a power of two 2^e (fast_row_scale:
+// the row's largest |fp16 value| lands in [2^13, 2^14)), so its fp16 values
+// neither overflow nor fall into the fp16 subnormals, whatever the row's d;
+// the GEMM's drain multiplies the row's outputs by 2^-e (exact).  The passes:
+// gemm_meta (exact-mode chunks, the row maxima), fast_row_scale (the maxima ->
+// 2^-e in place), fast_meta (chunks 3 and 4).  A block with a non-finite d or
+// dmin sets *unsafe and the weight's prefill keeps the exact arithmetic.
 // One thread per (row, super-block).
 // ---------------------------------------------------------------------------
-// Fast-mode weight values q * (d sc) - dmin m are fp16: a block whose values
-// could reach FAST_RANGE_LIMIT (half the fp16 maximum, a margin for the
-// rounding of d sc) sets *unsafe, and the weight's prefill then keeps the
-// exact arithmetic.  GGUF weights have small d; uniform fp16 test patterns
-// do not.
-constexpr float FAST_RANGE_LIMIT = 32768.f;
+constexpr int FAST_ROW_EXP = 14;  // a row's largest fast-mode |fp16 value| < 2^14
+
+__device__ __forceinline__ void row_max_update(unsigned* row_max, int row, float v, unsigned* unsafe) {
+    if (!isfinite(v)) {
+        atomicOr(unsafe, 1u);
+        return;
+    }
+    atomicMax(row_max + row, __float_as_uint(v));  // v >= 0: the bits order as the values
+}
 
 __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ meta,
-                                                      float* __restrict__ s_out, int n_pad, int nb, int tile_bytes,
-                                                      int qmax, unsigned* __restrict__ unsafe) {
+                                                      float* __restrict__ s_out, unsigned* __restrict__ row_max,
+                                                      int n_pad, int nb, int tile_bytes, int qmax,
+                                                      unsigned* __restrict__ unsafe) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)n_pad * nb) return;
     const int row = (int)(idx / nb), b = (int)(idx % nb);
@@ -622,10 +739,11 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
     const uint4 hdr = *reinterpret_cast<const uint4*>(tiles + tile * tile_bytes + r * 16);  // Q4_K / Q5_K header
     const BlockScale bs = q4k_block_scale(hdr.x);
     const float d = fp16_bits_to_float(hdr.x), dm = fp16_bits_to_float(hdr.x >> 16);
-    uint32_t sa[4], hi[4], lo[4], fs[4], fm[4];
+    uint32_t sa[4], hi[4], lo[4];
+    float vmax = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j += 2) {
-        uint16_t a2[2], h2[2], l2[2], s2[2], m2[2];
+        uint16_t a2[2], h2[2], l2[2];
 #pragma unroll
         for (int t = 0; t < 2; t++) {
             int sc, m;
@@ -635,39 +753,77 @@ __global__ void __launch_bounds__(256) q4k_meta_kernel(const uint8_t* __restrict
             const __half h = __float2half_rn(v);
             h2[t] = __half_as_ushort(h);
             l2[t] = __half_as_ushort(__float2half_rn(v - __half2float(h)));
-            s2[t] = __half_as_ushort(__float2half_rn(d * (float)sc));
-            m2[t] = __half_as_ushort(__float2half_rn(dm * (float)m));
+            vmax = fmaxf(vmax, fabsf(d) * (float)(sc * qmax) + fabsf(dm) * (float)m);
         }
         sa[j / 2] = a2[0] | ((uint32_t)a2[1] << 16);
         hi[j / 2] = h2[0] | ((uint32_t)h2[1] << 16);
         lo[j / 2] = l2[0] | ((uint32_t)l2[1] << 16);
-        fs[j / 2] = s2[0] | ((uint32_t)s2[1] << 16);
-        fm[j / 2] = m2[0] | ((uint32_t)m2[1] << 16);
     }
     uint8_t* mt = meta + tile * tcg::Q4K_META_TILE + r * 16;
     *reinterpret_cast<uint4*>(mt) = make_uint4(sa[0], sa[1], sa[2], sa[3]);
     *reinterpret_cast<uint4*>(mt + 512) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint4*>(mt + 1024) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4*>(mt + 1536) = make_uint4(fs[0], fs[1], fs[2], fs[3]);
-    *reinterpret_cast<uint4*>(mt + 2048) = make_uint4(fm[0], fm[1], fm[2], fm[3]);
     s_out[tile * 32 + r] = bs.s;
-    float vmax = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        int sc, m;
-        q4k_scale_min(j, hdr.y, hdr.z, hdr.w, sc, m);
-        vmax = fmaxf(vmax, fabsf(d) * (float)(sc * qmax) + fabsf(dm) * (float)m);
-    }
-    if (!(vmax < FAST_RANGE_LIMIT)) atomicOr(unsafe, 1u);
+    row_max_update(row_max, row, isfinite(d) && isfinite(dm) ? vmax : __int_as_float(0x7f800000), unsafe);
 }
 
-// Q6_K metadata: for the fast mode fp16 d * sc_s of the 16-value groups
+// Row maxima (float bits) -> the fast mode's row scales 2^-e in place, with
+// e = FAST_ROW_EXP - E for a maximum in [2^(E-1), 2^E); 1 for an all-zero row.
+__global__ void __launch_bounds__(256) fast_row_scale_kernel(float* __restrict__ rs, int n_pad) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= n_pad) return;
+    const float vmax = rs[row];
+    int E = 0;
+    if (!(vmax > 0.f && isfinite(vmax))) {
+        rs[row] = 1.f;
+        return;
+    }
+    frexpf(vmax, &E);
+    rs[row] = ldexpf(1.f, E - FAST_ROW_EXP);
+}
+
+__global__ void __launch_bounds__(256) q4k_fast_meta_kernel(const uint8_t* __restrict__ tiles,
+                                                           uint8_t* __restrict__ meta, const float* __restrict__ rs,
+                                                           int n_pad, int nb, int tile_bytes) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)n_pad * nb) return;
+    const int row = (int)(idx / nb), b = (int)(idx % nb);
+    const int g = row >> 5, r = row & 31;
+    const size_t tile = (size_t)g * nb + b;
+    const uint4 hdr = *reinterpret_cast<const uint4*>(tiles + tile * tile_bytes + r * 16);
+    const float up = 1.f / rs[row];  // 2^e: exact
+    const float d = fp16_bits_to_float(hdr.x) * up, dm = fp16_bits_to_float(hdr.x >> 16) * up;
+    uint32_t fs[4], fm[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        uint16_t s2[2], m2[2];
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+            int sc, m;
+            q4k_scale_min(j + t, hdr.y, hdr.z, hdr.w, sc, m);
+            s2[t] = __half_as_ushort(__float2half_rn(d * (float)sc));
+            m2[t] = __half_as_ushort(__float2half_rn(dm * (float)m));
+        }
+        fs[j / 2] = s2[0] | ((uint32_t)s2[1] << 16);
+        fm[j / 2] = m2[0] | ((uint32_t)m2[1] << 16);
+    }
+    uint8_t* mt = meta + tile * tcg::Q4K_META_TILE + r * 16;
+    *reinterpret_cast<uint4*>(mt + 1536) = make_uint4(fs[0], fs[1], fs[2], fs[3]);
+    *reinterpret_cast<uint4*>(mt + 2048) = make_uint4(fm[0], fm[1], fm[2], fm[3]);
+}
+
+// Q6_K metadata: for the fast mode fp16 2^e d * sc_s of the 16-value groups
 // s = 0..7 (chunk 0) and 8..15 (chunk 1), one 16-byte slot per row as above
-// (the producers form (q - 32) * (d sc_s) with one fp16 rounding); for the
-// exact mode the drain scale d of each row and super-block (the producers
+// (the producers form (q - 32) * (2^e d sc_s) with one fp16 rounding); for
+// the exact mode the drain scale d of each row and super-block (the producers
 // read the int8 scales from the tile itself).
-__global__ void __launch_bounds__(256) q6k_meta_kernel(const uint8_t* __restrict__ tiles, uint8_t* __restrict__ meta,
-                                                      float* __restrict__ s_out, int n_pad, int nb,
+__device__ __forceinline__ float q6k_group_scale(uint4 sv, int s) {
+    const uint32_t w = s < 4 ? sv.x : s < 8 ? sv.y : s < 12 ? sv.z : sv.w;
+    return (float)(int8_t)(w >> (8 * (s & 3)));
+}
+
+__global__ void __launch_bounds__(256) q6k_meta_kernel(const uint8_t* __restrict__ tiles, float* __restrict__ s_out,
+                                                      unsigned* __restrict__ row_max, int n_pad, int nb,
                                                       unsigned* __restrict__ unsafe) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)n_pad * nb) return;
@@ -678,19 +834,29 @@ __global__ void __launch_bounds__(256) q6k_meta_kernel(const uint8_t* __restrict
     const float d = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(t + Fmt<TYPE_Q6_K>::D_OFFSET + r * 2));
     s_out[tile * 32 + r] = d;
     const uint4 sv = *reinterpret_cast<const uint4*>(t + 12 * 512 + r * 16);
-    const uint32_t sc4[4] = {sv.x, sv.y, sv.z, sv.w};
-    uint32_t ds[8];
     float vmax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; i++) vmax = fmaxf(vmax, fabsf(d * (float)(int8_t)(sc4[i >> 2] >> (8 * (i & 3)))) * 32.f);
-    if (!(vmax < FAST_RANGE_LIMIT)) atomicOr(unsafe, 1u);
+    for (int s = 0; s < 16; s++) vmax = fmaxf(vmax, fabsf(d * q6k_group_scale(sv, s)) * 32.f);
+    row_max_update(row_max, row, isfinite(d) ? vmax : __int_as_float(0x7f800000), unsafe);
+}
+
+__global__ void __launch_bounds__(256) q6k_fast_meta_kernel(const uint8_t* __restrict__ tiles,
+                                                           uint8_t* __restrict__ meta, const float* __restrict__ rs,
+                                                           int n_pad, int nb) {
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)n_pad * nb) return;
+    const int row = (int)(idx / nb), b = (int)(idx % nb);
+    const int g = row >> 5, r = row & 31;
+    const size_t tile = (size_t)g * nb + b;
+    const uint8_t* t = tiles + tile * tcg::WFmt<TYPE_Q6_K>::TILE_BYTES;
+    const float d = fp16_bits_to_float(*reinterpret_cast<const uint16_t*>(t + Fmt<TYPE_Q6_K>::D_OFFSET + r * 2)) *
+                    (1.f / rs[row]);
+    const uint4 sv = *reinterpret_cast<const uint4*>(t + 12 * 512 + r * 16);
+    uint32_t ds[8];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int s0 = 2 * i, s1 = 2 * i + 1;
-        const float v0 = d * (float)(int8_t)(sc4[s0 >> 2] >> (8 * (s0 & 3)));
-        const float v1 = d * (float)(int8_t)(sc4[s1 >> 2] >> (8 * (s1 & 3)));
-        ds[i] = __half_as_ushort(__float2half_rn(v0)) | ((uint32_t)__half_as_ushort(__float2half_rn(v1)) << 16);
-    }
+    for (int i = 0; i < 8; i++)
+        ds[i] = __half_as_ushort(__float2half_rn(d * q6k_group_scale(sv, 2 * i))) |
+                ((uint32_t)__half_as_ushort(__float2half_rn(d * q6k_group_scale(sv, 2 * i + 1))) << 16);
     uint8_t* mt = meta + tile * tcg::WFmt<TYPE_Q6_K>::META_TILE + r * 16;
     *reinterpret_cast<uint4*>(mt) = make_uint4(ds[0], ds[1], ds[2], ds[3]);
     *reinterpret_cast<uint4*>(mt + 512) = make_uint4(ds[4], ds[5], ds[6], ds[7]);
@@ -1177,6 +1343,7 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
         const int q = warp & 3;    // lane quadrant = 32 weight rows of the tile
         const int th = dw >> 2;    // token half of the tile (TN / 2 tokens)
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        if constexpr (FAST) griddep_wait();  // the token scales come from the preparation kernel
         float out[64];
 #pragma unroll
         for (int j = 0; j < 64; j++) out[j] = 0.f;
@@ -1234,7 +1401,18 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
 
             if (b != nb - 1 && i != n_units - 1) continue;  // the tile's segment goes on
             int accb = 0;
+            // Fast mode: the scales that undo the operands' normalisation, the
+            // row's 2^-e_r and lane l's token scales 2^-e_t of tokens l and
+            // 32 + l of each pass, loaded while the accumulator fills.
+            float rsc = 0.f, ts_lo[PASSES], ts_hi[PASSES];
             if constexpr (FAST) {
+                rsc = (g < n_groups) ? a.scale[(size_t)a.n_pad * a.nb + row] : 0.f;
+#pragma unroll
+                for (int pp = 0; pp < PASSES; pp++) {
+                    const float* ts = a.xd + tt * TN + th * (TN / 2) + pp * 64;
+                    ts_lo[pp] = ts[lane];
+                    ts_hi[pp] = ts[32 + lane];
+                }
                 // One accumulator per tile segment: read it once, at the end.
                 accb = seg % ACC_BUFS;
                 if (!warp_wait_bar(acc_full + accb, (uint32_t)(seg / ACC_BUFS) & 1u, a.err, abort_flag, lane)) break;
@@ -1255,10 +1433,14 @@ __global__ void __launch_bounds__(tcg::THREADS, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(acc_empty + accb);  // all of it read
                 }
+                // Undo the operands' normalisation: times the row scale 2^-e_r,
+                // then the token scale 2^-e_t (each exact, barring underflow).
+                const float tlo = pp ? ts_lo[PASSES - 1] : ts_lo[0];
+                const float thi = pp ? ts_hi[PASSES - 1] : ts_hi[0];
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
-                    out[j] = __uint_as_float(r0[j]);
-                    out[32 + j] = __uint_as_float(r1[j]);
+                    out[j] = __uint_as_float(r0[j]) * rsc * __shfl_sync(0xffffffffu, tlo, j);
+                    out[32 + j] = __uint_as_float(r1[j]) * rsc * __shfl_sync(0xffffffffu, thi, j);
                 }
             }
             const int tok0 = tt * TN + th * (TN / 2) + pp * 64;
@@ -1373,24 +1555,35 @@ size_t gemm_meta_bytes(int type, int nb, int n_pad) {
 }
 size_t gemm_scale_bytes(int type, int nb, int n_pad) {
     (void)type;
-    return (size_t)n_pad * nb * sizeof(float);
+    // The exact mode's drain scale of every (row, super-block), then the fast
+    // mode's row scales 2^-e.
+    return ((size_t)n_pad * nb + n_pad) * sizeof(float);
 }
 
 cudaError_t launch_gemm_meta(int type, const uint8_t* tiles, uint8_t* meta, float* scale, int nb, int n_pad,
                              unsigned* unsafe, cudaStream_t s) {
     const long long n = (long long)n_pad * nb;
     if (n == 0) return cudaSuccess;
-    const unsigned grid = (unsigned)((n + 255) / 256);
+    float* rs = scale + n;
+    unsigned* row_max = reinterpret_cast<unsigned*>(rs);
+    cudaError_t e = cudaMemsetAsync(row_max, 0, (size_t)n_pad * sizeof(unsigned), s);
+    if (e != cudaSuccess) return e;
+    const unsigned grid = (unsigned)((n + 255) / 256), row_grid = (unsigned)((n_pad + 255) / 256);
     switch (type) {
     case TYPE_Q4_K:
-        q4k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, tcg::WFmt<TYPE_Q4_K>::TILE_BYTES, 15,
-                                             unsafe);
+    case TYPE_Q5_K: {
+        const int tile_bytes = type == TYPE_Q4_K ? tcg::WFmt<TYPE_Q4_K>::TILE_BYTES : tcg::WFmt<TYPE_Q5_K>::TILE_BYTES;
+        const int qmax = type == TYPE_Q4_K ? 15 : 31;
+        q4k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, row_max, n_pad, nb, tile_bytes, qmax, unsafe);
+        fast_row_scale_kernel<<<row_grid, 256, 0, s>>>(rs, n_pad);
+        q4k_fast_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, rs, n_pad, nb, tile_bytes);
         break;
-    case TYPE_Q5_K:
-        q4k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, tcg::WFmt<TYPE_Q5_K>::TILE_BYTES, 31,
-                                             unsafe);
+    }
+    case TYPE_Q6_K:
+        q6k_meta_kernel<<<grid, 256, 0, s>>>(tiles, scale, row_max, n_pad, nb, unsafe);
+        fast_row_scale_kernel<<<row_grid, 256, 0, s>>>(rs, n_pad);
+        q6k_fast_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, rs, n_pad, nb);
         break;
-    case TYPE_Q6_K: q6k_meta_kernel<<<grid, 256, 0, s>>>(tiles, meta, scale, n_pad, nb, unsafe); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -1482,17 +1675,33 @@ cudaError_t configure_tc_gemm() {
     return cudaSuccess;
 }
 
-cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd, bool fast,
-                             cudaStream_t s, const float* up) {
+cudaError_t launch_gemm_prep(const float* x, int k, int tokens, int m_pad, void* xq, void* xe, float* xd,
+                             unsigned* tmax, bool fast, cudaStream_t s, const float* up) {
     const int nb = k / QK;
     const long long warps = (long long)m_pad * nb;
     const int grid = (int)((warps + 7) / 8);
-    if (fast)
-        gemm_prep_kernel<true><<<grid, 256, 0, s>>>(x, up, k, tokens, m_pad, static_cast<__half*>(xq), nullptr, nullptr);
-    else
-        gemm_prep_kernel<false><<<grid, 256, 0, s>>>(x, up, k, tokens, m_pad, static_cast<__half*>(xq),
-                                                     static_cast<__half*>(xe), xd);
-    return cudaGetLastError();
+    if (!fast) {
+        gemm_prep_kernel<<<grid, 256, 0, s>>>(x, up, k, tokens, m_pad, static_cast<__half*>(xq),
+                                              static_cast<__half*>(xe), xd);
+        return cudaGetLastError();
+    }
+    if (tokens > 0) {
+        gemm_prep_fast_kernel<<<(int)(((long long)tokens * nb + 7) / 8), 256, 0, s>>>(
+            x, up, k, tokens, static_cast<__half*>(xq), tmax);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((m_pad + FAST_SCALE_TOKENS - 1) / FAST_SCALE_TOKENS);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_token_scale_kernel, x, up, k, tokens, m_pad, static_cast<__half*>(xq), xd,
+                              tmax);
 }
 
 template <int TYPE>

@@ -31,8 +31,9 @@ struct Q8Out {
 // as g / (1 + exp(-g)) in fp32 (Ops.SiLUMul, Qwen35Sharp.Model/Ops.cs:624-675).
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
-__device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, int lane, int (&q)[8],
-                                                 const float* __restrict__ up = nullptr) {
+// This lane's eight values of the block (silu(src) * up with `up`).
+__device__ __forceinline__ void warp_q8k_load(const float* __restrict__ src, int lane, float (&v)[8],
+                                              const float* __restrict__ up = nullptr) {
     float4 v0 = __ldg(reinterpret_cast<const float4*>(src) + lane);
     float4 v1 = __ldg(reinterpret_cast<const float4*>(src + 128) + lane);
     if (up) {
@@ -41,8 +42,12 @@ __device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, 
         v0 = make_float4(silu_mul(v0.x, u0.x), silu_mul(v0.y, u0.y), silu_mul(v0.z, u0.z), silu_mul(v0.w, u0.w));
         v1 = make_float4(silu_mul(v1.x, u1.x), silu_mul(v1.y, u1.y), silu_mul(v1.z, u1.z), silu_mul(v1.w, u1.w));
     }
-    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w;
+    v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
+}
 
+// The quantization of values loaded by warp_q8k_load.
+__device__ __forceinline__ float warp_q8k_quantize(const float (&v)[8], int lane, int (&q)[8]) {
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
@@ -81,6 +86,13 @@ __device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, 
         q[i] = min(127, max(-127, t));
     }
     return __fdiv_rn(1.f, iscale);
+}
+
+__device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, int lane, int (&q)[8],
+                                                 const float* __restrict__ up = nullptr) {
+    float v[8];
+    warp_q8k_load(src, lane, v, up);
+    return warp_q8k_quantize(v, lane, q);
 }
 
 // Sums of 16 of the values returned by warp_q8k_values: s0 = bsums[lane/4]

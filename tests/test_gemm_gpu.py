@@ -161,9 +161,14 @@ def test_gemm_device_pointer_path(ctx):
 
 # ---------------------------------------------------------------------------
 # Fast mode (q35k_set_gemm_mode(Q35K_GEMM_FAST)): fp16-rounded dequantized
-# weights and activations, one accumulator per tile.  Its own bar is the
-# contract's 1e-3; the design lands near 4e-4.
+# weights and activations, one accumulator per tile.  Every weight row and
+# every token whose largest |x| is outside [2^-4, 2^15) is normalised by a
+# power of two before the fp16 rounding (the drain undoes it exactly), so the
+# error is the fp16 rounding of the operands (2^-11 relative each) whatever
+# the scales: FAST_BOUND holds it, per config and per block of rows and
+# tokens of one scale; measured 2-4.5e-4 (5.9e-4 at most per block).
 # ---------------------------------------------------------------------------
+FAST_BOUND = 6e-4
 
 @pytest.fixture(scope="module")
 def fast_ctx():
@@ -184,7 +189,7 @@ def test_fast_mode_within_tolerance(fast_ctx, oracle_mod, k, n, m):
     err = rel_err(y, ref)
     print(f"fast m={m} k={k} n={n}: max|y-r|/max|r| = {err:.3e}")
     assert np.isfinite(y).all()
-    assert err <= TOL
+    assert err <= TOL and err <= FAST_BOUND
     W.free()
 
 
@@ -196,8 +201,68 @@ def test_fast_mode_edge_blocks(fast_ctx, oracle_mod):
     W = fast_ctx.upload(Q4_K, w, k, n)
     y = fast_ctx.matmul(W, x)
     ref = oracle_mod.Weight(Q4_K, w, k, n).matmul(x, threads=THREADS)
-    assert rel_err(y, ref) <= TOL
+    assert rel_err(y, ref) <= FAST_BOUND
     W.free()
+
+
+# Row groups scaled by these powers of two (d and dmin of every block), token
+# groups by these factors: fp16 subnormal weights (2^-14 d ~ 6e-7) and
+# activations (1e-7), and activations beyond the fp16 maximum (1e6).
+ROW_SCALES = (2.0 ** -14, 2.0 ** -6, 1.0, 2.0 ** 10)
+TOKEN_SCALES = (1e-7, 1e-3, 1.0, 1e6)
+
+
+def scaled_rows(qt, w, n, k):
+    """Blocks of `w` with row group i's d (and dmin) times ROW_SCALES[i]."""
+    size = {synth.Q4_K: 144, synth.Q5_K: 176, synth.Q6_K: 210}[qt]
+    b = w.reshape(n, k // 256, size).copy()
+    fields = [(208, 210)] if qt == synth.Q6_K else [(0, 2), (2, 4)]
+    for i, f in enumerate(ROW_SCALES):
+        rows = slice(i * n // 4, (i + 1) * n // 4)
+        for lo, hi in fields:
+            v = b[rows, :, lo:hi].copy().view(np.float16).astype(np.float32) * np.float32(f)
+            b[rows, :, lo:hi] = v.astype(np.float16).view(np.uint8)
+    return b.reshape(n, -1)
+
+
+@pytest.mark.parametrize("qt", [synth.Q4_K, synth.Q5_K, synth.Q6_K])
+def test_fast_mode_scale_spread(fast_ctx, oracle_mod, qt):
+    """Rows and tokens over 2^24 and 1e13 of scale: every (row group, token
+    group) block within FAST_BOUND of its own max |y|, none of it inf."""
+    k, n, m = 2560, 512, 256
+    w = scaled_rows(qt, synth.kquant_blocks(qt, n, k, seed=31, q5_uniform_d=False), n, k)
+    x = synth.activations(m, k, seed=32)
+    for j, f in enumerate(TOKEN_SCALES):
+        x[j * m // 4:(j + 1) * m // 4] *= np.float32(f)
+    W = fast_ctx.upload(qt, w, k, n)
+    y = fast_ctx.matmul(W, x)
+    W.free()
+    ref = oracle_mod.Weight(qt, w, k, n).matmul(x, threads=THREADS)
+    assert np.isfinite(y).all()
+    for i in range(4):
+        for j in range(4):
+            rows, toks = slice(i * n // 4, (i + 1) * n // 4), slice(j * m // 4, (j + 1) * m // 4)
+            err = rel_err(y[toks, rows], ref[toks, rows])
+            print(f"rows x{ROW_SCALES[i]:g} tokens x{TOKEN_SCALES[j]:g}: {err:.3e}")
+            assert err <= FAST_BOUND, (i, j, err)
+
+
+def test_fast_mode_long_rows(fast_ctx, oracle_mod):
+    """Rows of 65 super-blocks (more than one token-scale CTA's warps cover at
+    once when rewritten): tokens inside the fast preparation's e = 0 range and
+    outside it, against the oracle."""
+    k, n, m = 65 * 256, 256, 64
+    w = synth.kquant_blocks(Q4_K, n, k, seed=41)
+    x = synth.activations(m, k, seed=42)
+    x[:16] *= np.float32(1e-7)
+    x[16:32] *= np.float32(1e6)
+    W = fast_ctx.upload(Q4_K, w, k, n)
+    y = fast_ctx.matmul(W, x)
+    W.free()
+    ref = oracle_mod.Weight(Q4_K, w, k, n).matmul(x, threads=THREADS)
+    assert np.isfinite(y).all()
+    for toks in (slice(0, 16), slice(16, 32), slice(32, 64)):
+        assert rel_err(y[toks], ref[toks]) <= FAST_BOUND
 
 
 @pytest.mark.parametrize("m", [300, 700])  # 128- and 256-token tiles
@@ -222,5 +287,5 @@ def test_fast_mode_wide_tiles_match_narrow(fast_ctx, oracle_mod):
         y = fast_ctx.matmul(W, x)
         ref = oracle_mod.Weight(Q4_K, w, k, n).matmul(x, threads=THREADS)
         assert np.isfinite(y).all()
-        assert rel_err(y, ref) <= TOL
+        assert rel_err(y, ref) <= FAST_BOUND
         W.free()

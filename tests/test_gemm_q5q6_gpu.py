@@ -9,7 +9,9 @@ products sc * (q - 32) need up to 12 significant bits, so its exact mode
 splits every int8 scale as sc = 16 sh + sl (sl in [0, 15]) and multiplies
 the two exact fp16 parts sl (q - 32) and 16 sh (q - 32) against the same
 activations (two MMAs per K step); its error is fp32 rounding as well.
-Bar: max|y - r| / max|r| <= 1e-3, and DESIGN_BOUND for the exact mode.
+Bar: max|y - r| / max|r| <= 1e-3, DESIGN_BOUND for the exact mode and
+FAST_BOUND (the fp16 rounding of both operands, after the per-row and
+per-token power-of-two normalisation) for the fast mode.
 """
 
 import os
@@ -25,6 +27,7 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-3
 DESIGN_BOUND = 2e-5
+FAST_BOUND = 6e-4
 THREADS = os.cpu_count() or 1
 
 
@@ -101,7 +104,7 @@ def test_fast_mode(fast_ctx, oracle_mod, qt, k, n, m):
     err = rel_err(y, ref)
     print(f"{'Q5_K' if qt == Q5_K else 'Q6_K'} fast m={m} k={k} n={n}: {err:.3e}")
     assert np.isfinite(y).all()
-    assert err <= TOL
+    assert err <= TOL and err <= FAST_BOUND
 
 
 def _q5k_edge_blocks(n, k, seed):
@@ -143,23 +146,43 @@ def test_q5k_edge_blocks(ctx, fast_ctx, oracle_mod, fast):
         assert rel_err(y, ref) <= DESIGN_BOUND
 
 
-def test_fast_mode_keeps_out_of_range_weights_exact(ctx, fast_ctx, gemv_ctx, oracle_mod):
-    """Weights whose fp16 dequantized values could overflow (d up to the fp16
-    maximum) are flagged at upload: in the fast mode their prefill keeps the
-    exact GEMM, bit for bit."""
+def test_fast_mode_takes_the_whole_fp16_range(ctx, fast_ctx, oracle_mod):
+    """d and dmin anywhere in the finite fp16 range (up to 65504, products
+    far beyond the fp16 maximum): the per-row normalisation keeps the fast
+    mode's fp16 values in range, so these weights run the fast GEMM, within
+    FAST_BOUND."""
     k, n, m = 2560, 512, 64
-    w5 = synth.kquant_blocks(Q5_K, n, k, seed=13)  # uniform fp16 d and dmin
+    w5 = synth.kquant_blocks(Q5_K, n, k, seed=13)  # uniform finite fp16 d and dmin
     x = synth.activations(m, k, seed=14)
     y_fast = run(fast_ctx, Q5_K, w5, x, k, n)
     assert np.isfinite(y_fast).all()
-    assert (y_fast == run(ctx, Q5_K, w5, x, k, n)).all()
     ref = oracle_mod.Weight(Q5_K, w5, k, n).matmul(x, threads=THREADS)
-    assert rel_err(y_fast, ref) <= DESIGN_BOUND
+    assert rel_err(y_fast, ref) <= FAST_BOUND
+    assert not (y_fast == run(ctx, Q5_K, w5, x, k, n)).all()  # the fast arithmetic ran
     w6 = synth.kquant_blocks(Q6_K, n, k, seed=15).reshape(n, k // 256, 210)
     w6[0, 0, 208:210] = np.frombuffer(np.float16(1000.0).tobytes(), np.uint8)  # one block with d = 1000
     w6 = w6.reshape(n, -1)
     y6 = run(fast_ctx, Q6_K, w6, x, k, n)
-    assert (y6 == run(ctx, Q6_K, w6, x, k, n)).all()
+    assert rel_err(y6, oracle_mod.Weight(Q6_K, w6, k, n).matmul(x, threads=THREADS)) <= FAST_BOUND
+
+
+@pytest.mark.parametrize("qt", [Q5_K, Q6_K])
+def test_fast_mode_keeps_non_finite_scales_exact(ctx, fast_ctx, qt):
+    """A weight with an infinite or NaN block scale is flagged at upload: its
+    fast-mode prefill is the exact GEMM, bit for bit (the non-finite rows
+    included)."""
+    k, n, m = 1024, 256, 64
+    size = 176 if qt == Q5_K else 210
+    d_at = 0 if qt == Q5_K else 208
+    w = synth.kquant_blocks(qt, n, k, seed=16, q5_uniform_d=False).reshape(n, k // 256, size)
+    w[3, 1, d_at:d_at + 2] = np.frombuffer(np.float16(np.inf).tobytes(), np.uint8)
+    w[7, 2, d_at:d_at + 2] = np.frombuffer(np.float16(np.nan).tobytes(), np.uint8)
+    w = w.reshape(n, -1)
+    x = synth.activations(m, k, seed=17)
+    y_fast = run(fast_ctx, qt, w, x, k, n)
+    y_exact = run(ctx, qt, w, x, k, n)
+    assert np.array_equal(y_fast.view(np.uint32), y_exact.view(np.uint32))
+    assert np.isfinite(np.delete(y_exact, [3, 7], axis=1)).all()
 
 
 def test_q6k_fast_mode_ran_on_the_tensor_cores(fast_ctx, gemv_ctx):
