@@ -482,6 +482,8 @@ class Bench:
         # launch duration over K launches replayed from a CUDA graph, as the
         # timed steps are (at N = 1 a step is exactly this one kernel), and a
         # single launch between its own pair of events (launch latency included).
+        ctx.matmul_dev(W, dx, dy_local, M, self.sh)  # sizes this call's scratch before the capture
+        torch.cuda.synchronize()
         kgraph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(kgraph):
             cs = torch.cuda.current_stream().cuda_stream
