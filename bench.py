@@ -371,13 +371,30 @@ class Bench:
             rows += list(range(a, min(b, a + 64))) + list(range(max(a, b - 64), b))
         return sorted(set(rows))
 
-    def parity_vs_single_gpu(self, qt, k, n, x, y_mine, make_full):
+    def parity_vs_single_gpu(self, qt, k, n, x, y_mine, make_full, w_local, r0, r1):
         """Rank 0 runs the full matrix on its GPU alone (q35k_matmul_dev) and
         broadcasts y; every rank compares its gathered y with it.  Returns the
         largest relative difference over the ranks and whether every rank's y
-        has the same bits."""
+        has the same bits (the full matrix alone may take another launch plan
+        than a rank's rows, so its fp32 summation order may differ).  Also
+        whether the gather is lossless: each rank's own rows computed by one
+        plain call on its GPU equal its slice of the gathered y bit for bit,
+        and every rank gathered the same bits (a checksum compared across the
+        ranks)."""
         np, torch = self.np, self.torch
         m = x.shape[0]
+        Wl = self.ctx.upload(qt, w_local, k, r1 - r0)
+        alone = torch.empty((m, r1 - r0), dtype=torch.float32, device="cuda")
+        self.ctx.matmul_dev(Wl, torch.from_numpy(x).cuda(), alone, m, self.sh)
+        torch.cuda.synchronize()
+        Wl.free()
+        slice_ok = np.array_equal(alone.cpu().numpy().view(np.uint32),
+                                  np.ascontiguousarray(y_mine[:, r0:r1]).view(np.uint32))
+        bits = y_mine.view(np.uint32).astype(np.uint64).reshape(-1)
+        cs = int((bits * (np.arange(bits.size, dtype=np.uint64) | np.uint64(1))).sum() & np.uint64(2**62 - 1))
+        cmp = torch.tensor([cs, -cs, 0 if slice_ok else 1], device="cuda", dtype=torch.int64)
+        self.dist.all_reduce(cmp, op=self.dist.ReduceOp.MAX)
+        lossless = bool(cmp[0].item() == -cmp[1].item() and cmp[2].item() == 0)
         ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
         if self.rank == 0:
             wf = make_full()
@@ -394,7 +411,8 @@ class Bench:
         differ = 0.0 if np.array_equal(y_mine.view(np.uint32), r.view(np.uint32)) else 1.0
         t = torch.tensor([err, differ], device="cuda", dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
-        return {"max_rel_err_vs_1gpu": float(t[0].item()), "bit_equal_1gpu": bool(t[1].item() == 0.0)}
+        return {"max_rel_err_vs_1gpu": float(t[0].item()), "bit_equal_1gpu": bool(t[1].item() == 0.0),
+                "gather_bit_exact": lossless}
 
     # -- the headline: cfg1 vocab head --
     def headline(self):
@@ -520,7 +538,7 @@ class Bench:
         self.head_parity = {}
         if world > 1:
             self.head_parity = self.parity_vs_single_gpu(
-                qt, K, N, x, y_mine, lambda: synth.kquant_blocks(qt, N, K, seed=CFG["seed_w"]))
+                qt, K, N, x, y_mine, lambda: synth.kquant_blocks(qt, N, K, seed=CFG["seed_w"]), w, r0, r1)
         if rank == 0:
             self.cpu_jobs["cfg1"] = (qt, w if world == 1 else None, x, y_mine,
                                      None if world == 1 else self.boundary_rows(N))
@@ -738,7 +756,7 @@ class Bench:
             call()
             torch.cuda.synchronize()
             y = dy.cpu().numpy()
-            par = self.parity_vs_single_gpu(qt, k, n, x, y, lambda: synth.kquant_blocks(qt, n, k, seed=1))
+            par = self.parity_vs_single_gpu(qt, k, n, x, y, lambda: synth.kquant_blocks(qt, n, k, seed=1), w, r0, r1)
             if m >= 64:
                 v, u = 2.0 * m * n * k / (ms / 1e3) / 1e12, "TFLOP/s"
                 frac = v / peak_bf16 if peak_bf16 else None
@@ -750,6 +768,7 @@ class Bench:
             self.configs[f"{name}_p{self.world}"] = {
                 "v": v, "u": u, "frac_per_gpu": frac / self.world if frac is not None else None, "ms": ms,
                 "err_1gpu": par["max_rel_err_vs_1gpu"], "bit_eq_1gpu": par["bit_equal_1gpu"],
+                "gather_exact": par["gather_bit_exact"],
                 "what": f"Q4_K M={m} K={k} N={n} row-sharded over {self.world} GPUs, {gather}, whole job"}
             if self.rank == 0:
                 self.cpu_jobs[f"{name}_p{self.world}"] = (qt, None, x, y, self.boundary_rows(n))
@@ -803,7 +822,8 @@ class Bench:
             if "err" in c:
                 parts.append(f"err vs oracle {c['err']:.1e}")
             if "err_1gpu" in c:
-                parts.append(f"err vs 1 GPU {c['err_1gpu']:.1e} bit-equal {c['bit_eq_1gpu']}")
+                parts.append(f"err vs 1 GPU {c['err_1gpu']:.1e} bit-equal {c['bit_eq_1gpu']}, "
+                             f"slices bit-equal to their rows alone {c['gather_exact']}")
             print(" | ".join(parts) + f" | {c['what']}")
         line = {
             "metric": METRIC, "value": h["value"], "unit": "GB/s", "n_gpus": world, "steps": self.args.steps,
