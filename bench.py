@@ -151,6 +151,17 @@ def rel_err(y, r) -> float:
     return float(np.abs(y - r).max() / max(float(np.abs(r).max()), 1e-30))
 
 
+def elem_rel_err(y, r) -> float:
+    """Largest element-wise |y - r| / |r| over the outputs with |r| >= 1e-2
+    max |r| (the second parity figure, beside rel_err)."""
+    import numpy as np
+
+    y = np.asarray(y, dtype=np.float64)
+    r = np.asarray(r, dtype=np.float64)
+    big = np.abs(r) >= 1e-2 * max(float(np.abs(r).max()), 1e-30)
+    return float((np.abs(y - r)[big] / np.abs(r)[big]).max()) if big.any() else 0.0
+
+
 def count_launches(torch, step):
     """Kernels of libq35k launched by one step, counted with the CUDA
     profiler on an untimed step (NCCL and torch kernels excluded)."""
@@ -194,11 +205,13 @@ def cpu_leg(jobs, time_it: bool, budget_s: float = 1.0):
         res = {}
         if rows is not None:
             W = oracle.Weight(qt, np.ascontiguousarray(w[rows]), k, len(rows))
-            res["err"] = rel_err(gy[:, rows], W.matmul(x, threads=topo["logical"]))
+            ref = W.matmul(x, threads=topo["logical"])
+            res["err"], res["err_elem"] = rel_err(gy[:, rows], ref), elem_rel_err(gy[:, rows], ref)
             out[name] = res
             continue
         W = oracle.Weight(qt, w, k, n)
-        res["err"] = rel_err(gy, W.matmul(x, threads=topo["logical"]))
+        ref = W.matmul(x, threads=topo["logical"])
+        res["err"], res["err_elem"] = rel_err(gy, ref), elem_rel_err(gy, ref)
         if time_it:
             W.matmul(x, threads=workers)  # warm-up
             calls, t0 = 0, time.perf_counter()
@@ -799,8 +812,10 @@ class Bench:
             for name, r in res.items():
                 if name in self.configs:
                     self.configs[name]["err"] = r["err"]
+                    self.configs[name]["err_elem"] = r["err_elem"]
             if "cfg1" in res:
                 self.head_parity["max_rel_err_vs_oracle"] = res["cfg1"]["err"]
+                self.head_parity["max_elem_rel_err_vs_oracle"] = res["cfg1"]["err_elem"]
             if world == 1 and "value" in res.get("cfg1", {}):
                 c1 = res["cfg1"]
                 cpu_line = {"value": c1["value"], "unit": c1["unit"], "cores": c1["cores"], "kind": "port",
@@ -820,7 +835,7 @@ class Bench:
                 cc = cpu_line["configs"][name]
                 parts.append(f"cpu {cc['v']:.3g} {cc['u']} ({cc['cores']} cores)")
             if "err" in c:
-                parts.append(f"err vs oracle {c['err']:.1e}")
+                parts.append(f"err vs oracle {c['err']:.1e} (element-wise {c['err_elem']:.1e})")
             if "err_1gpu" in c:
                 parts.append(f"err vs 1 GPU {c['err_1gpu']:.1e} bit-equal {c['bit_eq_1gpu']}, "
                              f"slices bit-equal to their rows alone {c['gather_exact']}")
