@@ -130,6 +130,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in the barrier unit (up to `hint_ns`) instead of spinning on the
+// issue slots that the working warps of its sub-partition need.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Relaxed system-scope 64-bit access (values exchanged between GPUs; an
 // aligned 64-bit access is single-copy atomic).
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
@@ -149,14 +166,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Bounded wait on an mbarrier phase.  Gives up after `limit_ns` of wall time,
 // records DEV_ERR_TIMEOUT in *err and returns false: no device wait here can
-// spin forever.
+// spin forever.  The waiting warp sleeps in the barrier unit between tests
+// (suspend-time hint) rather than spending issue slots that the decoding
+// warps of its SM sub-partition need.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err,
                                                   uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t start = globaltimer_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 255u && globaltimer_ns() - start > limit_ns) {
+    const uint64_t start = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
+        if (globaltimer_ns() - start > limit_ns) {
             atomicOr(err, DEV_ERR_TIMEOUT);
             return false;
         }

@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float* __restrict_
     for (int i = 0; i < 8; i++) h[i] = __int2half_rn(q[i]);
     store_xq_group(xq + (size_t)r * k + (size_t)b * QK, lane, h);
     int s0, s1;
-    warp_q8k_bsums(q, s0, s1);
+    warp_q8k_bsums(pack_q4(q[0], q[1], q[2], q[3]), pack_q4(q[4], q[5], q[6], q[7]), s0, s1);
     if ((lane & 3) == 0) {
         __half* e = xe + (size_t)r * nb * 16 + (size_t)b * 16;
         e[lane >> 2] = __int2half_rn(s0);

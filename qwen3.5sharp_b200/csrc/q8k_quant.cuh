@@ -51,34 +51,30 @@ __device__ __forceinline__ float warp_q8k_quantize(const float (&v)[8], int lane
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    // fmaxf drops NaNs, so every lane's amax is a non-negative number, whose
+    // bit pattern orders like its value: one integer max over the warp.
+    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
 
     if (amax == 0.f) {
 #pragma unroll
         for (int i = 0; i < 8; i++) q[i] = 0;
         return 0.f;
     }
-    // First index whose |x| equals amax, and its signed value.
-    int idx = 1 << 30;
-    float val = 0.f;
+    // First index whose |x| equals amax, and its signed value.  Every index
+    // of the low half (4*lane + i, i < 4) precedes every index of the high
+    // half (128 + 4*lane + i - 4), and within a half lanes go in index
+    // order: the first hit is the lowest lane's first hit in the low half if
+    // any lane has one, else the lowest lane's first hit in the high half.
+    float vlo = 0.f, vhi = 0.f;
+    bool hlo = false, hhi = false;
 #pragma unroll
-    for (int i = 7; i >= 0; i--) {
-        const int pos = (i < 4) ? (4 * lane + i) : (128 + 4 * lane + (i - 4));
-        if (fabsf(v[i]) == amax) {
-            idx = pos;
-            val = v[i];
-        }
-    }
+    for (int i = 3; i >= 0; i--)
+        if (fabsf(v[i]) == amax) hlo = true, vlo = v[i];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        const float ov = __shfl_xor_sync(0xffffffffu, val, o);
-        if (oi < idx) {
-            idx = oi;
-            val = ov;
-        }
-    }
+    for (int i = 7; i >= 4; i--)
+        if (fabsf(v[i]) == amax) hhi = true, vhi = v[i];
+    const unsigned mlo = __ballot_sync(0xffffffffu, hlo), mhi = __ballot_sync(0xffffffffu, hhi);
+    const float val = __shfl_sync(0xffffffffu, mlo ? vlo : vhi, __ffs(mlo ? mlo : mhi) - 1);
     const float iscale = __fdiv_rn(-127.f, val);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
@@ -95,11 +91,16 @@ __device__ __forceinline__ float warp_q8k_values(const float* __restrict__ src, 
     return warp_q8k_quantize(v, lane, q);
 }
 
-// Sums of 16 of the values returned by warp_q8k_values: s0 = bsums[lane/4]
-// and s1 = bsums[8 + lane/4], valid on lanes with lane % 4 == 0.
-__device__ __forceinline__ void warp_q8k_bsums(const int (&q)[8], int& s0, int& s1) {
-    s0 = q[0] + q[1] + q[2] + q[3];
-    s1 = q[4] + q[5] + q[6] + q[7];
+// The four q values (each in [-127, 127]) as the bytes of one word, lowest first.
+__device__ __forceinline__ uint32_t pack_q4(int a, int b, int c, int d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Sums of 16 of the packed values: s0 = bsums[lane/4] and s1 = bsums[8 + lane/4],
+// valid on lanes with lane % 4 == 0.
+__device__ __forceinline__ void warp_q8k_bsums(uint32_t w0, uint32_t w1, int& s0, int& s1) {
+    s0 = __dp4a((int)w0, 0x01010101, 0);
+    s1 = __dp4a((int)w1, 0x01010101, 0);
     s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
     s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
     s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
@@ -112,14 +113,12 @@ __device__ __forceinline__ void warp_quantize_q8k_block(const float* __restrict_
     int q[8];
     const float d = warp_q8k_values(src, lane, q, up);
     if (lane == 0) *out.d = __float_as_uint(d);
-    const uint32_t w0 =
-        (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
-    const uint32_t w1 =
-        (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    const uint32_t w0 = pack_q4(q[0], q[1], q[2], q[3]);
+    const uint32_t w1 = pack_q4(q[4], q[5], q[6], q[7]);
     out.qs[lane * out.qs_stride] = w0;
     out.qs[(32 + lane) * out.qs_stride] = w1;
     int s0, s1;
-    warp_q8k_bsums(q, s0, s1);
+    warp_q8k_bsums(w0, w1, s0, s1);
     if ((lane & 3) == 0) {
         out.bs[lane >> 2] = static_cast<int16_t>(s0);
         out.bs[8 + (lane >> 2)] = static_cast<int16_t>(s1);
