@@ -173,16 +173,19 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
     bool ok = true;
     if (FUSED) {
         griddep_wait();  // x comes from the preceding kernel
-        for (int job = warp; job < M * kr; job += W) {
-            const int m = job / kr, t = job % kr;
-            Q8Out out;
-            out.d = reinterpret_cast<uint32_t*>(q8s + qs_bytes) + t * pl.rows4 + m;
-            out.qs = reinterpret_cast<uint32_t*>(q8s + (size_t)(t * M + m) * QK);
-            out.bs = reinterpret_cast<int16_t*>(q8s + qs_bytes + d_bytes) + (t * M + m) * 16;
-            const size_t off = (size_t)m * a.ldx + (size_t)(b0 + t) * QK;
-            warp_quantize_q8k_block(a.x + off, out, lane, a.up ? a.up + off : nullptr);
-        }
-        __syncthreads();
+        // Each warp quantizes the blocks of the tiles it decodes (all tokens),
+        // so it depends on no other warp.
+        for (int t = warp; t < kr; t += W)
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                Q8Out out;
+                out.d = reinterpret_cast<uint32_t*>(q8s + qs_bytes) + t * pl.rows4 + m;
+                out.qs = reinterpret_cast<uint32_t*>(q8s + (size_t)(t * M + m) * QK);
+                out.bs = reinterpret_cast<int16_t*>(q8s + qs_bytes + d_bytes) + (t * M + m) * 16;
+                const size_t off = (size_t)m * a.ldx + (size_t)(b0 + t) * QK;
+                warp_quantize_q8k_block(a.x + off, out, lane, a.up ? a.up + off : nullptr);
+            }
+        __syncwarp();
     } else if (Q8_GLOBAL) {
         griddep_wait();  // q8 comes from the preceding kernel
     } else {
