@@ -81,9 +81,11 @@ int q35k_ctx::ensure_host(void** p, size_t* cap, size_t bytes) {
 }
 
 int q35k_ctx::check_device_error() {
-    unsigned word = 0;
-    cudaError_t e = cudaMemcpy(&word, d_err, sizeof word, cudaMemcpyDeviceToHost);
+    // A pinned destination: one direct DMA instead of a staged pageable copy.
+    cudaError_t e = cudaMemcpyAsync(h_errw, d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+    const unsigned word = *reinterpret_cast<volatile unsigned*>(h_errw);
     if (word) return on_device_error(word);
     return Q35K_OK;
 }
@@ -145,7 +147,8 @@ int q35k_create(int device, q35k_ctx** out) {
     c->num_sms = prop.multiProcessorCount;
     if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaMalloc(&c->d_err, sizeof(unsigned))) != cudaSuccess ||
-        (e = cudaMemset(c->d_err, 0, sizeof(unsigned))) != cudaSuccess) {
+        (e = cudaMemset(c->d_err, 0, sizeof(unsigned))) != cudaSuccess ||
+        (e = cudaHostAlloc(reinterpret_cast<void**>(&c->h_errw), 64, cudaHostAllocDefault)) != cudaSuccess) {
         g_create_error = cudaGetErrorString(e);
         delete c;
         return Q35K_ECUDA;

@@ -41,6 +41,7 @@ struct q35k_ctx {
     int* d_counters = nullptr;  // split-K arrival counters; zero between calls
     size_t counters_cap = 0;
     unsigned* d_err = nullptr;  // device error word (bounded waits that expired)
+    unsigned* h_errw = nullptr;  // pinned host word the error word is read into at q35k_sync
 
     // Prefill GEMM scratch (gemm_tc.h): fp16 Q8_K operands, partial tiles and
     // arrival counters (zero between calls).
@@ -90,6 +91,7 @@ struct q35k_ctx {
         if (d_amax) cudaFree(d_amax);
         if (h_in) cudaFreeHost(h_in);
         if (h_out) cudaFreeHost(h_out);
+        if (h_errw) cudaFreeHost(h_errw);
         if (stream) cudaStreamDestroy(stream);
     }
 

@@ -86,6 +86,49 @@ def test_quantize_bit_exact_random(ctx, oracle_mod):
     assert (ctx.quantize_q8k(x) == oracle_mod.quantize_q8k(x)).all()
 
 
+def _tie_blocks():
+    """Blocks whose largest |x| occurs more than once, at positions that the
+    GPU quantizer's search (a warp lane owns values 4l..4l+3 and
+    128+4l..128+4l+3) must order like Q8K.ScaleBlock's scan from index 0."""
+    rng = np.random.default_rng(5)
+    blocks = []
+
+    def base():
+        return (rng.standard_normal(256) * 0.1).astype(np.float32)
+
+    def block(*hits):
+        b = base()
+        for pos, v in hits:
+            b[pos] = v
+        blocks.append(b)
+
+    block((3, 2.5), (1, -2.5))           # same lane, low half: index 1 first
+    block((127, -3.0), (128, 3.0))       # lane 31 low half before lane 0 high half
+    block((130, 1.75), (136, -1.75))     # high half only: lane 0 before lane 2
+    block((133, -4.0), (134, 4.0))       # same lane, high half
+    block((255, -0.5), (254, 0.5), (0, 0.25))
+    block((200, 7.0), (4, -7.0), (96, 7.0))
+    alt = np.where(np.arange(256) % 2 == 0, 1.0, -1.0).astype(np.float32)
+    blocks.append(alt)                   # every value a tie: index 0 first
+    blocks.append(-alt)
+    one = np.zeros(256, dtype=np.float32)
+    one[255] = -1e-3                     # a single nonzero value at the end
+    blocks.append(one)
+    return np.stack(blocks)
+
+
+def test_quantize_first_extremum_ties(ctx, oracle_mod):
+    x = _tie_blocks().reshape(1, -1)
+    assert (ctx.quantize_q8k(x) == oracle_mod.quantize_q8k(x)).all()
+    # The same blocks through the fused decode GEMV's in-CTA quantization.
+    qt, k, n = Q4_K, x.shape[1], 256
+    w = synth.kquant_blocks(qt, n, k, seed=9)
+    W = ctx.upload(qt, w, k, n)
+    y = ctx.matmul(W, x)
+    y2 = ctx.matmul_q8k(W, oracle_mod.quantize_q8k(x), 1)
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))
+
+
 CONFIGS = [
     ("cfg0_q4k_m1", Q4_K, 1, 2560, 9728, 1.0),
     ("cfg1_q6k_m1_vocab", Q6_K, 1, 2560, 151936, 1.0),
