@@ -714,13 +714,14 @@ int q35k_matmul_argmax_dev(q35k_ctx* c, const q35k_weight* w, const float* d_x, 
     if ((rc = check_alignment(c, d_x, 16, d_y, 4)) != Q35K_OK) return rc;
     cudaSetDevice(c->device);
     const cudaStream_t s = pick(c, stream);
-    if ((rc = c->ensure_dev((void**)&c->d_amax, &c->amax_cap, (size_t)tokens * sizeof(unsigned long long), false)) !=
+    // The keys are zeroed when allocated and cleared again by the index
+    // kernel of every call, so no reset precedes the GEMV (which then starts
+    // with programmatic dependent launch like any other decode call).
+    if ((rc = c->ensure_dev((void**)&c->d_amax, &c->amax_cap, (size_t)tokens * sizeof(unsigned long long), true)) !=
         Q35K_OK)
         return rc;
-    cudaError_t e = cudaMemsetAsync(c->d_amax, 0, (size_t)tokens * sizeof(unsigned long long), s);
-    if (e != cudaSuccess) return c->cuda_fail(e, "argmax key reset");
     if ((rc = c->matmul_into(w, d_x, d_y, w->n_out, tokens, s, nullptr, c->d_amax)) != Q35K_OK) return rc;
-    e = launch_argmax_index(c->d_amax, d_idx, tokens, s);
+    cudaError_t e = launch_argmax_index(c->d_amax, d_idx, tokens, s);
     if (e != cudaSuccess) return c->cuda_fail(e, "argmax index launch");
     return Q35K_OK;
 }

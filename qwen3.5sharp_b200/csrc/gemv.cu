@@ -420,15 +420,32 @@ bool gemv_fuses_quantize(int type, int nb, int n_out, int tokens, int num_sms) {
     return tokens * p.unit_blocks <= 2 * p.warps;
 }
 
-// Row index of each token's fused-argmax key.
-__global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys, int* __restrict__ idx, int tokens) {
+// Row index of each token's fused-argmax key; the key is then cleared for the
+// next call (the GEMV folds its outputs into it with atomicMax, after its own
+// grid-dependency wait, i.e. after this kernel completed).  Launched with
+// programmatic dependent launch: the next call's GEMV may start streaming its
+// weights while this kernel waits for the one before it.
+__global__ void argmax_index_kernel(unsigned long long* __restrict__ keys, int* __restrict__ idx, int tokens) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    griddep_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t < tokens) idx[t] = (int)(0xffffffffu - (uint32_t)(keys[t] & 0xffffffffull));
+    if (t < tokens) {
+        idx[t] = (int)(0xffffffffu - (uint32_t)(keys[t] & 0xffffffffull));
+        keys[t] = 0ull;
+    }
 }
 
-cudaError_t launch_argmax_index(const unsigned long long* keys, int* idx, int tokens, cudaStream_t s) {
-    argmax_index_kernel<<<(tokens + 127) / 128, 128, 0, s>>>(keys, idx, tokens);
-    return cudaGetLastError();
+cudaError_t launch_argmax_index(unsigned long long* keys, int* idx, int tokens, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((tokens + 127) / 128));
+    cfg.blockDim = dim3(128);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, argmax_index_kernel, keys, idx, tokens);
 }
 
 int gemv_plan_rows(const GemvArgs& a) {

@@ -103,7 +103,7 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms);
 int gemv_max_tokens(int nb);
 cudaError_t launch_gemv(int type, const GemvArgs& a, cudaStream_t s, bool pdl);
 // idx[t] = the row of keys[t] (fused argmax, see GemvArgs::argmax).
-cudaError_t launch_argmax_index(const unsigned long long* keys, int* idx, int tokens, cudaStream_t s);
+cudaError_t launch_argmax_index(unsigned long long* keys, int* idx, int tokens, cudaStream_t s);
 // Whether the GEMV for this shape quantizes its own activations (small
 // slices per CTA: decode) instead of reading planar Q8_K.
 bool gemv_fuses_quantize(int type, int nb, int n_out, int tokens, int num_sms);
