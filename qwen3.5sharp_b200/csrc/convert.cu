@@ -11,6 +11,23 @@
 
 namespace q35k {
 
+// Launch with programmatic stream serialization: the kernel may become
+// resident while the kernel before it in the stream drains (it waits on the
+// grid dependency before touching memory), and lets its own dependent start.
+template <typename... P, typename... A>
+static cudaError_t launch_dependent(void (*kernel)(P...), int grid, int block, cudaStream_t s, A... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)block);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<P>(args)...);
+}
+
 // ---------------------------------------------------------------------------
 // Q8_K quantization: one warp per 256-value super-block (q8k_quant.cuh).
 // Output goes either to BlockQ8K blocks (chunk == 0) or to the planar layout
@@ -49,6 +66,10 @@ __global__ void __launch_bounds__(256) quantize_q8k_kernel(const float* __restri
     // serialization may start now: it streams weights first and waits on the
     // grid dependency (full completion of this grid) before reading q8.
     asm volatile("griddepcontrol.launch_dependents;");
+    // This kernel is itself launched as a programmatic dependent: x comes
+    // from the kernel before it, and q8 may still be read by it (the
+    // previous call's GEMV).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= total_blocks) return;
@@ -63,9 +84,8 @@ cudaError_t launch_quantize_q8k(const float* x, uint8_t* q8, int k, int rows, in
     const int total = nb * rows;
     if (total == 0) return cudaSuccess;
     const int warps_per_cta = 8;
-    const int grid = (total + warps_per_cta - 1) / warps_per_cta;
-    quantize_q8k_kernel<<<grid, warps_per_cta * 32, 0, s>>>(x, up, q8, nb, total, rows, planar_chunk, ilv_rows);
-    return cudaGetLastError();
+    return launch_dependent(quantize_q8k_kernel, (total + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, s,
+                            x, up, q8, nb, total, rows, planar_chunk, ilv_rows);
 }
 
 // BlockQ8K rows (a caller's pre-quantized activations) -> the planar layout,
@@ -74,6 +94,7 @@ __global__ void __launch_bounds__(256) q8k_to_planar_kernel(const uint8_t* __res
                                                             int nb, int total_blocks, int rows, int chunk,
                                                             int ilv_rows) {
     asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // dst may still be read by the kernel before
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= total_blocks) return;
@@ -91,10 +112,8 @@ cudaError_t launch_q8k_to_planar(const uint8_t* src, uint8_t* dst, int k, int ro
     const int total = nb * rows;
     if (total == 0) return cudaSuccess;
     const int warps_per_cta = 8;
-    q8k_to_planar_kernel<<<(total + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, 0, s>>>(src, dst, nb,
-                                                                                                      total, rows, chunk,
-                                                                                                      ilv_rows);
-    return cudaGetLastError();
+    return launch_dependent(q8k_to_planar_kernel, (total + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, s,
+                            src, dst, nb, total, rows, chunk, ilv_rows);
 }
 
 // ---------------------------------------------------------------------------
