@@ -14,10 +14,13 @@
 //     chunk-major tile layout makes every 16-byte load a contiguous 512-byte
 //     line per warp) and all lanes read the same Q8_K words (shared-memory
 //     broadcast); integer dots live in gemv_dot.cuh;
-//   * the warps' partial sums are added in warp order; a row group split
-//     over several units is finished by whichever unit arrives last, summing
-//     the pieces in K order and resetting the group's arrival counter.  Every
-//     sum has a fixed order, so results are deterministic.
+//   * the warps' partial sums are added in warp order; the units of a row
+//     group split along K (2..8 of them) are one thread-block cluster, whose
+//     first CTA sums the pieces in K order through distributed shared memory;
+//     a row group split further is finished by whichever unit arrives last,
+//     summing the pieces in K order through global memory and resetting the
+//     group's arrival counter.  Every sum has a fixed order, so results are
+//     deterministic.
 #include "device_common.cuh"
 #include "gemv_dot.cuh"
 #include "kernels.h"
@@ -46,6 +49,7 @@ static_assert(GEMV_FUSED_MAX_TOKENS < q8_interleave_min_rows(TYPE_Q4_K) &&
 constexpr int GEMV_UNIT_BYTES = Q35K_GEMV_UNIT_KB * 1024;  // weight bytes per split-K work unit (target)
 constexpr int GEMV_ROW_BYTES = Q35K_GEMV_ROW_KB * 1024;    // largest whole-row unit
 constexpr int GEMV_SMEM_LIMIT = 227 * 1024;
+constexpr int GEMV_MAX_CLUSTER = 8;  // portable thread-block cluster size
 
 __host__ __device__ constexpr int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
@@ -70,6 +74,22 @@ __host__ __device__ inline SmemLayout gemv_smem_layout(int type, int tile_bytes,
 }
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Barrier over every thread of the thread-block cluster (release / acquire at
+// cluster scope: shared-memory writes before it are visible to the cluster's
+// CTAs after it).
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// The float at the same shared-memory offset as `p` in the cluster's CTA `rank`.
+__device__ __forceinline__ float ld_cluster_f32(const float* p, int rank) {
+    uint32_t addr;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(smem_u32(p)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 
 // Order-preserving key of (logit, row) for the fused argmax: the largest key
 // is the reference's ArgMax (Qwen35Sharp.Cli/Program.cs:127-140) -- the first
@@ -101,7 +121,9 @@ __device__ __forceinline__ void warp_argmax_commit(unsigned long long key, unsig
 // shared memory (q8k_quant.cuh, the same bytes as the standalone quantizer)
 // while the weight tiles are in flight, instead of staging planar Q8_K from
 // a.q8 -- one kernel per call, used when that slice is small (decode).
-template <int TYPE, int M, bool FUSED>
+// SPLIT: the launch splits row groups along K (several units per row group);
+// whole-row launches run an instantiation without the split-K code.
+template <int TYPE, int M, bool FUSED, bool SPLIT>
 __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvArgs a, GemvPlan p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
@@ -255,7 +277,7 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
             v[m] = red[m * 32 + lane];
             for (int w = 1; w < W; w++) v[m] += red[(w * M + m) * 32 + lane];
         }
-        if (p.splits == 1) {
+        if constexpr (!SPLIT) {
             if (row < n_out && y)
 #pragma unroll
                 for (int m = 0; m < M; m++) {
@@ -266,6 +288,13 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
 #pragma unroll
                 for (int m = 0; m < M; m++)
                     warp_argmax_commit(row < n_out ? argmax_key(v[m], row) : 0ull, a.argmax + m, lane);
+        } else if (p.cluster > 1) {
+            // The row group's K-ranges form one thread-block cluster: this
+            // piece stays in this CTA's shared memory (each lane overwrites
+            // only the entries it has just read), and the cluster's first
+            // CTA sums the pieces in K order below.
+#pragma unroll
+            for (int m = 0; m < M; m++) red[m * 32 + lane] = v[m];
         } else {
             // Publish this K-range's piece; the last piece to arrive sums all
             // pieces in K order and resets the row group's counter.
@@ -291,6 +320,32 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
                 }
                 if (lane == 0) a.counters[g] = 0;
             }
+        }
+    }
+    if constexpr (SPLIT) {
+        if (p.cluster > 1) {
+            cluster_barrier();  // every piece is in its CTA's shared memory
+            if (warp == 0 && s == 0) {
+                const int row = gl * TILE_ROWS + lane;
+                const unsigned ep = a.peers.n ? *a.peers.seq + 1u : 0u;
+                const size_t poff = (size_t)(ep & 1u) * a.peers.half;
+                // The same additions, in the same order, as the global-memory
+                // path: bit-identical results either way.
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    float sum = 0.f;
+                    sum += red[m * 32 + lane];
+                    for (int k = 1; k < p.splits; k++) sum += ld_cluster_f32(&red[m * 32 + lane], k);
+                    if (row < n_out && y) {
+                        y[(size_t)m * ldy + row] = sum;
+                        const unsigned long long word = ((unsigned long long)ep << 32) | __float_as_uint(sum);
+                        for (int k = 0; k < a.peers.n; k++)
+                            st_relaxed_sys_u64(a.peers.y[k] + poff + (size_t)m * a.peers.ldp + row, word);
+                    }
+                    if (a.argmax) warp_argmax_commit(row < n_out ? argmax_key(sum, row) : 0ull, a.argmax + m, lane);
+                }
+            }
+            cluster_barrier();  // the first CTA has read every piece: the CTAs may exit
         }
     }
     if (a.peers.trace && tid == 0) atomicMax(a.peers.trace + 1, (unsigned long long)globaltimer_ns());
@@ -336,6 +391,9 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.warps = std::min(u, max_warps);
     p.grid = p.groups * p.splits;
     p.smem_bytes = (size_t)gemv_smem_layout(type, tile, u, m, p.warps).total;
+    // Splits of a row group that fit one portable cluster are reduced through
+    // distributed shared memory.
+    p.cluster = (p.splits > 1 && p.splits <= GEMV_MAX_CLUSTER) ? p.splits : 0;
     p.partial_bytes = p.splits > 1 ? (size_t)p.groups * p.splits * GEMV_MAX_TOKENS * 32 * sizeof(float) : 0;
     p.counters = (size_t)p.groups;
     p.fits = p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;
@@ -352,12 +410,19 @@ int gemv_max_tokens(int nb) {
 
 // Opt-in shared memory for every instantiation on the current device
 // (called once per context).
+template <int TYPE, int M, bool SPLIT>
+static void configure_split() {
+    cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, false, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GEMV_SMEM_LIMIT);
+    if (M <= GEMV_FUSED_MAX_TOKENS)
+        cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS, SPLIT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+}
+
 template <int TYPE, int M>
 static void configure_typed() {
-    cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
-    if (M <= GEMV_FUSED_MAX_TOKENS)
-        cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+    configure_split<TYPE, M, false>();
+    configure_split<TYPE, M, true>();
 }
 
 template <int TYPE>
@@ -386,16 +451,29 @@ static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream
     cfg.blockDim = dim3((unsigned)p.threads);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n++].val.programmaticStreamSerializationAllowed = 1;
+    }
+    if (p.cluster > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = (unsigned)p.cluster;
+        attr[n].val.clusterDim.y = 1;
+        attr[n++].val.clusterDim.z = 1;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    // The fused variant exists for small token counts only.
-    if (a.x != nullptr && M <= GEMV_FUSED_MAX_TOKENS)
-        return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>, a, p);
-    if (a.x != nullptr) return cudaErrorInvalidValue;
-    return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, false>, a, p);
+    cfg.numAttrs = n;
+    // The fused variant exists for small token counts only.  Whole-row units
+    // (one unit per row group) run an instantiation without the split-K code.
+    constexpr bool F = M <= GEMV_FUSED_MAX_TOKENS;
+    if (a.x != nullptr && !F) return cudaErrorInvalidValue;
+    if (p.splits > 1)
+        return a.x != nullptr ? cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, F, true>, a, p)
+                              : cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, false, true>, a, p);
+    return a.x != nullptr ? cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, F, false>, a, p)
+                          : cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, false, false>, a, p);
 }
 
 template <int TYPE>

@@ -94,6 +94,10 @@ int gemv_plan_rows(const GemvArgs& a);
 // `partial_bytes` / `counters` size the split-K scratch it needs.
 struct GemvPlan {
     int groups, n_pad, grid, splits, unit_blocks, warps, threads;
+    // > 1: the splits of a row group form one thread-block cluster of this
+    // size and are summed through distributed shared memory; 0: through the
+    // partial-sum buffer and the arrival counters in global memory.
+    int cluster;
     size_t smem_bytes, partial_bytes, counters;
     bool fits;
 };

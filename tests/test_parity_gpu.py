@@ -151,6 +151,21 @@ def test_benchmark_configs(ctx, oracle_mod, name, qt, m, k, n, scale):
     assert err <= TOL
 
 
+@pytest.mark.parametrize("n", [64, 608, 2560], ids=["splits38_global", "splits8_cluster", "splits3_cluster"])
+@pytest.mark.parametrize("m", [1, 8])
+def test_split_k_reductions(ctx, oracle_mod, n, m):
+    """Row groups split along K (K = 9728): 2 to 8 pieces are summed through a
+    thread-block cluster's shared memory, more through global memory."""
+    qt, k = Q4_K, 9728
+    w = synth.kquant_blocks(qt, n, k, seed=21)
+    x = synth.activations(m, k, seed=22)
+    W = ctx.upload(qt, w, k, n)
+    y = ctx.matmul(W, x)
+    ref = oracle_mod.Weight(qt, w, k, n).matmul(x, threads=os.cpu_count() or 1)
+    assert rel_err(y, ref) <= TOL
+    assert np.array_equal(ctx.matmul(W, x).view(np.uint32), y.view(np.uint32))
+
+
 def test_device_pointer_path(ctx, oracle_mod):
     torch = pytest.importorskip("torch")
     qt, k, n, m = Q4_K, 2560, 1000, 3
