@@ -124,7 +124,7 @@ __device__ __forceinline__ void warp_argmax_commit(unsigned long long key, unsig
 // SPLIT: the launch splits row groups along K (several units per row group);
 // whole-row launches run an instantiation without the split-K code.
 template <int TYPE, int M, bool FUSED, bool SPLIT>
-__global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvArgs a, GemvPlan p) {
+__device__ __forceinline__ void decode_body(const GemvArgs& a, const GemvPlan& p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TILE = Fmt<TYPE>::TILE;
     const int U = p.unit_blocks, W = p.warps, nb = a.nb;
@@ -359,6 +359,21 @@ __global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvAr
     }
 }
 
+// The kernels.  q35k_decode_kernel takes every launch plan (up to 20 warps).
+// One- and two-token launches of at most GEMV_SPLIT_WARPS warps (whole rows of
+// up to 10 tiles, split-K units) run q35k_decode_kernel_10w instead, whose
+// bounds (three 10-warp CTAs per SM) let the compiler keep more of the decode
+// in registers.
+template <int TYPE, int M, bool FUSED, bool SPLIT>
+__global__ void __launch_bounds__(GEMV_MAX_WARPS * 32) q35k_decode_kernel(GemvArgs a, GemvPlan p) {
+    decode_body<TYPE, M, FUSED, SPLIT>(a, p);
+}
+
+template <int TYPE, int M, bool FUSED, bool SPLIT>
+__global__ void __launch_bounds__(GEMV_SPLIT_WARPS * 32, 3) q35k_decode_kernel_10w(GemvArgs a, GemvPlan p) {
+    decode_body<TYPE, M, FUSED, SPLIT>(a, p);
+}
+
 GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     GemvPlan p{};
     const int tile = TILE_ROWS * block_bytes(type);
@@ -410,19 +425,24 @@ int gemv_max_tokens(int nb) {
 
 // Opt-in shared memory for every instantiation on the current device
 // (called once per context).
-template <int TYPE, int M, bool SPLIT>
-static void configure_split() {
-    cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, false, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int TYPE, int M, bool FUSED>
+static void configure_fused() {
+    cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, FUSED, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          GEMV_SMEM_LIMIT);
-    if (M <= GEMV_FUSED_MAX_TOKENS)
-        cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS, SPLIT>,
+    cudaFuncSetAttribute(q35k_decode_kernel<TYPE, M, FUSED, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         GEMV_SMEM_LIMIT);
+    if constexpr (M <= GEMV_FUSED_MAX_TOKENS) {
+        cudaFuncSetAttribute(q35k_decode_kernel_10w<TYPE, M, FUSED, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+        cudaFuncSetAttribute(q35k_decode_kernel_10w<TYPE, M, FUSED, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+    }
 }
 
 template <int TYPE, int M>
 static void configure_typed() {
-    configure_split<TYPE, M, false>();
-    configure_split<TYPE, M, true>();
+    configure_fused<TYPE, M, false>();
+    if (M <= GEMV_FUSED_MAX_TOKENS) configure_fused<TYPE, M, M <= GEMV_FUSED_MAX_TOKENS>();
 }
 
 template <int TYPE>
@@ -441,6 +461,21 @@ void configure_gemv_kernels() {
     configure_all_m<TYPE_Q4_K>();
     configure_all_m<TYPE_Q5_K>();
     configure_all_m<TYPE_Q6_K>();
+}
+
+// Whole-row units (one unit per row group) run an instantiation without the
+// split-K code; one- and two-token units of at most GEMV_SPLIT_WARPS warps the
+// kernel with the larger register budget.
+template <int TYPE, int M, bool FUSED, bool SPLIT>
+static cudaError_t launch_variant(cudaLaunchConfig_t& cfg, const GemvArgs& a, const GemvPlan& p) {
+    if constexpr (M <= GEMV_FUSED_MAX_TOKENS)
+        if (p.warps <= GEMV_SPLIT_WARPS) return cudaLaunchKernelEx(&cfg, q35k_decode_kernel_10w<TYPE, M, FUSED, SPLIT>, a, p);
+    return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, FUSED, SPLIT>, a, p);
+}
+
+template <int TYPE, int M, bool FUSED>
+static cudaError_t launch_split(cudaLaunchConfig_t& cfg, const GemvArgs& a, const GemvPlan& p) {
+    return p.splits > 1 ? launch_variant<TYPE, M, FUSED, true>(cfg, a, p) : launch_variant<TYPE, M, FUSED, false>(cfg, a, p);
 }
 
 template <int TYPE, int M>
@@ -465,15 +500,10 @@ static cudaError_t launch_typed(const GemvArgs& a, const GemvPlan& p, cudaStream
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
-    // The fused variant exists for small token counts only.  Whole-row units
-    // (one unit per row group) run an instantiation without the split-K code.
+    // The fused variant exists for small token counts only.
     constexpr bool F = M <= GEMV_FUSED_MAX_TOKENS;
     if (a.x != nullptr && !F) return cudaErrorInvalidValue;
-    if (p.splits > 1)
-        return a.x != nullptr ? cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, F, true>, a, p)
-                              : cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, false, true>, a, p);
-    return a.x != nullptr ? cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, F, false>, a, p)
-                          : cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, false, false>, a, p);
+    return a.x != nullptr ? launch_split<TYPE, M, F>(cfg, a, p) : launch_split<TYPE, M, false>(cfg, a, p);
 }
 
 template <int TYPE>
