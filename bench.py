@@ -563,7 +563,7 @@ class Bench:
                     "peak_kind": (f"{self.peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if self.peak_kind == "measured"
                                   else "fallback"),
                     "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
-                    "kernel": "q35k_decode_kernel<Q6_K,1,fused>", "kernel_ms": gemv_ms,
+                    "kernel": "q35k_decode_kernel_10w<Q6_K,1,fused>", "kernel_ms": gemv_ms,
                     "kernel_timing": f"average of {args.steps} launches replayed from one CUDA graph, CUDA events "
                                      "on the launching stream",
                     "algorithmic_bytes_per_launch": nbytes_local}

@@ -361,7 +361,8 @@ __device__ __forceinline__ void decode_body(const GemvArgs& a, const GemvPlan& p
 
 // The kernels.  q35k_decode_kernel takes every launch plan (up to 20 warps).
 // One- and two-token launches of at most GEMV_SPLIT_WARPS warps (whole rows of
-// up to 10 tiles, split-K units) run q35k_decode_kernel_10w instead, whose
+// up to 10 tiles, split-K units) whose grid fits three CTAs per SM, or whose
+// shared memory allows no more, run q35k_decode_kernel_10w instead, whose
 // bounds (three 10-warp CTAs per SM) let the compiler keep more of the decode
 // in registers.
 template <int TYPE, int M, bool FUSED, bool SPLIT>
@@ -413,6 +414,10 @@ GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     p.counters = (size_t)p.groups;
     p.fits = p.smem_bytes <= (size_t)GEMV_SMEM_LIMIT;
     p.threads = p.warps * 32;
+    // Shared memory per SM: 228 KB, 1 KB of it reserved per CTA.
+    const long smem_fit = 233472L / ((long)p.smem_bytes + 1024);
+    p.three_per_sm = m <= GEMV_FUSED_MAX_TOKENS && p.warps <= GEMV_SPLIT_WARPS &&
+                     (smem_fit <= 3 || (long)p.grid <= 3L * num_sms);
     return p;
 }
 
@@ -464,12 +469,13 @@ void configure_gemv_kernels() {
 }
 
 // Whole-row units (one unit per row group) run an instantiation without the
-// split-K code; one- and two-token units of at most GEMV_SPLIT_WARPS warps the
-// kernel with the larger register budget.
+// split-K code; plans with three_per_sm the kernel with the larger register
+// budget (a plan that would fit four CTAs per SM and needs them keeps the
+// other).
 template <int TYPE, int M, bool FUSED, bool SPLIT>
 static cudaError_t launch_variant(cudaLaunchConfig_t& cfg, const GemvArgs& a, const GemvPlan& p) {
     if constexpr (M <= GEMV_FUSED_MAX_TOKENS)
-        if (p.warps <= GEMV_SPLIT_WARPS) return cudaLaunchKernelEx(&cfg, q35k_decode_kernel_10w<TYPE, M, FUSED, SPLIT>, a, p);
+        if (p.three_per_sm) return cudaLaunchKernelEx(&cfg, q35k_decode_kernel_10w<TYPE, M, FUSED, SPLIT>, a, p);
     return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, FUSED, SPLIT>, a, p);
 }
 

@@ -100,6 +100,10 @@ struct GemvPlan {
     int cluster;
     size_t smem_bytes, partial_bytes, counters;
     bool fits;
+    // Run the kernel variant bounded at three 10-warp CTAs per SM (more
+    // registers per thread): one or two tokens, at most 10 warps, and three
+    // CTAs per SM already the limit (shared memory) or enough for the grid.
+    bool three_per_sm;
 };
 GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms);
 // Largest token count per GEMV launch for nb super-blocks per row (0: the
