@@ -79,7 +79,9 @@ def test_shard_device_pointer_path(ctx):
 
 @pytest.mark.parametrize("ndev", [2, 4, 8])
 @pytest.mark.parametrize("qt,k,n,m", [(Q4_K, 5120, 27648, 1), (Q4_K, 5120, 27648, 8), (Q6_K, 2560, 151936, 1),
-                                      (Q4_K, 2560, 9728, 512), (Q5_K, 1024, 1000, 3)])
+                                      (Q4_K, 2560, 9728, 512), (Q5_K, 1024, 1000, 3),
+                                      # 108 row groups per rank at 2 GPUs (cfg4's share at 8): split-K clusters
+                                      (Q4_K, 5120, 6912, 1), (Q4_K, 5120, 6912, 8)])
 @pytest.mark.parametrize("mode", [q35k.GATHER_NCCL, q35k.GATHER_PEER, q35k.GATHER_FUSED])
 def test_multi_gpu_group(ctx, oracle_mod, ndev, qt, k, n, m, mode):
     if _ngpus() < ndev:
