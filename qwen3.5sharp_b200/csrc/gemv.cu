@@ -375,6 +375,14 @@ __global__ void __launch_bounds__(GEMV_SPLIT_WARPS * 32, 3) q35k_decode_kernel_1
     decode_body<TYPE, M, FUSED, SPLIT>(a, p);
 }
 
+// Q4_K whole rows of 11..20 tiles at one or two tokens: 20-warp CTAs bounded at
+// two per SM (48 registers; without the bound the two-token form takes 53-56
+// and only one CTA fits an SM).
+template <int TYPE, int M, bool FUSED>
+__global__ void __launch_bounds__(GEMV_MAX_WARPS * 32, 2) q35k_decode_kernel_20w(GemvArgs a, GemvPlan p) {
+    decode_body<TYPE, M, FUSED, false>(a, p);
+}
+
 GemvPlan plan_gemv(int type, int nb, int n_out, int tokens, int num_sms) {
     GemvPlan p{};
     const int tile = TILE_ROWS * block_bytes(type);
@@ -441,6 +449,9 @@ static void configure_fused() {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
         cudaFuncSetAttribute(q35k_decode_kernel_10w<TYPE, M, FUSED, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_LIMIT);
+        if constexpr (TYPE == TYPE_Q4_K)
+            cudaFuncSetAttribute(q35k_decode_kernel_20w<TYPE, M, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GEMV_SMEM_LIMIT);
     }
 }
 
@@ -476,6 +487,8 @@ template <int TYPE, int M, bool FUSED, bool SPLIT>
 static cudaError_t launch_variant(cudaLaunchConfig_t& cfg, const GemvArgs& a, const GemvPlan& p) {
     if constexpr (M <= GEMV_FUSED_MAX_TOKENS)
         if (p.three_per_sm) return cudaLaunchKernelEx(&cfg, q35k_decode_kernel_10w<TYPE, M, FUSED, SPLIT>, a, p);
+    if constexpr (M <= GEMV_FUSED_MAX_TOKENS && !SPLIT && TYPE == TYPE_Q4_K)
+        if (p.warps > GEMV_SPLIT_WARPS) return cudaLaunchKernelEx(&cfg, q35k_decode_kernel_20w<TYPE, M, FUSED>, a, p);
     return cudaLaunchKernelEx(&cfg, q35k_decode_kernel<TYPE, M, FUSED, SPLIT>, a, p);
 }
 

@@ -166,6 +166,23 @@ def test_split_k_reductions(ctx, oracle_mod, n, m):
     assert np.array_equal(ctx.matmul(W, x).view(np.uint32), y.view(np.uint32))
 
 
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("m", [1, 2])
+def test_wide_whole_row_units(ctx, oracle_mod, qt, m):
+    """Whole-row units of 11 to 20 tiles (one warp per tile, 20-warp CTAs) at
+    one and two tokens, against the oracle and through the pre-quantized path."""
+    k = {Q4_K: 5120, Q5_K: 4096, Q6_K: 3584}[qt]
+    n = 148 * 32 + 17  # at least one row group per SM (whole rows), ragged end
+    w = synth.kquant_blocks(qt, n, k, seed=31)
+    x = synth.activations(m, k, seed=32)
+    W = ctx.upload(qt, w, k, n)
+    y = ctx.matmul(W, x)
+    ref = oracle_mod.Weight(qt, w, k, n).matmul(x, threads=os.cpu_count() or 1)
+    assert rel_err(y, ref) <= TOL
+    y2 = ctx.matmul_q8k(W, oracle_mod.quantize_q8k(x), m)
+    assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))
+
+
 def test_device_pointer_path(ctx, oracle_mod):
     torch = pytest.importorskip("torch")
     qt, k, n, m = Q4_K, 2560, 1000, 3
