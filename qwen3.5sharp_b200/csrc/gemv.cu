@@ -482,7 +482,8 @@ void configure_gemv_kernels() {
 // Whole-row units (one unit per row group) run an instantiation without the
 // split-K code; plans with three_per_sm the kernel with the larger register
 // budget (a plan that would fit four CTAs per SM and needs them keeps the
-// other).
+// other); Q4_K whole rows of more than 10 warps at one or two tokens the
+// 20-warp kernel bounded at two CTAs per SM.
 template <int TYPE, int M, bool FUSED, bool SPLIT>
 static cudaError_t launch_variant(cudaLaunchConfig_t& cfg, const GemvArgs& a, const GemvPlan& p) {
     if constexpr (M <= GEMV_FUSED_MAX_TOKENS)
