@@ -1,6 +1,6 @@
 """GPU parity of libq35k against the CPU oracle, through the C ABI.
 
-Bars (SURVEY-independent statement of the contract):
+Bars (the parity contract of this library):
   * Q8_K bytes (qs, d bits, bsums) and dequantized weights: bit-exact;
   * y: max|y - r| / max|r| <= 1e-3 against the oracle's restatement of the
     reference's executed AVX2 path (the exact-integer design lands ~1e-6).
